@@ -1,0 +1,300 @@
+"""ctypes bindings of libatt1_b200.so (the C ABI in include/*.h).
+
+This is a thin host-side mirror of the ATT-1 C API for Python callers (the
+tests and bench.py): the same function names, argument meaning and status
+codes. All compute happens in the library's sm_100a kernels; there is no
+Python or CPU fallback - loading fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libatt1_b200.so")
+
+ATT1_OK = 0
+STATUS = {0: "OK", -1: "INVALID_ARG", -2: "OOM", -3: "IO", -4: "BAD_FORMAT", -5: "NOT_FOUND",
+          -6: "SHAPE", -7: "QUEUE_FULL", -8: "STATE", -9: "UNSUPPORTED", -10: "QUEUE_EMPTY",
+          -11: "TIMEOUT", -12: "ALREADY_STARTED"}
+WQ, WK, WV, WO, GATE, UP, DOWN, OUTPUT = 1, 2, 3, 4, 6, 7, 8, 9
+EPI_STORE, EPI_RESID, EPI_QKV, EPI_SWIGLU, EPI_LOGITS = range(5)
+ROWS_PLAIN, ROWS_GATEUP = 0, 1
+
+
+class Att1Error(RuntimeError):
+    def __init__(self, fn, rc):
+        super().__init__(f"{fn} failed: {STATUS.get(rc, rc)}")
+        self.rc = rc
+
+
+class Config(C.Structure):
+    """att1_b200_config (include/att1_b200.h)."""
+
+    _fields_ = [
+        ("vocab", C.c_uint32), ("n_layers", C.c_uint32), ("n_heads", C.c_uint32),
+        ("n_kv_heads", C.c_uint32), ("d_model", C.c_uint32), ("d_ff", C.c_uint32),
+        ("max_seq", C.c_uint32), ("group", C.c_uint32), ("dtype", C.c_uint32),
+        ("eps", C.c_float), ("final_eps", C.c_float), ("theta", C.c_float),
+    ]
+
+    @classmethod
+    def make(cls, vocab, n_layers, n_heads, n_kv_heads, d_model, d_ff, max_seq,
+             dtype=4, group=32, eps=1e-5, final_eps=None, theta=10000.0):
+        return cls(vocab, n_layers, n_heads, n_kv_heads, d_model, d_ff, max_seq, group, dtype,
+                   eps, eps if final_eps is None else final_eps, theta)
+
+
+class QWeight(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("row_scale", C.c_void_p), ("format", C.c_uint32),
+                ("rows", C.c_uint32), ("cols", C.c_uint32), ("tiles", C.c_uint32),
+                ("kunits", C.c_uint32)]
+
+
+class KVLayout(C.Structure):
+    _fields_ = [("k_pool", C.c_void_p), ("v_pool", C.c_void_p), ("page_table", C.c_void_p),
+                ("page_tokens", C.c_uint32), ("pages_per_seq", C.c_uint32),
+                ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32)]
+
+
+class GemvArgs(C.Structure):
+    _fields_ = [("w", QWeight), ("batch", C.c_uint32), ("x", C.c_void_p), ("x_stride", C.c_uint32),
+                ("norm_w", C.c_void_p), ("eps", C.c_float), ("epilogue", C.c_int),
+                ("out", C.c_void_p), ("out_stride", C.c_uint32), ("resid", C.c_void_p),
+                ("q_rows", C.c_uint32), ("kv_rows", C.c_uint32), ("rope_freq", C.c_void_p),
+                ("positions", C.c_void_p), ("kv", KVLayout), ("argmax", C.c_void_p),
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("err", C.c_void_p),
+                ("pdl", C.c_int), ("grid", C.c_int)]
+
+
+class AttnArgs(C.Structure):
+    _fields_ = [("batch", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("q", C.c_void_p), ("kv", KVLayout),
+                ("positions", C.c_void_p), ("max_ctx", C.c_uint32), ("ctx", C.c_void_p),
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("err", C.c_void_p),
+                ("pdl", C.c_int)]
+
+
+class ModelTensor(C.Structure):
+    _fields_ = [("name", C.c_char * 64), ("dtype", C.c_uint32), ("ndims", C.c_uint32),
+                ("shape", C.c_uint64 * 4), ("offset", C.c_uint64), ("nbytes", C.c_uint64),
+                ("shard_id", C.c_uint32), ("flags", C.c_uint32), ("data", C.c_void_p)]
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("vocab_size", "n_layers", "n_heads", "d_model", "d_ff",
+                                          "max_seq_len", "rope_dim", "n_tiles", "shard_count")]
+
+
+class Model(C.Structure):
+    _fields_ = [("config", ModelConfig), ("tensor_count", C.c_uint64),
+                ("tensors", C.POINTER(ModelTensor)), ("file_data", C.c_void_p),
+                ("file_size", C.c_size_t)]
+
+
+class TraceCounters(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in (
+        "tokens_decoded", "token_time_us_total", "token_time_us_max", "layer_time_us_total",
+        "activation_bytes_sent", "logits_bytes_produced", "fabric_packets_sent",
+        "fabric_packets_received", "fabric_payload_bytes_sent", "fabric_payload_bytes_received",
+        "kv_appends", "kv_key_reads", "kv_value_reads", "tile_layer_executions")]
+
+
+class ClusterConfig(C.Structure):
+    _fields_ = [("tile_count", C.c_size_t), ("fabric_queue_capacity", C.c_size_t),
+                ("fabric_max_payload_bytes", C.c_size_t), ("shard_plan_mode", C.c_int)]
+
+
+_P = C.c_void_p
+_U32 = C.c_uint32
+_SZ = C.c_size_t
+_F = C.c_float
+
+_SIGS = {
+    # model / infer API (att1_model.h, att1_infer.h)
+    "att1_model_load": (C.c_int, [C.c_char_p, C.POINTER(Model)]),
+    "att1_model_free": (None, [C.POINTER(Model)]),
+    "att1_model_find_tensor": (C.POINTER(ModelTensor), [C.POINTER(Model), C.c_char_p]),
+    "att1_infer_create": (C.c_int, [C.POINTER(Model), C.POINTER(_P)]),
+    "att1_infer_create_q4": (C.c_int, [C.POINTER(Model), C.POINTER(_P)]),
+    "att1_infer_destroy": (None, [_P]),
+    "att1_infer_decode_token": (C.c_int, [_P, _U32, C.POINTER(_U32)]),
+    "att1_infer_generate": (C.c_int, [_P, C.c_char_p, _SZ, _SZ, C.POINTER(_U32), _SZ, C.POINTER(_SZ)]),
+    "att1_infer_logits": (C.POINTER(_F), [_P, C.POINTER(_SZ)]),
+    "att1_infer_position": (C.c_int, [_P, C.POINTER(_SZ)]),
+    "att1_infer_layer_kv_length": (C.c_int, [_P, _U32, C.POINTER(_SZ)]),
+    "att1_infer_set_trace": (C.c_int, [_P, _P]),
+    "att1_infer_set_backend": (C.c_int, [_P, _P]),
+    # additions (att1_b200.h)
+    "att1_b200_infer_create_synth": (C.c_int, [C.POINTER(Config), C.c_uint64, _U32, C.POINTER(_P)]),
+    "att1_b200_infer_create_model": (C.c_int, [C.POINTER(Model), _U32, _F, _F, _F, C.POINTER(_P)]),
+    "att1_b200_infer_batch": (_U32, [_P]),
+    "att1_b200_infer_decode_batch": (C.c_int, [_P, C.POINTER(_U32), C.POINTER(_U32)]),
+    "att1_b200_infer_logits_batch": (C.POINTER(_F), [_P, C.POINTER(_SZ)]),
+    "att1_b200_infer_set_options": (C.c_int, [_P, C.c_int, C.c_int]),
+    "att1_b200_infer_run_steps": (C.c_int, [_P, _U32]),
+    "att1_b200_infer_sync": (C.c_int, [_P]),
+    "att1_b200_infer_stream": (_P, [_P]),
+    "att1_b200_infer_export_q4": (C.c_int, [_P, _U32, _U32, _P, _P]),
+    "att1_b200_infer_export_q8": (C.c_int, [_P, _U32, _U32, _P, _P]),
+    "att1_b200_infer_export_kv": (C.c_int, [_P, _U32, _U32, _SZ, _P, _P]),
+    "att1_b200_infer_device_bytes": (_SZ, [_P]),
+    # backend vtable (att1_backend.h)
+    "att1_backend_cuda_available": (C.c_int, []),
+    "att1_backend_cuda_create": (C.c_int, [C.POINTER(_P)]),
+    "att1_backend_cuda_q8_create": (C.c_int, [C.POINTER(_P)]),
+    "att1_backend_cuda_q4_create": (C.c_int, [C.POINTER(_P)]),
+    "att1_backend_default_create": (C.c_int, [C.POINTER(_P)]),
+    "att1_backend_destroy": (None, [_P]),
+    # trace
+    "att1_trace_create": (C.c_int, [_SZ, _SZ, C.POINTER(_P)]),
+    "att1_trace_destroy": (None, [_P]),
+    "att1_trace_snapshot": (C.c_int, [_P, C.POINTER(TraceCounters)]),
+    # cluster
+    "att1_cluster_infer_create_q4": (C.c_int, [C.POINTER(Model), C.POINTER(ClusterConfig), C.POINTER(_P)]),
+    "att1_cluster_infer_create": (C.c_int, [C.POINTER(Model), C.POINTER(ClusterConfig), C.POINTER(_P)]),
+    "att1_cluster_infer_destroy": (None, [_P]),
+    "att1_cluster_infer_decode_token": (C.c_int, [_P, _U32, C.POINTER(_U32)]),
+    "att1_cluster_infer_logits": (C.POINTER(_F), [_P, C.POINTER(_SZ)]),
+    # kernel ABI (b2_kernels.h)
+    "b2_q4_bytes": (_SZ, [_U32, _U32]),
+    "b2_q8_bytes": (_SZ, [_U32, _U32]),
+    "b2_q4_pack": (C.c_int, [_P, _U32, _U32, _U32, _P, _P, _P, _P, _U32, C.c_int, _P]),
+    "b2_q4_unpack": (C.c_int, [_P, _P, _P, _U32, _U32, _U32, C.c_int, C.c_int, _P]),
+    "b2_q4_synth": (C.c_int, [_P, _U32, _U32, _U32, C.c_uint64, C.c_uint64, C.c_uint64, _F, C.c_int, _P]),
+    "b2_q8_pack": (C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P, _P, _P, C.c_int, _P]),
+    "b2_q8_unpack": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _U32, C.c_int, C.c_int, _P]),
+    "b2_q8_synth": (C.c_int, [_P, _P, _U32, _U32, _U32, C.c_uint64, C.c_uint64, C.c_uint64, _F, C.c_int, _P]),
+    "b2_q8_quantize_f32": (C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P, C.c_int, C.c_int, _P]),
+    "b2_synth_f32": (C.c_int, [_P, _SZ, C.c_uint64, C.c_uint64, _F, _P]),
+    "b2_gemv_scratch_bytes": (_SZ, [C.POINTER(GemvArgs)]),
+    "b2_gemv": (C.c_int, [C.POINTER(GemvArgs), _P]),
+    "b2_attn_scratch_bytes": (_SZ, [C.POINTER(AttnArgs)]),
+    "b2_attn": (C.c_int, [C.POINTER(AttnArgs), _P]),
+    "b2_rmsnorm": (C.c_int, [_P, _P, _P, _U32, _F, _P]),
+    "b2_softmax": (C.c_int, [_P, _U32, _P]),
+    "b2_rope": (C.c_int, [_P, _U32, _U32, _F, _P]),
+    "b2_swiglu": (C.c_int, [_P, _P, _P, _U32, _P]),
+    "b2_argmax": (C.c_int, [_P, _U32, _P, _P]),
+    "b2_sm_count": (C.c_int, []),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libatt1_b200.so (built by att-1_b200/build.py); raise if missing."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python att-1_b200/build.py`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(fn: str, rc: int) -> None:
+    if rc != ATT1_OK:
+        raise Att1Error(fn, rc)
+
+
+def _ptr(a) -> int:
+    """Device or host address of a torch tensor / numpy array."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+class Infer:
+    """Owner of an att1_infer_t (single device)."""
+
+    def __init__(self, handle: int, vocab: int, batch: int):
+        self.h = C.c_void_p(handle)
+        self.vocab = vocab
+        self.batch = batch
+
+    @classmethod
+    def synth(cls, cfg: Config, seed: int, batch: int = 1) -> "Infer":
+        h = C.c_void_p()
+        check("att1_b200_infer_create_synth",
+              lib().att1_b200_infer_create_synth(C.byref(cfg), seed, batch, C.byref(h)))
+        return cls(h.value, cfg.vocab, batch)
+
+    def close(self):
+        if self.h and self.h.value:
+            lib().att1_infer_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def decode(self, token: int) -> int:
+        out = C.c_uint32(0)
+        check("att1_infer_decode_token", lib().att1_infer_decode_token(self.h, int(token), C.byref(out)))
+        return int(out.value)
+
+    def decode_batch(self, tokens) -> np.ndarray:
+        t = (C.c_uint32 * self.batch)(*[int(x) for x in tokens])
+        o = (C.c_uint32 * self.batch)()
+        check("att1_b200_infer_decode_batch", lib().att1_b200_infer_decode_batch(self.h, t, o))
+        return np.array(o[:], np.uint32)
+
+    def logits(self) -> np.ndarray:
+        n = C.c_size_t(0)
+        p = lib().att1_b200_infer_logits_batch(self.h, C.byref(n))
+        if not p:
+            raise Att1Error("att1_b200_infer_logits_batch", -8)
+        return np.ctypeslib.as_array(p, (n.value,)).reshape(self.batch, self.vocab).copy()
+
+    def position(self) -> int:
+        n = C.c_size_t(0)
+        check("att1_infer_position", lib().att1_infer_position(self.h, C.byref(n)))
+        return n.value
+
+    def set_options(self, graph=True, pdl=True):
+        check("att1_b200_infer_set_options", lib().att1_b200_infer_set_options(self.h, int(graph), int(pdl)))
+
+    def run_steps(self, n: int):
+        check("att1_b200_infer_run_steps", lib().att1_b200_infer_run_steps(self.h, n))
+
+    def sync(self):
+        check("att1_b200_infer_sync", lib().att1_b200_infer_sync(self.h))
+
+    def stream(self) -> int:
+        return lib().att1_b200_infer_stream(self.h)
+
+    def export_q4(self, layer: int, kind: int, rows: int, cols: int):
+        packed = np.zeros(rows * cols // 2, np.uint8)
+        scales = np.zeros(rows * (cols // 32), np.float32)
+        check("att1_b200_infer_export_q4",
+              lib().att1_b200_infer_export_q4(self.h, layer, kind, packed.ctypes.data, scales.ctypes.data))
+        return packed, scales
+
+    def export_q8(self, layer: int, kind: int, rows: int, cols: int):
+        values = np.zeros(rows * cols, np.int8)
+        scales = np.zeros(rows, np.float32)
+        check("att1_b200_infer_export_q8",
+              lib().att1_b200_infer_export_q8(self.h, layer, kind, values.ctypes.data, scales.ctypes.data))
+        return values, scales
+
+    def export_kv(self, item: int, layer: int, count: int, row: int):
+        k = np.zeros(count * row, np.float32)
+        v = np.zeros(count * row, np.float32)
+        check("att1_b200_infer_export_kv",
+              lib().att1_b200_infer_export_kv(self.h, item, layer, count, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def device_bytes(self) -> int:
+        return lib().att1_b200_infer_device_bytes(self.h)

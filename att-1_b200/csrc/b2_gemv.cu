@@ -1,0 +1,627 @@
+// b2_gemv.cu - q4/q8 block-dequant matrix-vector products for decode.
+//
+// Replaces att1_matmul_q4xf32 (src/quant.c:340-393) and att1_matmul_q8xf32
+// (src/matmul_q8.c:3-40) on the device, with the neighbouring element ops of
+// the block (src/transformer_block.c:417-557) fused in:
+//   prologue: optional RMSNorm (src/norm.c:5-34) of the input vector;
+//   epilogue: plain store, residual add, RoPE + KV-page append
+//             (src/attention.c:490-504), SwiGLU (src/ffn.c:10-30), or logits
+//             with the greedy argmax key (src/sampler.c:5-34).
+//
+// Arithmetic. Batch-1 decode reads every weight byte once, so the kernel is
+// HBM-bound; the design spends as few instructions per weight as possible:
+//   * the input vector x (f32) is written, per item, as an exact 22-bit fixed
+//     point number v = round(x * 2^-E) split into three signed byte digits
+//     (v = d0 + 256 d1 + 65536 d2); E is chosen from max|x| so |v| <= 2^22;
+//   * a q4 byte holding nibbles (a, b) yields the int8 values 16a and 16b with
+//     one shift and one AND each (a nibble in the top half of a byte is its
+//     two's-complement value times 16), q8 bytes are used as they are;
+//   * mma.sync m16n8k32 s8 x s8 -> s32 multiplies a 16x32 weight block with
+//     the digit columns exactly in integers; one group (32 columns) per MMA,
+//     so the per-group q4 scale is applied once per 32 weights in f32.
+// Products are exact; rounding happens only in the f32 scale/accumulate steps
+// and in the 2^-22 relative quantisation of x, far inside the 1e-3 logits
+// tolerance of the parity tests.
+//
+// Streaming. Weights sit in the unit layout of b2_kernels.h. Each warp owns a
+// contiguous range of units (stream-K over tile-major units, balanced to one
+// unit across the whole grid) and streams it through a private ring of
+// shared-memory slots filled by 1-D bulk copies (cp.async.bulk + mbarrier).
+// A tile shared by several warps is reduced by the last warp to finish it
+// (per-tile arrival counter), summing the partials in warp order, so results
+// are deterministic. Weight prefetch is issued before griddepcontrol.wait, so
+// under programmatic dependent launch it overlaps the previous kernel's tail.
+#include "b2_common.cuh"
+
+#include <cfloat>
+#include <cstdio>
+#include <cuda_runtime.h>
+
+namespace b2 {
+
+constexpr int kWarps = 8;        // consumer warps per CTA (each streams its own range)
+constexpr int kSlots = 4;        // ring slots per warp
+constexpr int kUnitsPerSlot = 2; // units per bulk copy
+constexpr int kMaxItems = 16;
+
+struct GemvParams {
+    const uint8_t *data;
+    const float *row_scale;
+    uint32_t rows, cols, tiles, kunits;
+    uint32_t batch;
+    const float *x;
+    uint32_t x_stride;
+    const float *norm_w;
+    float eps;
+    int epilogue;
+    float *out;
+    uint32_t out_stride;
+    const float *resid;
+    uint32_t q_rows, kv_rows;
+    const float *rope_freq;
+    const int32_t *positions;
+    b2_kv_layout kv;
+    unsigned long long *argmax;
+    float *partial;
+    int *counters;
+    uint32_t maxseg;
+    int32_t *err;
+    // shared-memory carve-up (bytes)
+    uint32_t off_ring, off_xdig, off_tile, off_misc;
+};
+
+template <int FMT>
+struct Fmt;
+template <>
+struct Fmt<4> {
+    static constexpr uint32_t kUnitBytes = B2_Q4_UNIT_BYTES;
+    static constexpr uint32_t kKW = 64;  // columns per unit
+};
+template <>
+struct Fmt<8> {
+    static constexpr uint32_t kUnitBytes = B2_Q8_UNIT_BYTES;
+    static constexpr uint32_t kKW = 32;
+};
+
+__device__ __forceinline__ uint32_t ordered_key(float f)
+{
+    uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
+template <int FMT>
+__device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
+{
+    constexpr uint32_t KW = Fmt<FMT>::kKW;
+    const uint32_t cols = p.cols;
+    for (uint32_t b = 0; b < p.batch; ++b) {
+        const float *xb = p.x + (size_t)b * p.x_stride;
+        float inv = 1.0f;
+        if (p.norm_w != nullptr) {
+            float ss = 0.0f;
+            for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
+                const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+            ss = block_sum(ss, red);
+            // src/norm.c:26-28
+            inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
+        }
+        float m = 0.0f;
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
+            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            if (p.norm_w != nullptr) {
+                const float4 w = *reinterpret_cast<const float4 *>(p.norm_w + k);
+                v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
+                v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
+                v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
+                v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
+            }
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            // a NaN compares false in fmaxf; detect it explicitly
+            if (!(fabsf(v.x) <= FLT_MAX && fabsf(v.y) <= FLT_MAX && fabsf(v.z) <= FLT_MAX &&
+                  fabsf(v.w) <= FLT_MAX))
+                m = INFINITY;
+        }
+        m = block_max(m, red);
+        int E = 0;
+        if (!(m <= FLT_MAX)) {
+            if (threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
+        } else if (m > 0.0f) {
+            E = ilogbf(m) - 21;
+            if (E < -125) E = -125;
+        }
+        const float sc = ldexpf(1.0f, -E);
+        if (threadIdx.x == 0) item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
+            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            if (p.norm_w != nullptr) {
+                const float4 w = *reinterpret_cast<const float4 *>(p.norm_w + k);
+                v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
+                v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
+                v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
+                v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
+            }
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                int q = (m <= FLT_MAX) ? __float2int_rn(__fmul_rn(vv[i], sc)) : 0;
+                const int d0 = ((q + 128) & 255) - 128;
+                const int q1 = (q - d0) >> 8;
+                const int d1 = ((q1 + 128) & 255) - 128;
+                const int d2 = (q1 - d1) >> 8;
+                w0 |= ((uint32_t)d0 & 0xFFu) << (8 * i);
+                w1 |= ((uint32_t)d1 & 0xFFu) << (8 * i);
+                w2 |= ((uint32_t)d2 & 0xFFu) << (8 * i);
+            }
+            const uint32_t unit = k / KW, kk = k % KW;
+            const uint32_t gi = kk >> 5, r = kk & 31;
+            const uint32_t half = r >> 4, t = (r & 15) >> 2;
+            uint8_t *base = xdig + ((size_t)(unit * p.batch + b) * 3) * KW + t * (KW / 4) + gi * 8 + half * 4;
+            *reinterpret_cast<uint32_t *>(base) = w0;
+            *reinterpret_cast<uint32_t *>(base + KW) = w1;
+            *reinterpret_cast<uint32_t *>(base + 2 * KW) = w2;
+        }
+    }
+}
+
+// ---- epilogue on one finished 16-row tile held in shared memory [16][batch] --
+__device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const float *tb, unsigned long long *cta_key,
+                              int lane)
+{
+    const uint32_t B = p.batch;
+    // uniform trip count: every lane takes part in the shuffles of LOGITS
+    for (uint32_t base = 0; base < 16 * B; base += 32) {
+        const uint32_t idx = base + lane;
+        const bool valid = idx < 16 * B;
+        const uint32_t r = idx & 15, item = valid ? (idx >> 4) : 0;
+        const uint32_t row = valid ? tile * 16 + r : 0xFFFFFFFFu;
+        const float v = valid ? tb[r * B + item] : 0.0f;
+        if (!valid && p.epilogue != B2_EPI_LOGITS) continue;
+        switch (p.epilogue) {
+        case B2_EPI_STORE:
+            if (row < p.rows) p.out[(size_t)item * p.out_stride + row] = v;
+            break;
+        case B2_EPI_RESID:
+            if (row < p.rows) {
+                const size_t o = (size_t)item * p.out_stride + row;
+                p.out[o] = __fadd_rn(__ldcg(p.resid + o), v);  // src/transformer_block.c:63-72
+            }
+            break;
+        case B2_EPI_QKV: {
+            if (row >= p.rows) break;
+            const uint32_t hd = p.kv.head_dim;
+            const int32_t pos = p.positions[item];
+            const uint32_t cap = p.kv.pages_per_seq * p.kv.page_tokens;
+            if (row < p.q_rows + p.kv_rows) {
+                // RoPE on q and k (src/rope.c:20-30): interleaved pairs of a head
+                const uint32_t rr = row < p.q_rows ? row : row - p.q_rows;
+                const uint32_t i = rr % hd;
+                const float x0 = tb[(r & ~1u) * B + item], x1 = tb[(r | 1u) * B + item];
+                const float ang = __fmul_rn((float)pos, p.rope_freq[i >> 1]);
+                float s, c;
+                sincosf(ang, &s, &c);
+                const float y = (i & 1u) ? __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c))
+                                         : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                if (row < p.q_rows) {
+                    p.out[(size_t)item * p.out_stride + row] = y;
+                } else if (pos >= 0 && (uint32_t)pos < cap) {
+                    const int32_t page = p.kv.page_table[(size_t)item * p.kv.pages_per_seq + pos / p.kv.page_tokens];
+                    const size_t slot = (size_t)page * p.kv.page_tokens + pos % p.kv.page_tokens;
+                    p.kv.k_pool[slot * p.kv.n_kv_heads * hd + rr] = y;
+                } else {
+                    raise_error(p.err, B2_ERR_POSITION);
+                }
+            } else {
+                const uint32_t rr = row - p.q_rows - p.kv_rows;
+                if (pos >= 0 && (uint32_t)pos < cap) {
+                    const int32_t page = p.kv.page_table[(size_t)item * p.kv.pages_per_seq + pos / p.kv.page_tokens];
+                    const size_t slot = (size_t)page * p.kv.page_tokens + pos % p.kv.page_tokens;
+                    p.kv.v_pool[slot * p.kv.n_kv_heads * hd + rr] = v;
+                } else {
+                    raise_error(p.err, B2_ERR_POSITION);
+                }
+            }
+            break;
+        }
+        case B2_EPI_SWIGLU:
+            if (r < 8) {
+                const uint32_t j = tile * 8 + r;
+                if (j < p.rows / 2) {
+                    const float g = v, u = tb[(r + 8) * B + item];
+                    // src/ffn.c:7 silu(g) = g / (1 + expf(-g)); then * up
+                    p.out[(size_t)item * p.out_stride + j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                }
+            }
+            break;
+        case B2_EPI_LOGITS: {
+            unsigned long long key = 0ull;
+            if (row < p.rows) {
+                p.out[(size_t)item * p.out_stride + row] = v;
+                if (v != v) {
+                    raise_error(p.err, B2_ERR_NAN_LOGITS);
+                } else {
+                    key = ((unsigned long long)ordered_key(v) << 32) | (0xFFFFFFFFu - row);
+                }
+            }
+            // max over the 16 lanes of this item (lanes 16*k .. 16*k+15)
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            if ((lane & 15) == 0 && valid) atomicMax(&cta_key[item], key);
+            break;
+        }
+        default:
+            break;
+        }
+    }
+}
+
+template <int FMT, int NI>
+__global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(const GemvParams p)
+{
+    constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
+    constexpr uint32_t KW = Fmt<FMT>::kKW;
+    extern __shared__ __align__(128) uint8_t smem[];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kSlots;
+    uint8_t *ring = smem + p.off_ring + (size_t)warp * kSlots * kUnitsPerSlot * UB;
+    uint8_t *xdig = smem + p.off_xdig;
+    float *tbuf = reinterpret_cast<float *>(smem + p.off_tile) + (size_t)warp * 16 * p.batch;
+    float *red = reinterpret_cast<float *>(smem + p.off_misc);            // 32 floats
+    float *item_scale = red + 32;                                          // 16 floats
+    unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);  // 16
+
+    // W active warps (never more than units, so every active warp owns >= 1
+    // unit and every warp that shares a tile arrives at its counter)
+    const uint64_t U = (uint64_t)p.tiles * p.kunits;
+    const uint64_t W = min((uint64_t)gridDim.x * kWarps, U);
+    const uint64_t w = (uint64_t)blockIdx.x * kWarps + warp;
+    const uint64_t ub = w < W ? w * U / W : U, ue = w < W ? (w + 1) * U / W : U;
+    const uint32_t nunits = (uint32_t)(ue - ub);
+    const uint32_t nchunks = (nunits + kUnitsPerSlot - 1) / kUnitsPerSlot;
+
+    if (lane == 0) {
+        for (int s = 0; s < kSlots; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
+    __syncwarp();
+    auto issue = [&](uint32_t c) {
+        const uint32_t s = c % kSlots;
+        const uint32_t u0 = c * kUnitsPerSlot;
+        const uint32_t n = min((uint32_t)kUnitsPerSlot, nunits - u0);
+        mbar_arrive_expect_tx(&bars[s], n * UB);
+        bulk_g2s(ring + (size_t)s * kUnitsPerSlot * UB, p.data + (ub + u0) * UB, n * UB, &bars[s]);
+    };
+    if (lane == 0) {
+        for (uint32_t c = 0; c < nchunks && c < (uint32_t)kSlots; ++c) issue(c);
+    }
+
+    // inputs produced by the previous kernel are read only after this point
+    pdl_wait();
+    pdl_launch_dependents();
+    prepare_x<FMT>(p, xdig, item_scale, red);
+    __syncthreads();
+
+    // per-lane B-fragment coordinates: column g -> (item pair j, item, digit)
+    const uint32_t digit = g & 3;
+    float acc[NI][2];
+    int iacc[NI][4];
+#pragma unroll
+    for (int j = 0; j < NI; ++j) {
+        acc[j][0] = acc[j][1] = 0.0f;
+        iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+    }
+
+    bool ok = true;
+    uint32_t cur_tile = nunits ? (uint32_t)(ub / p.kunits) : 0;
+
+    auto flush = [&](uint32_t tile) {
+        const uint32_t B = p.batch;
+        // tiles [wf, wl] hold the warps sharing this tile
+        const uint64_t u_first = (uint64_t)tile * p.kunits, u_last = u_first + p.kunits - 1;
+        const uint64_t wf = ((u_first + 1) * W - 1) / U, wl = ((u_last + 1) * W - 1) / U;
+        const uint32_t nseg = (uint32_t)(wl - wf + 1);
+        float *dst = (nseg == 1) ? tbuf : p.partial + ((size_t)tile * p.maxseg + (w - wf)) * 16 * B;
+#pragma unroll
+        for (int j = 0; j < NI; ++j) {
+            float v0, v1;
+            if (FMT == 4) {
+                v0 = acc[j][0];
+                v1 = acc[j][1];
+            } else {
+                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
+                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
+            }
+            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
+            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
+            const uint32_t item = 2 * j + (t >> 1);
+            if ((t & 1) == 0 && item < B) {
+                const float s = item_scale[item];
+                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
+                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+                if (FMT == 8) {
+                    y0 = __fmul_rn(y0, p.row_scale[tile * 16 + g]);
+                    y1 = __fmul_rn(y1, p.row_scale[tile * 16 + g + 8]);
+                }
+                dst[g * B + item] = y0;
+                dst[(g + 8) * B + item] = y1;
+            }
+            acc[j][0] = acc[j][1] = 0.0f;
+            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+        }
+        if (nseg > 1) {
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) return;
+            __threadfence();
+            const float *base = p.partial + (size_t)tile * p.maxseg * 16 * B;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+                float s = 0.0f;
+                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(base + (size_t)sg * 16 * B + idx));
+                tbuf[idx] = s;
+            }
+            if (lane == 0) p.counters[tile] = 0;
+        }
+        __syncwarp();
+        tile_epilogue(p, tile, tbuf, cta_key, lane);
+        __syncwarp();
+    };
+
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        const uint32_t s = c % kSlots;
+        const bool got = mbar_wait_bounded(&bars[s], (c / kSlots) & 1u, p.err);
+        if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            // drain copies still in flight into this warp's ring, with a bound
+            if (lane == 0) {
+                for (uint32_t c2 = c; c2 < nchunks && c2 < c + kSlots; ++c2)
+                    mbar_wait_bounded(&bars[c2 % kSlots], (c2 / kSlots) & 1u, p.err);
+            }
+            break;
+        }
+        const uint8_t *slot = ring + (size_t)s * kUnitsPerSlot * UB;
+        const uint32_t n = min((uint32_t)kUnitsPerSlot, nunits - c * kUnitsPerSlot);
+#pragma unroll
+        for (uint32_t k = 0; k < (uint32_t)kUnitsPerSlot; ++k) {
+            if (k < n) {
+                const uint64_t u = ub + (uint64_t)c * kUnitsPerSlot + k;
+                const uint32_t tile = (uint32_t)(u / p.kunits), ku = (uint32_t)(u % p.kunits);
+                if (tile != cur_tile) {
+                    flush(cur_tile);
+                    cur_tile = tile;
+                }
+                const uint8_t *unit = slot + (size_t)k * UB;
+                const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
+                if (FMT == 4) {
+                    const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
+                    const uint32_t M = 0xF0F0F0F0u;
+                    const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
+                    const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
+#pragma unroll
+                    for (int j = 0; j < NI; ++j) {
+                        const uint32_t item = 2 * j + (g >> 2);
+                        uint4 bf = make_uint4(0, 0, 0, 0);
+                        if (digit < 3 && item < p.batch)
+                            bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * p.batch + item) * 3 + digit) * KW + t * 16);
+                        int d[4], e[4];
+                        imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
+                        imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
+                        acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
+                        acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
+                        acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
+                        acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < NI; ++j) {
+                        const uint32_t item = 2 * j + (g >> 2);
+                        uint2 bf = make_uint2(0, 0);
+                        if (digit < 3 && item < p.batch)
+                            bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * p.batch + item) * 3 + digit) * KW + t * 8);
+                        imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                                   iacc[j][3]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && c + kSlots < nchunks) {
+            fence_proxy_async();
+            issue(c + kSlots);
+        }
+    }
+    if (ok && nunits > 0) flush(cur_tile);
+
+    if (p.epilogue == B2_EPI_LOGITS) {
+        __syncthreads();
+        if (threadIdx.x < p.batch && cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], cta_key[threadIdx.x]);
+    }
+}
+
+// ---- host side ------------------------------------------------------------------
+
+static int g_sm_count = 0;
+
+static int sm_count()
+{
+    if (g_sm_count == 0) {
+        int dev = 0, n = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return 148;
+        g_sm_count = n;
+    }
+    return g_sm_count;
+}
+
+struct GemvPlan {
+    int grid;
+    uint32_t maxseg;
+    size_t partial_bytes, counter_bytes;
+    uint32_t smem, off_ring, off_xdig, off_tile, off_misc;
+};
+
+static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
+{
+    const uint32_t fmt = a->w.format;
+    const uint32_t UB = fmt == 4 ? B2_Q4_UNIT_BYTES : B2_Q8_UNIT_BYTES;
+    const uint32_t KW = fmt == 4 ? 64u : 32u;
+    const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
+    if (U == 0) return false;
+    int grid = a->grid > 0 ? a->grid : sm_count();
+    const uint64_t want = (U + kWarps * 4 - 1) / (kWarps * 4);
+    if ((uint64_t)grid > want) grid = (int)(want > 0 ? want : 1);
+    pl.grid = grid;
+    uint64_t W = (uint64_t)grid * kWarps;
+    if (W > U) W = U;
+    const uint64_t minw = U / W;  // >= 1
+    uint64_t maxseg = (a->w.kunits + minw - 1) / minw + 1;
+    if (maxseg > a->w.kunits) maxseg = a->w.kunits;
+    pl.maxseg = (uint32_t)maxseg;
+    pl.partial_bytes = (size_t)a->w.tiles * maxseg * 16 * a->batch * sizeof(float);
+    pl.partial_bytes = (pl.partial_bytes + 255) & ~(size_t)255;
+    pl.counter_bytes = (size_t)a->w.tiles * sizeof(int);
+    uint32_t off = kWarps * kSlots * 8;
+    off = (off + 127) & ~127u;
+    pl.off_ring = off;
+    off += kWarps * kSlots * kUnitsPerSlot * UB;
+    pl.off_xdig = off;
+    off += a->w.kunits * a->batch * 3 * KW;
+    off = (off + 127) & ~127u;
+    pl.off_tile = off;
+    off += kWarps * 16 * a->batch * 4;
+    pl.off_misc = off;
+    off += (32 + kMaxItems) * 4 + kMaxItems * 8;
+    pl.smem = off;
+    return true;
+}
+
+template <int FMT, int NI>
+static cudaError_t launch_t(const GemvParams &p, const GemvPlan &pl, int pdl, cudaStream_t st)
+{
+    auto fn = gemv_kernel<FMT, NI>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, p);
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_sm_count(void) { return sm_count(); }
+
+extern "C" size_t b2_gemv_scratch_bytes(const b2_gemv_args *a)
+{
+    GemvPlan pl;
+    if (a == nullptr || a->batch == 0 || !plan_gemv(a, pl)) return 0;
+    return pl.partial_bytes + pl.counter_bytes;
+}
+
+extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
+{
+    if (a == nullptr || a->w.data == nullptr || a->x == nullptr || a->out == nullptr) return -1;
+    const b2_qweight &w = a->w;
+    if ((w.format != 4 && w.format != 8) || (w.format == 8 && w.row_scale == nullptr)) return -1;
+    if (a->batch == 0 || a->batch > kMaxItems || w.cols == 0 || w.cols % 32 || w.rows == 0) return -1;
+    if (w.tiles != (w.rows + 15) / 16 || w.kunits != (w.format == 4 ? (w.cols + 63) / 64 : (w.cols + 31) / 32)) return -1;
+    if (a->x_stride < w.cols || (a->x_stride & 3) || ((uintptr_t)a->x & 15)) return -1;
+    if (a->norm_w != nullptr && (((uintptr_t)a->norm_w & 15) || !(a->eps > 0.0f))) return -1;
+    if (((uintptr_t)w.data & 15)) return -1;
+    switch (a->epilogue) {
+    case B2_EPI_STORE:
+    case B2_EPI_LOGITS:
+        if (a->out_stride < w.rows) return -1;
+        if (a->epilogue == B2_EPI_LOGITS && a->argmax == nullptr) return -1;
+        break;
+    case B2_EPI_RESID:
+        if (a->out_stride < w.rows || a->resid == nullptr) return -1;
+        break;
+    case B2_EPI_SWIGLU:
+        if ((w.rows & 15) || a->out_stride < w.rows / 2) return -1;
+        break;
+    case B2_EPI_QKV: {
+        const b2_kv_layout &kv = a->kv;
+        if (!kv.k_pool || !kv.v_pool || !kv.page_table || !a->positions || !a->rope_freq) return -1;
+        if (kv.head_dim == 0 || kv.head_dim % 16 || kv.page_tokens == 0 || kv.pages_per_seq == 0) return -1;
+        if (a->q_rows % kv.head_dim || a->kv_rows != kv.n_kv_heads * kv.head_dim) return -1;
+        if (a->q_rows + 2 * a->kv_rows != w.rows || a->out_stride < a->q_rows) return -1;
+        break;
+    }
+    default:
+        return -1;
+    }
+    GemvPlan pl;
+    if (!plan_gemv(a, pl)) return -1;
+    if (pl.smem > 227 * 1024) return -9;  // batch x columns too large for on-chip digit planes
+    if (a->scratch == nullptr || a->scratch_bytes < pl.partial_bytes + pl.counter_bytes ||
+        ((uintptr_t)a->scratch & 255))
+        return -1;
+
+    GemvParams p = {};
+    p.data = (const uint8_t *)w.data;
+    p.row_scale = w.row_scale;
+    p.rows = w.rows;
+    p.cols = w.cols;
+    p.tiles = w.tiles;
+    p.kunits = w.kunits;
+    p.batch = a->batch;
+    p.x = a->x;
+    p.x_stride = a->x_stride;
+    p.norm_w = a->norm_w;
+    p.eps = a->eps;
+    p.epilogue = a->epilogue;
+    p.out = a->out;
+    p.out_stride = a->out_stride;
+    p.resid = a->resid;
+    p.q_rows = a->q_rows;
+    p.kv_rows = a->kv_rows;
+    p.rope_freq = a->rope_freq;
+    p.positions = a->positions;
+    p.kv = a->kv;
+    p.argmax = a->argmax;
+    p.partial = (float *)a->scratch;
+    p.counters = (int *)((uint8_t *)a->scratch + pl.partial_bytes);
+    p.maxseg = pl.maxseg;
+    p.err = a->err;
+    p.off_ring = pl.off_ring;
+    p.off_xdig = pl.off_xdig;
+    p.off_tile = pl.off_tile;
+    p.off_misc = pl.off_misc;
+
+    const int NI = (a->batch + 1) / 2;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    if (w.format == 4) {
+        if (NI <= 1) e = launch_t<4, 1>(p, pl, a->pdl, st);
+        else if (NI <= 2) e = launch_t<4, 2>(p, pl, a->pdl, st);
+        else if (NI <= 4) e = launch_t<4, 4>(p, pl, a->pdl, st);
+        else e = launch_t<4, 8>(p, pl, a->pdl, st);
+    } else {
+        if (NI <= 1) e = launch_t<8, 1>(p, pl, a->pdl, st);
+        else if (NI <= 2) e = launch_t<8, 2>(p, pl, a->pdl, st);
+        else if (NI <= 4) e = launch_t<8, 4>(p, pl, a->pdl, st);
+        else e = launch_t<8, 8>(p, pl, a->pdl, st);
+    }
+    return e == cudaSuccess ? 0 : -8;
+}

@@ -1,0 +1,220 @@
+// b2_ops.cu - per-token step kernels and the element ops of the backend vtable.
+//
+// step_begin: embedding row copy (src/infer.c:713-715) + argmax key reset.
+// step_end:   greedy token from the argmax key (src/sampler.c:5-34: lowest id
+//             wins ties), position advance (src/infer.c:878).
+// Element ops on device buffers, one per vtable slot of include/att1_backend.h:
+// rmsnorm (src/norm.c:5-34), softmax (src/norm.c:36-71), rope (src/rope.c:5-34),
+// swiglu (src/ffn.c:5-30), greedy argmax.
+#include "b2_common.cuh"
+
+#include <cfloat>
+#include <cuda_runtime.h>
+
+namespace b2 {
+
+static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, int pdl, cudaStream_t st, void **args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+__global__ void step_begin_kernel(const float *embed, uint32_t vocab, uint32_t d, const uint32_t *tokens, float *x,
+                                  unsigned long long *argmax, int32_t *err)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint32_t item = blockIdx.x;
+    const uint32_t tok = tokens[item];
+    float *xb = x + (size_t)item * d;
+    if (tok >= vocab) {
+        if (threadIdx.x == 0) raise_error(err, B2_ERR_TOKEN);
+        for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) xb[i] = 0.0f;
+    } else {
+        const float *row = embed + (size_t)tok * d;
+        for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) xb[i] = row[i];
+    }
+    if (threadIdx.x == 0) argmax[item] = 0ull;
+}
+
+__global__ void step_end_kernel(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens, int32_t *positions,
+                                int32_t *err)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint32_t item = threadIdx.x;
+    if (item >= batch) return;
+    const unsigned long long key = argmax[item];
+    if (key == 0ull) {
+        raise_error(err, B2_ERR_NAN_LOGITS);
+    } else {
+        tokens[item] = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
+    }
+    positions[item] += 1;
+}
+
+__global__ void rmsnorm_kernel(float *dst, const float *src, const float *w, uint32_t n, float eps)
+{
+    __shared__ float red[32];
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(src[i], src[i], ss);
+    ss = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __fmul_rn(__fmul_rn(src[i], inv), w[i]);
+}
+
+__global__ void softmax_kernel(float *v, uint32_t n)
+{
+    __shared__ float red[32];
+    float m = -INFINITY;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, v[i]);
+    m = block_max(m, red);
+    float s = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float e = expf(v[i] - m);
+        v[i] = e;
+        s += e;
+    }
+    s = block_sum(s, red);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) v[i] = __fdiv_rn(v[i], s);
+}
+
+__global__ void rope_kernel(float *v, uint32_t n, uint32_t pos, float theta)
+{
+    const uint32_t i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= n) return;
+    const float freq = __fdiv_rn(1.0f, powf(theta, __fdiv_rn((float)i, (float)n)));
+    const float ang = __fmul_rn((float)pos, freq);
+    float s, c;
+    sincosf(ang, &s, &c);
+    const float x0 = v[i], x1 = v[i + 1];
+    v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    v[i + 1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+__global__ void swiglu_kernel(float *dst, const float *g, const float *u, uint32_t n)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float x = g[i];
+        dst[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))), u[i]);
+    }
+}
+
+__device__ __forceinline__ uint32_t ordered_key32(float f)
+{
+    uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__global__ void argmax_kernel(const float *v, uint32_t n, unsigned long long *key)
+{
+    unsigned long long best = 0ull;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float f = v[i];
+        if (f != f) continue;  // NaN: leaves key at 0 when every value is NaN; caller checks separately
+        const unsigned long long k = ((unsigned long long)ordered_key32(f) << 32) | (0xFFFFFFFFu - i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0 && best != 0ull) atomicMax(key, best);
+}
+
+// dst[r][c] = sum_k lhs[r][k] * rhs[k][c], sequential over k per output
+// (src/matmul.c order); one thread per output element, rhs reads coalesced.
+__global__ void matmul_f32_kernel(float *dst, const float *lhs, const float *rhs, uint32_t rows, uint32_t cols,
+                                  uint32_t inner)
+{
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+    if (c >= cols) return;
+    float s = 0.0f;
+    for (uint32_t k = 0; k < inner; ++k) s = __fadd_rn(s, __fmul_rn(lhs[(size_t)r * inner + k], rhs[(size_t)k * cols + c]));
+    dst[(size_t)r * cols + c] = s;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" int b2_matmul_f32(float *dst, const float *lhs, const float *rhs, uint32_t rows, uint32_t cols,
+                             uint32_t inner, void *stream)
+{
+    if (!dst || !lhs || !rhs || rows == 0 || cols == 0 || inner == 0 || rows > 65535) return -1;
+    matmul_f32_kernel<<<dim3((cols + 127) / 128, rows), 128, 0, (cudaStream_t)stream>>>(dst, lhs, rhs, rows, cols,
+                                                                                        inner);
+    return cudaGetLastError() == cudaSuccess ? 0 : -8;
+}
+
+static int launched(cudaError_t e) { return e == cudaSuccess ? 0 : -8; }
+
+extern "C" int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_model, const uint32_t *tokens,
+                             uint32_t batch, float *x, unsigned long long *argmax, int32_t *err, int pdl,
+                             void *stream)
+{
+    if (!embed || !tokens || !x || !argmax || batch == 0 || d_model == 0 || vocab == 0) return -1;
+    void *args[] = {(void *)&embed, (void *)&vocab, (void *)&d_model, (void *)&tokens,
+                    (void *)&x,     (void *)&argmax, (void *)&err};
+    return launched(launch_pdl((const void *)step_begin_kernel, dim3(batch), dim3(256), pdl, (cudaStream_t)stream, args));
+}
+
+extern "C" int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens, int32_t *positions,
+                           int32_t *err, int pdl, void *stream)
+{
+    if (!argmax || !tokens || !positions || batch == 0 || batch > 1024) return -1;
+    void *args[] = {(void *)&argmax, (void *)&batch, (void *)&tokens, (void *)&positions, (void *)&err};
+    return launched(launch_pdl((const void *)step_end_kernel, dim3(1), dim3(((batch + 31) / 32) * 32), pdl,
+                               (cudaStream_t)stream, args));
+}
+
+extern "C" int b2_rmsnorm(float *dst, const float *src, const float *w, uint32_t n, float eps, void *stream)
+{
+    if (!dst || !src || !w || n == 0 || !(eps > 0.0f)) return -1;
+    rmsnorm_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(dst, src, w, n, eps);
+    return launched(cudaGetLastError());
+}
+
+extern "C" int b2_softmax(float *v, uint32_t n, void *stream)
+{
+    if (!v || n == 0) return -1;
+    softmax_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(v, n);
+    return launched(cudaGetLastError());
+}
+
+extern "C" int b2_rope(float *v, uint32_t n, uint32_t pos, float theta, void *stream)
+{
+    if (!v || n == 0 || (n & 1) || !(theta > 0.0f)) return -1;
+    const uint32_t pairs = n / 2;
+    rope_kernel<<<(pairs + 127) / 128, 128, 0, (cudaStream_t)stream>>>(v, n, pos, theta);
+    return launched(cudaGetLastError());
+}
+
+extern "C" int b2_swiglu(float *dst, const float *gate, const float *up, uint32_t n, void *stream)
+{
+    if (!dst || !gate || !up || n == 0) return -1;
+    uint32_t blocks = (n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    swiglu_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(dst, gate, up, n);
+    return launched(cudaGetLastError());
+}
+
+extern "C" int b2_argmax(const float *v, uint32_t n, unsigned long long *key, void *stream)
+{
+    if (!v || n == 0 || !key) return -1;
+    uint32_t blocks = (n + 255) / 256;
+    if (blocks > 1024) blocks = 1024;
+    cudaError_t e = cudaMemsetAsync(key, 0, sizeof(unsigned long long), (cudaStream_t)stream);
+    if (e != cudaSuccess) return -8;
+    argmax_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(v, n, key);
+    return launched(cudaGetLastError());
+}

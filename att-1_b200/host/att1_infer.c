@@ -1,0 +1,1144 @@
+/*
+ * att1_infer.c - device-resident decode behind the ATT-1 model API.
+ *
+ * Implements include/att1_infer.h and include/att1_b200.h: the decode step of
+ * ATT-1's src/infer.c:656-880 (embedding, n_layers pre-norm blocks of
+ * src/transformer_block.c:417-557, final RMSNorm, lm_head, greedy sampler)
+ * as a fixed sequence of sm_100a kernels per token:
+ *
+ *   step_begin                 x = embed[token]
+ *   per layer:
+ *     gemv QKV  (RMSNorm prologue; RoPE + KV-page append epilogue)
+ *     attn      (single query over the KV pages, GQA)
+ *     gemv WO   (residual epilogue)             h = x + Wo ctx
+ *     gemv GU   (RMSNorm prologue; SwiGLU epilogue over interleaved gate/up)
+ *     gemv DOWN (residual epilogue)             x = h + Wd s
+ *   gemv OUT  (RMSNorm prologue; logits + argmax key epilogue)
+ *   step_end                   token = argmax, position += 1
+ *
+ * The sequence is captured once as a CUDA graph with programmatic dependent
+ * launch edges and replayed per token; positions and tokens stay on the
+ * device, so a step needs only the token id in and the next id out.
+ */
+#define _POSIX_C_SOURCE 200809L
+#include "att1_infer.h"
+#include "att1_b200.h"
+#include "b2_host.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef struct dev_layer {
+    float *attn_norm, *ffn_norm;
+    b2_dev_mat qkv, wo, gu, down;
+    b2_gemv_args a_qkv, a_wo, a_gu, a_down;
+    b2_attn_args a_attn;
+} dev_layer;
+
+struct att1_infer {
+    att1_b200_config cfg;
+    uint32_t head_dim, batch, q_rows, kv_rows;
+    int device;
+    cudaStream_t stream;
+    dev_layer *layers;
+    float *embed, *out_norm, *rope_freq;
+    b2_dev_mat output;
+    b2_gemv_args a_out;
+    float *k_pool, *v_pool;
+    size_t layer_pool_elems;
+    int32_t *page_table;
+    uint32_t page_tokens, pages_per_seq;
+    float *x, *h1, *q, *ctx, *hs, *logits;
+    uint32_t *tokens_d;
+    int32_t *pos_d;
+    unsigned long long *argmax_d;
+    int32_t *err_d;
+    void *scratch;
+    size_t scratch_bytes;
+    uint32_t *tokens_h, *out_h;
+    int32_t *err_h;
+    float *logits_h;
+    int logits_valid;
+    size_t position;
+    int use_graph, use_pdl;
+    cudaGraphExec_t exec;
+    int graph_failed;
+    att1_backend *backend;
+    att1_trace_t *trace;
+    const att1_model *model;
+    size_t device_bytes;
+};
+
+/* ---- allocation ------------------------------------------------------------ */
+
+static att1_status_t dalloc(att1_infer_t *inf, void **p, size_t bytes)
+{
+    cudaError_t e;
+    *p = NULL;
+    if (bytes == 0) bytes = 256;
+    e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        *p = NULL;
+        return b2_cuda_status(e);
+    }
+    inf->device_bytes += bytes;
+    e = cudaMemsetAsync(*p, 0, bytes, inf->stream);
+    return b2_cuda_status(e);
+}
+
+static void dfree(void *p)
+{
+    if (p != NULL) cudaFree(p);
+}
+
+static att1_status_t mat_alloc(att1_infer_t *inf, b2_dev_mat *m, uint32_t fmt, uint32_t rows, uint32_t cols)
+{
+    att1_status_t st;
+    memset(m, 0, sizeof(*m));
+    m->w.format = fmt;
+    m->w.rows = rows;
+    m->w.cols = cols;
+    m->w.tiles = (rows + 15) / 16;
+    m->w.kunits = fmt == 4 ? (cols + 63) / 64 : (cols + 31) / 32;
+    st = dalloc(inf, &m->data, fmt == 4 ? b2_q4_bytes(rows, cols) : b2_q8_bytes(rows, cols));
+    if (st != ATT1_OK) return st;
+    if (fmt == 8) {
+        st = dalloc(inf, (void **)&m->row_scale, (size_t)m->w.tiles * 16 * sizeof(float));
+        if (st != ATT1_OK) return st;
+    }
+    m->w.data = m->data;
+    m->w.row_scale = m->row_scale;
+    return ATT1_OK;
+}
+
+static void mat_free(b2_dev_mat *m)
+{
+    dfree(m->data);
+    dfree(m->row_scale);
+    memset(m, 0, sizeof(*m));
+}
+
+static void release(att1_infer_t *inf)
+{
+    uint32_t l;
+    if (inf == NULL) return;
+    if (inf->stream) cudaStreamSynchronize(inf->stream);
+    if (inf->exec) cudaGraphExecDestroy(inf->exec);
+    if (inf->layers) {
+        for (l = 0; l < inf->cfg.n_layers; l++) {
+            dev_layer *L = &inf->layers[l];
+            dfree(L->attn_norm);
+            dfree(L->ffn_norm);
+            mat_free(&L->qkv);
+            mat_free(&L->wo);
+            mat_free(&L->gu);
+            mat_free(&L->down);
+        }
+        free(inf->layers);
+    }
+    mat_free(&inf->output);
+    dfree(inf->embed);
+    dfree(inf->out_norm);
+    dfree(inf->rope_freq);
+    dfree(inf->k_pool);
+    dfree(inf->v_pool);
+    dfree(inf->page_table);
+    dfree(inf->x);
+    dfree(inf->h1);
+    dfree(inf->q);
+    dfree(inf->ctx);
+    dfree(inf->hs);
+    dfree(inf->logits);
+    dfree(inf->tokens_d);
+    dfree(inf->pos_d);
+    dfree(inf->argmax_d);
+    dfree(inf->err_d);
+    dfree(inf->scratch);
+    if (inf->tokens_h) cudaFreeHost(inf->tokens_h);
+    if (inf->out_h) cudaFreeHost(inf->out_h);
+    if (inf->err_h) cudaFreeHost(inf->err_h);
+    if (inf->logits_h) cudaFreeHost(inf->logits_h);
+    if (inf->backend) att1_backend_destroy(inf->backend);
+    if (inf->stream) cudaStreamDestroy(inf->stream);
+    free(inf);
+}
+
+/* ---- configuration checks ---------------------------------------------------------- */
+
+static att1_status_t check_config(const att1_b200_config *c, uint32_t batch)
+{
+    uint32_t hd;
+    if (c == NULL || batch == 0 || batch > 16) return ATT1_ERR_INVALID_ARG;
+    if (c->vocab == 0 || c->n_layers == 0 || c->n_heads == 0 || c->n_kv_heads == 0 || c->d_model == 0 ||
+        c->d_ff == 0 || c->max_seq == 0)
+        return ATT1_ERR_INVALID_ARG;
+    if (c->dtype != 4 && c->dtype != 8) return ATT1_ERR_INVALID_ARG;
+    if (!(c->eps > 0.0f) || !(c->final_eps > 0.0f) || !(c->theta > 0.0f)) return ATT1_ERR_INVALID_ARG;
+    if (c->d_model % c->n_heads || c->n_heads % c->n_kv_heads) return ATT1_ERR_SHAPE;
+    hd = c->d_model / c->n_heads;
+    /* device layout limits: 16-row tiles per head, 32-column groups */
+    if (hd % 16 || hd > 128 || c->n_heads / c->n_kv_heads > 8) return ATT1_ERR_UNSUPPORTED;
+    if (c->d_model % 32 || c->d_ff % 32) return ATT1_ERR_UNSUPPORTED;
+    if (c->dtype == 4 && c->group != 32 && c->group != 0) return ATT1_ERR_UNSUPPORTED;
+    return ATT1_OK;
+}
+
+/* ---- kernel arguments ------------------------------------------------------------------ */
+
+static void gemv_base(att1_infer_t *inf, b2_gemv_args *a, const b2_dev_mat *m)
+{
+    memset(a, 0, sizeof(*a));
+    a->w = m->w;
+    a->batch = inf->batch;
+    a->err = inf->err_d;
+    a->pdl = inf->use_pdl;
+}
+
+static b2_kv_layout kv_layout(att1_infer_t *inf, uint32_t layer)
+{
+    b2_kv_layout kv;
+    kv.k_pool = inf->k_pool + (size_t)layer * inf->layer_pool_elems;
+    kv.v_pool = inf->v_pool + (size_t)layer * inf->layer_pool_elems;
+    kv.page_table = inf->page_table;
+    kv.page_tokens = inf->page_tokens;
+    kv.pages_per_seq = inf->pages_per_seq;
+    kv.n_kv_heads = inf->cfg.n_kv_heads;
+    kv.head_dim = inf->head_dim;
+    return kv;
+}
+
+static att1_status_t build_args(att1_infer_t *inf)
+{
+    const att1_b200_config *c = &inf->cfg;
+    size_t need = 0, s;
+    uint32_t l;
+    att1_status_t st;
+
+    for (l = 0; l < c->n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        b2_gemv_args *a;
+
+        a = &L->a_qkv;
+        gemv_base(inf, a, &L->qkv);
+        a->x = inf->x;
+        a->x_stride = c->d_model;
+        a->norm_w = L->attn_norm;
+        a->eps = c->eps;
+        a->epilogue = B2_EPI_QKV;
+        a->out = inf->q;
+        a->out_stride = inf->q_rows;
+        a->q_rows = inf->q_rows;
+        a->kv_rows = inf->kv_rows;
+        a->rope_freq = inf->rope_freq;
+        a->positions = inf->pos_d;
+        a->kv = kv_layout(inf, l);
+
+        memset(&L->a_attn, 0, sizeof(L->a_attn));
+        L->a_attn.batch = inf->batch;
+        L->a_attn.n_heads = c->n_heads;
+        L->a_attn.n_kv_heads = c->n_kv_heads;
+        L->a_attn.head_dim = inf->head_dim;
+        L->a_attn.q = inf->q;
+        L->a_attn.kv = kv_layout(inf, l);
+        L->a_attn.positions = inf->pos_d;
+        L->a_attn.max_ctx = c->max_seq;
+        L->a_attn.ctx = inf->ctx;
+        L->a_attn.err = inf->err_d;
+        L->a_attn.pdl = inf->use_pdl;
+
+        a = &L->a_wo;
+        gemv_base(inf, a, &L->wo);
+        a->x = inf->ctx;
+        a->x_stride = inf->q_rows;
+        a->epilogue = B2_EPI_RESID;
+        a->resid = inf->x;
+        a->out = inf->h1;
+        a->out_stride = c->d_model;
+
+        a = &L->a_gu;
+        gemv_base(inf, a, &L->gu);
+        a->x = inf->h1;
+        a->x_stride = c->d_model;
+        a->norm_w = L->ffn_norm;
+        a->eps = c->eps;
+        a->epilogue = B2_EPI_SWIGLU;
+        a->out = inf->hs;
+        a->out_stride = c->d_ff;
+
+        a = &L->a_down;
+        gemv_base(inf, a, &L->down);
+        a->x = inf->hs;
+        a->x_stride = c->d_ff;
+        a->epilogue = B2_EPI_RESID;
+        a->resid = inf->h1;
+        a->out = inf->x;
+        a->out_stride = c->d_model;
+    }
+    {
+        b2_gemv_args *a = &inf->a_out;
+        gemv_base(inf, a, &inf->output);
+        a->x = inf->x;
+        a->x_stride = c->d_model;
+        a->norm_w = inf->out_norm;
+        a->eps = c->final_eps;
+        a->epilogue = B2_EPI_LOGITS;
+        a->out = inf->logits;
+        a->out_stride = c->vocab;
+        a->argmax = inf->argmax_d;
+    }
+    /* one scratch region serves every kernel: they run one after another */
+    for (l = 0; l < c->n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        if ((s = b2_gemv_scratch_bytes(&L->a_qkv)) > need) need = s;
+        if ((s = b2_gemv_scratch_bytes(&L->a_wo)) > need) need = s;
+        if ((s = b2_gemv_scratch_bytes(&L->a_gu)) > need) need = s;
+        if ((s = b2_gemv_scratch_bytes(&L->a_down)) > need) need = s;
+        if ((s = b2_attn_scratch_bytes(&L->a_attn)) > need) need = s;
+    }
+    if ((s = b2_gemv_scratch_bytes(&inf->a_out)) > need) need = s;
+    st = dalloc(inf, &inf->scratch, need);
+    if (st != ATT1_OK) return st;
+    inf->scratch_bytes = need;
+    for (l = 0; l < c->n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        L->a_qkv.scratch = L->a_wo.scratch = L->a_gu.scratch = L->a_down.scratch = inf->scratch;
+        L->a_qkv.scratch_bytes = L->a_wo.scratch_bytes = L->a_gu.scratch_bytes = L->a_down.scratch_bytes = need;
+        L->a_attn.scratch = inf->scratch;
+        L->a_attn.scratch_bytes = need;
+    }
+    inf->a_out.scratch = inf->scratch;
+    inf->a_out.scratch_bytes = need;
+    return ATT1_OK;
+}
+
+static void set_pdl(att1_infer_t *inf, int pdl)
+{
+    uint32_t l;
+    for (l = 0; l < inf->cfg.n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        L->a_qkv.pdl = L->a_wo.pdl = L->a_gu.pdl = L->a_down.pdl = L->a_attn.pdl = pdl;
+    }
+    inf->a_out.pdl = pdl;
+    inf->use_pdl = pdl;
+}
+
+/* ---- buffers common to both creation paths ------------------------------------------------------ */
+
+static att1_status_t alloc_common(att1_infer_t *inf)
+{
+    const att1_b200_config *c = &inf->cfg;
+    const uint32_t B = inf->batch;
+    att1_status_t st;
+    uint32_t i, b;
+    int32_t *pt;
+    float *freq;
+    size_t pages;
+    cudaError_t e;
+
+    inf->page_tokens = c->max_seq < 64 ? c->max_seq : 64;
+    inf->pages_per_seq = (c->max_seq + inf->page_tokens - 1) / inf->page_tokens;
+    pages = (size_t)B * inf->pages_per_seq;
+    inf->layer_pool_elems = pages * inf->page_tokens * c->n_kv_heads * inf->head_dim;
+    if ((st = dalloc(inf, (void **)&inf->k_pool, inf->layer_pool_elems * c->n_layers * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->v_pool, inf->layer_pool_elems * c->n_layers * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->page_table, pages * sizeof(int32_t))) ||
+        (st = dalloc(inf, (void **)&inf->rope_freq, (inf->head_dim / 2) * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->x, (size_t)B * c->d_model * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->h1, (size_t)B * c->d_model * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->q, (size_t)B * inf->q_rows * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->ctx, (size_t)B * inf->q_rows * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->hs, (size_t)B * c->d_ff * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->logits, (size_t)B * c->vocab * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->tokens_d, 16 * sizeof(uint32_t))) ||
+        (st = dalloc(inf, (void **)&inf->pos_d, 16 * sizeof(int32_t))) ||
+        (st = dalloc(inf, (void **)&inf->argmax_d, 16 * sizeof(unsigned long long))) ||
+        (st = dalloc(inf, (void **)&inf->err_d, sizeof(int32_t))))
+        return st;
+    /* page table: sequence b owns pages [b*pages_per_seq, (b+1)*pages_per_seq) */
+    pt = malloc(pages * sizeof(int32_t));
+    freq = malloc((inf->head_dim / 2) * sizeof(float));
+    if (pt == NULL || freq == NULL) {
+        free(pt);
+        free(freq);
+        return ATT1_ERR_OOM;
+    }
+    for (b = 0; b < B; b++)
+        for (i = 0; i < inf->pages_per_seq; i++) pt[(size_t)b * inf->pages_per_seq + i] = (int32_t)(b * inf->pages_per_seq + i);
+    /* src/rope.c:21-22: freq of pair i/2 = 1 / powf(theta, i / head_dim), host libm */
+    for (i = 0; i < inf->head_dim / 2; i++) freq[i] = 1.0f / powf(c->theta, (float)(2 * i) / (float)inf->head_dim);
+    e = cudaMemcpy(inf->page_table, pt, pages * sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(inf->rope_freq, freq, (inf->head_dim / 2) * sizeof(float), cudaMemcpyHostToDevice);
+    free(pt);
+    free(freq);
+    if (e != cudaSuccess) return b2_cuda_status(e);
+    if (cudaMallocHost((void **)&inf->tokens_h, 16 * sizeof(uint32_t)) != cudaSuccess ||
+        cudaMallocHost((void **)&inf->out_h, 16 * sizeof(uint32_t)) != cudaSuccess ||
+        cudaMallocHost((void **)&inf->err_h, sizeof(int32_t)) != cudaSuccess ||
+        cudaMallocHost((void **)&inf->logits_h, (size_t)B * c->vocab * sizeof(float)) != cudaSuccess)
+        return ATT1_ERR_OOM;
+    return ATT1_OK;
+}
+
+static att1_status_t new_context(const att1_b200_config *cfg, uint32_t batch, att1_infer_t **out)
+{
+    att1_infer_t *inf;
+    att1_status_t st = check_config(cfg, batch);
+    if (st != ATT1_OK) return st;
+    inf = calloc(1, sizeof(*inf));
+    if (inf == NULL) return ATT1_ERR_OOM;
+    inf->cfg = *cfg;
+    if (inf->cfg.group == 0) inf->cfg.group = 32;
+    inf->batch = batch;
+    inf->head_dim = cfg->d_model / cfg->n_heads;
+    inf->q_rows = cfg->n_heads * inf->head_dim;
+    inf->kv_rows = cfg->n_kv_heads * inf->head_dim;
+    inf->use_graph = 1;
+    inf->use_pdl = 1;
+    if (cudaGetDevice(&inf->device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&inf->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        free(inf);
+        return ATT1_ERR_UNSUPPORTED;
+    }
+    inf->layers = calloc(cfg->n_layers, sizeof(dev_layer));
+    if (inf->layers == NULL) {
+        release(inf);
+        return ATT1_ERR_OOM;
+    }
+    *out = inf;
+    return ATT1_OK;
+}
+
+static att1_status_t alloc_weights(att1_infer_t *inf, uint32_t fmt)
+{
+    const att1_b200_config *c = &inf->cfg;
+    att1_status_t st;
+    uint32_t l;
+    for (l = 0; l < c->n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        if ((st = mat_alloc(inf, &L->qkv, fmt, inf->q_rows + 2 * inf->kv_rows, c->d_model)) ||
+            (st = mat_alloc(inf, &L->wo, fmt, c->d_model, inf->q_rows)) ||
+            (st = mat_alloc(inf, &L->gu, fmt, 2 * c->d_ff, c->d_model)) ||
+            (st = mat_alloc(inf, &L->down, fmt, c->d_model, c->d_ff)) ||
+            (st = dalloc(inf, (void **)&L->attn_norm, c->d_model * sizeof(float))) ||
+            (st = dalloc(inf, (void **)&L->ffn_norm, c->d_model * sizeof(float))))
+            return st;
+    }
+    if ((st = mat_alloc(inf, &inf->output, fmt, c->vocab, c->d_model)) ||
+        (st = dalloc(inf, (void **)&inf->embed, (size_t)c->vocab * c->d_model * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->out_norm, c->d_model * sizeof(float))))
+        return st;
+    return ATT1_OK;
+}
+
+static void free_weights(att1_infer_t *inf)
+{
+    uint32_t l;
+    for (l = 0; l < inf->cfg.n_layers; l++) {
+        mat_free(&inf->layers[l].qkv);
+        mat_free(&inf->layers[l].wo);
+        mat_free(&inf->layers[l].gu);
+        mat_free(&inf->layers[l].down);
+    }
+    mat_free(&inf->output);
+}
+
+static att1_status_t finish_create(att1_infer_t *inf)
+{
+    att1_status_t st = build_args(inf);
+    cudaError_t e;
+    if (st != ATT1_OK) return st;
+    e = cudaStreamSynchronize(inf->stream);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    return b2_cuda_status(e);
+}
+
+/* ---- synthetic model -------------------------------------------------------------------------------- */
+
+#define T_PER_LAYER 16u
+#define T_EMBED 0x7F000000ull
+#define T_OUTPUT 0x7F000002ull
+
+static int synth_mat(att1_infer_t *inf, b2_dev_mat *m, uint32_t tile_off, uint32_t rows, uint32_t cols,
+                     uint64_t seed, uint64_t tid, uint64_t tid2, int map)
+{
+    if (m->w.format == 4)
+        return b2_q4_synth(m->data, tile_off, rows, cols, seed, tid, tid2, 0.02f, map, inf->stream);
+    return b2_q8_synth(m->data, m->row_scale, tile_off, rows, cols, seed, tid, tid2, 0.02f, map, inf->stream);
+}
+
+att1_status_t att1_b200_infer_create_synth(const att1_b200_config *cfg, uint64_t seed, uint32_t batch,
+                                           att1_infer_t **out_infer)
+{
+    att1_infer_t *inf = NULL;
+    att1_status_t st;
+    uint32_t l;
+    int rc = 0;
+
+    if (out_infer == NULL) return ATT1_ERR_INVALID_ARG;
+    *out_infer = NULL;
+    st = new_context(cfg, batch, &inf);
+    if (st != ATT1_OK) return st;
+    if ((st = alloc_weights(inf, cfg->dtype)) || (st = alloc_common(inf))) goto fail;
+    for (l = 0; l < cfg->n_layers && rc == 0; l++) {
+        dev_layer *L = &inf->layers[l];
+        const uint64_t b = (uint64_t)l * T_PER_LAYER;
+        rc |= synth_mat(inf, &L->qkv, 0, inf->q_rows, cfg->d_model, seed, b + ATT1_B200_WQ, 0, B2_ROWS_PLAIN);
+        rc |= synth_mat(inf, &L->qkv, inf->q_rows / 16, inf->kv_rows, cfg->d_model, seed, b + ATT1_B200_WK, 0,
+                        B2_ROWS_PLAIN);
+        rc |= synth_mat(inf, &L->qkv, (inf->q_rows + inf->kv_rows) / 16, inf->kv_rows, cfg->d_model, seed,
+                        b + ATT1_B200_WV, 0, B2_ROWS_PLAIN);
+        rc |= synth_mat(inf, &L->wo, 0, cfg->d_model, inf->q_rows, seed, b + ATT1_B200_WO, 0, B2_ROWS_PLAIN);
+        rc |= synth_mat(inf, &L->gu, 0, 2 * cfg->d_ff, cfg->d_model, seed, b + ATT1_B200_GATE, b + ATT1_B200_UP,
+                        B2_ROWS_GATEUP);
+        rc |= synth_mat(inf, &L->down, 0, cfg->d_model, cfg->d_ff, seed, b + ATT1_B200_DOWN, 0, B2_ROWS_PLAIN);
+        rc |= b2_fill_f32(L->attn_norm, cfg->d_model, 1.0f, inf->stream);
+        rc |= b2_fill_f32(L->ffn_norm, cfg->d_model, 1.0f, inf->stream);
+    }
+    rc |= synth_mat(inf, &inf->output, 0, cfg->vocab, cfg->d_model, seed, T_OUTPUT, 0, B2_ROWS_PLAIN);
+    rc |= b2_synth_f32(inf->embed, (size_t)cfg->vocab * cfg->d_model, seed, T_EMBED, 0.02f, inf->stream);
+    rc |= b2_fill_f32(inf->out_norm, cfg->d_model, 1.0f, inf->stream);
+    if (rc != 0) {
+        st = ATT1_ERR_STATE;
+        goto fail;
+    }
+    if ((st = finish_create(inf)) != ATT1_OK) goto fail;
+    *out_infer = inf;
+    return ATT1_OK;
+fail:
+    release(inf);
+    return st;
+}
+
+/* ---- model from a .att1 file ------------------------------------------------------------------------ */
+
+static const att1_model_tensor *find_tensor(const att1_model *m, uint32_t layer, const char *suffix)
+{
+    char name[ATT1_MODEL_NAME_SIZE];
+    if (layer == UINT32_MAX) return att1_model_find_tensor(m, suffix);
+    if (snprintf(name, sizeof(name), "layers.%u.%s", layer, suffix) >= (int)sizeof(name)) return NULL;
+    return att1_model_find_tensor(m, name);
+}
+
+static int is_shape(const att1_model_tensor *t, uint32_t dtype, uint32_t nd, uint64_t d0, uint64_t d1)
+{
+    return t != NULL && t->dtype == dtype && t->ndims == nd && t->shape[0] == d0 && (nd < 2 || t->shape[1] == d1);
+}
+
+/* Upload a host tensor payload to a temporary device buffer. */
+static att1_status_t upload_tmp(att1_infer_t *inf, const att1_model_tensor *t, void **dev)
+{
+    cudaError_t e = cudaMalloc(dev, t->nbytes);
+    if (e != cudaSuccess) return b2_cuda_status(e);
+    e = cudaMemcpyAsync(*dev, t->data, t->nbytes, cudaMemcpyHostToDevice, inf->stream);
+    return b2_cuda_status(e);
+}
+
+static uint32_t q4_group_of(const att1_model_tensor *t)
+{
+    uint32_t g = t->flags & 0xFFu;
+    return g == 0 ? 32u : g;
+}
+
+/* q4 tensors (rows x cols each) -> units at tile_off, optionally interleaved. */
+static att1_status_t load_q4(att1_infer_t *inf, b2_dev_mat *m, uint32_t tile_off, const att1_model_tensor *t0,
+                             const att1_model_tensor *t1)
+{
+    void *d0 = NULL, *d1 = NULL;
+    att1_status_t st;
+    const uint32_t rows = (uint32_t)t0->shape[0], cols = (uint32_t)t0->shape[1];
+    const size_t pb = (size_t)rows * cols / 2;
+    int rc;
+    if ((st = upload_tmp(inf, t0, &d0)) != ATT1_OK) goto out;
+    if (t1 != NULL && (st = upload_tmp(inf, t1, &d1)) != ATT1_OK) goto out;
+    rc = b2_q4_pack(m->data, tile_off, t1 ? 2 * rows : rows, cols, (const uint8_t *)d0,
+                    (const float *)((const uint8_t *)d0 + pb), (const uint8_t *)d1,
+                    d1 ? (const float *)((const uint8_t *)d1 + pb) : NULL, q4_group_of(t0),
+                    t1 ? B2_ROWS_GATEUP : B2_ROWS_PLAIN, inf->stream);
+    st = rc == 0 ? ATT1_OK : (rc == -1 ? ATT1_ERR_UNSUPPORTED : ATT1_ERR_STATE);
+    if (st == ATT1_OK) st = b2_cuda_status(cudaStreamSynchronize(inf->stream));
+out:
+    if (d0) cudaFree(d0);
+    if (d1) cudaFree(d1);
+    return st;
+}
+
+/* q8 from file: q8 tensors [out][in], or f32 tensors [in][out] quantised
+ * per output row on the device (src/infer.c:196-233, 337-433). */
+static att1_status_t load_q8(att1_infer_t *inf, b2_dev_mat *m, uint32_t tile_off, const att1_model_tensor *t0,
+                             const att1_model_tensor *t1)
+{
+    void *d0 = NULL, *d1 = NULL;
+    att1_status_t st;
+    int rc;
+    if ((st = upload_tmp(inf, t0, &d0)) != ATT1_OK) goto out;
+    if (t1 != NULL && (st = upload_tmp(inf, t1, &d1)) != ATT1_OK) goto out;
+    if (t0->dtype == ATT1_MODEL_DTYPE_Q8) {
+        const uint32_t rows = (uint32_t)t0->shape[0], cols = (uint32_t)t0->shape[1];
+        const size_t vb = (size_t)rows * cols;
+        rc = b2_q8_pack(m->data, m->row_scale, tile_off, t1 ? 2 * rows : rows, cols, (const int8_t *)d0,
+                        (const float *)((const uint8_t *)d0 + vb), (const int8_t *)d1,
+                        d1 ? (const float *)((const uint8_t *)d1 + vb) : NULL, t1 ? B2_ROWS_GATEUP : B2_ROWS_PLAIN,
+                        inf->stream);
+    } else {
+        const uint32_t in = (uint32_t)t0->shape[0], outr = (uint32_t)t0->shape[1];
+        rc = b2_q8_quantize_f32(m->data, m->row_scale, tile_off, t1 ? 2 * outr : outr, in, (const float *)d0,
+                                (const float *)d1, 1, t1 ? B2_ROWS_GATEUP : B2_ROWS_PLAIN, inf->stream);
+    }
+    st = rc == 0 ? ATT1_OK : ATT1_ERR_STATE;
+    if (st == ATT1_OK) st = b2_cuda_status(cudaStreamSynchronize(inf->stream));
+out:
+    if (d0) cudaFree(d0);
+    if (d1) cudaFree(d1);
+    return st;
+}
+
+static att1_status_t upload_f32(att1_infer_t *inf, float *dst, const att1_model_tensor *t)
+{
+    return b2_cuda_status(cudaMemcpyAsync(dst, t->data, t->nbytes, cudaMemcpyHostToDevice, inf->stream));
+}
+
+/* Validate (src/model_view.c:221-366) and upload one precision's weights. */
+static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, uint32_t fmt)
+{
+    const att1_model_config *mc = &m->config;
+    const uint64_t d = mc->d_model, f = mc->d_ff, V = mc->vocab_size;
+    const att1_model_tensor *emb = find_tensor(m, UINT32_MAX, "tok_embeddings.weight");
+    const att1_model_tensor *onorm = find_tensor(m, UINT32_MAX, "output_norm.weight");
+    const att1_model_tensor *outw = find_tensor(m, UINT32_MAX, "output.weight");
+    const int file_q8 = outw != NULL && outw->dtype == ATT1_MODEL_DTYPE_Q8;
+    att1_status_t st;
+    uint32_t l;
+
+    if (emb == NULL || onorm == NULL || outw == NULL) return ATT1_ERR_NOT_FOUND;
+    if (!is_shape(emb, ATT1_MODEL_DTYPE_F32, 2, V, d) || !is_shape(onorm, ATT1_MODEL_DTYPE_F32, 1, d, 1))
+        return ATT1_ERR_SHAPE;
+    if (fmt == 4 && !is_shape(outw, ATT1_MODEL_DTYPE_Q4, 2, V, d)) return ATT1_ERR_SHAPE;
+    if (fmt == 8 && !(file_q8 ? is_shape(outw, ATT1_MODEL_DTYPE_Q8, 2, V, d)
+                              : is_shape(outw, ATT1_MODEL_DTYPE_F32, 2, d, V)))
+        return ATT1_ERR_SHAPE;
+    for (l = 0; l < mc->n_layers; l++) {
+        const att1_model_tensor *an = find_tensor(m, l, "attention_norm.weight");
+        const att1_model_tensor *fn = find_tensor(m, l, "ffn_norm.weight");
+        const char *names[7] = {"attention.wq.weight", "attention.wk.weight", "attention.wv.weight",
+                                "attention.wo.weight", "ffn.w_gate.weight",   "ffn.w_up.weight",
+                                "ffn.w_down.weight"};
+        const att1_model_tensor *t[7];
+        int k;
+        if (an == NULL || fn == NULL) return ATT1_ERR_NOT_FOUND;
+        if (!is_shape(an, ATT1_MODEL_DTYPE_F32, 1, d, 1) || !is_shape(fn, ATT1_MODEL_DTYPE_F32, 1, d, 1))
+            return ATT1_ERR_SHAPE;
+        for (k = 0; k < 7; k++) {
+            /* [out][in] for q4/q8 tensors, [in][out] for f32 */
+            const uint64_t out_d = (k >= 4 && k <= 5) ? f : d, in_d = (k == 6) ? f : d;
+            t[k] = find_tensor(m, l, names[k]);
+            if (t[k] == NULL) return ATT1_ERR_NOT_FOUND;
+            if (fmt == 4 && !is_shape(t[k], ATT1_MODEL_DTYPE_Q4, 2, out_d, in_d)) return ATT1_ERR_SHAPE;
+            if (fmt == 8 && !(file_q8 ? is_shape(t[k], ATT1_MODEL_DTYPE_Q8, 2, out_d, in_d)
+                                      : is_shape(t[k], ATT1_MODEL_DTYPE_F32, 2, in_d, out_d)))
+                return ATT1_ERR_SHAPE;
+        }
+        {
+            dev_layer *L = &inf->layers[l];
+            att1_status_t (*load)(att1_infer_t *, b2_dev_mat *, uint32_t, const att1_model_tensor *,
+                                  const att1_model_tensor *) = fmt == 4 ? load_q4 : load_q8;
+            if ((st = load(inf, &L->qkv, 0, t[0], NULL)) || (st = load(inf, &L->qkv, inf->q_rows / 16, t[1], NULL)) ||
+                (st = load(inf, &L->qkv, (inf->q_rows + inf->kv_rows) / 16, t[2], NULL)) ||
+                (st = load(inf, &L->wo, 0, t[3], NULL)) || (st = load(inf, &L->gu, 0, t[4], t[5])) ||
+                (st = load(inf, &L->down, 0, t[6], NULL)) || (st = upload_f32(inf, L->attn_norm, an)) ||
+                (st = upload_f32(inf, L->ffn_norm, fn)))
+                return st;
+        }
+    }
+    if ((st = (fmt == 4 ? load_q4 : load_q8)(inf, &inf->output, 0, outw, NULL)) ||
+        (st = upload_f32(inf, inf->embed, emb)) || (st = upload_f32(inf, inf->out_norm, onorm)))
+        return st;
+    return b2_cuda_status(cudaStreamSynchronize(inf->stream));
+}
+
+att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dtype, float eps, float final_eps,
+                                           float theta, att1_infer_t **out_infer)
+{
+    att1_b200_config c;
+    att1_infer_t *inf = NULL;
+    att1_status_t st;
+    if (out_infer == NULL) return ATT1_ERR_INVALID_ARG;
+    *out_infer = NULL;
+    if (model == NULL) return ATT1_ERR_INVALID_ARG;
+    memset(&c, 0, sizeof(c));
+    c.vocab = model->config.vocab_size;
+    c.n_layers = model->config.n_layers;
+    c.n_heads = model->config.n_heads;
+    c.n_kv_heads = model->config.n_heads;
+    c.d_model = model->config.d_model;
+    c.d_ff = model->config.d_ff;
+    c.max_seq = model->config.max_seq_len;
+    c.group = 32;
+    c.dtype = dtype;
+    c.eps = eps;
+    c.final_eps = final_eps;
+    c.theta = theta;
+    if (c.vocab == 0 || c.n_layers == 0 || c.n_heads == 0 || c.d_model == 0 || c.d_ff == 0 || c.max_seq == 0 ||
+        c.d_model % c.n_heads || ((c.d_model / c.n_heads) % 2))
+        return ATT1_ERR_INVALID_ARG;
+    st = new_context(&c, 1, &inf);
+    if (st != ATT1_OK) return st;
+    inf->model = model;
+    if ((st = alloc_weights(inf, dtype)) || (st = alloc_common(inf)) ||
+        (st = load_model_weights(inf, model, dtype)) || (st = finish_create(inf)))
+        goto fail;
+    *out_infer = inf;
+    return ATT1_OK;
+fail:
+    release(inf);
+    return st;
+}
+
+att1_status_t att1_infer_create_q4(const att1_model *model, att1_infer_t **out_infer)
+{
+    /* src/infer.c:721-722 and :823: eps 1e-6, theta 10000 for file models */
+    att1_status_t st = att1_b200_infer_create_model(model, 4, 0.000001f, 0.000001f, 10000.0f, out_infer);
+    if (st == ATT1_OK && att1_backend_cuda_q4_create(&(*out_infer)->backend) != ATT1_OK) {
+        att1_infer_destroy(*out_infer);
+        *out_infer = NULL;
+        return ATT1_ERR_STATE;
+    }
+    return st;
+}
+
+att1_status_t att1_infer_create(const att1_model *model, att1_infer_t **out_infer)
+{
+    att1_status_t st = att1_b200_infer_create_model(model, 8, 0.000001f, 0.000001f, 10000.0f, out_infer);
+    if (st == ATT1_OK && att1_backend_cuda_q8_create(&(*out_infer)->backend) != ATT1_OK) {
+        att1_infer_destroy(*out_infer);
+        *out_infer = NULL;
+        return ATT1_ERR_STATE;
+    }
+    return st;
+}
+
+void att1_infer_destroy(att1_infer_t *infer)
+{
+    release(infer);
+}
+
+uint32_t att1_b200_infer_batch(const att1_infer_t *infer)
+{
+    return infer ? infer->batch : 0;
+}
+
+size_t att1_b200_infer_device_bytes(const att1_infer_t *infer)
+{
+    return infer ? infer->device_bytes : 0;
+}
+
+void *att1_b200_infer_stream(const att1_infer_t *infer)
+{
+    return infer ? (void *)infer->stream : NULL;
+}
+
+/* ---- the decode step ------------------------------------------------------------------------------------- */
+
+static int enqueue_kernels(att1_infer_t *inf)
+{
+    const att1_b200_config *c = &inf->cfg;
+    cudaStream_t st = inf->stream;
+    uint32_t l;
+    int rc = b2_step_begin(inf->embed, c->vocab, c->d_model, inf->tokens_d, inf->batch, inf->x, inf->argmax_d,
+                           inf->err_d, inf->use_pdl, st);
+    for (l = 0; l < c->n_layers && rc == 0; l++) {
+        dev_layer *L = &inf->layers[l];
+        rc |= b2_gemv(&L->a_qkv, st);
+        rc |= b2_attn(&L->a_attn, st);
+        rc |= b2_gemv(&L->a_wo, st);
+        rc |= b2_gemv(&L->a_gu, st);
+        rc |= b2_gemv(&L->a_down, st);
+    }
+    if (rc == 0) rc = b2_gemv(&inf->a_out, st);
+    if (rc == 0) rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    return rc;
+}
+
+static int launch_step(att1_infer_t *inf)
+{
+    if (inf->use_graph && !inf->graph_failed) {
+        if (inf->exec == NULL) {
+            cudaGraph_t g = NULL;
+            int rc;
+            if (cudaStreamBeginCapture(inf->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+                inf->graph_failed = 1;
+                cudaGetLastError();
+                return enqueue_kernels(inf);
+            }
+            rc = enqueue_kernels(inf);
+            if (cudaStreamEndCapture(inf->stream, &g) != cudaSuccess || rc != 0 ||
+                cudaGraphInstantiate(&inf->exec, g, 0) != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                inf->exec = NULL;
+                inf->graph_failed = 1;
+                cudaGetLastError();
+                return enqueue_kernels(inf);
+            }
+            cudaGraphDestroy(g);
+        }
+        return cudaGraphLaunch(inf->exec, inf->stream) == cudaSuccess ? 0 : -8;
+    }
+    return enqueue_kernels(inf);
+}
+
+/* After a kernel-reported fault: clear the error word, the tile counters in
+ * scratch, and put the device position back to the host position. */
+static att1_status_t recover(att1_infer_t *inf, int32_t err)
+{
+    int32_t pos[16];
+    uint32_t b;
+    for (b = 0; b < inf->batch; b++) pos[b] = (int32_t)inf->position;
+    cudaMemsetAsync(inf->err_d, 0, sizeof(int32_t), inf->stream);
+    cudaMemsetAsync(inf->scratch, 0, inf->scratch_bytes, inf->stream);
+    cudaMemcpyAsync(inf->pos_d, pos, inf->batch * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream);
+    cudaStreamSynchronize(inf->stream);
+    if (err & B2_ERR_TIMEOUT) return ATT1_ERR_TIMEOUT;
+    if (err & B2_ERR_TOKEN) return ATT1_ERR_INVALID_ARG;
+    return ATT1_ERR_STATE;
+}
+
+static att1_status_t step(att1_infer_t *inf, const uint32_t *tokens, uint32_t *out_tokens)
+{
+    const att1_b200_config *c = &inf->cfg;
+    uint64_t t0 = 0;
+    uint32_t b;
+    cudaError_t e;
+
+    if (inf->position >= c->max_seq) return ATT1_ERR_INVALID_ARG;
+    for (b = 0; b < inf->batch; b++) {
+        if (tokens[b] >= c->vocab) return ATT1_ERR_INVALID_ARG;
+        inf->tokens_h[b] = tokens[b];
+    }
+    if (inf->trace) t0 = att1_trace_now_us();
+    if (inf->position == 0) {
+        int32_t zero[16] = {0};
+        if (cudaMemcpyAsync(inf->pos_d, zero, inf->batch * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream) !=
+            cudaSuccess)
+            return ATT1_ERR_STATE;
+    }
+    if (cudaMemcpyAsync(inf->tokens_d, inf->tokens_h, inf->batch * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                        inf->stream) != cudaSuccess)
+        return ATT1_ERR_STATE;
+    if (launch_step(inf) != 0) return ATT1_ERR_STATE;
+    cudaMemcpyAsync(inf->out_h, inf->tokens_d, inf->batch * sizeof(uint32_t), cudaMemcpyDeviceToHost, inf->stream);
+    cudaMemcpyAsync(inf->err_h, inf->err_d, sizeof(int32_t), cudaMemcpyDeviceToHost, inf->stream);
+    e = cudaStreamSynchronize(inf->stream);
+    if (e != cudaSuccess) return b2_cuda_status(e);
+    inf->logits_valid = 0;
+    if (*inf->err_h != 0) return recover(inf, *inf->err_h);
+    for (b = 0; b < inf->batch; b++) out_tokens[b] = inf->out_h[b];
+    if (inf->trace) {
+        const uint64_t us = att1_trace_now_us() - t0;
+        const uint64_t reads = (uint64_t)(inf->position + 1) * c->n_heads;
+        uint32_t l;
+        for (l = 0; l < c->n_layers; l++) att1_trace_record_layer(inf->trace, l, us / c->n_layers, 1, reads, reads);
+        att1_trace_record_logits(inf->trace, 0, (uint64_t)c->vocab * sizeof(float));
+        att1_trace_record_token(inf->trace, us);
+    }
+    inf->position++;
+    return ATT1_OK;
+}
+
+static int backend_ok(const att1_infer_t *inf)
+{
+    /* routing by name as in src/infer.c:143-159: the context's precision must
+     * match the backend's */
+    const char *n = inf->backend ? b2_backend_name(inf->backend) : NULL;
+    if (n == NULL) return 1; /* contexts from att1_b200_* have no backend object */
+    if (strcmp(n, "cuda-q4") == 0) return inf->cfg.dtype == 4;
+    if (strcmp(n, "cuda-q8") == 0) return inf->cfg.dtype == 8;
+    return 0;
+}
+
+att1_status_t att1_infer_decode_token(att1_infer_t *infer, uint32_t token_id, uint32_t *out_token)
+{
+    if (infer == NULL || out_token == NULL) return ATT1_ERR_INVALID_ARG;
+    if (infer->batch != 1) return ATT1_ERR_STATE;
+    if (token_id >= infer->cfg.vocab || infer->position >= infer->cfg.max_seq) return ATT1_ERR_INVALID_ARG;
+    if (!backend_ok(infer)) return ATT1_ERR_STATE;
+    return step(infer, &token_id, out_token);
+}
+
+att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *tokens, uint32_t *out_tokens)
+{
+    if (infer == NULL || tokens == NULL || out_tokens == NULL) return ATT1_ERR_INVALID_ARG;
+    if (!backend_ok(infer)) return ATT1_ERR_STATE;
+    return step(infer, tokens, out_tokens);
+}
+
+att1_status_t att1_infer_generate(att1_infer_t *infer, const unsigned char *prompt, size_t prompt_bytes,
+                                  size_t generated_token_count, uint32_t *out_tokens, size_t out_token_capacity,
+                                  size_t *out_token_count)
+{
+    uint32_t token = 0;
+    size_t i;
+    att1_status_t st;
+    /* same contract as src/infer.c:882-928 */
+    if (infer == NULL || prompt == NULL || out_tokens == NULL || out_token_count == NULL) return ATT1_ERR_INVALID_ARG;
+    if (prompt_bytes == 0 || out_token_capacity < generated_token_count) return ATT1_ERR_INVALID_ARG;
+    for (i = 0; i < prompt_bytes; i++) {
+        uint32_t next = 0;
+        st = att1_infer_decode_token(infer, (uint32_t)prompt[i], &next);
+        if (st != ATT1_OK) return st;
+        token = next;
+    }
+    for (i = 0; i < generated_token_count; i++) {
+        uint32_t next = 0;
+        out_tokens[i] = token;
+        if (i + 1 < generated_token_count) {
+            st = att1_infer_decode_token(infer, token, &next);
+            if (st != ATT1_OK) return st;
+            token = next;
+        }
+    }
+    *out_token_count = generated_token_count;
+    return ATT1_OK;
+}
+
+static const float *logits_host(const att1_infer_t *cinfer, size_t *out_count, size_t n)
+{
+    att1_infer_t *infer = (att1_infer_t *)cinfer; /* lazy copy-back is internal state */
+    if (infer == NULL) {
+        if (out_count) *out_count = 0;
+        return NULL;
+    }
+    if (!infer->logits_valid) {
+        if (cudaMemcpy(infer->logits_h, infer->logits, (size_t)infer->batch * infer->cfg.vocab * sizeof(float),
+                       cudaMemcpyDeviceToHost) != cudaSuccess) {
+            if (out_count) *out_count = 0;
+            return NULL;
+        }
+        infer->logits_valid = 1;
+    }
+    if (out_count) *out_count = n;
+    return infer->logits_h;
+}
+
+const float *att1_infer_logits(const att1_infer_t *infer, size_t *out_count)
+{
+    return logits_host(infer, out_count, infer ? infer->cfg.vocab : 0);
+}
+
+const float *att1_b200_infer_logits_batch(const att1_infer_t *infer, size_t *out_count)
+{
+    return logits_host(infer, out_count, infer ? (size_t)infer->batch * infer->cfg.vocab : 0);
+}
+
+att1_status_t att1_infer_position(const att1_infer_t *infer, size_t *out_position)
+{
+    if (infer == NULL || out_position == NULL) return ATT1_ERR_INVALID_ARG;
+    *out_position = infer->position;
+    return ATT1_OK;
+}
+
+att1_status_t att1_infer_layer_kv_length(const att1_infer_t *infer, uint32_t layer_id, size_t *out_length)
+{
+    if (infer == NULL || out_length == NULL || layer_id >= infer->cfg.n_layers) return ATT1_ERR_INVALID_ARG;
+    *out_length = infer->position;
+    return ATT1_OK;
+}
+
+att1_status_t att1_infer_set_trace(att1_infer_t *infer, att1_trace_t *trace)
+{
+    if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    infer->trace = trace;
+    return ATT1_OK;
+}
+
+att1_status_t att1_infer_set_backend(att1_infer_t *infer, att1_backend *backend)
+{
+    const char *n;
+    uint32_t want;
+    att1_status_t st;
+    if (infer == NULL || backend == NULL || backend->ops == NULL) return ATT1_ERR_INVALID_ARG;
+    n = b2_backend_name(backend);
+    if (n == NULL || !b2_backend_is_cuda(backend)) return ATT1_ERR_UNSUPPORTED;
+    if (strcmp(n, "cuda-q4") == 0) want = 4;
+    else if (strcmp(n, "cuda-q8") == 0) want = 8;
+    else return ATT1_ERR_UNSUPPORTED; /* the f32 "cuda" backend has no device decode path */
+    if (want != infer->cfg.dtype) {
+        /* switch precision: re-prepare weights from the model (src/infer.c:982-1012) */
+        if (infer->model == NULL) return ATT1_ERR_UNSUPPORTED;
+        cudaStreamSynchronize(infer->stream);
+        if (infer->exec) {
+            cudaGraphExecDestroy(infer->exec);
+            infer->exec = NULL;
+        }
+        free_weights(infer);
+        infer->cfg.dtype = want;
+        if ((st = alloc_weights(infer, want)) || (st = load_model_weights(infer, infer->model, want))) return st;
+        dfree(infer->scratch);
+        infer->scratch = NULL;
+        if ((st = build_args(infer)) != ATT1_OK) return st;
+    }
+    if (infer->backend) att1_backend_destroy(infer->backend);
+    infer->backend = backend;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_set_options(att1_infer_t *infer, int use_graph, int use_pdl)
+{
+    if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    cudaStreamSynchronize(infer->stream);
+    if (infer->exec) {
+        cudaGraphExecDestroy(infer->exec);
+        infer->exec = NULL;
+    }
+    infer->graph_failed = 0;
+    infer->use_graph = use_graph ? 1 : 0;
+    set_pdl(infer, use_pdl ? 1 : 0);
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps)
+{
+    uint32_t i;
+    if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    if (infer->position + steps > infer->cfg.max_seq) return ATT1_ERR_INVALID_ARG;
+    if (infer->position == 0) {
+        int32_t zero[16] = {0};
+        if (cudaMemcpyAsync(infer->pos_d, zero, infer->batch * sizeof(int32_t), cudaMemcpyHostToDevice,
+                            infer->stream) != cudaSuccess)
+            return ATT1_ERR_STATE;
+    }
+    for (i = 0; i < steps; i++) {
+        if (launch_step(infer) != 0) return ATT1_ERR_STATE;
+    }
+    infer->position += steps;
+    infer->logits_valid = 0;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_sync(att1_infer_t *infer)
+{
+    cudaError_t e;
+    if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    cudaMemcpyAsync(infer->err_h, infer->err_d, sizeof(int32_t), cudaMemcpyDeviceToHost, infer->stream);
+    e = cudaStreamSynchronize(infer->stream);
+    if (e != cudaSuccess) return b2_cuda_status(e);
+    if (*infer->err_h != 0) {
+        infer->position = 0; /* device positions are unknown after a fault */
+        return recover(infer, *infer->err_h);
+    }
+    return ATT1_OK;
+}
+
+/* ---- read-back for parity tests ---------------------------------------------------------------------------- */
+
+static att1_status_t locate(const att1_infer_t *inf, uint32_t layer, uint32_t kind, const b2_dev_mat **m,
+                            uint32_t *tile_off, uint32_t *rows, uint32_t *cols, int *map, int *which)
+{
+    const att1_b200_config *c = &inf->cfg;
+    *tile_off = 0;
+    *map = B2_ROWS_PLAIN;
+    *which = 0;
+    if (kind == ATT1_B200_OUTPUT) {
+        *m = &inf->output;
+        *rows = c->vocab;
+        *cols = c->d_model;
+        return ATT1_OK;
+    }
+    if (layer >= c->n_layers) return ATT1_ERR_INVALID_ARG;
+    switch (kind) {
+    case ATT1_B200_WQ: *m = &inf->layers[layer].qkv; *rows = inf->q_rows; *cols = c->d_model; break;
+    case ATT1_B200_WK:
+        *m = &inf->layers[layer].qkv; *tile_off = inf->q_rows / 16; *rows = inf->kv_rows; *cols = c->d_model; break;
+    case ATT1_B200_WV:
+        *m = &inf->layers[layer].qkv; *tile_off = (inf->q_rows + inf->kv_rows) / 16; *rows = inf->kv_rows;
+        *cols = c->d_model; break;
+    case ATT1_B200_WO: *m = &inf->layers[layer].wo; *rows = c->d_model; *cols = inf->q_rows; break;
+    case ATT1_B200_GATE:
+    case ATT1_B200_UP:
+        *m = &inf->layers[layer].gu; *rows = c->d_ff; *cols = c->d_model; *map = B2_ROWS_GATEUP;
+        *which = kind == ATT1_B200_UP; break;
+    case ATT1_B200_DOWN: *m = &inf->layers[layer].down; *rows = c->d_model; *cols = c->d_ff; break;
+    default: return ATT1_ERR_INVALID_ARG;
+    }
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_export_q4(const att1_infer_t *infer, uint32_t layer, uint32_t kind, uint8_t *packed,
+                                        float *scales)
+{
+    const b2_dev_mat *m;
+    uint32_t toff, rows, cols;
+    int map, which, rc;
+    void *dp = NULL, *ds = NULL;
+    att1_status_t st;
+    if (infer == NULL || packed == NULL || scales == NULL || infer->cfg.dtype != 4) return ATT1_ERR_INVALID_ARG;
+    if ((st = locate(infer, layer, kind, &m, &toff, &rows, &cols, &map, &which)) != ATT1_OK) return st;
+    if (cudaMalloc(&dp, (size_t)rows * cols / 2) != cudaSuccess ||
+        cudaMalloc(&ds, (size_t)rows * (cols / 32) * sizeof(float)) != cudaSuccess) {
+        st = ATT1_ERR_OOM;
+        goto out;
+    }
+    rc = b2_q4_unpack(dp, ds, m->data, toff, rows, cols, map, which, infer->stream);
+    if (rc != 0) {
+        st = ATT1_ERR_STATE;
+        goto out;
+    }
+    if (cudaStreamSynchronize(infer->stream) != cudaSuccess ||
+        cudaMemcpy(packed, dp, (size_t)rows * cols / 2, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(scales, ds, (size_t)rows * (cols / 32) * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        st = ATT1_ERR_STATE;
+out:
+    if (dp) cudaFree(dp);
+    if (ds) cudaFree(ds);
+    return st;
+}
+
+att1_status_t att1_b200_infer_export_q8(const att1_infer_t *infer, uint32_t layer, uint32_t kind, int8_t *values,
+                                        float *scales)
+{
+    const b2_dev_mat *m;
+    uint32_t toff, rows, cols;
+    int map, which, rc;
+    void *dv = NULL, *ds = NULL;
+    att1_status_t st;
+    if (infer == NULL || values == NULL || scales == NULL || infer->cfg.dtype != 8) return ATT1_ERR_INVALID_ARG;
+    if ((st = locate(infer, layer, kind, &m, &toff, &rows, &cols, &map, &which)) != ATT1_OK) return st;
+    if (cudaMalloc(&dv, (size_t)rows * cols) != cudaSuccess || cudaMalloc(&ds, (size_t)rows * sizeof(float)) != cudaSuccess) {
+        st = ATT1_ERR_OOM;
+        goto out;
+    }
+    rc = b2_q8_unpack(dv, ds, m->data, m->row_scale, toff, rows, cols, map, which, infer->stream);
+    if (rc != 0) {
+        st = ATT1_ERR_STATE;
+        goto out;
+    }
+    if (cudaStreamSynchronize(infer->stream) != cudaSuccess ||
+        cudaMemcpy(values, dv, (size_t)rows * cols, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(scales, ds, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        st = ATT1_ERR_STATE;
+out:
+    if (dv) cudaFree(dv);
+    if (ds) cudaFree(ds);
+    return st;
+}
+
+att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item, uint32_t layer, size_t count,
+                                        float *keys, float *values)
+{
+    const size_t row = (size_t)infer->cfg.n_kv_heads * infer->head_dim;
+    size_t p;
+    if (infer == NULL || keys == NULL || values == NULL || item >= infer->batch || layer >= infer->cfg.n_layers ||
+        count > infer->cfg.max_seq)
+        return ATT1_ERR_INVALID_ARG;
+    if (cudaStreamSynchronize(infer->stream) != cudaSuccess) return ATT1_ERR_STATE;
+    for (p = 0; p < count; p++) {
+        /* identity page table: sequence item's pages are contiguous */
+        const size_t page = (size_t)item * infer->pages_per_seq + p / infer->page_tokens;
+        const size_t slot = page * infer->page_tokens + p % infer->page_tokens;
+        const size_t off = (size_t)layer * infer->layer_pool_elems + slot * row;
+        if (cudaMemcpy(keys + p * row, infer->k_pool + off, row * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemcpy(values + p * row, infer->v_pool + off, row * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+            return ATT1_ERR_STATE;
+    }
+    return ATT1_OK;
+}

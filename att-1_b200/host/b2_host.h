@@ -1,0 +1,40 @@
+/*
+ * b2_host.h - internal declarations shared by the host C files.
+ */
+#ifndef B2_HOST_H
+#define B2_HOST_H
+
+#include "att1_b200.h"
+#include "att1_backend.h"
+#include "b2_kernels.h"
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+/* one quantised matrix on the device */
+typedef struct b2_dev_mat {
+    void *data;
+    float *row_scale;   /* q8 only */
+    b2_qweight w;
+} b2_dev_mat;
+
+/* backend internals shared with the infer context (set_backend routing) */
+int b2_backend_is_cuda(const att1_backend *backend);
+const char *b2_backend_name(const att1_backend *backend);
+
+/* status of a CUDA runtime call */
+static inline att1_status_t b2_cuda_status(cudaError_t e)
+{
+    if (e == cudaSuccess) return ATT1_OK;
+    if (e == cudaErrorMemoryAllocation) return ATT1_ERR_OOM;
+    return ATT1_ERR_STATE;
+}
+
+/* status of a b2_* kernel entry point (0 or a negative att1 code) */
+static inline att1_status_t b2_status(int rc)
+{
+    return rc == 0 ? ATT1_OK : (att1_status_t)rc;
+}
+
+#endif

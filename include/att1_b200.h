@@ -1,0 +1,89 @@
+/*
+ * att1_b200.h - additions to the ATT-1 API for the B200 decode path.
+ *
+ * Nothing here changes an existing ATT-1 signature. The additions cover what
+ * the .att1 format and the batch-1 API cannot express:
+ *   - model shape beyond the .att1 config: grouped-query attention
+ *     (n_kv_heads), RMSNorm eps and RoPE theta (hard-coded to 1e-6 / 10000 in
+ *     the reference, src/infer.c:721-722);
+ *   - seeded synthetic models generated and quantised on the device (the
+ *     benchmark models are tens of GB; the generator is bit-identical to the
+ *     CPU one the parity tests use);
+ *   - batched decode: B independent sequences in one device step;
+ *   - device-side step loops and timing hooks for benchmarks, and read-back
+ *     of device weights / KV pages for parity tests.
+ */
+#ifndef ATT1_B200_H
+#define ATT1_B200_H
+
+#include "att1_infer.h"
+#include "att1_status.h"
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct att1_b200_config {
+    uint32_t vocab, n_layers, n_heads, n_kv_heads, d_model, d_ff, max_seq;
+    uint32_t group;      /* q4 group size: 32 */
+    uint32_t dtype;      /* 4 = q4, 8 = q8 */
+    float eps;           /* block RMSNorm eps */
+    float final_eps;     /* output RMSNorm eps */
+    float theta;         /* RoPE base */
+} att1_b200_config;
+
+/* Weight kinds for export (same numbering as the synthetic tensor ids). */
+enum {
+    ATT1_B200_WQ = 1, ATT1_B200_WK = 2, ATT1_B200_WV = 3, ATT1_B200_WO = 4,
+    ATT1_B200_GATE = 6, ATT1_B200_UP = 7, ATT1_B200_DOWN = 8, ATT1_B200_OUTPUT = 9
+};
+
+/* Synthetic model on the current device: every matrix N(0, 0.02) from
+ * (seed, tensor id) quantised by the reference rule, norm gains 1.0,
+ * embedding N(0, 0.02) in f32. `batch` sequences decode together. */
+att1_status_t att1_b200_infer_create_synth(const att1_b200_config *cfg, uint64_t seed,
+                                           uint32_t batch, att1_infer_t **out_infer);
+/* Same, from a loaded .att1 model with explicit eps/theta (n_kv_heads must
+ * equal n_heads: the format stores full K/V projections). */
+att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dtype, float eps,
+                                           float final_eps, float theta,
+                                           att1_infer_t **out_infer);
+uint32_t att1_b200_infer_batch(const att1_infer_t *infer);
+
+/* One step for all sequences: tokens[batch] in, greedy next tokens out. */
+att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *tokens,
+                                           uint32_t *out_tokens);
+/* Host copy of the last step's logits [batch][vocab]. */
+const float *att1_b200_infer_logits_batch(const att1_infer_t *infer, size_t *out_count);
+
+/* use_graph: replay one captured CUDA graph per step (default 1);
+ * use_pdl: programmatic dependent launch between kernels (default 1). */
+att1_status_t att1_b200_infer_set_options(att1_infer_t *infer, int use_graph, int use_pdl);
+
+/* Enqueue `steps` decode steps on the device, each feeding its greedy token
+ * into the next, without host synchronisation (benchmark loop). The host
+ * position advances by `steps`; call att1_b200_infer_sync to wait. */
+att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps);
+att1_status_t att1_b200_infer_sync(att1_infer_t *infer);
+/* CUDA stream (cudaStream_t) all work of this context is enqueued on. */
+void *att1_b200_infer_stream(const att1_infer_t *infer);
+
+/* Read back device weights in the reference layout. */
+att1_status_t att1_b200_infer_export_q4(const att1_infer_t *infer, uint32_t layer, uint32_t kind,
+                                        uint8_t *packed, float *scales);
+att1_status_t att1_b200_infer_export_q8(const att1_infer_t *infer, uint32_t layer, uint32_t kind,
+                                        int8_t *values, float *scales);
+/* Read back KV of one sequence and layer, positions [0, count), as
+ * [count][n_kv_heads][head_dim] f32. */
+att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item, uint32_t layer,
+                                        size_t count, float *keys, float *values);
+/* Device bytes held by the context (weights, KV pages, buffers). */
+size_t att1_b200_infer_device_bytes(const att1_infer_t *infer);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

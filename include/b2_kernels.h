@@ -1,0 +1,197 @@
+/*
+ * b2_kernels.h - thin C ABI over the sm_100a kernels of the decode path.
+ *
+ * Every entry point takes device pointers, sizes and a CUDA stream (passed as
+ * void *), launches asynchronously and returns 0 or a negative att1_status_t
+ * code (argument errors are detected on the host before any launch). Kernels
+ * report run-time faults (a timed-out wait, a non-finite input) by OR-ing
+ * B2_ERR_* bits into a caller-supplied device error word.
+ *
+ * The host C11 library (att1_infer_*, att1_backend_*) is the only intended
+ * caller; these functions are exported so that tests and other hosts can
+ * drive single kernels.
+ */
+#ifndef B2_KERNELS_H
+#define B2_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* run-time error bits written into the device error word */
+#define B2_ERR_TIMEOUT     0x1  /* a bounded wait gave up */
+#define B2_ERR_NONFINITE   0x2  /* non-finite GEMV input vector */
+#define B2_ERR_POSITION    0x4  /* position outside the KV capacity */
+#define B2_ERR_NAN_LOGITS  0x8  /* NaN in logits (greedy sampler rejects) */
+#define B2_ERR_TOKEN       0x10 /* token id outside the vocabulary */
+
+/* ---- quantised weights in device layout ---------------------------------- */
+/*
+ * q4 "unit" layout: a matrix [rows][cols] is cut into 16-row tiles and
+ * 64-column group pairs (two q4 groups of 32). Each (tile, pair) unit is 640
+ * contiguous bytes, units ordered tile-major:
+ *   bytes [0,512):  32 lanes x 16 B; lane l = 4*r + t (r = row in tile mod 8)
+ *                   holds words {row r g0, row r+8 g0, row r g1, row r+8 g1};
+ *                   byte i of a word = nibble(col 4t+i) | nibble(col 16+4t+i)<<4
+ *                   (cols relative to the group), the same 4-bit two's
+ *                   complement values as the reference's packed bytes.
+ *   bytes [512,640): 8 x float4 {s(r,g0), s(r,g1), s(r+8,g0), s(r+8,g1)}.
+ * Padding rows/columns hold zero nibbles and zero scales. The mapping is a
+ * permutation of the reference's nibbles (b2_q4_unpack inverts it).
+ *
+ * q8 unit layout: (16-row tile, 32-column block) units of 512 bytes, lane l
+ * holds 16 int8 {row r k 4t..4t+3, row r+8 k 4t.., row r k 16+4t.., row r+8
+ * k 16+4t..}; one f32 scale per row in a separate array [tiles*16].
+ */
+#define B2_Q4_UNIT_BYTES 640u
+#define B2_Q8_UNIT_BYTES 512u
+
+enum b2_row_map {
+    B2_ROWS_PLAIN = 0,   /* device row i = source row i */
+    B2_ROWS_GATEUP = 1   /* tile t: rows 0..7 = gate rows 8t.., rows 8..15 = up rows 8t.. */
+};
+
+typedef struct b2_qweight {
+    const void *data;        /* device units */
+    const float *row_scale;  /* q8: device [tiles*16]; q4: NULL */
+    uint32_t format;         /* 4 or 8 */
+    uint32_t rows, cols;     /* logical device rows (2*F for gate/up) and columns */
+    uint32_t tiles;          /* ceil(rows / 16) */
+    uint32_t kunits;         /* q4: ceil(cols / 64); q8: ceil(cols / 32) */
+} b2_qweight;
+
+size_t b2_q4_bytes(uint32_t rows, uint32_t cols);
+size_t b2_q8_bytes(uint32_t rows, uint32_t cols);        /* units only */
+
+/* Reference layout (packed [rows][cols/2] + scales [rows][cols/group]) ->
+ * units, written at `tile_offset` tiles into dst. group in {32, 64, 128}.
+ * map = B2_ROWS_GATEUP takes src (gate) and src2 (up), each [rows/2][cols]. */
+int b2_q4_pack(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols,
+               const uint8_t *packed, const float *scales,
+               const uint8_t *packed2, const float *scales2,
+               uint32_t group, int map, void *stream);
+/* Units -> reference layout (group 32) of source `which` (0, or 1 = up for
+ * B2_ROWS_GATEUP) with `rows` source rows. */
+int b2_q4_unpack(uint8_t *packed, float *scales, const void *src, uint32_t tile_offset,
+                 uint32_t rows, uint32_t cols, int map, int which, void *stream);
+/* Generate N(0, std) weights for tensor (seed, tensor_id) [rows][cols] and
+ * quantise them exactly as the reference q4 quantiser (group 32) directly
+ * into units. GATEUP: tensor_id = gate, tensor_id2 = up, each [dst_rows/2]. */
+int b2_q4_synth(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols,
+                uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2, float std,
+                int map, void *stream);
+
+int b2_q8_pack(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows,
+               uint32_t cols, const int8_t *values, const float *scales,
+               const int8_t *values2, const float *scales2, int map, void *stream);
+int b2_q8_unpack(int8_t *values, float *scales, const void *src, const float *row_scale,
+                 uint32_t tile_offset, uint32_t rows, uint32_t cols, int map, int which,
+                 void *stream);
+int b2_q8_synth(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows,
+                uint32_t cols, uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2,
+                float std, int map, void *stream);
+
+/* Quantise an f32 device matrix per output row by the reference q8 rule
+ * (src/quant.c:61-116) into units. transposed = 1 reads w as [cols][rows]
+ * (the reference's [in][out] f32 layout, src/infer.c:196-233). */
+int b2_q8_quantize_f32(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows,
+                       uint32_t cols, const float *w, const float *w2, int transposed, int map,
+                       void *stream);
+/* f32 GEMM for the "cuda" backend: dst[rows][cols] = lhs[rows][inner] * rhs[inner][cols]. */
+int b2_matmul_f32(float *dst, const float *lhs, const float *rhs, uint32_t rows, uint32_t cols,
+                  uint32_t inner, void *stream);
+
+/* f32 tensor of N(0, std) values (bit-identical to the oracle generator). */
+int b2_synth_f32(float *dst, size_t count, uint64_t seed, uint64_t tensor_id, float std,
+                 void *stream);
+int b2_fill_f32(float *dst, size_t count, float value, void *stream);
+
+/* ---- GEMV: y[b][r] = sum_c W[r][c] * prologue(x)[b][c], fused epilogue ---- */
+enum b2_epilogue {
+    B2_EPI_STORE = 0,   /* out[b][r] = y */
+    B2_EPI_RESID = 1,   /* out[b][r] = resid[b][r] + y */
+    B2_EPI_QKV = 2,     /* q rows -> out (RoPE); k rows -> K cache (RoPE); v rows -> V cache */
+    B2_EPI_SWIGLU = 3,  /* gate/up rows -> out[b][j] = silu(gate) * up */
+    B2_EPI_LOGITS = 4   /* out[b][r] = y and greedy argmax key per item */
+};
+
+typedef struct b2_kv_layout {
+    float *k_pool, *v_pool;       /* page pools of one layer */
+    const int32_t *page_table;    /* [batch][pages_per_seq] physical page ids */
+    uint32_t page_tokens;         /* tokens per page */
+    uint32_t pages_per_seq;
+    uint32_t n_kv_heads, head_dim;/* page = [page_tokens][n_kv_heads][head_dim] f32 */
+} b2_kv_layout;
+
+typedef struct b2_gemv_args {
+    b2_qweight w;
+    uint32_t batch;               /* 1..16 */
+    const float *x;               /* [batch][x_stride] */
+    uint32_t x_stride;
+    const float *norm_w;          /* RMSNorm gains [cols] (prologue), NULL = none */
+    float eps;
+    int epilogue;                 /* b2_epilogue */
+    float *out;                   /* [batch][out_stride] */
+    uint32_t out_stride;
+    const float *resid;           /* B2_EPI_RESID */
+    /* B2_EPI_QKV */
+    uint32_t q_rows, kv_rows;     /* rows [0,q_rows) q, [q_rows, q_rows+kv_rows) k, rest v */
+    const float *rope_freq;       /* [head_dim/2], freq[i] = 1/powf(theta, 2i/head_dim) */
+    const int32_t *positions;     /* [batch] position of the token being decoded */
+    b2_kv_layout kv;
+    /* B2_EPI_LOGITS */
+    unsigned long long *argmax;   /* [batch] packed (ordered value, ~index) keys */
+    /* scratch: partial sums + per-tile counters, zeroed once by the caller */
+    void *scratch;
+    size_t scratch_bytes;
+    int32_t *err;                 /* device error word */
+    int pdl;                      /* launch with programmatic dependent launch */
+    int grid;                     /* 0 = one CTA per SM */
+} b2_gemv_args;
+
+size_t b2_gemv_scratch_bytes(const b2_gemv_args *a);
+int b2_gemv(const b2_gemv_args *a, void *stream);
+
+/* ---- single-query attention over the paged KV cache (split over positions) */
+typedef struct b2_attn_args {
+    uint32_t batch, n_heads, n_kv_heads, head_dim;
+    const float *q;               /* [batch][n_heads*head_dim] (RoPE applied) */
+    b2_kv_layout kv;
+    const int32_t *positions;     /* [batch]: attend positions 0..pos inclusive */
+    uint32_t max_ctx;             /* capacity bound used to size the grid */
+    float *ctx;                   /* [batch][n_heads*head_dim] */
+    void *scratch;
+    size_t scratch_bytes;
+    int32_t *err;
+    int pdl;
+} b2_attn_args;
+
+size_t b2_attn_scratch_bytes(const b2_attn_args *a);
+int b2_attn(const b2_attn_args *a, void *stream);
+
+/* ---- per-token step kernels ------------------------------------------------ */
+/* x[b] = embed[tokens[b]]; argmax keys reset. Validates token ids. */
+int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_model, const uint32_t *tokens,
+                  uint32_t batch, float *x, unsigned long long *argmax, int32_t *err,
+                  int pdl, void *stream);
+/* tokens[b] = argmax index; positions[b] += 1. */
+int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens,
+                int32_t *positions, int32_t *err, int pdl, void *stream);
+
+/* ---- element ops (backend vtable on device buffers) ---------------------- */
+int b2_rmsnorm(float *dst, const float *src, const float *w, uint32_t n, float eps, void *stream);
+int b2_softmax(float *v, uint32_t n, void *stream);
+int b2_rope(float *v, uint32_t n, uint32_t pos, float theta, void *stream);
+int b2_swiglu(float *dst, const float *gate, const float *up, uint32_t n, void *stream);
+int b2_argmax(const float *v, uint32_t n, unsigned long long *key, void *stream);
+
+/* device properties used for launch shapes */
+int b2_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,168 @@
+"""End-to-end decode parity on the GPU against the oracle.
+
+Teacher-forced: both sides consume the same token stream and the logits of
+every step must satisfy max|gpu - cpu| / max|cpu| <= 1e-3 (the tolerance of
+the parity contract). Greedy tokens must agree wherever the oracle's top two
+logits are separated by more than that tolerance.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+LOGITS_RTOL = 1e-3
+
+
+def rel_err(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def tokens_agree(gpu_tok, cpu_logits):
+    top2 = np.sort(cpu_logits)[-2:]
+    gap = (top2[1] - top2[0]) / max(np.abs(cpu_logits).max(), 1e-30)
+    return gap <= 2 * LOGITS_RTOL or int(gpu_tok) == int(np.argmax(cpu_logits))
+
+
+def run_parity(b2, orc, ocfg, steps, seed=1234, batch=1, threads=8, worst=None):
+    cfg = b2.Config.make(ocfg.vocab, ocfg.n_layers, ocfg.n_heads, ocfg.n_kv_heads, ocfg.d_model,
+                         ocfg.d_ff, ocfg.max_seq, dtype=ocfg.dtype, eps=ocfg.eps,
+                         final_eps=ocfg.final_eps, theta=ocfg.theta)
+    inf = b2.Infer.synth(cfg, seed, batch=batch)
+    oms = [orc.model(ocfg, seed, threads=threads) for _ in range(batch)]
+    toks = [orc.synth_tokens(seed + b, steps, ocfg.vocab) for b in range(batch)]
+    errs = []
+    for s in range(steps):
+        step_toks = [int(toks[b][s]) for b in range(batch)]
+        gtok = inf.decode_batch(step_toks) if batch > 1 else [inf.decode(step_toks[0])]
+        glog = inf.logits()
+        for b in range(batch):
+            clog, _ = oms[b].decode(step_toks[b])
+            e = rel_err(glog[b], clog)
+            errs.append(e)
+            assert e <= LOGITS_RTOL, f"step {s} item {b}: rel err {e:.3e}"
+            assert tokens_agree(gtok[b], clog), f"step {s} item {b}: token {gtok[b]}"
+    inf.close()
+    if worst is not None:
+        worst.append(max(errs))
+    return max(errs)
+
+
+def test_tiny_q8_full_workload(b2, orc):
+    """Tiny q8 decoder: dim 288, 6 layers, 6 heads (hd 48), SwiGLU 768,
+    vocab 32000, eps 1e-5, theta 1e4, 16-token prompt + 128 decoded."""
+    ocfg = O.Config.make(vocab=32000, n_layers=6, n_heads=6, n_kv_heads=6, d_model=288, d_ff=768,
+                         max_seq=256, dtype=O.Q8, eps=1e-5, theta=10000.0)
+    assert run_parity(b2, orc, ocfg, steps=144) <= LOGITS_RTOL
+
+
+def test_small_gqa_q4(b2, orc):
+    """Small GQA decoder shape: dim 576, 30 layers, 9/3 heads (hd 64), SwiGLU
+    1536, vocab 49152, theta 1e4 (first 24 positions)."""
+    ocfg = O.Config.make(vocab=49152, n_layers=30, n_heads=9, n_kv_heads=3, d_model=576, d_ff=1536,
+                         max_seq=2048, dtype=O.Q4, eps=1e-5, theta=10000.0)
+    assert run_parity(b2, orc, ocfg, steps=24) <= LOGITS_RTOL
+
+
+def test_8b_width_two_layers_q4(b2, orc):
+    """Llama-3-8B widths (dim 4096, 32/8 heads, SwiGLU 14336, theta 5e5) at
+    2 layers and a 4096-entry vocabulary so the CPU oracle stays fast."""
+    ocfg = O.Config.make(vocab=4096, n_layers=2, n_heads=32, n_kv_heads=8, d_model=4096, d_ff=14336,
+                         max_seq=64, dtype=O.Q4, eps=1e-5, theta=500000.0)
+    assert run_parity(b2, orc, ocfg, steps=6) <= LOGITS_RTOL
+
+
+def test_batched_decode_matches_oracle(b2, orc):
+    ocfg = O.Config.make(vocab=1000, n_layers=2, n_heads=4, n_kv_heads=2, d_model=128, d_ff=256,
+                         max_seq=64, dtype=O.Q4, eps=1e-5, theta=10000.0)
+    assert run_parity(b2, orc, ocfg, steps=10, batch=3) <= LOGITS_RTOL
+
+
+def test_long_context_crosses_pages(b2, orc):
+    """More than one 64-token KV page and more than one 128-position
+    attention chunk."""
+    ocfg = O.Config.make(vocab=512, n_layers=1, n_heads=4, n_kv_heads=1, d_model=128, d_ff=128,
+                         max_seq=320, dtype=O.Q4, eps=1e-5, theta=10000.0)
+    assert run_parity(b2, orc, ocfg, steps=300, threads=1) <= LOGITS_RTOL
+
+
+def test_graph_and_direct_launch_agree(b2, orc):
+    cfg = b2.Config.make(2000, 2, 4, 2, 128, 256, 32, dtype=4)
+    outs = []
+    for graph, pdl in ((True, True), (False, False), (False, True)):
+        inf = b2.Infer.synth(cfg, 5)
+        inf.set_options(graph=graph, pdl=pdl)
+        toks = [inf.decode(t) for t in (1, 2, 3, 4)]
+        outs.append((toks, inf.logits()))
+        inf.close()
+    for toks, lg in outs[1:]:
+        assert toks == outs[0][0]
+        assert (lg == outs[0][1]).all()
+
+
+def test_kv_pages_hold_roped_keys(b2, orc):
+    ocfg = O.Config.make(vocab=300, n_layers=2, n_heads=4, n_kv_heads=2, d_model=64, d_ff=64,
+                         max_seq=16, dtype=O.Q4, eps=1e-5, theta=10000.0)
+    cfg = b2.Config.make(300, 2, 4, 2, 64, 64, 16, dtype=4)
+    inf = b2.Infer.synth(cfg, 9)
+    om = orc.model(ocfg, 9)
+    for t in (5, 6, 7):
+        inf.decode(t)
+        om.decode(t)
+    row = 2 * 16
+    for layer in range(2):
+        k, v = inf.export_kv(0, layer, 3, row)
+        assert rel_err(k, om.keys(layer)[: 3 * row]) < 1e-4
+        assert rel_err(v, om.values(layer)[: 3 * row]) < 1e-4
+
+
+def test_device_weights_bit_exact(b2, orc):
+    ocfg = O.Config.make(vocab=500, n_layers=1, n_heads=4, n_kv_heads=2, d_model=128, d_ff=96,
+                         max_seq=8, dtype=O.Q4)
+    cfg = b2.Config.make(500, 1, 4, 2, 128, 96, 8, dtype=4)
+    inf = b2.Infer.synth(cfg, 3)
+    om = orc.model(ocfg, 3)
+    for kind in (b2.WQ, b2.WK, b2.WV, b2.WO, b2.GATE, b2.UP, b2.DOWN, b2.OUTPUT):
+        p, s, rows, cols = om.q4(0, kind)
+        gp, gs = inf.export_q4(0, kind, rows, cols)
+        assert (gp == p).all(), kind
+        assert (gs.view(np.uint32) == s.view(np.uint32)).all(), kind
+    ocfg8 = O.Config.make(vocab=500, n_layers=1, n_heads=4, n_kv_heads=2, d_model=128, d_ff=96,
+                          max_seq=8, dtype=O.Q8)
+    cfg8 = b2.Config.make(500, 1, 4, 2, 128, 96, 8, dtype=8)
+    inf8 = b2.Infer.synth(cfg8, 3)
+    om8 = orc.model(ocfg8, 3)
+    for kind in (b2.WQ, b2.WK, b2.WV, b2.WO, b2.GATE, b2.UP, b2.DOWN, b2.OUTPUT):
+        v, s, rows, cols = om8.q8(0, kind)
+        gv, gs = inf8.export_q8(0, kind, rows, cols)
+        assert (gv == v).all(), kind
+        assert (gs == s).all(), kind
+
+
+def test_position_limit_and_bad_token(b2):
+    cfg = b2.Config.make(100, 1, 2, 2, 64, 64, 3, dtype=4)
+    inf = b2.Infer.synth(cfg, 1)
+    with pytest.raises(b2.Att1Error) as e:
+        inf.decode(100)
+    assert e.value.rc == -1
+    for t in (1, 2, 3):
+        inf.decode(t)
+    with pytest.raises(b2.Att1Error) as e:
+        inf.decode(1)
+    assert e.value.rc == -1
+    assert inf.position() == 3
+
+
+def test_run_steps_matches_decode(b2):
+    cfg = b2.Config.make(3000, 2, 4, 2, 128, 256, 64, dtype=4)
+    a, b = b2.Infer.synth(cfg, 8), b2.Infer.synth(cfg, 8)
+    tok = a.decode(17)
+    seq = [tok]
+    for _ in range(5):
+        tok = a.decode(tok)
+        seq.append(tok)
+    b.decode(17)
+    b.run_steps(5)
+    b.sync()
+    assert b.position() == a.position()
+    assert (b.logits() == a.logits()).all()
