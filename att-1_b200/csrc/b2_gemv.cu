@@ -40,7 +40,7 @@
 namespace b2 {
 
 constexpr int kWarps = 8;        // consumer warps per CTA (each streams its own range)
-constexpr int kSlots = 4;        // ring slots per warp
+constexpr int kSlots = 6;        // ring slots per warp
 constexpr int kUnitsPerSlot = 2; // units per bulk copy
 constexpr int kMaxItems = 16;
 
@@ -90,79 +90,134 @@ __device__ __forceinline__ uint32_t ordered_key(float f)
 }
 
 // ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
+// The input vector is read once into registers (all loads of a thread issued
+// together, so the prologue costs one L2 round trip instead of one per
+// element group); vectors longer than kPrologueVec * 4 * blockDim fall back
+// to re-reading chunks.
+constexpr int kPrologueVec = 16;  // float4 per thread held in registers
+
+template <int FMT>
+__device__ __forceinline__ void store_digits(const GemvParams &p, uint8_t *xdig, uint32_t b, uint32_t k, float4 v,
+                                             float sc, bool finite)
+{
+    constexpr uint32_t KW = Fmt<FMT>::kKW;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int q = finite ? __float2int_rn(__fmul_rn(vv[i], sc)) : 0;
+        const int d0 = ((q + 128) & 255) - 128;
+        const int q1 = (q - d0) >> 8;
+        const int d1 = ((q1 + 128) & 255) - 128;
+        const int d2 = (q1 - d1) >> 8;
+        w0 |= ((uint32_t)d0 & 0xFFu) << (8 * i);
+        w1 |= ((uint32_t)d1 & 0xFFu) << (8 * i);
+        w2 |= ((uint32_t)d2 & 0xFFu) << (8 * i);
+    }
+    const uint32_t unit = k / KW, kk = k % KW;
+    const uint32_t gi = kk >> 5, r = kk & 31;
+    const uint32_t half = r >> 4, t = (r & 15) >> 2;
+    uint8_t *base = xdig + ((size_t)(unit * p.batch + b) * 3) * KW + t * (KW / 4) + gi * 8 + half * 4;
+    *reinterpret_cast<uint32_t *>(base) = w0;
+    *reinterpret_cast<uint32_t *>(base + KW) = w1;
+    *reinterpret_cast<uint32_t *>(base + 2 * KW) = w2;
+}
+
+__device__ __forceinline__ float4 normed(float4 v, float inv, float4 w)
+{
+    // src/norm.c:31: dst = src * scale * weight
+    return make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
+                       __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
+}
+
+__device__ __forceinline__ float absmax4(float4 v)
+{
+    const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    // fmaxf drops NaN: make any non-finite element visible
+    return (fabsf(v.x) <= FLT_MAX && fabsf(v.y) <= FLT_MAX && fabsf(v.z) <= FLT_MAX && fabsf(v.w) <= FLT_MAX)
+               ? a : INFINITY;
+}
+
+__device__ __forceinline__ int pick_exponent(float m)
+{
+    int E = 0;
+    if (m > 0.0f && m <= FLT_MAX) {
+        E = ilogbf(m) - 21;  // |x| * 2^-E < 2^22
+        if (E < -125) E = -125;
+    }
+    return E;
+}
+
 template <int FMT>
 __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
 {
-    constexpr uint32_t KW = Fmt<FMT>::kKW;
     const uint32_t cols = p.cols;
+    const uint32_t stride = blockDim.x * 4;
     for (uint32_t b = 0; b < p.batch; ++b) {
         const float *xb = p.x + (size_t)b * p.x_stride;
-        float inv = 1.0f;
-        if (p.norm_w != nullptr) {
-            float ss = 0.0f;
-            for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
-                const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            }
-            ss = block_sum(ss, red);
-            // src/norm.c:26-28
-            inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
-        }
-        float m = 0.0f;
-        for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
-            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
-            if (p.norm_w != nullptr) {
-                const float4 w = *reinterpret_cast<const float4 *>(p.norm_w + k);
-                v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
-            }
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-            // a NaN compares false in fmaxf; detect it explicitly
-            if (!(fabsf(v.x) <= FLT_MAX && fabsf(v.y) <= FLT_MAX && fabsf(v.z) <= FLT_MAX &&
-                  fabsf(v.w) <= FLT_MAX))
-                m = INFINITY;
-        }
-        m = block_max(m, red);
-        int E = 0;
-        if (!(m <= FLT_MAX)) {
-            if (threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
-        } else if (m > 0.0f) {
-            E = ilogbf(m) - 21;
-            if (E < -125) E = -125;
-        }
-        const float sc = ldexpf(1.0f, -E);
-        if (threadIdx.x == 0) item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
-        for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
-            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
-            if (p.norm_w != nullptr) {
-                const float4 w = *reinterpret_cast<const float4 *>(p.norm_w + k);
-                v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
-            }
-            const float vv[4] = {v.x, v.y, v.z, v.w};
-            uint32_t w0 = 0, w1 = 0, w2 = 0;
+        if (cols <= stride * kPrologueVec) {
+            float4 v[kPrologueVec];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                int q = (m <= FLT_MAX) ? __float2int_rn(__fmul_rn(vv[i], sc)) : 0;
-                const int d0 = ((q + 128) & 255) - 128;
-                const int q1 = (q - d0) >> 8;
-                const int d1 = ((q1 + 128) & 255) - 128;
-                const int d2 = (q1 - d1) >> 8;
-                w0 |= ((uint32_t)d0 & 0xFFu) << (8 * i);
-                w1 |= ((uint32_t)d1 & 0xFFu) << (8 * i);
-                w2 |= ((uint32_t)d2 & 0xFFu) << (8 * i);
+            for (int i = 0; i < kPrologueVec; ++i) {
+                const uint32_t k = threadIdx.x * 4 + i * stride;
+                v[i] = k < cols ? __ldcg(reinterpret_cast<const float4 *>(xb + k)) : make_float4(0, 0, 0, 0);
             }
-            const uint32_t unit = k / KW, kk = k % KW;
-            const uint32_t gi = kk >> 5, r = kk & 31;
-            const uint32_t half = r >> 4, t = (r & 15) >> 2;
-            uint8_t *base = xdig + ((size_t)(unit * p.batch + b) * 3) * KW + t * (KW / 4) + gi * 8 + half * 4;
-            *reinterpret_cast<uint32_t *>(base) = w0;
-            *reinterpret_cast<uint32_t *>(base + KW) = w1;
-            *reinterpret_cast<uint32_t *>(base + 2 * KW) = w2;
+            if (p.norm_w != nullptr) {
+                float ss = 0.0f;
+#pragma unroll
+                for (int i = 0; i < kPrologueVec; ++i)
+                    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+                ss = block_sum(ss, red);
+                // src/norm.c:26-28
+                const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
+#pragma unroll
+                for (int i = 0; i < kPrologueVec; ++i) {
+                    const uint32_t k = threadIdx.x * 4 + i * stride;
+                    if (k < cols) v[i] = normed(v[i], inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
+                }
+            }
+            float m = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kPrologueVec; ++i) m = fmaxf(m, absmax4(v[i]));
+            m = block_max(m, red);
+            const bool finite = m <= FLT_MAX;
+            if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
+            const int E = pick_exponent(m);
+            const float sc = ldexpf(1.0f, -E);
+            if (threadIdx.x == 0) item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
+#pragma unroll
+            for (int i = 0; i < kPrologueVec; ++i) {
+                const uint32_t k = threadIdx.x * 4 + i * stride;
+                if (k < cols) store_digits<FMT>(p, xdig, b, k, v[i], sc, finite);
+            }
+        } else {
+            float inv = 1.0f;
+            if (p.norm_w != nullptr) {
+                float ss = 0.0f;
+                for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
+                ss = block_sum(ss, red);
+                inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
+            }
+            float m = 0.0f;
+            for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+                float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+                if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
+                m = fmaxf(m, absmax4(v));
+            }
+            m = block_max(m, red);
+            const bool finite = m <= FLT_MAX;
+            if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
+            const int E = pick_exponent(m);
+            const float sc = ldexpf(1.0f, -E);
+            if (threadIdx.x == 0) item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
+            for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+                float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+                if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
+                store_digits<FMT>(p, xdig, b, k, v, sc, finite);
+            }
         }
     }
 }
@@ -262,7 +317,7 @@ __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const float *t
 }
 
 template <int FMT, int NI>
-__global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
     constexpr uint32_t KW = Fmt<FMT>::kKW;

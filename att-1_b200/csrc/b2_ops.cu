@@ -91,7 +91,10 @@ __global__ void rope_kernel(float *v, uint32_t n, uint32_t pos, float theta)
 {
     const uint32_t i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
     if (i >= n) return;
-    const float freq = __fdiv_rn(1.0f, powf(theta, __fdiv_rn((float)i, (float)n)));
+    // src/rope.c:21-22 in f32; powf evaluated in double and rounded once, so
+    // it agrees with a correctly rounded host powf
+    const float e = __fdiv_rn((float)i, (float)n);
+    const float freq = __fdiv_rn(1.0f, (float)pow((double)theta, (double)e));
     const float ang = __fmul_rn((float)pos, freq);
     float s, c;
     sincosf(ang, &s, &c);

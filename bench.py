@@ -1,0 +1,360 @@
+#!/usr/bin/env python
+"""Decode benchmark: Llama-3-8B-shaped q4 decoder, batch 1, context 4096.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (the 8B configuration of the q4 decode metric): dim 4096, 32 layers,
+32 query / 8 KV heads (head_dim 128), SwiGLU 14336, vocab 128256, RoPE theta
+5e5, RMSNorm eps 1e-5; weights N(0, 0.02) quantised to q4 (group 32) by the
+reference rule, generated on the device from a seed (synthetic data, no
+checkpoint). A 512-token random prompt is fed, greedy decode fills the
+context, and the timed steps decode at context ~4096. One step = one token
+for every sequence of the batch.
+
+value: tokens/s from CUDA events around K device-side steps (weights and KV
+are 5.8 GB per step, far above the 126 MB L2, so no flush is needed).
+e2e:   tokens/s through att1_infer_decode_token (token id in from the host,
+       next token id and the error word back each step), CUDA events around
+       the loop on the library's stream.
+roofline: the dominant kernel (the q4 GEMV at the gate/up shape, 28672x4096)
+       timed alone with CUDA events over rotating weight copies (294 MB, so
+       every launch streams from HBM), algorithmic bytes / time vs the
+       measured HBM copy bandwidth.
+cpu_baseline: the reference CPU implementation (compiled from its sources,
+       oracle/_ref) on a bounded sample of the same workload, all host cores
+       for its matmuls.
+
+--impl reference runs only that reference CPU measurement (rank 0).
+Under torchrun (N>1) ranks run tensor-parallel shards when the build
+supports it; the JSON line reports whole-job tokens/s (max time over ranks).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))
+
+SHAPE = dict(vocab=128256, n_layers=32, n_heads=32, n_kv_heads=8, d_model=4096, d_ff=14336,
+             theta=500000.0, eps=1e-5)
+METRIC = "q4 decode tokens/s (Llama-3-8B shape, batch 1, ctx 4096)"
+
+
+def q4_bytes(r, c):
+    return r * c // 2 + r * (c // 32) * 4
+
+
+def step_bytes(ctx, batch=1, s=SHAPE):
+    d, H, Hkv, F, V, L = s["d_model"], s["n_heads"], s["n_kv_heads"], s["d_ff"], s["vocab"], s["n_layers"]
+    hd = d // H
+    w = L * (q4_bytes(H * hd, d) + 2 * q4_bytes(Hkv * hd, d) + q4_bytes(d, H * hd) + 2 * q4_bytes(F, d) +
+             q4_bytes(d, F)) + q4_bytes(V, d)
+    kv = batch * L * 2 * ctx * Hkv * hd * 4
+    app = batch * (L * 2 * Hkv * hd * 4 + d * 4)
+    return w + kv + app
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples (SM clock, throttle reasons) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------
+# reference CPU path (oracle/_ref: the ATT-1 sources compiled as they are)
+# ---------------------------------------------------------------------------------------------
+
+def reference_cpu_sample(ctx, steps=2):
+    """Time the reference decode on a bounded sample of the 8B workload:
+    full-width layers with GQA expanded to the reference's MHA layout, KV
+    filled to ctx-1 positions, a 4096-entry lm_head; 1- and 2-layer models
+    separate the per-layer and the per-token parts, extrapolated to 32
+    layers and the 128256-entry vocabulary."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    ref = O.Reference()
+    times = {}
+    vs = 4096
+    for layers in (1, 2):
+        cfg = O.Config.make(vocab=vs, n_layers=layers, n_heads=32, n_kv_heads=8, d_model=4096, d_ff=14336,
+                            max_seq=ctx, dtype=O.Q4, eps=1e-5, theta=500000.0)
+        m = ref.model(cfg, 11, threads=cores)
+        m.fill(ctx - 1 - steps)
+        m.decode(5)  # warm caches
+        t0 = time.perf_counter()
+        for i in range(steps):
+            m.decode(7 + i)
+        times[layers] = (time.perf_counter() - t0) / steps
+        m.close()
+    t_layer = max(times[2] - times[1], 1e-9)
+    t_head = max(times[1] - t_layer, 0.0)
+    t_tok = SHAPE["n_layers"] * t_layer + t_head * SHAPE["vocab"] / vs
+    sample = (f"reference att1 decode (oracle/_ref) at ctx {ctx}: 1- and 2-layer full-width models "
+              f"(GQA expanded to MHA), lm_head 4096 rows, {steps} steps each; "
+              f"{t_layer * 1e3:.1f} ms/layer, extrapolated to 32 layers + 128256-row lm_head")
+    return 1.0 / t_tok, cores, sample
+
+
+# ---------------------------------------------------------------------------------------------
+# B200 path
+# ---------------------------------------------------------------------------------------------
+
+def time_dominant_gemv(b2, torch, reps=30):
+    """q4 GEMV at the gate/up shape on 4 rotating weight copies (294 MB)."""
+    import ctypes as C
+    L = b2.lib()
+    rows, cols = 2 * SHAPE["d_ff"], SHAPE["d_model"]
+    nbuf = 4
+    bufs = [torch.zeros(L.b2_q4_bytes(rows, cols), dtype=torch.uint8, device="cuda") for _ in range(nbuf)]
+    for i, b in enumerate(bufs):
+        assert L.b2_q4_synth(b.data_ptr(), 0, rows, cols, 5, 100 + 2 * i, 101 + 2 * i, 0.02, b2.ROWS_GATEUP,
+                             None) == 0
+    x = torch.randn(cols, device="cuda")
+    g = torch.ones(cols, device="cuda")
+    out = torch.zeros(SHAPE["d_ff"], device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = []
+    for b in bufs:
+        a = b2.GemvArgs()
+        a.w = b2.QWeight(b.data_ptr(), None, 4, rows, cols, rows // 16, cols // 64)
+        a.batch = 1
+        a.x = x.data_ptr()
+        a.x_stride = cols
+        a.norm_w = g.data_ptr()
+        a.eps = 1e-5
+        a.epilogue = b2.EPI_SWIGLU
+        a.out = out.data_ptr()
+        a.out_stride = SHAPE["d_ff"]
+        a.err = err.data_ptr()
+        args.append(a)
+    need = L.b2_gemv_scratch_bytes(C.byref(args[0]))
+    scratch = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    for a in args:
+        a.scratch = scratch.data_ptr()
+        a.scratch_bytes = need
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            assert L.b2_gemv(C.byref(args[i % nbuf]), C.c_void_p(sp)) == 0
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for i in range(reps):
+            ev[i][0].record(stream)
+            L.b2_gemv(C.byref(args[i % nbuf]), C.c_void_p(sp))
+            ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    algo = q4_bytes(rows, cols) + cols * 4 * 2 + SHAPE["d_ff"] * 4
+    del bufs
+    return algo, ms
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+def run_b200(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    import att1_b200 as b2
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    ctx = args.ctx
+    e2e_steps = max(args.steps, 8)
+    cfg = b2.Config.make(SHAPE["vocab"], SHAPE["n_layers"], SHAPE["n_heads"], SHAPE["n_kv_heads"],
+                         SHAPE["d_model"], SHAPE["d_ff"], ctx, dtype=4, eps=SHAPE["eps"], theta=SHAPE["theta"])
+    inf = b2.Infer.synth(cfg, args.seed, batch=args.batch)
+    rng = np.random.default_rng(args.seed + rank)
+    prompt = rng.integers(0, SHAPE["vocab"], size=(args.prompt, args.batch), dtype=np.int64)
+    for t in prompt:
+        tok = inf.decode_batch(t)
+    fill = ctx - args.warmup - args.steps - e2e_steps - args.prompt
+    if fill > 0:
+        inf.run_steps(fill)
+    inf.sync()
+    st = torch.cuda.ExternalStream(inf.stream())
+
+    # warm-up
+    inf.run_steps(args.warmup)
+    inf.sync()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    inf.run_steps(args.steps)
+    e1.record(st)
+    inf.sync()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    pos_timed = inf.position()
+
+    # end to end through att1_infer_decode_token / att1_b200_infer_decode_batch
+    toks = inf.decode_batch(np.asarray(tok))
+    if dist:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(st)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps - 1):
+        if args.batch == 1:
+            toks = [inf.decode(int(toks[0]))]
+        else:
+            toks = inf.decode_batch(toks)
+    f1.record(st)
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) / (e2e_steps - 1)
+    e2e_ms = max(f0.elapsed_time(f1) / (e2e_steps - 1), wall * 1e3)
+
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+
+    algo, kms = time_dominant_gemv(b2, torch)
+    inf.close()
+    peak, peak_kind = measured_peak()
+    achieved = algo / (kms * 1e-3) / 1e9
+    traffic = load_traffic().get("gemv_q4_gateup_28672x4096")
+    bytes_step = step_bytes(pos_timed - args.steps // 2, args.batch)
+    out = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            v, cores, sample = reference_cpu_sample(ctx)
+            cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}
+        value = args.batch * world * 1000.0 / ms if False else args.batch * 1000.0 / ms * (world if args.replicas else 1)
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if args.replicas else "strong", "vs_baseline": None, "dtype": "q4xf32",
+            "data": "synthetic (seeded N(0,0.02) weights quantised on device; random 512-token prompt)",
+            "config": {"workload": "llama3-8b-shape q4 decode", "global_batch": args.batch * (world if args.replicas else 1),
+                       "seq_len": ctx, "context_at_timed_steps": pos_timed,
+                       "parallelism": (f"replicas{world}" if args.replicas else f"tp{world}"),
+                       "l2": "inputs larger than L2 (5.8 GB streamed per step)",
+                       "step_bytes": bytes_step,
+                       "step_hbm_frac": bytes_step / (ms * 1e-3) / (peak * 1e9)},
+            "e2e": {"value": args.batch * 1000.0 / e2e_ms * (world if args.replicas else 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch + 4},
+            "gpu_launches": args.steps * (3 + 5 * SHAPE["n_layers"]),
+            "roofline": {"bound": "hbm", "kernel": "gemv_q4 gate/up 28672x4096 (RMSNorm+SwiGLU fused)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": algo,
+                         "launch_ms": kms},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return out
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    v, cores, sample = reference_cpu_sample(args.ctx, steps=max(1, min(args.steps, 3)))
+    return {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "q4xf32", "data": "synthetic",
+        "config": {"workload": "llama3-8b-shape q4 decode", "global_batch": 1, "seq_len": args.ctx,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    args.replicas = world > 1
+    out = run_reference(args, rank) if args.impl == "reference" else run_b200(args, rank, world, local_rank)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

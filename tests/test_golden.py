@@ -90,3 +90,31 @@ def test_library_file_decode_matches_reference(b2, orc, tmp_path, name, dtype):
     finally:
         L.att1_infer_destroy(h)
         L.att1_model_free(C.byref(m))
+
+
+@pytest.mark.gpu
+def test_file_q8_weights_match_reference_quantiser(b2, orc, tmp_path):
+    """f32 .att1 model -> att1_infer_create: the device q8 weights equal the
+    reference rule applied to the transposed f32 tensors (src/infer.c:196-233)."""
+    g = load("file_q8.npz")
+    path = write_file(tmp_path, orc, g, "f32")
+    L = b2.lib()
+    m = b2.Model()
+    assert L.att1_model_load(path.encode(), C.byref(m)) == 0
+    h = C.c_void_p()
+    assert L.att1_infer_create(C.byref(m), C.byref(h)) == 0
+    inf = b2.Infer(h.value, int(g["vocab"]), 1)
+    d, f, V, seed = int(g["d_model"]), int(g["d_ff"]), int(g["vocab"]), int(g["seed"])
+    shapes = {b2.WQ: (d, d), b2.WK: (d, d), b2.WV: (d, d), b2.WO: (d, d), b2.GATE: (f, d), b2.UP: (f, d),
+              b2.DOWN: (d, f), b2.OUTPUT: (V, d)}
+    try:
+        for layer in range(int(g["n_layers"])):
+            for kind, (rows, cols) in shapes.items():
+                tid = O.T_OUTPUT if kind == b2.OUTPUT else layer * O.T_PER_LAYER + kind
+                v, s = orc.q8_quantize(orc.synth_normal(seed, tid, rows * cols).reshape(rows, cols))
+                gv, gs = inf.export_q8(layer, kind, rows, cols)
+                assert (gv == v).all(), (layer, kind)
+                assert (gs == s).all(), (layer, kind)
+    finally:
+        inf.close()
+        L.att1_model_free(C.byref(m))
