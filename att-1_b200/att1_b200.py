@@ -65,16 +65,16 @@ class GemvArgs(C.Structure):
                 ("out", C.c_void_p), ("out_stride", C.c_uint32), ("resid", C.c_void_p),
                 ("q_rows", C.c_uint32), ("kv_rows", C.c_uint32), ("rope_freq", C.c_void_p),
                 ("positions", C.c_void_p), ("kv", KVLayout), ("argmax", C.c_void_p),
-                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("err", C.c_void_p),
-                ("pdl", C.c_int), ("grid", C.c_int)]
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("counters", C.c_void_p),
+                ("counters_len", C.c_uint32), ("err", C.c_void_p), ("pdl", C.c_int), ("grid", C.c_int)]
 
 
 class AttnArgs(C.Structure):
     _fields_ = [("batch", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
                 ("head_dim", C.c_uint32), ("q", C.c_void_p), ("kv", KVLayout),
                 ("positions", C.c_void_p), ("max_ctx", C.c_uint32), ("ctx", C.c_void_p),
-                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("err", C.c_void_p),
-                ("pdl", C.c_int)]
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("counters", C.c_void_p),
+                ("counters_len", C.c_uint32), ("err", C.c_void_p), ("pdl", C.c_int)]
 
 
 class ModelTensor(C.Structure):
@@ -170,6 +170,8 @@ _SIGS = {
     "b2_q8_quantize_f32": (C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P, C.c_int, C.c_int, _P]),
     "b2_synth_f32": (C.c_int, [_P, _SZ, C.c_uint64, C.c_uint64, _F, _P]),
     "b2_gemv_scratch_bytes": (_SZ, [C.POINTER(GemvArgs)]),
+    "b2_gemv_counters_len": (_U32, [C.POINTER(GemvArgs)]),
+    "b2_attn_counters_len": (_U32, [C.POINTER(AttnArgs)]),
     "b2_gemv": (C.c_int, [C.POINTER(GemvArgs), _P]),
     "b2_attn_scratch_bytes": (_SZ, [C.POINTER(AttnArgs)]),
     "b2_attn": (C.c_int, [C.POINTER(AttnArgs), _P]),

@@ -203,22 +203,31 @@ static cudaError_t launch_attn(const AttnParams &p, dim3 grid, int pdl, cudaStre
 
 using namespace b2;
 
-static void attn_sizes(const b2_attn_args *a, uint32_t &nchunks, size_t &partial, size_t &counters)
+static void attn_sizes(const b2_attn_args *a, uint32_t &nchunks, size_t &partial, uint32_t &counters)
 {
     nchunks = (a->max_ctx + kChunk - 1) / kChunk;
     const uint32_t G = a->n_heads / a->n_kv_heads;
     partial = (size_t)a->batch * a->n_kv_heads * nchunks * G * (a->head_dim + 2) * sizeof(float);
     partial = (partial + 255) & ~(size_t)255;
-    counters = (size_t)a->batch * a->n_kv_heads * sizeof(int);
+    counters = a->batch * a->n_kv_heads;
 }
 
 extern "C" size_t b2_attn_scratch_bytes(const b2_attn_args *a)
 {
     if (a == nullptr || a->n_kv_heads == 0 || a->batch == 0) return 0;
-    uint32_t n;
-    size_t pb, cb;
-    attn_sizes(a, n, pb, cb);
-    return pb + cb;
+    uint32_t n, cl;
+    size_t pb;
+    attn_sizes(a, n, pb, cl);
+    return pb;
+}
+
+extern "C" uint32_t b2_attn_counters_len(const b2_attn_args *a)
+{
+    if (a == nullptr || a->n_kv_heads == 0 || a->batch == 0) return 0;
+    uint32_t n, cl;
+    size_t pb;
+    attn_sizes(a, n, pb, cl);
+    return cl;
 }
 
 extern "C" int b2_attn(const b2_attn_args *a, void *stream)
@@ -233,10 +242,11 @@ extern "C" int b2_attn(const b2_attn_args *a, void *stream)
     if (!kv.k_pool || !kv.v_pool || !kv.page_table || kv.page_tokens == 0 || kv.head_dim != a->head_dim ||
         kv.n_kv_heads != a->n_kv_heads || a->max_ctx > kv.page_tokens * kv.pages_per_seq)
         return -1;
-    uint32_t nchunks;
-    size_t pb, cb;
-    attn_sizes(a, nchunks, pb, cb);
-    if (a->scratch == nullptr || a->scratch_bytes < pb + cb || ((uintptr_t)a->scratch & 255)) return -1;
+    uint32_t nchunks, cl;
+    size_t pb;
+    attn_sizes(a, nchunks, pb, cl);
+    if (a->scratch == nullptr || a->scratch_bytes < pb || ((uintptr_t)a->scratch & 255)) return -1;
+    if (a->counters == nullptr || a->counters_len < cl) return -1;
     AttnParams p = {};
     p.batch = a->batch;
     p.n_heads = a->n_heads;
@@ -250,7 +260,7 @@ extern "C" int b2_attn(const b2_attn_args *a, void *stream)
     p.positions = a->positions;
     p.ctx = a->ctx;
     p.partial = (float *)a->scratch;
-    p.counters = (int *)((uint8_t *)a->scratch + pb);
+    p.counters = (int *)a->counters;
     p.inv_sqrt = 1.0f / sqrtf((float)a->head_dim);  // src/attention.c:512
     p.err = a->err;
     const cudaError_t e = launch_attn(p, dim3(nchunks, a->n_kv_heads, a->batch), a->pdl, (cudaStream_t)stream);

@@ -522,7 +522,8 @@ static int sm_count()
 struct GemvPlan {
     int grid;
     uint32_t maxseg;
-    size_t partial_bytes, counter_bytes;
+    size_t partial_bytes;
+    uint32_t counter_len;
     uint32_t smem, off_ring, off_xdig, off_tile, off_misc;
 };
 
@@ -545,7 +546,7 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     pl.maxseg = (uint32_t)maxseg;
     pl.partial_bytes = (size_t)a->w.tiles * maxseg * 16 * a->batch * sizeof(float);
     pl.partial_bytes = (pl.partial_bytes + 255) & ~(size_t)255;
-    pl.counter_bytes = (size_t)a->w.tiles * sizeof(int);
+    pl.counter_len = a->w.tiles;
     uint32_t off = kWarps * kSlots * 8;
     off = (off + 127) & ~127u;
     pl.off_ring = off;
@@ -590,7 +591,14 @@ extern "C" size_t b2_gemv_scratch_bytes(const b2_gemv_args *a)
 {
     GemvPlan pl;
     if (a == nullptr || a->batch == 0 || !plan_gemv(a, pl)) return 0;
-    return pl.partial_bytes + pl.counter_bytes;
+    return pl.partial_bytes;
+}
+
+extern "C" uint32_t b2_gemv_counters_len(const b2_gemv_args *a)
+{
+    GemvPlan pl;
+    if (a == nullptr || a->batch == 0 || !plan_gemv(a, pl)) return 0;
+    return pl.counter_len;
 }
 
 extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
@@ -629,9 +637,8 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
     GemvPlan pl;
     if (!plan_gemv(a, pl)) return -1;
     if (pl.smem > 227 * 1024) return -9;  // batch x columns too large for on-chip digit planes
-    if (a->scratch == nullptr || a->scratch_bytes < pl.partial_bytes + pl.counter_bytes ||
-        ((uintptr_t)a->scratch & 255))
-        return -1;
+    if (a->scratch == nullptr || a->scratch_bytes < pl.partial_bytes || ((uintptr_t)a->scratch & 255)) return -1;
+    if (a->counters == nullptr || a->counters_len < pl.counter_len) return -1;
 
     GemvParams p = {};
     p.data = (const uint8_t *)w.data;
@@ -656,7 +663,7 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
     p.kv = a->kv;
     p.argmax = a->argmax;
     p.partial = (float *)a->scratch;
-    p.counters = (int *)((uint8_t *)a->scratch + pl.partial_bytes);
+    p.counters = (int *)a->counters;
     p.maxseg = pl.maxseg;
     p.err = a->err;
     p.off_ring = pl.off_ring;

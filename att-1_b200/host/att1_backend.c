@@ -31,6 +31,8 @@ typedef struct cuda_backend {
     size_t cap[3];
     void *scratch;
     size_t scratch_cap;
+    int32_t *counters;
+    uint32_t counters_cap;
     int32_t *err;
     unsigned long long *key;
     cached_mat *cache;
@@ -70,8 +72,19 @@ static int ensure_scratch(cuda_backend *c, size_t bytes)
     c->scratch = NULL;
     c->scratch_cap = 0;
     if (cudaMalloc(&c->scratch, bytes) != cudaSuccess) return -1;
-    if (cudaMemset(c->scratch, 0, bytes) != cudaSuccess) return -1;
     c->scratch_cap = bytes;
+    return 0;
+}
+
+static int ensure_counters(cuda_backend *c, uint32_t n)
+{
+    if (c->counters_cap >= n) return 0;
+    if (c->counters) cudaFree(c->counters);
+    c->counters = NULL;
+    c->counters_cap = 0;
+    if (cudaMalloc((void **)&c->counters, (size_t)n * sizeof(int32_t)) != cudaSuccess) return -1;
+    if (cudaMemset(c->counters, 0, (size_t)n * sizeof(int32_t)) != cudaSuccess) return -1;
+    c->counters_cap = n;
     return 0;
 }
 
@@ -82,7 +95,7 @@ static int finish(cuda_backend *c)
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return -1;
     if (err != 0) {
         cudaMemset(c->err, 0, sizeof(int32_t));
-        if (c->scratch) cudaMemset(c->scratch, 0, c->scratch_cap);
+        if (c->counters) cudaMemset(c->counters, 0, (size_t)c->counters_cap * sizeof(int32_t));
         return -1;
     }
     return 0;
@@ -238,9 +251,11 @@ static int run_gemv(cuda_backend *c, const b2_dev_mat *m, float *dst, const floa
         a.out_stride = (uint32_t)rows;
         a.err = c->err;
         need = b2_gemv_scratch_bytes(&a);
-        if (ensure_scratch(c, need)) return -1;
+        if (ensure_scratch(c, need) || ensure_counters(c, b2_gemv_counters_len(&a))) return -1;
         a.scratch = c->scratch;
         a.scratch_bytes = c->scratch_cap;
+        a.counters = c->counters;
+        a.counters_len = c->counters_cap;
         if (b2_gemv(&a, c->stream) != 0) return -1;
         done += nb;
     }
@@ -423,6 +438,7 @@ void att1_backend_destroy(att1_backend *b)
         for (i = 0; i < 3; i++)
             if (c->buf[i]) cudaFree(c->buf[i]);
         if (c->scratch) cudaFree(c->scratch);
+        if (c->counters) cudaFree(c->counters);
         if (c->err) cudaFree(c->err);
         if (c->key) cudaFree(c->key);
         cudaStreamDestroy(c->stream);

@@ -57,6 +57,8 @@ struct att1_infer {
     int32_t *err_d;
     void *scratch;
     size_t scratch_bytes;
+    int32_t *counters;
+    uint32_t counters_len;
     uint32_t *tokens_h, *out_h;
     int32_t *err_h;
     float *logits_h;
@@ -156,6 +158,7 @@ static void release(att1_infer_t *inf)
     dfree(inf->argmax_d);
     dfree(inf->err_d);
     dfree(inf->scratch);
+    dfree(inf->counters);
     if (inf->tokens_h) cudaFreeHost(inf->tokens_h);
     if (inf->out_h) cudaFreeHost(inf->out_h);
     if (inf->err_h) cudaFreeHost(inf->err_h);
@@ -288,28 +291,51 @@ static att1_status_t build_args(att1_infer_t *inf)
         a->out_stride = c->vocab;
         a->argmax = inf->argmax_d;
     }
-    /* one scratch region serves every kernel: they run one after another */
-    for (l = 0; l < c->n_layers; l++) {
-        dev_layer *L = &inf->layers[l];
-        if ((s = b2_gemv_scratch_bytes(&L->a_qkv)) > need) need = s;
-        if ((s = b2_gemv_scratch_bytes(&L->a_wo)) > need) need = s;
-        if ((s = b2_gemv_scratch_bytes(&L->a_gu)) > need) need = s;
-        if ((s = b2_gemv_scratch_bytes(&L->a_down)) > need) need = s;
-        if ((s = b2_attn_scratch_bytes(&L->a_attn)) > need) need = s;
+    /* One partial-sum region and one counter array serve every kernel: they
+     * run one after another and each leaves its counters at zero. */
+    {
+        uint32_t cmax = 0, cl;
+        for (l = 0; l < c->n_layers; l++) {
+            dev_layer *L = &inf->layers[l];
+            b2_gemv_args *g[4] = {&L->a_qkv, &L->a_wo, &L->a_gu, &L->a_down};
+            int k;
+            for (k = 0; k < 4; k++) {
+                if ((s = b2_gemv_scratch_bytes(g[k])) > need) need = s;
+                if ((cl = b2_gemv_counters_len(g[k])) > cmax) cmax = cl;
+            }
+            if ((s = b2_attn_scratch_bytes(&L->a_attn)) > need) need = s;
+            if ((cl = b2_attn_counters_len(&L->a_attn)) > cmax) cmax = cl;
+        }
+        if ((s = b2_gemv_scratch_bytes(&inf->a_out)) > need) need = s;
+        if ((cl = b2_gemv_counters_len(&inf->a_out)) > cmax) cmax = cl;
+        dfree(inf->scratch);
+        dfree(inf->counters);
+        inf->scratch = NULL;
+        inf->counters = NULL;
+        if ((st = dalloc(inf, &inf->scratch, need)) != ATT1_OK) return st;
+        if ((st = dalloc(inf, (void **)&inf->counters, (size_t)cmax * sizeof(int32_t))) != ATT1_OK) return st;
+        inf->scratch_bytes = need;
+        inf->counters_len = cmax;
     }
-    if ((s = b2_gemv_scratch_bytes(&inf->a_out)) > need) need = s;
-    st = dalloc(inf, &inf->scratch, need);
-    if (st != ATT1_OK) return st;
-    inf->scratch_bytes = need;
     for (l = 0; l < c->n_layers; l++) {
         dev_layer *L = &inf->layers[l];
-        L->a_qkv.scratch = L->a_wo.scratch = L->a_gu.scratch = L->a_down.scratch = inf->scratch;
-        L->a_qkv.scratch_bytes = L->a_wo.scratch_bytes = L->a_gu.scratch_bytes = L->a_down.scratch_bytes = need;
+        b2_gemv_args *g[4] = {&L->a_qkv, &L->a_wo, &L->a_gu, &L->a_down};
+        int k;
+        for (k = 0; k < 4; k++) {
+            g[k]->scratch = inf->scratch;
+            g[k]->scratch_bytes = need;
+            g[k]->counters = inf->counters;
+            g[k]->counters_len = inf->counters_len;
+        }
         L->a_attn.scratch = inf->scratch;
         L->a_attn.scratch_bytes = need;
+        L->a_attn.counters = inf->counters;
+        L->a_attn.counters_len = inf->counters_len;
     }
     inf->a_out.scratch = inf->scratch;
     inf->a_out.scratch_bytes = need;
+    inf->a_out.counters = inf->counters;
+    inf->a_out.counters_len = inf->counters_len;
     return ATT1_OK;
 }
 
@@ -795,7 +821,7 @@ static att1_status_t recover(att1_infer_t *inf, int32_t err)
     uint32_t b;
     for (b = 0; b < inf->batch; b++) pos[b] = (int32_t)inf->position;
     cudaMemsetAsync(inf->err_d, 0, sizeof(int32_t), inf->stream);
-    cudaMemsetAsync(inf->scratch, 0, inf->scratch_bytes, inf->stream);
+    cudaMemsetAsync(inf->counters, 0, (size_t)inf->counters_len * sizeof(int32_t), inf->stream);
     cudaMemcpyAsync(inf->pos_d, pos, inf->batch * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream);
     cudaStreamSynchronize(inf->stream);
     if (err & B2_ERR_TIMEOUT) return ATT1_ERR_TIMEOUT;
@@ -973,8 +999,6 @@ att1_status_t att1_infer_set_backend(att1_infer_t *infer, att1_backend *backend)
         free_weights(infer);
         infer->cfg.dtype = want;
         if ((st = alloc_weights(infer, want)) || (st = load_model_weights(infer, infer->model, want))) return st;
-        dfree(infer->scratch);
-        infer->scratch = NULL;
         if ((st = build_args(infer)) != ATT1_OK) return st;
     }
     if (infer->backend) att1_backend_destroy(infer->backend);

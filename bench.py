@@ -184,9 +184,12 @@ def time_dominant_gemv(b2, torch, reps=30):
         args.append(a)
     need = L.b2_gemv_scratch_bytes(C.byref(args[0]))
     scratch = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    counters = torch.zeros(L.b2_gemv_counters_len(C.byref(args[0])), dtype=torch.int32, device="cuda")
     for a in args:
         a.scratch = scratch.data_ptr()
         a.scratch_bytes = need
+        a.counters = counters.data_ptr()
+        a.counters_len = counters.numel()
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
     torch.cuda.synchronize()

@@ -144,15 +144,20 @@ typedef struct b2_gemv_args {
     b2_kv_layout kv;
     /* B2_EPI_LOGITS */
     unsigned long long *argmax;   /* [batch] packed (ordered value, ~index) keys */
-    /* scratch: partial sums + per-tile counters, zeroed once by the caller */
+    /* scratch: partial sums of tiles split between warps (any contents) */
     void *scratch;
     size_t scratch_bytes;
+    /* per-tile arrival counters: zeroed once by the caller, every launch
+     * leaves them zero again; may be shared by kernels that run in order */
+    int32_t *counters;
+    uint32_t counters_len;
     int32_t *err;                 /* device error word */
     int pdl;                      /* launch with programmatic dependent launch */
     int grid;                     /* 0 = one CTA per SM */
 } b2_gemv_args;
 
 size_t b2_gemv_scratch_bytes(const b2_gemv_args *a);
+uint32_t b2_gemv_counters_len(const b2_gemv_args *a);
 int b2_gemv(const b2_gemv_args *a, void *stream);
 
 /* ---- single-query attention over the paged KV cache (split over positions) */
@@ -163,13 +168,16 @@ typedef struct b2_attn_args {
     const int32_t *positions;     /* [batch]: attend positions 0..pos inclusive */
     uint32_t max_ctx;             /* capacity bound used to size the grid */
     float *ctx;                   /* [batch][n_heads*head_dim] */
-    void *scratch;
+    void *scratch;                /* chunk partials (any contents) */
     size_t scratch_bytes;
+    int32_t *counters;            /* zeroed once by the caller, left zero */
+    uint32_t counters_len;
     int32_t *err;
     int pdl;
 } b2_attn_args;
 
 size_t b2_attn_scratch_bytes(const b2_attn_args *a);
+uint32_t b2_attn_counters_len(const b2_attn_args *a);
 int b2_attn(const b2_attn_args *a, void *stream);
 
 /* ---- per-token step kernels ------------------------------------------------ */
