@@ -108,7 +108,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnParams 
                 if (gq < (int)G) {
                     float dot = 0.0f;
 #pragma unroll
-                    for (int i = 0; i < DPL; ++i) dot = fmaf(q_s[gq * 32 * DPL + lane + 32 * i], kd[j][i], dot);
+                    for (int i = 0; i < DPL; ++i) {
+                        // q_s beyond head_dim is never written: do not read it
+                        const float qv = (lane + 32 * i < (int)hd) ? q_s[gq * 32 * DPL + lane + 32 * i] : 0.0f;
+                        dot = fmaf(qv, kd[j][i], dot);
+                    }
                     dot = warp_sum(dot);
                     const float s = __fmul_rn(dot, p.inv_sqrt);  // src/attention.c:521-523
                     const float nm = fmaxf(m[gq], s);

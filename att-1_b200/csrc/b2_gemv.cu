@@ -376,7 +376,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p
     }
 
     bool ok = true;
+    // tile / unit-in-tile of the next unit, advanced incrementally (no
+    // division in the streaming loop)
     uint32_t cur_tile = nunits ? (uint32_t)(ub / p.kunits) : 0;
+    uint32_t ku = nunits ? (uint32_t)(ub % p.kunits) : 0;
 
     auto flush = [&](uint32_t tile) {
         const uint32_t B = p.batch;
@@ -450,11 +453,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p
 #pragma unroll
         for (uint32_t k = 0; k < (uint32_t)kUnitsPerSlot; ++k) {
             if (k < n) {
-                const uint64_t u = ub + (uint64_t)c * kUnitsPerSlot + k;
-                const uint32_t tile = (uint32_t)(u / p.kunits), ku = (uint32_t)(u % p.kunits);
-                if (tile != cur_tile) {
+                if (ku == p.kunits) {
                     flush(cur_tile);
-                    cur_tile = tile;
+                    ++cur_tile;
+                    ku = 0;
                 }
                 const uint8_t *unit = slot + (size_t)k * UB;
                 const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
@@ -488,6 +490,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p
                                    iacc[j][3]);
                     }
                 }
+                ++ku;
             }
         }
         __syncwarp();
@@ -534,19 +537,7 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t KW = fmt == 4 ? 64u : 32u;
     const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
     if (U == 0) return false;
-    int grid = a->grid > 0 ? a->grid : sm_count();
-    const uint64_t want = (U + kWarps * 4 - 1) / (kWarps * 4);
-    if ((uint64_t)grid > want) grid = (int)(want > 0 ? want : 1);
-    pl.grid = grid;
-    uint64_t W = (uint64_t)grid * kWarps;
-    if (W > U) W = U;
-    const uint64_t minw = U / W;  // >= 1
-    uint64_t maxseg = (a->w.kunits + minw - 1) / minw + 1;
-    if (maxseg > a->w.kunits) maxseg = a->w.kunits;
-    pl.maxseg = (uint32_t)maxseg;
-    pl.partial_bytes = (size_t)a->w.tiles * maxseg * 16 * a->batch * sizeof(float);
-    pl.partial_bytes = (pl.partial_bytes + 255) & ~(size_t)255;
-    pl.counter_len = a->w.tiles;
+    // shared memory: mbarriers | weight rings | digit planes | tile buffers | misc
     uint32_t off = kWarps * kSlots * 8;
     off = (off + 127) & ~127u;
     pl.off_ring = off;
@@ -559,6 +550,21 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     pl.off_misc = off;
     off += (32 + kMaxItems) * 4 + kMaxItems * 8;
     pl.smem = off;
+    // up to two CTAs per SM when they fit (228 KB per SM, 1 KB reserved per CTA)
+    const int ctas_per_sm = (233472u / (pl.smem + 1024u)) >= 2 ? 2 : 1;
+    int grid = a->grid > 0 ? a->grid : sm_count() * ctas_per_sm;
+    const uint64_t want = (U + kWarps * 4 - 1) / (kWarps * 4);
+    if ((uint64_t)grid > want) grid = (int)(want > 0 ? want : 1);
+    pl.grid = grid;
+    uint64_t W = (uint64_t)grid * kWarps;
+    if (W > U) W = U;
+    const uint64_t minw = U / W;  // >= 1
+    uint64_t maxseg = (a->w.kunits + minw - 1) / minw + 1;
+    if (maxseg > a->w.kunits) maxseg = a->w.kunits;
+    pl.maxseg = (uint32_t)maxseg;
+    pl.partial_bytes = (size_t)a->w.tiles * maxseg * 16 * a->batch * sizeof(float);
+    pl.partial_bytes = (pl.partial_bytes + 255) & ~(size_t)255;
+    pl.counter_len = a->w.tiles;
     return true;
 }
 
