@@ -23,14 +23,18 @@
 // and in the 2^-22 relative quantisation of x, far inside the 1e-3 logits
 // tolerance of the parity tests.
 //
-// Streaming. Weights sit in the unit layout of b2_kernels.h. Each warp owns a
+// Streaming. Weights sit in the unit layout of b2_kernels.h. Each CTA owns a
 // contiguous range of units (stream-K over tile-major units, balanced to one
-// unit across the whole grid) and streams it through a private ring of
-// shared-memory slots filled by 1-D bulk copies (cp.async.bulk + mbarrier).
-// A tile shared by several warps is reduced by the last warp to finish it
-// (per-tile arrival counter), summing the partials in warp order, so results
-// are deterministic. Weight prefetch is issued before griddepcontrol.wait, so
-// under programmatic dependent launch it overlaps the previous kernel's tail.
+// unit across the grid). One producer warp streams the range through a ring
+// of shared-memory stages with large 1-D bulk copies (cp.async.bulk, full /
+// empty mbarriers); a stage never straddles a 16-row tile. Eight consumer
+// warps split every stage, and at the end of a tile their partial sums are
+// added through shared memory. The (at most two) tiles a CTA shares with a
+// neighbour are reduced by the last CTA to finish them (per-tile arrival
+// counter), which adds the partials in CTA order, so results are
+// deterministic. The producer starts streaming before griddepcontrol.wait, so
+// under programmatic dependent launch the weight fetch overlaps the previous
+// kernel's tail.
 #include "b2_common.cuh"
 
 #include <cfloat>
@@ -39,10 +43,13 @@
 
 namespace b2 {
 
-constexpr int kWarps = 8;        // consumer warps per CTA (each streams its own range)
-constexpr int kSlots = 6;        // ring slots per warp
-constexpr int kUnitsPerSlot = 2; // units per bulk copy
+constexpr int kConsumerWarps = 8;                   // warps doing the math
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;           // + one producer warp
+constexpr int kStages = 4;                          // ring depth
+constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
 constexpr int kMaxItems = 16;
+constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
 
 struct GemvParams {
     const uint8_t *data;
@@ -92,7 +99,7 @@ __device__ __forceinline__ uint32_t ordered_key(float f)
 // ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
 // The input vector is read once into registers (all loads of a thread issued
 // together, so the prologue costs one L2 round trip instead of one per
-// element group); vectors longer than kPrologueVec * 4 * blockDim fall back
+// element group); vectors longer than kPrologueVec * 4 * kConsumers fall back
 // to re-reading chunks.
 constexpr int kPrologueVec = 16;  // float4 per thread held in registers
 
@@ -148,11 +155,37 @@ __device__ __forceinline__ int pick_exponent(float m)
     return E;
 }
 
+__device__ __forceinline__ void consumer_sync()
+{
+    asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumers) : "memory");
+}
+
+// Sum / max over the consumer threads (deterministic tree); all get the result.
+__device__ __forceinline__ float consumer_sum(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    consumer_sync();
+    if (lane == 0) red[warp] = v;
+    consumer_sync();
+    return warp_sum(lane < kConsumerWarps ? red[lane] : 0.0f);
+}
+
+__device__ __forceinline__ float consumer_max(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    consumer_sync();
+    if (lane == 0) red[warp] = v;
+    consumer_sync();
+    return warp_max(lane < kConsumerWarps ? red[lane] : 0.0f);
+}
+
 template <int FMT>
 __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
 {
     const uint32_t cols = p.cols;
-    const uint32_t stride = blockDim.x * 4;
+    const uint32_t stride = kConsumers * 4;
     for (uint32_t b = 0; b < p.batch; ++b) {
         const float *xb = p.x + (size_t)b * p.x_stride;
         if (cols <= stride * kPrologueVec) {
@@ -167,7 +200,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
 #pragma unroll
                 for (int i = 0; i < kPrologueVec; ++i)
                     ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-                ss = block_sum(ss, red);
+                ss = consumer_sum(ss, red);
                 // src/norm.c:26-28
                 const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
 #pragma unroll
@@ -179,7 +212,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
             float m = 0.0f;
 #pragma unroll
             for (int i = 0; i < kPrologueVec; ++i) m = fmaxf(m, absmax4(v[i]));
-            m = block_max(m, red);
+            m = consumer_max(m, red);
             const bool finite = m <= FLT_MAX;
             if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
             const int E = pick_exponent(m);
@@ -198,7 +231,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
                     const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
                     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                 }
-                ss = block_sum(ss, red);
+                ss = consumer_sum(ss, red);
                 inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
             }
             float m = 0.0f;
@@ -207,7 +240,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
                 if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
                 m = fmaxf(m, absmax4(v));
             }
-            m = block_max(m, red);
+            m = consumer_max(m, red);
             const bool finite = m <= FLT_MAX;
             if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
             const int E = pick_exponent(m);
@@ -316,56 +349,107 @@ __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const float *t
     }
 }
 
+// The stage sequence of a CTA: stage i covers units [u, u + n) with
+// n = min(kStageUnits, end of the CTA range, end of the current tile).
+struct StageWalk {
+    uint64_t u, ce, tend;
+    uint32_t tile, kunits;
+    __device__ StageWalk(uint64_t cb, uint64_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
+    {
+        tile = (uint32_t)(cb / kunits_);
+        tend = (uint64_t)(tile + 1) * kunits_;
+    }
+    __device__ bool more() const { return u < ce; }
+    __device__ uint32_t n() const
+    {
+        uint64_t e = u + kStageUnits;
+        if (e > ce) e = ce;
+        if (e > tend) e = tend;
+        return (uint32_t)(e - u);
+    }
+    __device__ void advance(uint32_t n)
+    {
+        u += n;
+        if (u == tend) {
+            ++tile;
+            tend += kunits;
+        }
+    }
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 template <int FMT, int NI>
-__global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
     constexpr uint32_t KW = Fmt<FMT>::kKW;
     extern __shared__ __align__(128) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * kSlots;
-    uint8_t *ring = smem + p.off_ring + (size_t)warp * kSlots * kUnitsPerSlot * UB;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kStages;
+    uint8_t *ring = smem + p.off_ring;
     uint8_t *xdig = smem + p.off_xdig;
-    float *tbuf = reinterpret_cast<float *>(smem + p.off_tile) + (size_t)warp * 16 * p.batch;
-    float *red = reinterpret_cast<float *>(smem + p.off_misc);            // 32 floats
-    float *item_scale = red + 32;                                          // 16 floats
-    unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);  // 16
+    float *redbuf = reinterpret_cast<float *>(smem + p.off_tile);      // [2][kConsumerWarps][16*B]
+    float *tbuf = redbuf + 2 * kConsumerWarps * 16 * p.batch;          // [16*B]
+    float *red = reinterpret_cast<float *>(smem + p.off_misc);          // 32 floats
+    float *item_scale = red + 32;                                       // 16 floats
+    unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);
 
-    // W active warps (never more than units, so every active warp owns >= 1
-    // unit and every warp that shares a tile arrives at its counter)
     const uint64_t U = (uint64_t)p.tiles * p.kunits;
-    const uint64_t W = min((uint64_t)gridDim.x * kWarps, U);
-    const uint64_t w = (uint64_t)blockIdx.x * kWarps + warp;
-    const uint64_t ub = w < W ? w * U / W : U, ue = w < W ? (w + 1) * U / W : U;
-    const uint32_t nunits = (uint32_t)(ue - ub);
-    const uint32_t nchunks = (nunits + kUnitsPerSlot - 1) / kUnitsPerSlot;
+    const uint64_t G = gridDim.x;  // host guarantees G <= U
+    const uint64_t cb = blockIdx.x * U / G, ce = (blockIdx.x + 1) * U / G;
 
-    if (lane == 0) {
-        for (int s = 0; s < kSlots; ++s) mbar_init(&bars[s], 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
         fence_mbar_init();
     }
     if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
-    __syncwarp();
-    auto issue = [&](uint32_t c) {
-        const uint32_t s = c % kSlots;
-        const uint32_t u0 = c * kUnitsPerSlot;
-        const uint32_t n = min((uint32_t)kUnitsPerSlot, nunits - u0);
-        mbar_arrive_expect_tx(&bars[s], n * UB);
-        bulk_g2s(ring + (size_t)s * kUnitsPerSlot * UB, p.data + (ub + u0) * UB, n * UB, &bars[s]);
-    };
-    if (lane == 0) {
-        for (uint32_t c = 0; c < nchunks && c < (uint32_t)kSlots; ++c) issue(c);
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer: stream the CTA's units -------------------------
+        if (lane == 0) {
+            StageWalk sw(cb, ce, p.kunits);
+            bool waited = false;
+            for (uint32_t i = 0; sw.more(); ++i) {
+                const uint32_t slot = i % kStages, n = sw.n();
+                if (i >= (uint32_t)kStages) {
+                    if (!waited) {
+                        // inputs of the previous kernel are not touched here, but
+                        // signal dependents only once this grid's data is ready
+                        pdl_wait();
+                        pdl_launch_dependents();
+                        waited = true;
+                    }
+                    if (!mbar_wait_bounded(&empty[slot], ((i / kStages) - 1) & 1u, p.err)) break;
+                }
+                mbar_arrive_expect_tx(&full[slot], n * UB);
+                bulk_g2s(ring + (size_t)slot * kStageUnits * UB, p.data + sw.u * UB, n * UB, &full[slot]);
+                sw.advance(n);
+            }
+            if (!waited) {
+                pdl_wait();
+                pdl_launch_dependents();
+            }
+        }
+        return;
     }
 
-    // inputs produced by the previous kernel are read only after this point
+    // ---------------- consumers ----------------------------------------------------------
     pdl_wait();
     pdl_launch_dependents();
     prepare_x<FMT>(p, xdig, item_scale, red);
-    __syncthreads();
+    consumer_sync();
 
-    // per-lane B-fragment coordinates: column g -> (item pair j, item, digit)
+    const int g = lane >> 2, t = lane & 3;
     const uint32_t digit = g & 3;
     float acc[NI][2];
     int iacc[NI][4];
@@ -374,91 +458,22 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p
         acc[j][0] = acc[j][1] = 0.0f;
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
+    bool dead = false;      // a wait timed out: keep the barrier protocol, skip math
+    uint32_t flushes = 0;
 
-    bool ok = true;
-    // tile / unit-in-tile of the next unit, advanced incrementally (no
-    // division in the streaming loop)
-    uint32_t cur_tile = nunits ? (uint32_t)(ub / p.kunits) : 0;
-    uint32_t ku = nunits ? (uint32_t)(ub % p.kunits) : 0;
-
-    auto flush = [&](uint32_t tile) {
-        const uint32_t B = p.batch;
-        // tiles [wf, wl] hold the warps sharing this tile
-        const uint64_t u_first = (uint64_t)tile * p.kunits, u_last = u_first + p.kunits - 1;
-        const uint64_t wf = ((u_first + 1) * W - 1) / U, wl = ((u_last + 1) * W - 1) / U;
-        const uint32_t nseg = (uint32_t)(wl - wf + 1);
-        float *dst = (nseg == 1) ? tbuf : p.partial + ((size_t)tile * p.maxseg + (w - wf)) * 16 * B;
-#pragma unroll
-        for (int j = 0; j < NI; ++j) {
-            float v0, v1;
-            if (FMT == 4) {
-                v0 = acc[j][0];
-                v1 = acc[j][1];
-            } else {
-                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
-                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
-            }
-            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
-            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
-            const uint32_t item = 2 * j + (t >> 1);
-            if ((t & 1) == 0 && item < B) {
-                const float s = item_scale[item];
-                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
-                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
-                if (FMT == 8) {
-                    y0 = __fmul_rn(y0, p.row_scale[tile * 16 + g]);
-                    y1 = __fmul_rn(y1, p.row_scale[tile * 16 + g + 8]);
-                }
-                dst[g * B + item] = y0;
-                dst[(g + 8) * B + item] = y1;
-            }
-            acc[j][0] = acc[j][1] = 0.0f;
-            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+    StageWalk sw(cb, ce, p.kunits);
+    for (uint32_t i = 0; sw.more(); ++i) {
+        const uint32_t slot = i % kStages, n = sw.n();
+        const uint32_t ku0 = (uint32_t)(sw.u - (uint64_t)sw.tile * p.kunits);
+        if (!dead) {
+            const bool got = mbar_wait_bounded(&full[slot], (i / kStages) & 1u, p.err);
+            dead = !__all_sync(0xffffffffu, got);
         }
-        if (nseg > 1) {
-            __threadfence();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) return;
-            __threadfence();
-            const float *base = p.partial + (size_t)tile * p.maxseg * 16 * B;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
-                float s = 0.0f;
-                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(base + (size_t)sg * 16 * B + idx));
-                tbuf[idx] = s;
-            }
-            if (lane == 0) p.counters[tile] = 0;
-        }
-        __syncwarp();
-        tile_epilogue(p, tile, tbuf, cta_key, lane);
-        __syncwarp();
-    };
-
-    for (uint32_t c = 0; c < nchunks; ++c) {
-        const uint32_t s = c % kSlots;
-        const bool got = mbar_wait_bounded(&bars[s], (c / kSlots) & 1u, p.err);
-        if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            // drain copies still in flight into this warp's ring, with a bound
-            if (lane == 0) {
-                for (uint32_t c2 = c; c2 < nchunks && c2 < c + kSlots; ++c2)
-                    mbar_wait_bounded(&bars[c2 % kSlots], (c2 / kSlots) & 1u, p.err);
-            }
-            break;
-        }
-        const uint8_t *slot = ring + (size_t)s * kUnitsPerSlot * UB;
-        const uint32_t n = min((uint32_t)kUnitsPerSlot, nunits - c * kUnitsPerSlot);
-#pragma unroll
-        for (uint32_t k = 0; k < (uint32_t)kUnitsPerSlot; ++k) {
-            if (k < n) {
-                if (ku == p.kunits) {
-                    flush(cur_tile);
-                    ++cur_tile;
-                    ku = 0;
-                }
-                const uint8_t *unit = slot + (size_t)k * UB;
+        if (!dead) {
+            const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
+            for (uint32_t k = warp; k < n; k += kConsumerWarps) {
+                const uint8_t *unit = stage + (size_t)k * UB;
+                const uint32_t ku = ku0 + k;
                 const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
                 if (FMT == 4) {
                     const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
@@ -490,19 +505,81 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const GemvParams p
                                    iacc[j][3]);
                     }
                 }
-                ++ku;
             }
         }
         __syncwarp();
-        if (lane == 0 && c + kSlots < nchunks) {
-            fence_proxy_async();
-            issue(c + kSlots);
-        }
-    }
-    if (ok && nunits > 0) flush(cur_tile);
+        if (lane == 0) mbar_arrive(&empty[slot]);
 
+        const uint32_t tile = sw.tile;
+        const uint64_t tfirst = (uint64_t)tile * p.kunits, tend = sw.tend;
+        sw.advance(n);
+        if (sw.u != tend && sw.u != ce) continue;
+
+        // ---------------- end of this CTA's part of `tile`: reduce the warps ---------------
+        const uint32_t B = p.batch;
+        float *rb = redbuf + (size_t)(flushes & 1u) * kConsumerWarps * 16 * B;
+        ++flushes;
+#pragma unroll
+        for (int j = 0; j < NI; ++j) {
+            float v0, v1;
+            if (FMT == 4) {
+                v0 = acc[j][0];
+                v1 = acc[j][1];
+            } else {
+                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
+                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
+            }
+            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
+            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
+            const uint32_t item = 2 * j + (t >> 1);
+            if ((t & 1) == 0 && item < B) {
+                const float s = item_scale[item];
+                rb[warp * 16 * B + g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
+                rb[warp * 16 * B + (g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+            }
+            acc[j][0] = acc[j][1] = 0.0f;
+            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+        }
+        consumer_sync();
+        if (warp != 0) continue;
+        // warp 0: CTA sum (warp order), then epilogue or cross-CTA reduction
+        const bool whole = tfirst >= cb && tend <= ce;
+        for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) s = __fadd_rn(s, rb[w * 16 * B + idx]);
+            if (FMT == 8) s = __fmul_rn(s, p.row_scale[tile * 16 + idx / B]);
+            tbuf[idx] = s;
+        }
+        if (!whole) {
+            const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = (tend * G - 1) / U;
+            const uint32_t nseg = (uint32_t)(cl - cf + 1);
+            float *base = p.partial + (size_t)tile * p.maxseg * 16 * B;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) base[(blockIdx.x - cf) * 16 * B + idx] = tbuf[idx];
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence();
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+                float s = 0.0f;
+                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(base + (size_t)sg * 16 * B + idx));
+                tbuf[idx] = s;
+            }
+            if (lane == 0) p.counters[tile] = 0;
+        }
+        __syncwarp();
+        if (!dead) tile_epilogue(p, tile, tbuf, cta_key, lane);
+        __syncwarp();
+    }
+    if (dead && warp == 0 && lane == 0) {
+        // the ring may still be filling: wait (bounded) for each stage's last phase
+        for (int s = 0; s < kStages; ++s) (void)mbar_try_wait(&full[s], 0), (void)mbar_try_wait(&full[s], 1);
+    }
     if (p.epilogue == B2_EPI_LOGITS) {
-        __syncthreads();
+        consumer_sync();
         if (threadIdx.x < p.batch && cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], cta_key[threadIdx.x]);
     }
 }
@@ -537,29 +614,29 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t KW = fmt == 4 ? 64u : 32u;
     const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
     if (U == 0) return false;
-    // shared memory: mbarriers | weight rings | digit planes | tile buffers | misc
-    uint32_t off = kWarps * kSlots * 8;
+    // shared memory: mbarriers | stage ring | digit planes | reduction buffers | misc
+    uint32_t off = 2 * kStages * 8;
     off = (off + 127) & ~127u;
     pl.off_ring = off;
-    off += kWarps * kSlots * kUnitsPerSlot * UB;
+    off += kStages * kStageUnits * UB;
     pl.off_xdig = off;
     off += a->w.kunits * a->batch * 3 * KW;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
-    off += kWarps * 16 * a->batch * 4;
+    off += (2 * kConsumerWarps + 1) * 16 * a->batch * 4;
+    off = (off + 15) & ~15u;
     pl.off_misc = off;
     off += (32 + kMaxItems) * 4 + kMaxItems * 8;
     pl.smem = off;
-    // up to two CTAs per SM when they fit (228 KB per SM, 1 KB reserved per CTA)
-    const int ctas_per_sm = (233472u / (pl.smem + 1024u)) >= 2 ? 2 : 1;
-    int grid = a->grid > 0 ? a->grid : sm_count() * ctas_per_sm;
-    const uint64_t want = (U + kWarps * 4 - 1) / (kWarps * 4);
-    if ((uint64_t)grid > want) grid = (int)(want > 0 ? want : 1);
+    // one CTA per SM; at least a stage's worth of units per CTA
+    int grid = a->grid > 0 ? a->grid : sm_count();
+    const uint64_t want = (U + kConsumerWarps * 2 - 1) / (kConsumerWarps * 2);
+    if ((uint64_t)grid > want) grid = (int)want;
+    if ((uint64_t)grid > U) grid = (int)U;
+    if (grid < 1) grid = 1;
     pl.grid = grid;
-    uint64_t W = (uint64_t)grid * kWarps;
-    if (W > U) W = U;
-    const uint64_t minw = U / W;  // >= 1
-    uint64_t maxseg = (a->w.kunits + minw - 1) / minw + 1;
+    const uint64_t minc = U / (uint64_t)grid;  // >= 1
+    uint64_t maxseg = (a->w.kunits + minc - 1) / minc + 1;
     if (maxseg > a->w.kunits) maxseg = a->w.kunits;
     pl.maxseg = (uint32_t)maxseg;
     pl.partial_bytes = (size_t)a->w.tiles * maxseg * 16 * a->batch * sizeof(float);
@@ -576,7 +653,7 @@ static cudaError_t launch_t(const GemvParams &p, const GemvPlan &pl, int pdl, cu
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.grid);
-    cfg.blockDim = dim3(kWarps * 32);
+    cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
