@@ -50,6 +50,11 @@ constexpr int kStages = 4;                          // ring depth
 constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
 constexpr int kMaxItems = 16;
 constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
+// Tile-partial slots: a warp may be writing tile j while others still work on
+// tiles j-3..j-1 (the ring lets warps drift kStages-1 stages apart, and a
+// stage never spans two tiles) and the last warp of tile j-4 may still be
+// reducing it: kStages + 2 slots keep them all apart.
+constexpr int kTileSlots = kStages + 2;
 
 struct GemvParams {
     const uint8_t *data;
@@ -394,11 +399,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
     uint64_t *empty = full + kStages;
     uint8_t *ring = smem + p.off_ring;
     uint8_t *xdig = smem + p.off_xdig;
-    float *redbuf = reinterpret_cast<float *>(smem + p.off_tile);      // [2][kConsumerWarps][16*B]
-    float *tbuf = redbuf + 2 * kConsumerWarps * 16 * p.batch;          // [16*B]
+    float *tslots = reinterpret_cast<float *>(smem + p.off_tile);      // [kTileSlots][warps][16*B]
+    float *tbuf = tslots + kTileSlots * kConsumerWarps * 16 * p.batch; // [warps][16*B]
     float *red = reinterpret_cast<float *>(smem + p.off_misc);          // 32 floats
     float *item_scale = red + 32;                                       // 16 floats
     unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);
+    int *tcount = reinterpret_cast<int *>(cta_key + kMaxItems);         // [kTileSlots]
 
     const uint64_t U = (uint64_t)p.tiles * p.kunits;
     const uint64_t G = gridDim.x;  // host guarantees G <= U
@@ -412,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         fence_mbar_init();
     }
     if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
+    if (threadIdx.x < kTileSlots) tcount[threadIdx.x] = 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -458,8 +465,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         acc[j][0] = acc[j][1] = 0.0f;
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
-    bool dead = false;      // a wait timed out: keep the barrier protocol, skip math
-    uint32_t flushes = 0;
+    bool dead = false;      // a wait timed out: keep the stage protocol, skip the math
+    uint32_t tile_seq = 0;  // tiles this CTA has finished (same count in every warp)
+    const uint32_t B = p.batch;
+    float *mytbuf = tbuf + (size_t)warp * 16 * B;
 
     StageWalk sw(cb, ce, p.kunits);
     for (uint32_t i = 0; sw.more(); ++i) {
@@ -471,38 +480,43 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         }
         if (!dead) {
             const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
-            for (uint32_t k = warp; k < n; k += kConsumerWarps) {
-                const uint8_t *unit = stage + (size_t)k * UB;
-                const uint32_t ku = ku0 + k;
-                const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
-                if (FMT == 4) {
-                    const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
-                    const uint32_t M = 0xF0F0F0F0u;
-                    const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
-                    const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
+            // this warp's units of the stage, unrolled so their loads overlap
 #pragma unroll
-                    for (int j = 0; j < NI; ++j) {
-                        const uint32_t item = 2 * j + (g >> 2);
-                        uint4 bf = make_uint4(0, 0, 0, 0);
-                        if (digit < 3 && item < p.batch)
-                            bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * p.batch + item) * 3 + digit) * KW + t * 16);
-                        int d[4], e[4];
-                        imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
-                        imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
-                        acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
-                        acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
-                        acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
-                        acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
-                    }
-                } else {
+            for (int m = 0; m < kStageUnits / kConsumerWarps; ++m) {
+                const uint32_t k = warp + m * kConsumerWarps;
+                if (k < n) {
+                    const uint8_t *unit = stage + (size_t)k * UB;
+                    const uint32_t ku = ku0 + k;
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
+                    if (FMT == 4) {
+                        const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
+                        const uint32_t M = 0xF0F0F0F0u;
+                        const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
+                        const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
 #pragma unroll
-                    for (int j = 0; j < NI; ++j) {
-                        const uint32_t item = 2 * j + (g >> 2);
-                        uint2 bf = make_uint2(0, 0);
-                        if (digit < 3 && item < p.batch)
-                            bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * p.batch + item) * 3 + digit) * KW + t * 8);
-                        imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
-                                   iacc[j][3]);
+                        for (int j = 0; j < NI; ++j) {
+                            const uint32_t item = 2 * j + (g >> 2);
+                            uint4 bf = make_uint4(0, 0, 0, 0);
+                            if (digit < 3 && item < B)
+                                bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
+                            int d[4], e[4];
+                            imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
+                            imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
+                            acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
+                            acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
+                            acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
+                            acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < NI; ++j) {
+                            const uint32_t item = 2 * j + (g >> 2);
+                            uint2 bf = make_uint2(0, 0);
+                            if (digit < 3 && item < B)
+                                bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
+                            imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                                       iacc[j][3]);
+                        }
                     }
                 }
             }
@@ -515,10 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         sw.advance(n);
         if (sw.u != tend && sw.u != ce) continue;
 
-        // ---------------- end of this CTA's part of `tile`: reduce the warps ---------------
-        const uint32_t B = p.batch;
-        float *rb = redbuf + (size_t)(flushes & 1u) * kConsumerWarps * 16 * B;
-        ++flushes;
+        // ---- end of this CTA's part of `tile`: drop this warp's partial into the
+        // tile slot; the last warp to arrive reduces (in warp order) and finishes
+        const uint32_t ts = tile_seq++ % kTileSlots;
+        float *part = tslots + ((size_t)ts * kConsumerWarps + warp) * 16 * B;
 #pragma unroll
         for (int j = 0; j < NI; ++j) {
             float v0, v1;
@@ -534,28 +548,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
             const uint32_t item = 2 * j + (t >> 1);
             if ((t & 1) == 0 && item < B) {
                 const float s = item_scale[item];
-                rb[warp * 16 * B + g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
-                rb[warp * 16 * B + (g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+                part[g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
+                part[(g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
             }
             acc[j][0] = acc[j][1] = 0.0f;
             iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
         }
-        consumer_sync();
-        if (warp != 0) continue;
-        // warp 0: CTA sum (warp order), then epilogue or cross-CTA reduction
-        const bool whole = tfirst >= cb && tend <= ce;
+        __threadfence_block();
+        __syncwarp();
+        int lastw = 0;
+        if (lane == 0) lastw = (atomicAdd(&tcount[ts], 1) == kConsumerWarps - 1);
+        lastw = __shfl_sync(0xffffffffu, lastw, 0);
+        if (!lastw) continue;
+        __threadfence_block();
+        const float *parts = tslots + (size_t)ts * kConsumerWarps * 16 * B;
         for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
             float s = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) s = __fadd_rn(s, rb[w * 16 * B + idx]);
+            for (int w = 0; w < kConsumerWarps; ++w) s = __fadd_rn(s, parts[w * 16 * B + idx]);
             if (FMT == 8) s = __fmul_rn(s, p.row_scale[tile * 16 + idx / B]);
-            tbuf[idx] = s;
+            mytbuf[idx] = s;
         }
-        if (!whole) {
+        __syncwarp();
+        if (lane == 0) tcount[ts] = 0;
+        if (!(tfirst >= cb && tend <= ce)) {
+            // tile shared with neighbouring CTAs: the last CTA adds all partials
             const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = (tend * G - 1) / U;
             const uint32_t nseg = (uint32_t)(cl - cf + 1);
             float *base = p.partial + (size_t)tile * p.maxseg * 16 * B;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) base[(blockIdx.x - cf) * 16 * B + idx] = tbuf[idx];
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) base[(blockIdx.x - cf) * 16 * B + idx] = mytbuf[idx];
             __threadfence();
             __syncwarp();
             int last = 0;
@@ -566,12 +587,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
             for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
                 float s = 0.0f;
                 for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(base + (size_t)sg * 16 * B + idx));
-                tbuf[idx] = s;
+                mytbuf[idx] = s;
             }
             if (lane == 0) p.counters[tile] = 0;
+            __syncwarp();
         }
-        __syncwarp();
-        if (!dead) tile_epilogue(p, tile, tbuf, cta_key, lane);
+        if (!dead) tile_epilogue(p, tile, mytbuf, cta_key, lane);
         __syncwarp();
     }
     if (dead && warp == 0 && lane == 0) {
@@ -623,10 +644,10 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     off += a->w.kunits * a->batch * 3 * KW;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
-    off += (2 * kConsumerWarps + 1) * 16 * a->batch * 4;
+    off += (kTileSlots + 1) * kConsumerWarps * 16 * a->batch * 4;
     off = (off + 15) & ~15u;
     pl.off_misc = off;
-    off += (32 + kMaxItems) * 4 + kMaxItems * 8;
+    off += (32 + kMaxItems) * 4 + kMaxItems * 8 + kTileSlots * 4;
     pl.smem = off;
     // one CTA per SM; at least a stage's worth of units per CTA
     int grid = a->grid > 0 ? a->grid : sm_count();
