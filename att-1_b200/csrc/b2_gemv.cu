@@ -23,18 +23,22 @@
 // and in the 2^-22 relative quantisation of x, far inside the 1e-3 logits
 // tolerance of the parity tests.
 //
-// Streaming. Weights sit in the unit layout of b2_kernels.h. Each CTA owns a
+// Streaming. Weights sit in the unit layout of b2_kernels.h. Every warp owns a
 // contiguous range of units (stream-K over tile-major units, balanced to one
-// unit across the grid). One producer warp streams the range through a ring
-// of shared-memory stages with large 1-D bulk copies (cp.async.bulk, full /
-// empty mbarriers); a stage never straddles a 16-row tile. Eight consumer
-// warps split every stage, and at the end of a tile their partial sums are
-// added through shared memory. The (at most two) tiles a CTA shares with a
-// neighbour are reduced by the last CTA to finish them (per-tile arrival
-// counter), which adds the partials in CTA order, so results are
-// deterministic. The producer starts streaming before griddepcontrol.wait, so
-// under programmatic dependent launch the weight fetch overlaps the previous
-// kernel's tail.
+// unit across the grid) and streams it with 128-bit non-coherent loads,
+// keeping kPrefetch units in flight in registers (one 512-byte coalesced
+// request per unit and warp). A tile that lies inside one warp's range is
+// finished by that warp on the spot. Tiles split between warps of a CTA are
+// added through shared memory once the CTA's warps are done, in warp order;
+// tiles split between CTAs are added by the last CTA to finish them (per-tile
+// arrival counter), in CTA order, so results are deterministic. The first
+// weight loads are issued before griddepcontrol.wait, so under programmatic
+// dependent launch they overlap the previous kernel's tail.
+//
+// (A producer-warp design feeding a shared-memory ring with 1-D bulk copies
+// was measured first: one SM completed roughly one bulk copy per 0.4-0.6 us
+// whatever its size up to 20 KB, which capped the stream well below HBM
+// bandwidth; plain vector loads from all warps keep far more bytes in flight.)
 #include "b2_common.cuh"
 
 #include <cfloat>
@@ -43,18 +47,10 @@
 
 namespace b2 {
 
-constexpr int kConsumerWarps = 8;                   // warps doing the math
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;           // + one producer warp
-constexpr int kStages = 4;                          // ring depth
-constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
+constexpr int kWarps = 8;                           // warps per CTA, each with its own unit range
+constexpr int kThreads = kWarps * 32;
+constexpr int kPrefetch = 6;                        // units in flight per warp
 constexpr int kMaxItems = 16;
-constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
-// Tile-partial slots: a warp may be writing tile j while others still work on
-// tiles j-3..j-1 (the ring lets warps drift kStages-1 stages apart, and a
-// stage never spans two tiles) and the last warp of tile j-4 may still be
-// reducing it: kStages + 2 slots keep them all apart.
-constexpr int kTileSlots = kStages + 2;
 
 struct GemvParams {
     const uint8_t *data;
@@ -104,7 +100,7 @@ __device__ __forceinline__ uint32_t ordered_key(float f)
 // ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
 // The input vector is read once into registers (all loads of a thread issued
 // together, so the prologue costs one L2 round trip instead of one per
-// element group); vectors longer than kPrologueVec * 4 * kConsumers fall back
+// element group); vectors longer than kPrologueVec * 4 * kThreads fall back
 // to re-reading chunks.
 constexpr int kPrologueVec = 16;  // float4 per thread held in registers
 
@@ -160,37 +156,11 @@ __device__ __forceinline__ int pick_exponent(float m)
     return E;
 }
 
-__device__ __forceinline__ void consumer_sync()
-{
-    asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumers) : "memory");
-}
-
-// Sum / max over the consumer threads (deterministic tree); all get the result.
-__device__ __forceinline__ float consumer_sum(float v, float *red)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    consumer_sync();
-    if (lane == 0) red[warp] = v;
-    consumer_sync();
-    return warp_sum(lane < kConsumerWarps ? red[lane] : 0.0f);
-}
-
-__device__ __forceinline__ float consumer_max(float v, float *red)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_max(v);
-    consumer_sync();
-    if (lane == 0) red[warp] = v;
-    consumer_sync();
-    return warp_max(lane < kConsumerWarps ? red[lane] : 0.0f);
-}
-
 template <int FMT>
 __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
 {
     const uint32_t cols = p.cols;
-    const uint32_t stride = kConsumers * 4;
+    const uint32_t stride = kThreads * 4;
     for (uint32_t b = 0; b < p.batch; ++b) {
         const float *xb = p.x + (size_t)b * p.x_stride;
         if (cols <= stride * kPrologueVec) {
@@ -205,7 +175,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
 #pragma unroll
                 for (int i = 0; i < kPrologueVec; ++i)
                     ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-                ss = consumer_sum(ss, red);
+                ss = block_sum(ss, red);
                 // src/norm.c:26-28
                 const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
 #pragma unroll
@@ -217,7 +187,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
             float m = 0.0f;
 #pragma unroll
             for (int i = 0; i < kPrologueVec; ++i) m = fmaxf(m, absmax4(v[i]));
-            m = consumer_max(m, red);
+            m = block_max(m, red);
             const bool finite = m <= FLT_MAX;
             if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
             const int E = pick_exponent(m);
@@ -236,7 +206,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
                     const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
                     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                 }
-                ss = consumer_sum(ss, red);
+                ss = block_sum(ss, red);
                 inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
             }
             float m = 0.0f;
@@ -245,7 +215,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
                 if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
                 m = fmaxf(m, absmax4(v));
             }
-            m = consumer_max(m, red);
+            m = block_max(m, red);
             const bool finite = m <= FLT_MAX;
             if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
             const int E = pick_exponent(m);
@@ -354,109 +324,71 @@ __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const float *t
     }
 }
 
-// The stage sequence of a CTA: stage i covers units [u, u + n) with
-// n = min(kStageUnits, end of the CTA range, end of the current tile).
-struct StageWalk {
-    uint64_t u, ce, tend;
-    uint32_t tile, kunits;
-    __device__ StageWalk(uint64_t cb, uint64_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
-    {
-        tile = (uint32_t)(cb / kunits_);
-        tend = (uint64_t)(tile + 1) * kunits_;
-    }
-    __device__ bool more() const { return u < ce; }
-    __device__ uint32_t n() const
-    {
-        uint64_t e = u + kStageUnits;
-        if (e > ce) e = ce;
-        if (e > tend) e = tend;
-        return (uint32_t)(e - u);
-    }
-    __device__ void advance(uint32_t n)
-    {
-        u += n;
-        if (u == tend) {
-            ++tile;
-            tend += kunits;
-        }
-    }
-};
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+__device__ __forceinline__ uint4 ldg_stream(const void *ptr)
 {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ptr));
+    return r;
 }
 
+__device__ __forceinline__ float4 ldg_f4(const void *ptr)
+{
+    float4 r;
+    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(ptr));
+    return r;
+}
+
+// Warp index that owns unit u when U units are split over W warps.
+__device__ __forceinline__ uint64_t warp_of(uint64_t u, uint64_t U, uint64_t W) { return ((u + 1) * W - 1) / U; }
+
 template <int FMT, int NI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
     constexpr uint32_t KW = Fmt<FMT>::kKW;
     extern __shared__ __align__(128) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + kStages;
-    uint8_t *ring = smem + p.off_ring;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t B = p.batch;
     uint8_t *xdig = smem + p.off_xdig;
-    float *tslots = reinterpret_cast<float *>(smem + p.off_tile);      // [kTileSlots][warps][16*B]
-    float *tbuf = tslots + kTileSlots * kConsumerWarps * 16 * p.batch; // [warps][16*B]
+    float *segs = reinterpret_cast<float *>(smem + p.off_tile);        // [kWarps][2][16*B]
+    float *tbufs = segs + kWarps * 2 * 16 * B;                          // [kWarps][16*B]
     float *red = reinterpret_cast<float *>(smem + p.off_misc);          // 32 floats
     float *item_scale = red + 32;                                       // 16 floats
     unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);
-    int *tcount = reinterpret_cast<int *>(cta_key + kMaxItems);         // [kTileSlots]
+    int *seg_tile = reinterpret_cast<int *>(cta_key + kMaxItems);       // [kWarps][2]
+    float *tbuf = tbufs + (size_t)warp * 16 * B;
 
     const uint64_t U = (uint64_t)p.tiles * p.kunits;
-    const uint64_t G = gridDim.x;  // host guarantees G <= U
-    const uint64_t cb = blockIdx.x * U / G, ce = (blockIdx.x + 1) * U / G;
+    const uint64_t W = min((uint64_t)gridDim.x * kWarps, U);  // active warps, each >= 1 unit
+    const uint64_t w = (uint64_t)blockIdx.x * kWarps + warp;
+    const uint64_t ub = w < W ? w * U / W : U, ue = w < W ? (w + 1) * U / W : U;
+    const uint32_t n = (uint32_t)(ue - ub);
+    const uint8_t *src = p.data + ub * UB;
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+    // weights do not depend on the previous kernel: start streaming now
+    uint4 wv[kPrefetch];
+    float4 sv[kPrefetch];
+#pragma unroll
+    for (int q = 0; q < kPrefetch; ++q) {
+        if ((uint32_t)q < n) {
+            wv[q] = ldg_stream(src + (size_t)q * UB + lane * 16);
+            if (FMT == 4) sv[q] = ldg_f4(src + (size_t)q * UB + 512 + g * 16);
         }
-        fence_mbar_init();
     }
     if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
-    if (threadIdx.x < kTileSlots) tcount[threadIdx.x] = 0;
-    __syncthreads();
+    if (threadIdx.x < kWarps * 2) seg_tile[threadIdx.x] = -1;
 
-    if (warp == kConsumerWarps) {
-        // ---------------- producer: stream the CTA's units -------------------------
-        if (lane == 0) {
-            StageWalk sw(cb, ce, p.kunits);
-            bool waited = false;
-            for (uint32_t i = 0; sw.more(); ++i) {
-                const uint32_t slot = i % kStages, n = sw.n();
-                if (i >= (uint32_t)kStages) {
-                    if (!waited) {
-                        // inputs of the previous kernel are not touched here, but
-                        // signal dependents only once this grid's data is ready
-                        pdl_wait();
-                        pdl_launch_dependents();
-                        waited = true;
-                    }
-                    if (!mbar_wait_bounded(&empty[slot], ((i / kStages) - 1) & 1u, p.err)) break;
-                }
-                mbar_arrive_expect_tx(&full[slot], n * UB);
-                bulk_g2s(ring + (size_t)slot * kStageUnits * UB, p.data + sw.u * UB, n * UB, &full[slot]);
-                sw.advance(n);
-            }
-            if (!waited) {
-                pdl_wait();
-                pdl_launch_dependents();
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumers ----------------------------------------------------------
     pdl_wait();
     pdl_launch_dependents();
     prepare_x<FMT>(p, xdig, item_scale, red);
-    consumer_sync();
+    __syncthreads();
 
-    const int g = lane >> 2, t = lane & 3;
     const uint32_t digit = g & 3;
     float acc[NI][2];
     int iacc[NI][4];
@@ -465,74 +397,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         acc[j][0] = acc[j][1] = 0.0f;
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
-    bool dead = false;      // a wait timed out: keep the stage protocol, skip the math
-    uint32_t tile_seq = 0;  // tiles this CTA has finished (same count in every warp)
-    const uint32_t B = p.batch;
-    float *mytbuf = tbuf + (size_t)warp * 16 * B;
+    uint32_t tile = n ? (uint32_t)(ub / p.kunits) : 0;
+    uint32_t ku = n ? (uint32_t)(ub % p.kunits) : 0;
+    bool started_here = (ku == 0);
 
-    StageWalk sw(cb, ce, p.kunits);
-    for (uint32_t i = 0; sw.more(); ++i) {
-        const uint32_t slot = i % kStages, n = sw.n();
-        const uint32_t ku0 = (uint32_t)(sw.u - (uint64_t)sw.tile * p.kunits);
-        if (!dead) {
-            const bool got = mbar_wait_bounded(&full[slot], (i / kStages) & 1u, p.err);
-            dead = !__all_sync(0xffffffffu, got);
+    // Tile `tile` is done for this warp: combine the lanes into [16][B] and
+    // either finish it (whole tile in this warp) or park it as a segment.
+    auto close_tile = [&](bool complete) {
+        float *dst;
+        int slot = -1;
+        if (started_here && complete) {
+            dst = tbuf;
+        } else {
+            slot = started_here ? 1 : 0;
+            dst = segs + ((size_t)warp * 2 + slot) * 16 * B;
         }
-        if (!dead) {
-            const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
-            // this warp's units of the stage, unrolled so their loads overlap
-#pragma unroll
-            for (int m = 0; m < kStageUnits / kConsumerWarps; ++m) {
-                const uint32_t k = warp + m * kConsumerWarps;
-                if (k < n) {
-                    const uint8_t *unit = stage + (size_t)k * UB;
-                    const uint32_t ku = ku0 + k;
-                    const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
-                    if (FMT == 4) {
-                        const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
-                        const uint32_t M = 0xF0F0F0F0u;
-                        const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
-                        const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
-#pragma unroll
-                        for (int j = 0; j < NI; ++j) {
-                            const uint32_t item = 2 * j + (g >> 2);
-                            uint4 bf = make_uint4(0, 0, 0, 0);
-                            if (digit < 3 && item < B)
-                                bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
-                            int d[4], e[4];
-                            imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
-                            imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
-                            acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
-                            acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
-                            acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
-                            acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < NI; ++j) {
-                            const uint32_t item = 2 * j + (g >> 2);
-                            uint2 bf = make_uint2(0, 0);
-                            if (digit < 3 && item < B)
-                                bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
-                            imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
-                                       iacc[j][3]);
-                        }
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-
-        const uint32_t tile = sw.tile;
-        const uint64_t tfirst = (uint64_t)tile * p.kunits, tend = sw.tend;
-        sw.advance(n);
-        if (sw.u != tend && sw.u != ce) continue;
-
-        // ---- end of this CTA's part of `tile`: drop this warp's partial into the
-        // tile slot; the last warp to arrive reduces (in warp order) and finishes
-        const uint32_t ts = tile_seq++ % kTileSlots;
-        float *part = tslots + ((size_t)ts * kConsumerWarps + warp) * 16 * B;
 #pragma unroll
         for (int j = 0; j < NI; ++j) {
             float v0, v1;
@@ -548,60 +427,126 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
             const uint32_t item = 2 * j + (t >> 1);
             if ((t & 1) == 0 && item < B) {
                 const float s = item_scale[item];
-                part[g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
-                part[(g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
+                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+                if (FMT == 8) {
+                    y0 = __fmul_rn(y0, p.row_scale[tile * 16 + g]);
+                    y1 = __fmul_rn(y1, p.row_scale[tile * 16 + g + 8]);
+                }
+                dst[g * B + item] = y0;
+                dst[(g + 8) * B + item] = y1;
             }
             acc[j][0] = acc[j][1] = 0.0f;
             iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
         }
-        __threadfence_block();
         __syncwarp();
-        int lastw = 0;
-        if (lane == 0) lastw = (atomicAdd(&tcount[ts], 1) == kConsumerWarps - 1);
-        lastw = __shfl_sync(0xffffffffu, lastw, 0);
-        if (!lastw) continue;
-        __threadfence_block();
-        const float *parts = tslots + (size_t)ts * kConsumerWarps * 16 * B;
+        if (slot < 0) {
+            tile_epilogue(p, tile, tbuf, cta_key, lane);
+            __syncwarp();
+        } else if (lane == 0) {
+            seg_tile[warp * 2 + slot] = (int)tile;
+        }
+    };
+
+    for (uint32_t base = 0; base < n; base += kPrefetch) {
+#pragma unroll
+        for (int q = 0; q < kPrefetch; ++q) {
+            const uint32_t i = base + q;
+            if (i < n) {
+                if (ku == p.kunits) {
+                    close_tile(true);
+                    ++tile;
+                    ku = 0;
+                    started_here = true;
+                }
+                const uint4 wq = wv[q];
+                if (FMT == 4) {
+                    const float4 sc = sv[q];
+                    const uint32_t M = 0xF0F0F0F0u;
+                    const uint32_t a00 = (wq.x << 4) & M, a01 = (wq.y << 4) & M, a02 = wq.x & M, a03 = wq.y & M;
+                    const uint32_t a10 = (wq.z << 4) & M, a11 = (wq.w << 4) & M, a12 = wq.z & M, a13 = wq.w & M;
+#pragma unroll
+                    for (int j = 0; j < NI; ++j) {
+                        const uint32_t item = 2 * j + (g >> 2);
+                        uint4 bf = make_uint4(0, 0, 0, 0);
+                        if (digit < 3 && item < B)
+                            bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
+                        int d[4], e[4];
+                        imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
+                        imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
+                        acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
+                        acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
+                        acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
+                        acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < NI; ++j) {
+                        const uint32_t item = 2 * j + (g >> 2);
+                        uint2 bf = make_uint2(0, 0);
+                        if (digit < 3 && item < B)
+                            bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
+                        imma_16832(iacc[j], wq.x, wq.y, wq.z, wq.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                                   iacc[j][3]);
+                    }
+                }
+                if (i + kPrefetch < n) {
+                    wv[q] = ldg_stream(src + (size_t)(i + kPrefetch) * UB + lane * 16);
+                    if (FMT == 4) sv[q] = ldg_f4(src + (size_t)(i + kPrefetch) * UB + 512 + g * 16);
+                }
+                ++ku;
+            }
+        }
+    }
+    if (n > 0) close_tile(ku == p.kunits);
+    __syncthreads();
+
+    // ---- tiles split between warps: the lowest warp holding a segment of a
+    // tile adds the segments of all warps in warp order, then finishes the
+    // tile or hands it on to the cross-CTA reduction
+    for (int slot = 0; slot < 2; ++slot) {
+        const int tl = seg_tile[warp * 2 + slot];
+        if (tl < 0) continue;
+        bool mine = true;
+        for (int w2 = 0; w2 < warp; ++w2) mine &= (seg_tile[w2 * 2] != tl && seg_tile[w2 * 2 + 1] != tl);
+        if (!mine) continue;
         for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
             float s = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) s = __fadd_rn(s, parts[w * 16 * B + idx]);
-            if (FMT == 8) s = __fmul_rn(s, p.row_scale[tile * 16 + idx / B]);
-            mytbuf[idx] = s;
+            for (int w2 = 0; w2 < kWarps; ++w2) {
+                for (int s2 = 0; s2 < 2; ++s2)
+                    if (seg_tile[w2 * 2 + s2] == tl) s = __fadd_rn(s, segs[((size_t)w2 * 2 + s2) * 16 * B + idx]);
+            }
+            tbuf[idx] = s;
         }
         __syncwarp();
-        if (lane == 0) tcount[ts] = 0;
-        if (!(tfirst >= cb && tend <= ce)) {
-            // tile shared with neighbouring CTAs: the last CTA adds all partials
-            const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = (tend * G - 1) / U;
+        const uint32_t tt = (uint32_t)tl;
+        const uint64_t tfirst = (uint64_t)tt * p.kunits, tlast = tfirst + p.kunits - 1;
+        const uint64_t cf = warp_of(tfirst, U, W) / kWarps, cl = warp_of(tlast, U, W) / kWarps;
+        if (cf != cl) {
             const uint32_t nseg = (uint32_t)(cl - cf + 1);
-            float *base = p.partial + (size_t)tile * p.maxseg * 16 * B;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) base[(blockIdx.x - cf) * 16 * B + idx] = mytbuf[idx];
+            float *pb = p.partial + (size_t)tt * p.maxseg * 16 * B;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = tbuf[idx];
             __threadfence();
             __syncwarp();
             int last = 0;
-            if (lane == 0) last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
+            if (lane == 0) last = (atomicAdd(&p.counters[tt], 1) == (int)nseg - 1);
             last = __shfl_sync(0xffffffffu, last, 0);
             if (!last) continue;
             __threadfence();
             for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
                 float s = 0.0f;
-                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(base + (size_t)sg * 16 * B + idx));
-                mytbuf[idx] = s;
+                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(pb + (size_t)sg * 16 * B + idx));
+                tbuf[idx] = s;
             }
-            if (lane == 0) p.counters[tile] = 0;
+            if (lane == 0) p.counters[tt] = 0;
             __syncwarp();
         }
-        if (!dead) tile_epilogue(p, tile, mytbuf, cta_key, lane);
+        tile_epilogue(p, tt, tbuf, cta_key, lane);
         __syncwarp();
     }
-    if (dead && warp == 0 && lane == 0) {
-        // the ring may still be filling: wait (bounded) for each stage's last phase
-        for (int s = 0; s < kStages; ++s) (void)mbar_try_wait(&full[s], 0), (void)mbar_try_wait(&full[s], 1);
-    }
     if (p.epilogue == B2_EPI_LOGITS) {
-        consumer_sync();
-        if (threadIdx.x < p.batch && cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], cta_key[threadIdx.x]);
+        __syncthreads();
+        if (threadIdx.x < B && cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], cta_key[threadIdx.x]);
     }
 }
 
@@ -635,28 +580,29 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t KW = fmt == 4 ? 64u : 32u;
     const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
     if (U == 0) return false;
-    // shared memory: mbarriers | stage ring | digit planes | reduction buffers | misc
-    uint32_t off = 2 * kStages * 8;
-    off = (off + 127) & ~127u;
-    pl.off_ring = off;
-    off += kStages * kStageUnits * UB;
+    (void)UB;
+    // shared memory: digit planes | warp segments + tile buffers | misc
+    uint32_t off = 0;
+    pl.off_ring = 0;
     pl.off_xdig = off;
     off += a->w.kunits * a->batch * 3 * KW;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
-    off += (kTileSlots + 1) * kConsumerWarps * 16 * a->batch * 4;
+    off += 3 * kWarps * 16 * a->batch * 4;
     off = (off + 15) & ~15u;
     pl.off_misc = off;
-    off += (32 + kMaxItems) * 4 + kMaxItems * 8 + kTileSlots * 4;
+    off += (32 + kMaxItems) * 4 + kMaxItems * 8 + kWarps * 2 * 4;
     pl.smem = off;
-    // one CTA per SM; at least a stage's worth of units per CTA
-    int grid = a->grid > 0 ? a->grid : sm_count();
-    const uint64_t want = (U + kConsumerWarps * 2 - 1) / (kConsumerWarps * 2);
+    // two CTAs per SM when they fit, and at least 4 units per warp
+    const int per_sm = (233472u / (pl.smem + 1024u)) >= 2 ? 2 : 1;
+    int grid = a->grid > 0 ? a->grid : sm_count() * per_sm;
+    const uint64_t want = (U + kWarps * 4 - 1) / (kWarps * 4);
     if ((uint64_t)grid > want) grid = (int)want;
-    if ((uint64_t)grid > U) grid = (int)U;
     if (grid < 1) grid = 1;
     pl.grid = grid;
-    const uint64_t minc = U / (uint64_t)grid;  // >= 1
+    uint64_t W = (uint64_t)grid * kWarps;
+    if (W > U) W = U;
+    const uint64_t minc = (U / W) * (W >= kWarps ? kWarps : W);  // units of the smallest CTA
     uint64_t maxseg = (a->w.kunits + minc - 1) / minc + 1;
     if (maxseg > a->w.kunits) maxseg = a->w.kunits;
     pl.maxseg = (uint32_t)maxseg;
