@@ -23,22 +23,24 @@
 // and in the 2^-22 relative quantisation of x, far inside the 1e-3 logits
 // tolerance of the parity tests.
 //
-// Streaming. Weights sit in the unit layout of b2_kernels.h. Every warp owns a
+// Streaming. Weights sit in the unit layout of b2_kernels.h. Each CTA owns a
 // contiguous range of units (stream-K over tile-major units, balanced to one
-// unit across the grid) and streams it with 128-bit non-coherent loads,
-// keeping kPrefetch units in flight in registers (one 512-byte coalesced
-// request per unit and warp). A tile that lies inside one warp's range is
-// finished by that warp on the spot. Tiles split between warps of a CTA are
-// added through shared memory once the CTA's warps are done, in warp order;
-// tiles split between CTAs are added by the last CTA to finish them (per-tile
-// arrival counter), in CTA order, so results are deterministic. The first
-// weight loads are issued before griddepcontrol.wait, so under programmatic
-// dependent launch they overlap the previous kernel's tail.
+// unit across the grid), so at any moment the GPU reads ~one compact window
+// per CTA. The range is cut into stages of up to kStageUnits units that never
+// straddle a 16-row tile; all threads copy stages into a kStages-deep
+// shared-memory ring with 16-byte cp.async (one barrier per stage), and each
+// warp multiplies its share of the stage. At a tile end the warps' partial
+// sums meet in shared memory and one warp finishes the tile; the (at most
+// two) tiles a CTA shares with a neighbour are added by the last CTA to
+// finish them (per-tile arrival counter), in CTA order, so results are
+// deterministic. The first stages are requested before griddepcontrol.wait,
+// so under programmatic dependent launch they overlap the previous kernel.
 //
-// (A producer-warp design feeding a shared-memory ring with 1-D bulk copies
-// was measured first: one SM completed roughly one bulk copy per 0.4-0.6 us
-// whatever its size up to 20 KB, which capped the stream well below HBM
-// bandwidth; plain vector loads from all warps keep far more bytes in flight.)
+// Measured alternatives, slower: a producer warp issuing 1-D bulk copies
+// (cp.async.bulk) into the ring completed about one copy per 0.4-0.6 us per
+// SM whatever its size up to 20 KB; per-warp contiguous ranges read with
+// register prefetch scattered ~2400 small streams over HBM and reached less
+// than 2.5 TB/s even without any arithmetic.
 #include "b2_common.cuh"
 
 #include <cfloat>
@@ -47,9 +49,10 @@
 
 namespace b2 {
 
-constexpr int kWarps = 8;                           // warps per CTA, each with its own unit range
+constexpr int kWarps = 8;                           // warps per CTA
 constexpr int kThreads = kWarps * 32;
-constexpr int kPrefetch = 6;                        // units in flight per warp
+constexpr int kStages = 6;                          // ring depth
+constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
 constexpr int kMaxItems = 16;
 
 struct GemvParams {
@@ -324,29 +327,55 @@ __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const float *t
     }
 }
 
-__device__ __forceinline__ uint4 ldg_stream(const void *ptr)
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
 {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(ptr));
-    return r;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__device__ __forceinline__ float4 ldg_f4(const void *ptr)
+// The stage sequence of a CTA: stage i covers units [u, u + n) with
+// n = min(kStageUnits, end of the CTA range, end of the current tile).
+struct StageWalk {
+    uint64_t u, ce, tend;
+    uint32_t tile, kunits;
+    __device__ StageWalk(uint64_t cb, uint64_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
+    {
+        tile = (uint32_t)(cb / kunits_);
+        tend = (uint64_t)(tile + 1) * kunits_;
+    }
+    __device__ bool more() const { return u < ce; }
+    __device__ uint32_t n() const
+    {
+        uint64_t e = u + kStageUnits;
+        if (e > ce) e = ce;
+        if (e > tend) e = tend;
+        return (uint32_t)(e - u);
+    }
+    __device__ void advance(uint32_t n)
+    {
+        u += n;
+        if (u == tend) {
+            ++tile;
+            tend += kunits;
+        }
+    }
+};
+
+// All threads copy stage [u, u+n) into ring slot `slot` (16 bytes each).
+template <uint32_t UB>
+__device__ __forceinline__ void issue_stage(const GemvParams &p, uint8_t *ring, uint32_t slot, uint64_t u, uint32_t n)
 {
-    float4 r;
-    asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
-                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
-                 : "l"(ptr));
-    return r;
+    constexpr uint32_t CH = UB / 16;
+    uint8_t *dst = ring + (size_t)slot * kStageUnits * UB;
+    const uint8_t *src = p.data + u * UB;
+    const uint32_t total = n * CH;
+    for (uint32_t c = threadIdx.x; c < total; c += kThreads) cp_async16(dst + c * 16, src + (size_t)c * 16);
 }
-
-// Warp index that owns unit u when U units are split over W warps.
-__device__ __forceinline__ uint64_t warp_of(uint64_t u, uint64_t U, uint64_t W) { return ((u + 1) * W - 1) / U; }
 
 template <int FMT, int NI>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
     constexpr uint32_t KW = Fmt<FMT>::kKW;
@@ -355,39 +384,33 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t B = p.batch;
+    uint8_t *ring = smem + p.off_ring;
     uint8_t *xdig = smem + p.off_xdig;
-    float *segs = reinterpret_cast<float *>(smem + p.off_tile);        // [kWarps][2][16*B]
-    float *tbufs = segs + kWarps * 2 * 16 * B;                          // [kWarps][16*B]
+    float *tslots = reinterpret_cast<float *>(smem + p.off_tile);      // [2][kWarps][16*B]
+    float *tbuf = tslots + 2 * kWarps * 16 * B;                         // [16*B]
     float *red = reinterpret_cast<float *>(smem + p.off_misc);          // 32 floats
     float *item_scale = red + 32;                                       // 16 floats
     unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);
-    int *seg_tile = reinterpret_cast<int *>(cta_key + kMaxItems);       // [kWarps][2]
-    float *tbuf = tbufs + (size_t)warp * 16 * B;
 
     const uint64_t U = (uint64_t)p.tiles * p.kunits;
-    const uint64_t W = min((uint64_t)gridDim.x * kWarps, U);  // active warps, each >= 1 unit
-    const uint64_t w = (uint64_t)blockIdx.x * kWarps + warp;
-    const uint64_t ub = w < W ? w * U / W : U, ue = w < W ? (w + 1) * U / W : U;
-    const uint32_t n = (uint32_t)(ue - ub);
-    const uint8_t *src = p.data + ub * UB;
+    const uint64_t G = gridDim.x;  // host guarantees G <= U
+    const uint64_t cb = blockIdx.x * U / G, ce = (blockIdx.x + 1) * U / G;
 
-    // weights do not depend on the previous kernel: start streaming now
-    uint4 wv[kPrefetch];
-    float4 sv[kPrefetch];
-#pragma unroll
-    for (int q = 0; q < kPrefetch; ++q) {
-        if ((uint32_t)q < n) {
-            wv[q] = ldg_stream(src + (size_t)q * UB + lane * 16);
-            if (FMT == 4) sv[q] = ldg_f4(src + (size_t)q * UB + 512 + g * 16);
+    // weights do not depend on the previous kernel: request the first stages now
+    StageWalk ahead(cb, ce, p.kunits);
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (ahead.more()) {
+            const uint32_t n = ahead.n();
+            issue_stage<UB>(p, ring, s, ahead.u, n);
+            ahead.advance(n);
         }
+        cp_async_commit();
     }
     if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
-    if (threadIdx.x < kWarps * 2) seg_tile[threadIdx.x] = -1;
 
     pdl_wait();
     pdl_launch_dependents();
     prepare_x<FMT>(p, xdig, item_scale, red);
-    __syncthreads();
 
     const uint32_t digit = g & 3;
     float acc[NI][2];
@@ -397,74 +420,81 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p)
         acc[j][0] = acc[j][1] = 0.0f;
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
-    uint32_t tile = n ? (uint32_t)(ub / p.kunits) : 0;
-    uint32_t ku = n ? (uint32_t)(ub % p.kunits) : 0;
-    bool started_here = (ku == 0);
+    uint32_t tile_seq = 0;
+    // a tile finished in the previous stage, reduced by warp 0 after the barrier
+    int pend_tile = -1, pend_buf = 0;
+    bool pend_whole = false;
 
-    // Tile `tile` is done for this warp: combine the lanes into [16][B] and
-    // either finish it (whole tile in this warp) or park it as a segment.
-    auto close_tile = [&](bool complete) {
-        float *dst;
-        int slot = -1;
-        if (started_here && complete) {
-            dst = tbuf;
-        } else {
-            slot = started_here ? 1 : 0;
-            dst = segs + ((size_t)warp * 2 + slot) * 16 * B;
+    StageWalk sw(cb, ce, p.kunits);
+    for (uint32_t i = 0;; ++i) {
+        const bool have = sw.more();
+        cp_async_wait<kStages - 2>();
+        __syncthreads();  // stage i landed for every thread; stage i-1 consumed by every warp
+        if (ahead.more()) {
+            const uint32_t n = ahead.n();
+            issue_stage<UB>(p, ring, (i + kStages - 1) % kStages, ahead.u, n);
+            ahead.advance(n);
         }
+        cp_async_commit();
+
+        // warp 0 finishes the tile that ended in the previous stage
+        if (pend_tile >= 0 && warp == 0) {
+            const float *parts = tslots + (size_t)pend_buf * kWarps * 16 * B;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+                float s = 0.0f;
 #pragma unroll
-        for (int j = 0; j < NI; ++j) {
-            float v0, v1;
-            if (FMT == 4) {
-                v0 = acc[j][0];
-                v1 = acc[j][1];
-            } else {
-                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
-                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
+                for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, parts[w * 16 * B + idx]);
+                if (FMT == 8) s = __fmul_rn(s, p.row_scale[(uint32_t)pend_tile * 16 + idx / B]);
+                tbuf[idx] = s;
             }
-            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
-            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
-            const uint32_t item = 2 * j + (t >> 1);
-            if ((t & 1) == 0 && item < B) {
-                const float s = item_scale[item];
-                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
-                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
-                if (FMT == 8) {
-                    y0 = __fmul_rn(y0, p.row_scale[tile * 16 + g]);
-                    y1 = __fmul_rn(y1, p.row_scale[tile * 16 + g + 8]);
-                }
-                dst[g * B + item] = y0;
-                dst[(g + 8) * B + item] = y1;
-            }
-            acc[j][0] = acc[j][1] = 0.0f;
-            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
-        }
-        __syncwarp();
-        if (slot < 0) {
-            tile_epilogue(p, tile, tbuf, cta_key, lane);
             __syncwarp();
-        } else if (lane == 0) {
-            seg_tile[warp * 2 + slot] = (int)tile;
-        }
-    };
-
-    for (uint32_t base = 0; base < n; base += kPrefetch) {
-#pragma unroll
-        for (int q = 0; q < kPrefetch; ++q) {
-            const uint32_t i = base + q;
-            if (i < n) {
-                if (ku == p.kunits) {
-                    close_tile(true);
-                    ++tile;
-                    ku = 0;
-                    started_here = true;
+            bool finish = true;
+            if (!pend_whole) {
+                // shared with neighbouring CTAs: the last CTA adds all partials
+                const uint32_t tt = (uint32_t)pend_tile;
+                const uint64_t tfirst = (uint64_t)tt * p.kunits, tlast = tfirst + p.kunits - 1;
+                const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = ((tlast + 1) * G - 1) / U;
+                const uint32_t nseg = (uint32_t)(cl - cf + 1);
+                float *pb = p.partial + (size_t)tt * p.maxseg * 16 * B;
+                for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = tbuf[idx];
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) last = (atomicAdd(&p.counters[tt], 1) == (int)nseg - 1);
+                last = __shfl_sync(0xffffffffu, last, 0);
+                finish = last != 0;
+                if (finish) {
+                    __threadfence();
+                    for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+                        float s = 0.0f;
+                        for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(pb + (size_t)sg * 16 * B + idx));
+                        tbuf[idx] = s;
+                    }
+                    if (lane == 0) p.counters[tt] = 0;
+                    __syncwarp();
                 }
-                const uint4 wq = wv[q];
+            }
+            if (finish) tile_epilogue(p, (uint32_t)pend_tile, tbuf, cta_key, lane);
+            __syncwarp();
+        }
+        pend_tile = -1;
+        if (!have) break;
+
+        const uint32_t slot = i % kStages, n = sw.n();
+        const uint32_t ku0 = (uint32_t)(sw.u - (uint64_t)sw.tile * p.kunits);
+        const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
+#pragma unroll
+        for (int m = 0; m < kStageUnits / kWarps; ++m) {
+            const uint32_t k = warp + m * kWarps;
+            if (k < n) {
+                const uint8_t *unit = stage + (size_t)k * UB;
+                const uint32_t ku = ku0 + k;
+                const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
                 if (FMT == 4) {
-                    const float4 sc = sv[q];
+                    const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
                     const uint32_t M = 0xF0F0F0F0u;
-                    const uint32_t a00 = (wq.x << 4) & M, a01 = (wq.y << 4) & M, a02 = wq.x & M, a03 = wq.y & M;
-                    const uint32_t a10 = (wq.z << 4) & M, a11 = (wq.w << 4) & M, a12 = wq.z & M, a13 = wq.w & M;
+                    const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
+                    const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
 #pragma unroll
                     for (int j = 0; j < NI; ++j) {
                         const uint32_t item = 2 * j + (g >> 2);
@@ -486,64 +516,47 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p)
                         uint2 bf = make_uint2(0, 0);
                         if (digit < 3 && item < B)
                             bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
-                        imma_16832(iacc[j], wq.x, wq.y, wq.z, wq.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                        imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
                                    iacc[j][3]);
                     }
                 }
-                if (i + kPrefetch < n) {
-                    wv[q] = ldg_stream(src + (size_t)(i + kPrefetch) * UB + lane * 16);
-                    if (FMT == 4) sv[q] = ldg_f4(src + (size_t)(i + kPrefetch) * UB + 512 + g * 16);
-                }
-                ++ku;
             }
         }
-    }
-    if (n > 0) close_tile(ku == p.kunits);
-    __syncthreads();
+        const uint32_t tile = sw.tile;
+        const uint64_t tfirst = (uint64_t)tile * p.kunits, tend = sw.tend;
+        sw.advance(n);
+        if (sw.u != tend && sw.u != ce) continue;
 
-    // ---- tiles split between warps: the lowest warp holding a segment of a
-    // tile adds the segments of all warps in warp order, then finishes the
-    // tile or hands it on to the cross-CTA reduction
-    for (int slot = 0; slot < 2; ++slot) {
-        const int tl = seg_tile[warp * 2 + slot];
-        if (tl < 0) continue;
-        bool mine = true;
-        for (int w2 = 0; w2 < warp; ++w2) mine &= (seg_tile[w2 * 2] != tl && seg_tile[w2 * 2 + 1] != tl);
-        if (!mine) continue;
-        for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
-            float s = 0.0f;
-            for (int w2 = 0; w2 < kWarps; ++w2) {
-                for (int s2 = 0; s2 < 2; ++s2)
-                    if (seg_tile[w2 * 2 + s2] == tl) s = __fadd_rn(s, segs[((size_t)w2 * 2 + s2) * 16 * B + idx]);
+        // end of this CTA's part of `tile`: park the warps' partials; warp 0
+        // adds them after the next barrier
+        const uint32_t buf = tile_seq++ & 1u;
+        float *part = tslots + ((size_t)buf * kWarps + warp) * 16 * B;
+#pragma unroll
+        for (int j = 0; j < NI; ++j) {
+            float v0, v1;
+            if (FMT == 4) {
+                v0 = acc[j][0];
+                v1 = acc[j][1];
+            } else {
+                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
+                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
             }
-            tbuf[idx] = s;
-        }
-        __syncwarp();
-        const uint32_t tt = (uint32_t)tl;
-        const uint64_t tfirst = (uint64_t)tt * p.kunits, tlast = tfirst + p.kunits - 1;
-        const uint64_t cf = warp_of(tfirst, U, W) / kWarps, cl = warp_of(tlast, U, W) / kWarps;
-        if (cf != cl) {
-            const uint32_t nseg = (uint32_t)(cl - cf + 1);
-            float *pb = p.partial + (size_t)tt * p.maxseg * 16 * B;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = tbuf[idx];
-            __threadfence();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = (atomicAdd(&p.counters[tt], 1) == (int)nseg - 1);
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) continue;
-            __threadfence();
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
-                float s = 0.0f;
-                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(pb + (size_t)sg * 16 * B + idx));
-                tbuf[idx] = s;
+            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
+            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
+            const uint32_t item = 2 * j + (t >> 1);
+            if ((t & 1) == 0 && item < B) {
+                const float s = item_scale[item];
+                part[g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
+                part[(g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
             }
-            if (lane == 0) p.counters[tt] = 0;
-            __syncwarp();
+            acc[j][0] = acc[j][1] = 0.0f;
+            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
         }
-        tile_epilogue(p, tt, tbuf, cta_key, lane);
-        __syncwarp();
+        pend_tile = (int)tile;
+        pend_buf = (int)buf;
+        pend_whole = tfirst >= cb && tend <= ce;
     }
+    cp_async_wait<0>();
     if (p.epilogue == B2_EPI_LOGITS) {
         __syncthreads();
         if (threadIdx.x < B && cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], cta_key[threadIdx.x]);
@@ -580,29 +593,27 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t KW = fmt == 4 ? 64u : 32u;
     const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
     if (U == 0) return false;
-    (void)UB;
-    // shared memory: digit planes | warp segments + tile buffers | misc
+    // shared memory: stage ring | digit planes | tile partials | misc
     uint32_t off = 0;
-    pl.off_ring = 0;
+    pl.off_ring = off;
+    off += kStages * kStageUnits * UB;
     pl.off_xdig = off;
     off += a->w.kunits * a->batch * 3 * KW;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
-    off += 3 * kWarps * 16 * a->batch * 4;
+    off += (2 * kWarps + 1) * 16 * a->batch * 4;
     off = (off + 15) & ~15u;
     pl.off_misc = off;
-    off += (32 + kMaxItems) * 4 + kMaxItems * 8 + kWarps * 2 * 4;
+    off += (32 + kMaxItems) * 4 + kMaxItems * 8;
     pl.smem = off;
-    // two CTAs per SM when they fit, and at least 4 units per warp
-    const int per_sm = (233472u / (pl.smem + 1024u)) >= 2 ? 2 : 1;
-    int grid = a->grid > 0 ? a->grid : sm_count() * per_sm;
-    const uint64_t want = (U + kWarps * 4 - 1) / (kWarps * 4);
+    // one CTA per SM, at least 16 units per CTA
+    int grid = a->grid > 0 ? a->grid : sm_count();
+    const uint64_t want = (U + 15) / 16;
     if ((uint64_t)grid > want) grid = (int)want;
+    if ((uint64_t)grid > U) grid = (int)U;
     if (grid < 1) grid = 1;
     pl.grid = grid;
-    uint64_t W = (uint64_t)grid * kWarps;
-    if (W > U) W = U;
-    const uint64_t minc = (U / W) * (W >= kWarps ? kWarps : W);  // units of the smallest CTA
+    const uint64_t minc = U / (uint64_t)grid;  // units of the smallest CTA, >= 1
     uint64_t maxseg = (a->w.kunits + minc - 1) / minc + 1;
     if (maxseg > a->w.kunits) maxseg = a->w.kunits;
     pl.maxseg = (uint32_t)maxseg;
