@@ -49,7 +49,7 @@
 
 namespace b2 {
 
-constexpr int kWarps = 8;                           // warps per CTA
+constexpr int kWarps = 16;                          // warps per CTA (16 hide the math latency)
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 6;                          // ring depth
 constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
