@@ -27,20 +27,25 @@
 // contiguous range of units (stream-K over tile-major units, balanced to one
 // unit across the grid), so at any moment the GPU reads ~one compact window
 // per CTA. The range is cut into stages of up to kStageUnits units that never
-// straddle a 16-row tile; all threads copy stages into a kStages-deep
-// shared-memory ring with 16-byte cp.async (one barrier per stage), and each
-// warp multiplies its share of the stage. At a tile end the warps' partial
-// sums meet in shared memory and one warp finishes the tile; the (at most
-// two) tiles a CTA shares with a neighbour are added by the last CTA to
-// finish them (per-tile arrival counter), in CTA order, so results are
-// deterministic. The first stages are requested before griddepcontrol.wait,
-// so under programmatic dependent launch they overlap the previous kernel.
+// straddle a 16-row tile. A producer warp copies stages into a shared-memory
+// ring of up to kMaxStages stages with 16-byte cp.async, each stage signalled on its own
+// "full" mbarrier; sixteen consumer warps wait only for the stage they need,
+// multiply their share of it and release it on its "empty" mbarrier, so the
+// warps never meet at a CTA barrier while streaming. At a tile end each warp
+// drops its partial sums into a shared-memory slot and the last warp to
+// arrive adds them in warp order and finishes the tile; the (at most two)
+// tiles a CTA shares with a neighbour are added by the last CTA to finish
+// them (per-tile arrival counter), in CTA order, so results are
+// deterministic. The producer requests the first stages before
+// griddepcontrol.wait, so under programmatic dependent launch the weight
+// fetch overlaps the previous kernel.
 //
-// Measured alternatives, slower: a producer warp issuing 1-D bulk copies
-// (cp.async.bulk) into the ring completed about one copy per 0.4-0.6 us per
-// SM whatever its size up to 20 KB; per-warp contiguous ranges read with
-// register prefetch scattered ~2400 small streams over HBM and reached less
-// than 2.5 TB/s even without any arithmetic.
+// Measured alternatives, slower: 1-D bulk copies (cp.async.bulk) completed
+// about one copy per 0.4-0.6 us per SM whatever their size up to 20 KB;
+// per-warp contiguous ranges read with register prefetch scattered ~2400
+// small streams over HBM and reached less than 2.5 TB/s without arithmetic;
+// a ring refilled by all threads behind one CTA barrier per stage left two
+// units of work per warp between barriers and drained the math pipeline.
 #include "b2_common.cuh"
 
 #include <cfloat>
@@ -49,11 +54,18 @@
 
 namespace b2 {
 
-constexpr int kWarps = 16;                          // warps per CTA (16 hide the math latency)
-constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 6;                          // ring depth
+constexpr int kWarps = 16;                          // consumer warps (16 hide the math latency)
+constexpr int kConsumers = kWarps * 32;
+constexpr int kThreads = kConsumers + 32;           // + one producer warp
 constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
+constexpr int kMaxStages = 8;                       // ring depth, chosen per launch
 constexpr int kMaxItems = 16;
+constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
+// Tile-partial slots (stages + 2 of them): warps drift at most (stages - 1)
+// stages apart and a stage never spans two tiles, so a warp writing tile j
+// can meet warps still on tiles j-stages+1 .. j-1 and the last warp of tile
+// j-stages reducing it.
+constexpr int kMaxTileSlots = kMaxStages + 2;
 
 struct GemvParams {
     const uint8_t *data;
@@ -78,7 +90,7 @@ struct GemvParams {
     uint32_t maxseg;
     int32_t *err;
     // shared-memory carve-up (bytes)
-    uint32_t off_ring, off_xdig, off_tile, off_misc;
+    uint32_t off_ring, off_xdig, off_tile, off_misc, stages;
 };
 
 template <int FMT>
@@ -103,7 +115,7 @@ __device__ __forceinline__ uint32_t ordered_key(float f)
 // ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
 // The input vector is read once into registers (all loads of a thread issued
 // together, so the prologue costs one L2 round trip instead of one per
-// element group); vectors longer than kPrologueVec * 4 * kThreads fall back
+// element group); vectors longer than kPrologueVec * 4 * kConsumers fall back
 // to re-reading chunks.
 constexpr int kPrologueVec = 16;  // float4 per thread held in registers
 
@@ -159,11 +171,37 @@ __device__ __forceinline__ int pick_exponent(float m)
     return E;
 }
 
+__device__ __forceinline__ void consumer_sync()
+{
+    asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumers) : "memory");
+}
+
+// Sum / max over the consumer threads (deterministic tree); all get the result.
+__device__ __forceinline__ float consumer_sum(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    consumer_sync();
+    if (lane == 0) red[warp] = v;
+    consumer_sync();
+    return warp_sum(lane < kWarps ? red[lane] : 0.0f);
+}
+
+__device__ __forceinline__ float consumer_max(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    consumer_sync();
+    if (lane == 0) red[warp] = v;
+    consumer_sync();
+    return warp_max(lane < kWarps ? red[lane] : 0.0f);
+}
+
 template <int FMT>
 __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
 {
     const uint32_t cols = p.cols;
-    const uint32_t stride = kThreads * 4;
+    const uint32_t stride = kConsumers * 4;
     for (uint32_t b = 0; b < p.batch; ++b) {
         const float *xb = p.x + (size_t)b * p.x_stride;
         if (cols <= stride * kPrologueVec) {
@@ -178,7 +216,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
 #pragma unroll
                 for (int i = 0; i < kPrologueVec; ++i)
                     ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-                ss = block_sum(ss, red);
+                ss = consumer_sum(ss, red);
                 // src/norm.c:26-28
                 const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
 #pragma unroll
@@ -190,7 +228,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
             float m = 0.0f;
 #pragma unroll
             for (int i = 0; i < kPrologueVec; ++i) m = fmaxf(m, absmax4(v[i]));
-            m = block_max(m, red);
+            m = consumer_max(m, red);
             const bool finite = m <= FLT_MAX;
             if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
             const int E = pick_exponent(m);
@@ -209,7 +247,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
                     const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
                     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
                 }
-                ss = block_sum(ss, red);
+                ss = consumer_sum(ss, red);
                 inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
             }
             float m = 0.0f;
@@ -218,7 +256,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
                 if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
                 m = fmaxf(m, absmax4(v));
             }
-            m = block_max(m, red);
+            m = consumer_max(m, red);
             const bool finite = m <= FLT_MAX;
             if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
             const int E = pick_exponent(m);
@@ -331,9 +369,17 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src)
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// The mbarrier arrives once this thread's cp.async copies issued so far land.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 // The stage sequence of a CTA: stage i covers units [u, u + n) with
 // n = min(kStageUnits, end of the CTA range, end of the current tile).
@@ -363,17 +409,6 @@ struct StageWalk {
     }
 };
 
-// All threads copy stage [u, u+n) into ring slot `slot` (16 bytes each).
-template <uint32_t UB>
-__device__ __forceinline__ void issue_stage(const GemvParams &p, uint8_t *ring, uint32_t slot, uint64_t u, uint32_t n)
-{
-    constexpr uint32_t CH = UB / 16;
-    uint8_t *dst = ring + (size_t)slot * kStageUnits * UB;
-    const uint8_t *src = p.data + u * UB;
-    const uint32_t total = n * CH;
-    for (uint32_t c = threadIdx.x; c < total; c += kThreads) cp_async16(dst + c * 16, src + (size_t)c * 16);
-}
-
 template <int FMT, int NI>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
 {
@@ -382,35 +417,69 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
     extern __shared__ __align__(128) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
     const uint32_t B = p.batch;
+    const uint32_t NS = p.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kMaxStages;
     uint8_t *ring = smem + p.off_ring;
     uint8_t *xdig = smem + p.off_xdig;
-    float *tslots = reinterpret_cast<float *>(smem + p.off_tile);      // [2][kWarps][16*B]
-    float *tbuf = tslots + 2 * kWarps * 16 * B;                         // [16*B]
+    const uint32_t NT = NS + 2;                                         // tile-partial slots
+    float *tslots = reinterpret_cast<float *>(smem + p.off_tile);      // [NT][kWarps][16*B]
+    float *tbufs = tslots + NT * kWarps * 16 * B;                       // [kWarps][16*B]
     float *red = reinterpret_cast<float *>(smem + p.off_misc);          // 32 floats
     float *item_scale = red + 32;                                       // 16 floats
     unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);
+    int *tcount = reinterpret_cast<int *>(cta_key + kMaxItems);         // [NT]
 
     const uint64_t U = (uint64_t)p.tiles * p.kunits;
     const uint64_t G = gridDim.x;  // host guarantees G <= U
     const uint64_t cb = blockIdx.x * U / G, ce = (blockIdx.x + 1) * U / G;
 
-    // weights do not depend on the previous kernel: request the first stages now
-    StageWalk ahead(cb, ce, p.kunits);
-    for (int s = 0; s < kStages - 1; ++s) {
-        if (ahead.more()) {
-            const uint32_t n = ahead.n();
-            issue_stage<UB>(p, ring, s, ahead.u, n);
-            ahead.advance(n);
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 32);         // the producer warp's 32 lanes
+            mbar_init(&empty[s], kWarps);    // one arrival per consumer warp
         }
-        cp_async_commit();
+        fence_mbar_init();
     }
     if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
+    if (threadIdx.x < kMaxTileSlots) tcount[threadIdx.x] = 0;
+    __syncthreads();
 
+    if (warp == kWarps) {
+        // ---------------- producer warp: copy the CTA's stages ---------------------
+        StageWalk sw(cb, ce, p.kunits);
+        bool waited = false;
+        for (uint32_t i = 0; sw.more(); ++i) {
+            const uint32_t slot = i % NS, n = sw.n();
+            if (i >= NS) {
+                if (!waited) {
+                    pdl_wait();
+                    pdl_launch_dependents();
+                    waited = true;
+                }
+                if (!mbar_wait_bounded(&empty[slot], ((i / NS) - 1) & 1u, p.err)) break;
+            }
+            uint8_t *dst = ring + (size_t)slot * kStageUnits * UB;
+            const uint8_t *src = p.data + sw.u * UB;
+            for (uint32_t c = lane; c < n * (UB / 16); c += 32) cp_async16(dst + c * 16, src + (size_t)c * 16);
+            cp_async_arrive(&full[slot]);
+            sw.advance(n);
+        }
+        if (!waited) {
+            pdl_wait();
+            pdl_launch_dependents();
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        return;
+    }
+
+    // ---------------- consumer warps ----------------------------------------------------
+    const int g = lane >> 2, t = lane & 3;
     pdl_wait();
     pdl_launch_dependents();
     prepare_x<FMT>(p, xdig, item_scale, red);
+    consumer_sync();
 
     const uint32_t digit = g & 3;
     float acc[NI][2];
@@ -420,117 +489,72 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         acc[j][0] = acc[j][1] = 0.0f;
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
-    uint32_t tile_seq = 0;
-    // a tile finished in the previous stage, reduced by warp 0 after the barrier
-    int pend_tile = -1, pend_buf = 0;
-    bool pend_whole = false;
+    bool dead = false;       // a wait timed out: keep the stage protocol, skip the math
+    uint32_t tile_seq = 0;   // tiles this CTA finished (same count in every warp)
+    float *mytbuf = tbufs + (size_t)warp * 16 * B;
 
     StageWalk sw(cb, ce, p.kunits);
-    for (uint32_t i = 0;; ++i) {
-        const bool have = sw.more();
-        cp_async_wait<kStages - 2>();
-        __syncthreads();  // stage i landed for every thread; stage i-1 consumed by every warp
-        if (ahead.more()) {
-            const uint32_t n = ahead.n();
-            issue_stage<UB>(p, ring, (i + kStages - 1) % kStages, ahead.u, n);
-            ahead.advance(n);
-        }
-        cp_async_commit();
-
-        // warp 0 finishes the tile that ended in the previous stage
-        if (pend_tile >= 0 && warp == 0) {
-            const float *parts = tslots + (size_t)pend_buf * kWarps * 16 * B;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
-                float s = 0.0f;
-#pragma unroll
-                for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, parts[w * 16 * B + idx]);
-                if (FMT == 8) s = __fmul_rn(s, p.row_scale[(uint32_t)pend_tile * 16 + idx / B]);
-                tbuf[idx] = s;
-            }
-            __syncwarp();
-            bool finish = true;
-            if (!pend_whole) {
-                // shared with neighbouring CTAs: the last CTA adds all partials
-                const uint32_t tt = (uint32_t)pend_tile;
-                const uint64_t tfirst = (uint64_t)tt * p.kunits, tlast = tfirst + p.kunits - 1;
-                const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = ((tlast + 1) * G - 1) / U;
-                const uint32_t nseg = (uint32_t)(cl - cf + 1);
-                float *pb = p.partial + (size_t)tt * p.maxseg * 16 * B;
-                for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = tbuf[idx];
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) last = (atomicAdd(&p.counters[tt], 1) == (int)nseg - 1);
-                last = __shfl_sync(0xffffffffu, last, 0);
-                finish = last != 0;
-                if (finish) {
-                    __threadfence();
-                    for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
-                        float s = 0.0f;
-                        for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(pb + (size_t)sg * 16 * B + idx));
-                        tbuf[idx] = s;
-                    }
-                    if (lane == 0) p.counters[tt] = 0;
-                    __syncwarp();
-                }
-            }
-            if (finish) tile_epilogue(p, (uint32_t)pend_tile, tbuf, cta_key, lane);
-            __syncwarp();
-        }
-        pend_tile = -1;
-        if (!have) break;
-
-        const uint32_t slot = i % kStages, n = sw.n();
+    for (uint32_t i = 0; sw.more(); ++i) {
+        const uint32_t slot = i % NS, n = sw.n();
         const uint32_t ku0 = (uint32_t)(sw.u - (uint64_t)sw.tile * p.kunits);
-        const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
+        if (!dead) {
+            const bool got = mbar_wait_bounded(&full[slot], (i / NS) & 1u, p.err);
+            dead = !__all_sync(0xffffffffu, got);
+        }
+        if (!dead) {
+            const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
 #pragma unroll
-        for (int m = 0; m < kStageUnits / kWarps; ++m) {
-            const uint32_t k = warp + m * kWarps;
-            if (k < n) {
-                const uint8_t *unit = stage + (size_t)k * UB;
-                const uint32_t ku = ku0 + k;
-                const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
-                if (FMT == 4) {
-                    const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
-                    const uint32_t M = 0xF0F0F0F0u;
-                    const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
-                    const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
+            for (int m = 0; m < kStageUnits / kWarps; ++m) {
+                const uint32_t k = warp + m * kWarps;
+                if (k < n) {
+                    const uint8_t *unit = stage + (size_t)k * UB;
+                    const uint32_t ku = ku0 + k;
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
+                    if (FMT == 4) {
+                        const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
+                        const uint32_t M = 0xF0F0F0F0u;
+                        const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
+                        const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
 #pragma unroll
-                    for (int j = 0; j < NI; ++j) {
-                        const uint32_t item = 2 * j + (g >> 2);
-                        uint4 bf = make_uint4(0, 0, 0, 0);
-                        if (digit < 3 && item < B)
-                            bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
-                        int d[4], e[4];
-                        imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
-                        imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
-                        acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
-                        acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
-                        acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
-                        acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
-                    }
-                } else {
+                        for (int j = 0; j < NI; ++j) {
+                            const uint32_t item = 2 * j + (g >> 2);
+                            uint4 bf = make_uint4(0, 0, 0, 0);
+                            if (digit < 3 && item < B)
+                                bf = *reinterpret_cast<const uint4 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
+                            int d[4], e[4];
+                            imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
+                            imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
+                            acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
+                            acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
+                            acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
+                            acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
+                        }
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < NI; ++j) {
-                        const uint32_t item = 2 * j + (g >> 2);
-                        uint2 bf = make_uint2(0, 0);
-                        if (digit < 3 && item < B)
-                            bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
-                        imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
-                                   iacc[j][3]);
+                        for (int j = 0; j < NI; ++j) {
+                            const uint32_t item = 2 * j + (g >> 2);
+                            uint2 bf = make_uint2(0, 0);
+                            if (digit < 3 && item < B)
+                                bf = *reinterpret_cast<const uint2 *>(xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
+                            imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                                       iacc[j][3]);
+                        }
                     }
                 }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+
         const uint32_t tile = sw.tile;
         const uint64_t tfirst = (uint64_t)tile * p.kunits, tend = sw.tend;
         sw.advance(n);
         if (sw.u != tend && sw.u != ce) continue;
 
-        // end of this CTA's part of `tile`: park the warps' partials; warp 0
-        // adds them after the next barrier
-        const uint32_t buf = tile_seq++ & 1u;
-        float *part = tslots + ((size_t)buf * kWarps + warp) * 16 * B;
+        // ---- end of this CTA's part of `tile`: drop this warp's partial into a
+        // slot; the last warp to arrive adds them in warp order and finishes
+        const uint32_t ts = tile_seq++ % NT;
+        float *part = tslots + ((size_t)ts * kWarps + warp) * 16 * B;
 #pragma unroll
         for (int j = 0; j < NI; ++j) {
             float v0, v1;
@@ -552,13 +576,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
             acc[j][0] = acc[j][1] = 0.0f;
             iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
         }
-        pend_tile = (int)tile;
-        pend_buf = (int)buf;
-        pend_whole = tfirst >= cb && tend <= ce;
+        __threadfence_block();
+        __syncwarp();
+        int lastw = 0;
+        if (lane == 0) lastw = (atomicAdd(&tcount[ts], 1) == kWarps - 1);
+        lastw = __shfl_sync(0xffffffffu, lastw, 0);
+        if (!lastw) continue;
+        __threadfence_block();
+        const float *parts = tslots + (size_t)ts * kWarps * 16 * B;
+        for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, parts[w * 16 * B + idx]);
+            if (FMT == 8) s = __fmul_rn(s, p.row_scale[tile * 16 + idx / B]);
+            mytbuf[idx] = s;
+        }
+        __syncwarp();
+        if (lane == 0) tcount[ts] = 0;
+        if (!(tfirst >= cb && tend <= ce)) {
+            // shared with neighbouring CTAs: the last CTA adds all partials
+            const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = (tend * G - 1) / U;
+            const uint32_t nseg = (uint32_t)(cl - cf + 1);
+            float *pb = p.partial + (size_t)tile * p.maxseg * 16 * B;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = mytbuf[idx];
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence();
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+                float s = 0.0f;
+                for (uint32_t sg = 0; sg < nseg; ++sg) s = __fadd_rn(s, ld_cg(pb + (size_t)sg * 16 * B + idx));
+                mytbuf[idx] = s;
+            }
+            if (lane == 0) p.counters[tile] = 0;
+            __syncwarp();
+        }
+        if (!dead) tile_epilogue(p, tile, mytbuf, cta_key, lane);
+        __syncwarp();
     }
-    cp_async_wait<0>();
     if (p.epilogue == B2_EPI_LOGITS) {
-        __syncthreads();
+        consumer_sync();
         if (threadIdx.x < B && cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], cta_key[threadIdx.x]);
     }
 }
@@ -583,7 +643,7 @@ struct GemvPlan {
     uint32_t maxseg;
     size_t partial_bytes;
     uint32_t counter_len;
-    uint32_t smem, off_ring, off_xdig, off_tile, off_misc;
+    uint32_t smem, off_ring, off_xdig, off_tile, off_misc, stages;
 };
 
 static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
@@ -593,18 +653,31 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t KW = fmt == 4 ? 64u : 32u;
     const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
     if (U == 0) return false;
-    // shared memory: stage ring | digit planes | tile partials | misc
-    uint32_t off = 0;
+    // shared memory: mbarriers | stage ring | digit planes | tile partials | misc;
+    // the ring takes what the rest leaves, up to kMaxStages stages, with two
+    // more tile-partial slots than stages
+    const uint32_t xdig = a->w.kunits * a->batch * 3 * KW;
+    const uint32_t slot_b = kWarps * 16 * a->batch * 4;
+    const uint32_t misc = (32 + kMaxItems) * 4 + kMaxItems * 8 + kMaxTileSlots * 4;
+    const uint32_t fixed = 2 * kMaxStages * 8 + 128 + xdig + 128 + 3 * slot_b + 16 + misc;
+    const uint32_t per_stage = kStageUnits * UB + slot_b;
+    const uint32_t limit = 227u * 1024u;
+    if (fixed + 2 * per_stage > limit) return false;
+    uint32_t ns = (limit - fixed) / per_stage;
+    if (ns > kMaxStages) ns = kMaxStages;
+    pl.stages = ns;
+    uint32_t off = 2 * kMaxStages * 8;
+    off = (off + 127) & ~127u;
     pl.off_ring = off;
-    off += kStages * kStageUnits * UB;
+    off += ns * kStageUnits * UB;
     pl.off_xdig = off;
-    off += a->w.kunits * a->batch * 3 * KW;
+    off += xdig;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
-    off += (2 * kWarps + 1) * 16 * a->batch * 4;
+    off += (ns + 3) * slot_b;
     off = (off + 15) & ~15u;
     pl.off_misc = off;
-    off += (32 + kMaxItems) * 4 + kMaxItems * 8;
+    off += misc;
     pl.smem = off;
     // one CTA per SM, at least 16 units per CTA
     int grid = a->grid > 0 ? a->grid : sm_count();
@@ -696,8 +769,7 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
         return -1;
     }
     GemvPlan pl;
-    if (!plan_gemv(a, pl)) return -1;
-    if (pl.smem > 227 * 1024) return -9;  // batch x columns too large for on-chip digit planes
+    if (!plan_gemv(a, pl)) return -9;  // batch x columns too large for on-chip digit planes
     if (a->scratch == nullptr || a->scratch_bytes < pl.partial_bytes || ((uintptr_t)a->scratch & 255)) return -1;
     if (a->counters == nullptr || a->counters_len < pl.counter_len) return -1;
 
@@ -728,6 +800,7 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
     p.maxseg = pl.maxseg;
     p.err = a->err;
     p.off_ring = pl.off_ring;
+    p.stages = pl.stages;
     p.off_xdig = pl.off_xdig;
     p.off_tile = pl.off_tile;
     p.off_misc = pl.off_misc;
