@@ -27,9 +27,9 @@
 // contiguous range of units (stream-K over tile-major units, balanced to one
 // unit across the grid), so at any moment the GPU reads ~one compact window
 // per CTA. The range is cut into stages of up to kStageUnits units that never
-// straddle a 16-row tile. A producer warp copies stages into a shared-memory
-// ring of up to kMaxStages stages with 16-byte cp.async, each stage signalled on its own
-// "full" mbarrier; sixteen consumer warps wait only for the stage they need,
+// straddle a 16-row tile. One producer lane copies each stage into a
+// shared-memory ring of up to kMaxStages stages with a single 1-D bulk copy
+// (cp.async.bulk, completion counted in bytes on the stage's "full" mbarrier); sixteen consumer warps wait only for the stage they need,
 // multiply their share of it and release it on its "empty" mbarrier, so the
 // warps never meet at a CTA barrier while streaming. At a tile end each warp
 // drops its partial sums into a shared-memory slot and the last warp to
@@ -40,12 +40,14 @@
 // griddepcontrol.wait, so under programmatic dependent launch the weight
 // fetch overlaps the previous kernel.
 //
-// Measured alternatives, slower: 1-D bulk copies (cp.async.bulk) completed
-// about one copy per 0.4-0.6 us per SM whatever their size up to 20 KB;
-// per-warp contiguous ranges read with register prefetch scattered ~2400
-// small streams over HBM and reached less than 2.5 TB/s without arithmetic;
-// a ring refilled by all threads behind one CTA barrier per stage left two
-// units of work per warp between barriers and drained the math pipeline.
+// Measured alternatives, slower: an SM completes roughly one bulk copy per
+// 0.4-0.6 us almost whatever its size, so small copies starve the ring and
+// large ones (tens of KB) are needed; per-warp contiguous ranges read with
+// register prefetch scattered ~2400 small streams over HBM and reached less
+// than 2.5 TB/s without arithmetic; a ring refilled by 16-byte cp.async from
+// one warp streamed no faster; a ring refilled by all threads behind one CTA
+// barrier per stage left two units per warp between barriers and drained the
+// math pipeline.
 #include "b2_common.cuh"
 
 #include <cfloat>
@@ -57,7 +59,7 @@ namespace b2 {
 constexpr int kWarps = 16;                          // consumer warps (16 hide the math latency)
 constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;           // + one producer warp
-constexpr int kStageUnits = 32;                     // units per stage (20 KB of q4)
+constexpr int kStageUnits = 64;                     // units per stage (40 KB of q4, one bulk copy)
 constexpr int kMaxStages = 8;                       // ring depth, chosen per launch
 constexpr int kMaxItems = 16;
 constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
@@ -437,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 32);         // the producer warp's 32 lanes
+            mbar_init(&full[s], 1);          // producer lane 0 + the copy's bytes
             mbar_init(&empty[s], kWarps);    // one arrival per consumer warp
         }
         fence_mbar_init();
@@ -460,17 +462,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
                 }
                 if (!mbar_wait_bounded(&empty[slot], ((i / NS) - 1) & 1u, p.err)) break;
             }
-            uint8_t *dst = ring + (size_t)slot * kStageUnits * UB;
-            const uint8_t *src = p.data + sw.u * UB;
-            for (uint32_t c = lane; c < n * (UB / 16); c += 32) cp_async16(dst + c * 16, src + (size_t)c * 16);
-            cp_async_arrive(&full[slot]);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[slot], n * UB);
+                bulk_g2s(ring + (size_t)slot * kStageUnits * UB, p.data + sw.u * UB, n * UB, &full[slot]);
+            }
+            __syncwarp();
             sw.advance(n);
         }
         if (!waited) {
             pdl_wait();
             pdl_launch_dependents();
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
         return;
     }
 
