@@ -27,22 +27,25 @@ static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, int pdl, cu
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+// grid (blocks per row, batch): each thread moves float4s of the row
 __global__ void step_begin_kernel(const float *embed, uint32_t vocab, uint32_t d, const uint32_t *tokens, float *x,
                                   unsigned long long *argmax, int32_t *err)
 {
     pdl_wait();
     pdl_launch_dependents();
-    const uint32_t item = blockIdx.x;
+    const uint32_t item = blockIdx.y;
     const uint32_t tok = tokens[item];
-    float *xb = x + (size_t)item * d;
+    float4 *xb = reinterpret_cast<float4 *>(x + (size_t)item * d);
+    const uint32_t n4 = d / 4;
+    const uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x, step = gridDim.x * blockDim.x;
     if (tok >= vocab) {
-        if (threadIdx.x == 0) raise_error(err, B2_ERR_TOKEN);
-        for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) xb[i] = 0.0f;
+        if (i0 == 0) raise_error(err, B2_ERR_TOKEN);
+        for (uint32_t i = i0; i < n4; i += step) xb[i] = make_float4(0, 0, 0, 0);
     } else {
-        const float *row = embed + (size_t)tok * d;
-        for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) xb[i] = row[i];
+        const float4 *row = reinterpret_cast<const float4 *>(embed + (size_t)tok * d);
+        for (uint32_t i = i0; i < n4; i += step) xb[i] = __ldg(row + i);
     }
-    if (threadIdx.x == 0) argmax[item] = 0ull;
+    if (i0 == 0) argmax[item] = 0ull;
 }
 
 __global__ void step_end_kernel(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens, int32_t *positions,
@@ -165,10 +168,14 @@ extern "C" int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_mode
                              uint32_t batch, float *x, unsigned long long *argmax, int32_t *err, int pdl,
                              void *stream)
 {
-    if (!embed || !tokens || !x || !argmax || batch == 0 || d_model == 0 || vocab == 0) return -1;
+    if (!embed || !tokens || !x || !argmax || batch == 0 || batch > 65535 || d_model == 0 || (d_model & 3) ||
+        vocab == 0 || ((uintptr_t)embed & 15) || ((uintptr_t)x & 15))
+        return -1;
     void *args[] = {(void *)&embed, (void *)&vocab, (void *)&d_model, (void *)&tokens,
                     (void *)&x,     (void *)&argmax, (void *)&err};
-    return launched(launch_pdl((const void *)step_begin_kernel, dim3(batch), dim3(256), pdl, (cudaStream_t)stream, args));
+    const uint32_t blocks = (d_model / 4 + 127) / 128;
+    return launched(launch_pdl((const void *)step_begin_kernel, dim3(blocks, batch), dim3(128), pdl,
+                               (cudaStream_t)stream, args));
 }
 
 extern "C" int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens, int32_t *positions,

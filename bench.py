@@ -196,14 +196,16 @@ def time_dominant_gemv(b2, torch, reps=30):
     with torch.cuda.stream(stream):
         for i in range(8):
             assert L.b2_gemv(C.byref(args[i % nbuf]), C.c_void_p(sp)) == 0
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        # back-to-back launches on one stream (each streams a different 73 MB
+        # copy from HBM); the average is the per-launch device time
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
         for i in range(reps):
-            ev[i][0].record(stream)
             L.b2_gemv(C.byref(args[i % nbuf]), C.c_void_p(sp))
-            ev[i][1].record(stream)
+        e1.record(stream)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    ms = e0.elapsed_time(e1) / reps
     algo = q4_bytes(rows, cols) + cols * 4 * 2 + SHAPE["d_ff"] * 4
     del bufs
     return algo, ms
@@ -295,7 +297,7 @@ def run_b200(args, rank, world, local_rank):
         if world == 1 and not args.no_cpu:
             v, cores, sample = reference_cpu_sample(ctx)
             cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}
-        value = args.batch * world * 1000.0 / ms if False else args.batch * 1000.0 / ms * (world if args.replicas else 1)
+        value = args.batch * 1000.0 / ms * (world if args.replicas else 1)
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,

@@ -402,6 +402,42 @@ void or_synth_normal(uint64_t seed, uint64_t tensor_id, uint64_t first,
     }
 }
 
+typedef struct synth_job {
+    uint64_t seed, tid, first;
+    size_t count;
+    float std;
+    float *out;
+} synth_job;
+
+static void *synth_thread(void *arg)
+{
+    const synth_job *j = (const synth_job *)arg;
+    or_synth_normal(j->seed, j->tid, j->first, j->count, j->std, j->out);
+    return NULL;
+}
+
+void or_synth_normal_mt(uint64_t seed, uint64_t tensor_id, uint64_t first, size_t count, float std,
+                        float *out, int threads)
+{
+    synth_job jobs[64];
+    pthread_t tid[64];
+    int started[64];
+    int n = threads < 1 ? 1 : (threads > 64 ? 64 : threads), t;
+    if (count < 65536 || n == 1) {
+        or_synth_normal(seed, tensor_id, first, count, std, out);
+        return;
+    }
+    for (t = 0; t < n; t++) {
+        const size_t a = count * (size_t)t / (size_t)n, b = count * (size_t)(t + 1) / (size_t)n;
+        jobs[t].seed = seed; jobs[t].tid = tensor_id; jobs[t].first = first + a;
+        jobs[t].count = b - a; jobs[t].std = std; jobs[t].out = out + a;
+        started[t] = pthread_create(&tid[t], NULL, synth_thread, &jobs[t]) == 0;
+        if (!started[t]) synth_thread(&jobs[t]);
+    }
+    for (t = 0; t < n; t++)
+        if (started[t]) pthread_join(tid[t], NULL);
+}
+
 uint32_t or_synth_token(uint64_t seed, uint64_t index, uint32_t vocab)
 {
     const uint64_t r = or_splitmix64(synth_key(seed, 0x70000000ull) + index);
@@ -445,11 +481,10 @@ static int mat_build(or_mat *m, const or_config *cfg, uint64_t seed,
 {
     float *w = malloc(rows * cols * sizeof(float));
     int rc;
-    (void)threads;
     if (w == NULL) {
         return -1;
     }
-    or_synth_normal(seed, tid, 0, rows * cols, 0.02f, w);
+    or_synth_normal_mt(seed, tid, 0, rows * cols, 0.02f, w, threads);
     m->rows = rows;
     m->cols = cols;
     if (cfg->dtype == OR_Q4) {
@@ -509,7 +544,7 @@ or_model *or_model_synth(const or_config *cfg, uint64_t seed, int threads)
     m->out_norm = ones(d);
     m->layers = calloc(cfg->n_layers, sizeof(or_layer));
     if (!m->embed || !m->out_norm || !m->layers) goto fail;
-    or_synth_normal(seed, OR_T_EMBED, 0, (size_t)cfg->vocab * d, 0.02f, m->embed);
+    or_synth_normal_mt(seed, OR_T_EMBED, 0, (size_t)cfg->vocab * d, 0.02f, m->embed, threads);
     for (l = 0; l < cfg->n_layers; l++) {
         or_layer *L = &m->layers[l];
         const uint64_t base = (uint64_t)l * OR_T_PER_LAYER;

@@ -59,6 +59,9 @@ int or_argmax(const float *logits, size_t n, uint32_t *out);
  * f32 multiply: identical bits on any IEEE-754 machine. */
 void or_synth_normal(uint64_t seed, uint64_t tensor_id, uint64_t first,
                      size_t count, float std, float *out);
+/* Same values, generated on `threads` threads. */
+void or_synth_normal_mt(uint64_t seed, uint64_t tensor_id, uint64_t first, size_t count, float std,
+                        float *out, int threads);
 uint32_t or_synth_token(uint64_t seed, uint64_t index, uint32_t vocab);
 uint64_t or_splitmix64(uint64_t x);
 

@@ -174,7 +174,7 @@ static int rh_mat(rh_model *m, uint64_t seed, uint64_t tid, size_t rows,
     size_t r;
 
     if (w == NULL) return -1;
-    or_synth_normal(seed, tid, 0, rows * cols, 0.02f, w);
+    or_synth_normal_mt(seed, tid, 0, rows * cols, 0.02f, w, m->threads);
     if (rep > 1) {
         e = malloc(out_rows * cols * sizeof(float));
         if (e == NULL) { free(w); return -1; }
@@ -220,7 +220,7 @@ rh_model *rh_model_synth(const or_config *cfg, uint64_t seed, int threads)
     m->out_norm = rh_ones(d);
     m->layers = calloc(cfg->n_layers, sizeof(rh_layer));
     if (!m->embed || !m->out_norm || !m->layers) goto fail;
-    or_synth_normal(seed, OR_T_EMBED, 0, (size_t)cfg->vocab * d, 0.02f, m->embed);
+    or_synth_normal_mt(seed, OR_T_EMBED, 0, (size_t)cfg->vocab * d, 0.02f, m->embed, threads);
     for (l = 0; l < cfg->n_layers; l++) {
         rh_layer *L = &m->layers[l];
         const uint64_t b = (uint64_t)l * OR_T_PER_LAYER;
