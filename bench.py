@@ -232,9 +232,11 @@ def run_b200(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
     ctx = args.ctx
     e2e_steps = max(args.steps, 8)
-    cfg = b2.Config.make(SHAPE["vocab"], SHAPE["n_layers"], SHAPE["n_heads"], SHAPE["n_kv_heads"],
+    cfg = b2.Config.make(SHAPE["vocab"], args.layers, SHAPE["n_heads"], SHAPE["n_kv_heads"],
                          SHAPE["d_model"], SHAPE["d_ff"], ctx, dtype=4, eps=SHAPE["eps"], theta=SHAPE["theta"])
     inf = b2.Infer.synth(cfg, args.seed, batch=args.batch)
+    if args.no_graph:
+        inf.set_options(graph=False, pdl=False)
     rng = np.random.default_rng(args.seed + rank)
     prompt = rng.integers(0, SHAPE["vocab"], size=(args.prompt, args.batch), dtype=np.int64)
     for t in prompt:
@@ -285,7 +287,7 @@ def run_b200(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
 
-    algo, kms = time_dominant_gemv(b2, torch)
+    algo, kms = time_dominant_gemv(b2, torch, reps=4 if args.no_graph else 30)
     inf.close()
     peak, peak_kind = measured_peak()
     achieved = algo / (kms * 1e-3) / 1e9
@@ -311,7 +313,7 @@ def run_b200(args, rank, world, local_rank):
                        "step_hbm_frac": bytes_step / (ms * 1e-3) / (peak * 1e9)},
             "e2e": {"value": args.batch * 1000.0 / e2e_ms * (world if args.replicas else 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch + 4},
-            "gpu_launches": args.steps * (3 + 5 * SHAPE["n_layers"]),
+            "gpu_launches": args.steps * (3 + 5 * args.layers),
             "roofline": {"bound": "hbm", "kernel": "gemv_q4 gate/up 28672x4096 (RMSNorm+SwiGLU fused)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": algo,
@@ -343,7 +345,7 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=1)
@@ -351,11 +353,25 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch kernels one by one without graph or PDL (for ncu launch lists)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the dominant GEMV (gate/up shape) and print it (for ncu captures)")
+    ap.add_argument("--layers", type=int, default=SHAPE["n_layers"],
+                    help="decoder depth (profiling runs only; the metric is defined at 32)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     args.replicas = world > 1
+    if args.kernel_only:
+        import torch
+        import att1_b200 as b2
+        torch.cuda.set_device(local_rank)
+        algo, kms = time_dominant_gemv(b2, torch, reps=args.steps)
+        print(json.dumps({"kernel": "gemv_q4 gate/up 28672x4096", "launch_ms": kms,
+                          "algorithmic_bytes": algo, "GB/s": algo / (kms * 1e-3) / 1e9}), flush=True)
+        return
     out = run_reference(args, rank) if args.impl == "reference" else run_b200(args, rank, world, local_rank)
     if out is not None:
         print(json.dumps(out), flush=True)
