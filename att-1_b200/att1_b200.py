@@ -173,6 +173,7 @@ _SIGS = {
     "b2_gemv_counters_len": (_U32, [C.POINTER(GemvArgs)]),
     "b2_attn_counters_len": (_U32, [C.POINTER(AttnArgs)]),
     "b2_gemv": (C.c_int, [C.POINTER(GemvArgs), _P]),
+    "b2_gemv_noalloc": (C.c_int, [C.POINTER(GemvArgs), _P]),
     "b2_attn_scratch_bytes": (_SZ, [C.POINTER(AttnArgs)]),
     "b2_attn": (C.c_int, [C.POINTER(AttnArgs), _P]),
     "b2_rmsnorm": (C.c_int, [_P, _P, _P, _U32, _F, _P]),
