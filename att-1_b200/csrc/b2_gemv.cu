@@ -23,31 +23,33 @@
 // and in the 2^-22 relative quantisation of x, far inside the 1e-3 logits
 // tolerance of the parity tests.
 //
-// Streaming. Weights sit in the unit layout of b2_kernels.h. Each CTA owns a
-// contiguous range of units (stream-K over tile-major units, balanced to one
-// unit across the grid), so at any moment the GPU reads ~one compact window
-// per CTA. The range is cut into stages of up to kStageUnits units that never
-// straddle a 16-row tile. One producer lane copies each stage into a
-// shared-memory ring of up to kMaxStages stages with a single 1-D bulk copy
-// (cp.async.bulk, completion counted in bytes on the stage's "full" mbarrier); sixteen consumer warps wait only for the stage they need,
-// multiply their share of it and release it on its "empty" mbarrier, so the
-// warps never meet at a CTA barrier while streaming. At a tile end each warp
-// drops its partial sums into a shared-memory slot and the last warp to
-// arrive adds them in warp order and finishes the tile; the (at most two)
-// tiles a CTA shares with a neighbour are added by the last CTA to finish
-// them (per-tile arrival counter), in CTA order, so results are
-// deterministic. The producer requests the first stages before
-// griddepcontrol.wait, so under programmatic dependent launch the weight
-// fetch overlaps the previous kernel.
+// Streaming. Weights sit in the panel/unit layout of b2_kernels.h: a panel
+// is 16 row tiles, stored k-column by k-column (the 16 units of one column
+// pair, contiguous). Each CTA owns a contiguous range of k-columns (stream-K
+// over panel-major columns, balanced to one column across the grid), so at
+// any moment the GPU reads ~one compact window per CTA. The range is cut into
+// stages of up to kStageCols columns that never straddle a panel. One
+// producer lane copies each stage into a shared-memory ring of up to
+// kMaxStages stages with a single 1-D bulk copy (cp.async.bulk, completion
+// counted in bytes on the stage's "full" mbarrier). Consumer warp w owns tile
+// w of every panel: it multiplies unit (column, w) of each staged column,
+// keeps the tile's sums in registers across stages, and releases each stage
+// on its "empty" mbarrier, so the warps never meet at a CTA barrier and never
+// add each other's partial sums. When the CTA's part of a panel ends, each
+// warp finishes its own tile; a panel shared with neighbouring CTAs is added
+// by the last CTA to finish each tile (per-tile arrival counter), in CTA
+// order, so results are deterministic. The producer requests the first
+// stages before griddepcontrol.wait, so under programmatic dependent launch
+// the weight fetch overlaps the previous kernel.
 //
-// Measured alternatives, slower: an SM completes roughly one bulk copy per
-// 0.4-0.6 us almost whatever its size, so small copies starve the ring and
-// large ones (tens of KB) are needed; per-warp contiguous ranges read with
-// register prefetch scattered ~2400 small streams over HBM and reached less
-// than 2.5 TB/s without arithmetic; a ring refilled by 16-byte cp.async from
-// one warp streamed no faster; a ring refilled by all threads behind one CTA
-// barrier per stage left two units per warp between barriers and drained the
-// math pipeline.
+// Measured alternatives, slower: tile-major units split by k between the 16
+// warps (every tile then needs a cross-warp reduction in shared memory, and
+// the warp doing it lags and holds back the ring: half the speed of this
+// layout at 4096 columns); small bulk copies (an SM completes roughly one
+// bulk copy per 0.4-0.6 us almost whatever its size, so tens of KB per copy
+// are needed); per-warp contiguous ranges read with register prefetch
+// (~2400 small streams over HBM, under 2.5 TB/s without arithmetic); a ring
+// refilled by 16-byte cp.async from one warp.
 #include "b2_common.cuh"
 
 #include <cfloat>
@@ -60,20 +62,18 @@ namespace b2 {
 constexpr int kWarps = 16;                          // consumer warps (16 hide the math latency)
 constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;           // + one producer warp
-constexpr int kStageUnits = 64;                     // units per stage (40 KB of q4, one bulk copy)
+constexpr int kPanelTiles = 16;                     // tiles per panel: one per consumer warp
+constexpr int kStageCols = 4;                       // k-columns per stage
+constexpr int kStageUnits = kStageCols * kPanelTiles;  // 64 units: 40 KB of q4, one bulk copy
 constexpr int kMaxStages = 8;                       // ring depth, chosen per launch
 constexpr int kMaxItems = 16;
 constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
-// Tile-partial slots (stages + 2 of them): warps drift at most (stages - 1)
-// stages apart and a stage never spans two tiles, so a warp writing tile j
-// can meet warps still on tiles j-stages+1 .. j-1 and the last warp of tile
-// j-stages reducing it.
-constexpr int kMaxTileSlots = kMaxStages + 2;
+static_assert(kPanelTiles == kWarps, "each consumer warp owns one tile of a panel");
 
 struct GemvParams {
     const uint8_t *data;
     const float *row_scale;
-    uint32_t rows, cols, tiles, kunits;
+    uint32_t rows, cols, tiles, kunits, panels;
     uint32_t batch;
     const float *x;
     uint32_t x_stride;
@@ -116,11 +116,15 @@ __device__ __forceinline__ uint32_t ordered_key(float f)
 }
 
 // ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
-// The input vector is read once into registers (all loads of a thread issued
-// together, so the prologue costs one L2 round trip instead of one per
-// element group); vectors longer than kPrologueVec * 4 * kConsumers fall back
-// to re-reading chunks.
-constexpr int kPrologueVec = 16;  // float4 per thread held in registers
+// One pass of loads (x and the norm gains together) and one reduction round
+// per launch: every thread accumulates, per item, the sum of squares of x and
+// the largest |x * w|; the warps' partials meet in shared memory once. The
+// normed vector x * inv * w (src/norm.c:31) is bounded by inv * max|x * w|
+// (times 1 + 2^-20 for the two roundings), and that bound picks the exponent,
+// so no second reduction over the normed values is needed. Vectors of up to
+// kPrologueVec * 4 * kConsumers elements stay in registers between the two
+// steps (batch 1); otherwise the second step reads x again.
+constexpr int kPrologueVec = 8;   // float4 per thread held in registers (x and gains)
 
 template <int FMT>
 __device__ __forceinline__ void store_digits(const GemvParams &p, uint8_t *xdig, uint32_t b, uint32_t k, float4 v,
@@ -156,6 +160,13 @@ __device__ __forceinline__ float4 normed(float4 v, float inv, float4 w)
                        __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
 }
 
+__device__ __forceinline__ float4 mul4(float4 a, float4 b)
+{
+    return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+
+__device__ __forceinline__ float sumsq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
 __device__ __forceinline__ float absmax4(float4 v)
 {
     const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
@@ -179,25 +190,27 @@ __device__ __forceinline__ void consumer_sync()
     asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumers) : "memory");
 }
 
-// Sum / max over the consumer threads (deterministic tree); all get the result.
-__device__ __forceinline__ float consumer_sum(float v, float *red)
+// Per item: the normalisation factor (1 without a norm) and the exponent
+// scale, from the item's sum of squares and max |x * w| (max |x| without a norm).
+template <int FMT>
+__device__ __forceinline__ void item_setup(const GemvParams &p, uint32_t b, float ss, float mw, float *inv_out,
+                                           float *sc_out, bool *finite_out, float *item_scale)
 {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    consumer_sync();
-    if (lane == 0) red[warp] = v;
-    consumer_sync();
-    return warp_sum(lane < kWarps ? red[lane] : 0.0f);
-}
-
-__device__ __forceinline__ float consumer_max(float v, float *red)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_max(v);
-    consumer_sync();
-    if (lane == 0) red[warp] = v;
-    consumer_sync();
-    return warp_max(lane < kWarps ? red[lane] : 0.0f);
+    float inv = 1.0f, bound = mw;
+    if (p.norm_w != nullptr) {
+        // src/norm.c:26-28
+        inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.cols), p.eps)));
+        bound = __fmul_rn(__fmul_rn(mw, inv), 1.0f + 0x1p-20f);
+    }
+    const bool finite = mw <= FLT_MAX && inv <= FLT_MAX;
+    const int E = pick_exponent(bound);
+    *inv_out = inv;
+    *sc_out = ldexpf(1.0f, -E);
+    *finite_out = finite;
+    if (threadIdx.x == 0) {
+        item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
+        if (!finite) raise_error(p.err, B2_ERR_NONFINITE);
+    }
 }
 
 template <int FMT>
@@ -205,71 +218,79 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
 {
     const uint32_t cols = p.cols;
     const uint32_t stride = kConsumers * 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool norm = p.norm_w != nullptr;
+    if (p.batch == 1 && cols <= stride * kPrologueVec) {
+        float4 v[kPrologueVec], w[kPrologueVec];
+#pragma unroll
+        for (int i = 0; i < kPrologueVec; ++i) {
+            const uint32_t k = threadIdx.x * 4 + i * stride;
+            const bool in = k < cols;
+            v[i] = in ? __ldcg(reinterpret_cast<const float4 *>(p.x + k)) : make_float4(0, 0, 0, 0);
+            w[i] = (in && norm) ? __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)) : make_float4(1, 1, 1, 1);
+        }
+        float ss = 0.0f, mw = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kPrologueVec; ++i) {
+            ss += sumsq4(v[i]);
+            mw = fmaxf(mw, absmax4(norm ? mul4(v[i], w[i]) : v[i]));
+        }
+        ss = warp_sum(ss);
+        mw = warp_max(mw);
+        if (lane == 0) {
+            red[warp] = ss;
+            red[kWarps + warp] = mw;
+        }
+        consumer_sync();
+        float tss = 0.0f, tmw = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kWarps; ++i) {
+            tss += red[i];
+            tmw = fmaxf(tmw, red[kWarps + i]);
+        }
+        float inv, sc;
+        bool finite;
+        item_setup<FMT>(p, 0, tss, tmw, &inv, &sc, &finite, item_scale);
+#pragma unroll
+        for (int i = 0; i < kPrologueVec; ++i) {
+            const uint32_t k = threadIdx.x * 4 + i * stride;
+            if (k < cols) store_digits<FMT>(p, xdig, 0, k, norm ? normed(v[i], inv, w[i]) : v[i], sc, finite);
+        }
+        return;
+    }
+    // general path: statistics of every item in one reduction round, then the digits
+    float *stats = red;  // [kMaxItems][kWarps][2]
     for (uint32_t b = 0; b < p.batch; ++b) {
         const float *xb = p.x + (size_t)b * p.x_stride;
-        if (cols <= stride * kPrologueVec) {
-            float4 v[kPrologueVec];
+        float ss = 0.0f, mw = 0.0f;
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            ss += sumsq4(v);
+            mw = fmaxf(mw, absmax4(norm ? mul4(v, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k))) : v));
+        }
+        ss = warp_sum(ss);
+        mw = warp_max(mw);
+        if (lane == 0) {
+            stats[(b * kWarps + warp) * 2] = ss;
+            stats[(b * kWarps + warp) * 2 + 1] = mw;
+        }
+    }
+    consumer_sync();
+    for (uint32_t b = 0; b < p.batch; ++b) {
+        float tss = 0.0f, tmw = 0.0f;
 #pragma unroll
-            for (int i = 0; i < kPrologueVec; ++i) {
-                const uint32_t k = threadIdx.x * 4 + i * stride;
-                v[i] = k < cols ? __ldcg(reinterpret_cast<const float4 *>(xb + k)) : make_float4(0, 0, 0, 0);
-            }
-            if (p.norm_w != nullptr) {
-                float ss = 0.0f;
-#pragma unroll
-                for (int i = 0; i < kPrologueVec; ++i)
-                    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-                ss = consumer_sum(ss, red);
-                // src/norm.c:26-28
-                const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
-#pragma unroll
-                for (int i = 0; i < kPrologueVec; ++i) {
-                    const uint32_t k = threadIdx.x * 4 + i * stride;
-                    if (k < cols) v[i] = normed(v[i], inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
-                }
-            }
-            float m = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kPrologueVec; ++i) m = fmaxf(m, absmax4(v[i]));
-            m = consumer_max(m, red);
-            const bool finite = m <= FLT_MAX;
-            if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
-            const int E = pick_exponent(m);
-            const float sc = ldexpf(1.0f, -E);
-            if (threadIdx.x == 0) item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
-#pragma unroll
-            for (int i = 0; i < kPrologueVec; ++i) {
-                const uint32_t k = threadIdx.x * 4 + i * stride;
-                if (k < cols) store_digits<FMT>(p, xdig, b, k, v[i], sc, finite);
-            }
-        } else {
-            float inv = 1.0f;
-            if (p.norm_w != nullptr) {
-                float ss = 0.0f;
-                for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                }
-                ss = consumer_sum(ss, red);
-                inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)cols), p.eps)));
-            }
-            float m = 0.0f;
-            for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-                float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
-                if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
-                m = fmaxf(m, absmax4(v));
-            }
-            m = consumer_max(m, red);
-            const bool finite = m <= FLT_MAX;
-            if (!finite && threadIdx.x == 0) raise_error(p.err, B2_ERR_NONFINITE);
-            const int E = pick_exponent(m);
-            const float sc = ldexpf(1.0f, -E);
-            if (threadIdx.x == 0) item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
-            for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-                float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
-                if (p.norm_w != nullptr) v = normed(v, inv, *reinterpret_cast<const float4 *>(p.norm_w + k));
-                store_digits<FMT>(p, xdig, b, k, v, sc, finite);
-            }
+        for (int i = 0; i < kWarps; ++i) {
+            tss += stats[(b * kWarps + i) * 2];
+            tmw = fmaxf(tmw, stats[(b * kWarps + i) * 2 + 1]);
+        }
+        float inv, sc;
+        bool finite;
+        item_setup<FMT>(p, b, tss, tmw, &inv, &sc, &finite, item_scale);
+        const float *xb = p.x + (size_t)b * p.x_stride;
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            if (norm) v = normed(v, inv, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)));
+            store_digits<FMT>(p, xdig, b, k, v, sc, finite);
         }
     }
 }
@@ -384,30 +405,31 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// The stage sequence of a CTA: stage i covers units [u, u + n) with
-// n = min(kStageUnits, end of the CTA range, end of the current tile).
+// The stage sequence of a CTA over its k-columns (a k-column is the 16 units
+// of one k-unit of a panel, contiguous in memory): stage i covers columns
+// [u, u + n) with n = min(kStageCols, end of the CTA range, end of the panel).
 struct StageWalk {
-    uint64_t u, ce, tend;
-    uint32_t tile, kunits;
-    __device__ StageWalk(uint64_t cb, uint64_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
+    uint32_t u, ce, pend;
+    uint32_t panel, kunits;
+    __device__ StageWalk(uint32_t cb, uint32_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
     {
-        tile = (uint32_t)(cb / kunits_);
-        tend = (uint64_t)(tile + 1) * kunits_;
+        panel = cb / kunits_;
+        pend = (panel + 1) * kunits_;
     }
     __device__ bool more() const { return u < ce; }
     __device__ uint32_t n() const
     {
-        uint64_t e = u + kStageUnits;
+        uint32_t e = u + kStageCols;
         if (e > ce) e = ce;
-        if (e > tend) e = tend;
-        return (uint32_t)(e - u);
+        if (e > pend) e = pend;
+        return e - u;
     }
     __device__ void advance(uint32_t n)
     {
         u += n;
-        if (u == tend) {
-            ++tile;
-            tend += kunits;
+        if (u == pend) {
+            ++panel;
+            pend += kunits;
         }
     }
 };
@@ -417,6 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
     constexpr uint32_t KW = Fmt<FMT>::kKW;
+    constexpr uint32_t CB = kPanelTiles * UB;  // bytes of one k-column
     extern __shared__ __align__(128) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -426,17 +449,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
     uint64_t *empty = full + kMaxStages;
     uint8_t *ring = smem + p.off_ring;
     uint8_t *xdig = smem + p.off_xdig;
-    const uint32_t NT = NS + 2;                                         // tile-partial slots
-    float *tslots = reinterpret_cast<float *>(smem + p.off_tile);      // [NT][kWarps][16*B]
-    float *tbufs = tslots + NT * kWarps * 16 * B;                       // [kWarps][16*B]
-    float *red = reinterpret_cast<float *>(smem + p.off_misc);          // 32 floats
-    float *item_scale = red + 32;                                       // 16 floats
+    float *tbufs = reinterpret_cast<float *>(smem + p.off_tile);      // [kWarps][16*B]
+    float *red = reinterpret_cast<float *>(smem + p.off_misc);        // [kMaxItems][kWarps][2]
+    float *item_scale = red + kMaxItems * kWarps * 2;                 // [kMaxItems]
     unsigned long long *cta_key = reinterpret_cast<unsigned long long *>(item_scale + kMaxItems);
-    int *tcount = reinterpret_cast<int *>(cta_key + kMaxItems);         // [NT]
 
-    const uint64_t U = (uint64_t)p.tiles * p.kunits;
-    const uint64_t G = gridDim.x;  // host guarantees G <= U
-    const uint64_t cb = blockIdx.x * U / G, ce = (blockIdx.x + 1) * U / G;
+    // k-columns; the host guarantees G <= C and C * G < 2^32
+    const uint32_t C = p.panels * p.kunits, G = gridDim.x;
+    const uint32_t cb = blockIdx.x * C / G, ce = (blockIdx.x + 1) * C / G;
 
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < NS; ++s) {
@@ -446,7 +466,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         fence_mbar_init();
     }
     if (threadIdx.x < kMaxItems) cta_key[threadIdx.x] = 0ull;
-    if (threadIdx.x < kMaxTileSlots) tcount[threadIdx.x] = 0;
     __syncthreads();
 
     if (warp == kWarps) {
@@ -464,8 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
                 if (!mbar_wait_bounded(&empty[slot], ((i / NS) - 1) & 1u, p.err)) break;
             }
             if (lane == 0) {
-                mbar_arrive_expect_tx(&full[slot], n * UB);
-                bulk_g2s(ring + (size_t)slot * kStageUnits * UB, p.data + sw.u * UB, n * UB, &full[slot]);
+                mbar_arrive_expect_tx(&full[slot], n * CB);
+                bulk_g2s(ring + (size_t)slot * kStageUnits * UB, p.data + (size_t)sw.u * CB, n * CB, &full[slot]);
             }
             __syncwarp();
             sw.advance(n);
@@ -477,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         return;
     }
 
-    // ---------------- consumer warps ----------------------------------------------------
+    // ---------------- consumer warps: warp w owns tile w of every panel ----------------
     const int g = lane >> 2, t = lane & 3;
     pdl_wait();
     pdl_launch_dependents();
@@ -493,13 +512,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
     bool dead = false;       // a wait timed out: keep the stage protocol, skip the math
-    uint32_t tile_seq = 0;   // tiles this CTA finished (same count in every warp)
     float *mytbuf = tbufs + (size_t)warp * 16 * B;
 
     StageWalk sw(cb, ce, p.kunits);
     for (uint32_t i = 0; sw.more(); ++i) {
         const uint32_t slot = i % NS, n = sw.n();
-        const uint32_t ku0 = (uint32_t)(sw.u - (uint64_t)sw.tile * p.kunits);
+        const uint32_t ku0 = sw.u - sw.panel * p.kunits;
         if (!dead) {
             const bool got = mbar_wait_bounded(&full[slot], (i / NS) & 1u, p.err);
             dead = !__all_sync(0xffffffffu, got);
@@ -507,11 +525,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         if (!dead) {
             const uint8_t *stage = ring + (size_t)slot * kStageUnits * UB;
 #pragma unroll
-            for (int m = 0; m < kStageUnits / kWarps; ++m) {
-                const uint32_t k = warp + m * kWarps;
-                if (k < n) {
-                    const uint8_t *unit = stage + (size_t)k * UB;
-                    const uint32_t ku = ku0 + k;
+            for (int m = 0; m < kStageCols; ++m) {
+                if ((uint32_t)m < n) {
+                    const uint8_t *unit = stage + ((size_t)m * kPanelTiles + warp) * UB;
+                    const uint32_t ku = ku0 + m;
                     const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
                     if (FMT == 4) {
                         const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
@@ -549,15 +566,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
 
-        const uint32_t tile = sw.tile;
-        const uint64_t tfirst = (uint64_t)tile * p.kunits, tend = sw.tend;
+        const uint32_t panel = sw.panel;
+        const uint32_t pfirst = panel * p.kunits, pend = sw.pend;
         sw.advance(n);
-        if (sw.u != tend && sw.u != ce) continue;
+        if (sw.u != pend && sw.u != ce) continue;
 
-        // ---- end of this CTA's part of `tile`: drop this warp's partial into a
-        // slot; the last warp to arrive adds them in warp order and finishes
-        const uint32_t ts = tile_seq++ % NT;
-        float *part = tslots + ((size_t)ts * kWarps + warp) * 16 * B;
+        // ---- end of this CTA's part of the panel: this warp's tile is complete
+        // over the CTA's columns; no other warp holds a share of it
+        const uint32_t tile = panel * kPanelTiles + warp;
 #pragma unroll
         for (int j = 0; j < NI; ++j) {
             float v0, v1;
@@ -573,33 +589,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
             const uint32_t item = 2 * j + (t >> 1);
             if ((t & 1) == 0 && item < B) {
                 const float s = item_scale[item];
-                part[g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
-                part[(g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), s);
+                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), s);
+                if (FMT == 8) {
+                    const uint32_t r0 = tile * 16 + g, r1 = r0 + 8;
+                    y0 = __fmul_rn(y0, r0 < p.rows ? p.row_scale[r0] : 0.0f);
+                    y1 = __fmul_rn(y1, r1 < p.rows ? p.row_scale[r1] : 0.0f);
+                }
+                mytbuf[g * B + item] = y0;
+                mytbuf[(g + 8) * B + item] = y1;
             }
             acc[j][0] = acc[j][1] = 0.0f;
             iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
         }
-        __threadfence_block();
         __syncwarp();
-        int lastw = 0;
-        if (lane == 0) lastw = (atomicAdd(&tcount[ts], 1) == kWarps - 1);
-        lastw = __shfl_sync(0xffffffffu, lastw, 0);
-        if (!lastw) continue;
-        __threadfence_block();
-        const float *parts = tslots + (size_t)ts * kWarps * 16 * B;
-        for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
-            float s = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) s = __fadd_rn(s, parts[w * 16 * B + idx]);
-            if (FMT == 8) s = __fmul_rn(s, p.row_scale[tile * 16 + idx / B]);
-            mytbuf[idx] = s;
-        }
-        __syncwarp();
-        if (lane == 0) tcount[ts] = 0;
-        if (!(tfirst >= cb && tend <= ce)) {
-            // shared with neighbouring CTAs: the last CTA adds all partials
-            const uint64_t cf = ((tfirst + 1) * G - 1) / U, cl = (tend * G - 1) / U;
-            const uint32_t nseg = (uint32_t)(cl - cf + 1);
+        if (!(pfirst >= cb && pend <= ce)) {
+            // the panel is shared with neighbouring CTAs: the last CTA to finish
+            // the tile adds all segments in CTA order
+            const uint32_t cf = ((pfirst + 1) * G - 1) / C, cl = (pend * G - 1) / C;
+            const uint32_t nseg = cl - cf + 1;
             float *pb = p.partial + (size_t)tile * p.maxseg * 16 * B;
             for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = mytbuf[idx];
             __threadfence();
@@ -646,7 +654,7 @@ struct GemvPlan {
     uint32_t maxseg;
     size_t partial_bytes;
     uint32_t counter_len;
-    uint32_t smem, off_ring, off_xdig, off_tile, off_misc, stages;
+    uint32_t smem, off_ring, off_xdig, off_tile, off_misc, stages, panels;
 };
 
 static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
@@ -654,16 +662,17 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t fmt = a->w.format;
     const uint32_t UB = fmt == 4 ? B2_Q4_UNIT_BYTES : B2_Q8_UNIT_BYTES;
     const uint32_t KW = fmt == 4 ? 64u : 32u;
-    const uint64_t U = (uint64_t)a->w.tiles * a->w.kunits;
-    if (U == 0) return false;
-    // shared memory: mbarriers | stage ring | digit planes | tile partials | misc;
-    // the ring takes what the rest leaves, up to kMaxStages stages, with two
-    // more tile-partial slots than stages
+    const uint32_t panels = (a->w.tiles + kPanelTiles - 1) / kPanelTiles;
+    const uint64_t C = (uint64_t)panels * a->w.kunits;  // k-columns
+    if (C == 0) return false;
+    pl.panels = panels;
+    // shared memory: mbarriers | stage ring | digit planes | per-warp tile
+    // buffers | misc; the ring takes what the rest leaves, up to kMaxStages
     const uint32_t xdig = a->w.kunits * a->batch * 3 * KW;
-    const uint32_t slot_b = kWarps * 16 * a->batch * 4;
-    const uint32_t misc = (32 + kMaxItems) * 4 + kMaxItems * 8 + kMaxTileSlots * 4;
-    const uint32_t fixed = 2 * kMaxStages * 8 + 128 + xdig + 128 + 3 * slot_b + 16 + misc;
-    const uint32_t per_stage = kStageUnits * UB + slot_b;
+    const uint32_t tbuf = kWarps * 16 * a->batch * 4;
+    const uint32_t misc = (kMaxItems * kWarps * 2 + kMaxItems) * 4 + kMaxItems * 8;
+    const uint32_t fixed = 2 * kMaxStages * 8 + 128 + xdig + 128 + tbuf + 16 + misc;
+    const uint32_t per_stage = kStageUnits * UB;
     const uint32_t limit = 227u * 1024u;
     if (fixed + 2 * per_stage > limit) return false;
     uint32_t ns = (limit - fixed) / per_stage;
@@ -677,25 +686,25 @@ static bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     off += xdig;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
-    off += (ns + 3) * slot_b;
+    off += tbuf;
     off = (off + 15) & ~15u;
     pl.off_misc = off;
     off += misc;
     pl.smem = off;
-    // one CTA per SM, at least 16 units per CTA
+    // one CTA per SM, at least one k-column per CTA
     int grid = a->grid > 0 ? a->grid : sm_count();
-    const uint64_t want = (U + 15) / 16;
-    if ((uint64_t)grid > want) grid = (int)want;
-    if ((uint64_t)grid > U) grid = (int)U;
+    if ((uint64_t)grid > C) grid = (int)C;
     if (grid < 1) grid = 1;
+    if (C * (uint64_t)grid >= (1ull << 32)) return false;  // 32-bit index arithmetic in the kernel
     pl.grid = grid;
-    const uint64_t minc = U / (uint64_t)grid;  // units of the smallest CTA, >= 1
+    // CTAs sharing one panel: each holds at least minc of its kunits columns
+    const uint64_t minc = C / (uint64_t)grid;
     uint64_t maxseg = (a->w.kunits + minc - 1) / minc + 1;
     if (maxseg > a->w.kunits) maxseg = a->w.kunits;
     pl.maxseg = (uint32_t)maxseg;
-    pl.partial_bytes = (size_t)a->w.tiles * maxseg * 16 * a->batch * sizeof(float);
+    pl.partial_bytes = (size_t)panels * kPanelTiles * maxseg * 16 * a->batch * sizeof(float);
     pl.partial_bytes = (pl.partial_bytes + 255) & ~(size_t)255;
-    pl.counter_len = a->w.tiles;
+    pl.counter_len = panels * kPanelTiles;
     return true;
 }
 
@@ -783,6 +792,7 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
     p.cols = w.cols;
     p.tiles = w.tiles;
     p.kunits = w.kunits;
+    p.panels = pl.panels;
     p.batch = a->batch;
     p.x = a->x;
     p.x_stride = a->x_stride;

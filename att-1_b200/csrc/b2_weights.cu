@@ -34,6 +34,13 @@ __device__ __forceinline__ uint32_t dev_row(int map, uint32_t which, uint32_t sr
     return src_row;
 }
 
+// Index of unit (tile, k-unit): panels of 16 tiles, k-unit-major inside a
+// panel, so the 16 units of one k-unit of a panel are contiguous.
+__device__ __forceinline__ size_t unit_index(uint32_t tile, uint32_t ku, uint32_t kunits)
+{
+    return ((size_t)(tile >> 4) * kunits + ku) * 16 + (tile & 15);
+}
+
 // Byte offset of the nibble word for (device row, 32-col group, t) inside the
 // unit array, relative to the first unit of the tensor.
 __device__ __forceinline__ size_t q4_word_offset(uint32_t row, uint32_t g32, uint32_t t, uint32_t kunits)
@@ -42,14 +49,14 @@ __device__ __forceinline__ size_t q4_word_offset(uint32_t row, uint32_t g32, uin
     const uint32_t gp = g32 >> 1, gi = g32 & 1;
     const uint32_t lane = (r & 7) * 4 + t;
     const uint32_t word = gi * 2 + (r >> 3);
-    return ((size_t)tile * kunits + gp) * B2_Q4_UNIT_BYTES + lane * 16 + word * 4;
+    return unit_index(tile, gp, kunits) * B2_Q4_UNIT_BYTES + lane * 16 + word * 4;
 }
 
 __device__ __forceinline__ size_t q4_scale_offset(uint32_t row, uint32_t g32, uint32_t kunits)
 {
     const uint32_t tile = row >> 4, r = row & 15;
     const uint32_t gp = g32 >> 1, gi = g32 & 1;
-    return ((size_t)tile * kunits + gp) * B2_Q4_UNIT_BYTES + 512 + (r & 7) * 16 + ((r >> 3) * 2 + gi) * 4;
+    return unit_index(tile, gp, kunits) * B2_Q4_UNIT_BYTES + 512 + (r & 7) * 16 + ((r >> 3) * 2 + gi) * 4;
 }
 
 // Write one quantised group (32 signed nibbles, q[i] in [-7,7]) of device row.
@@ -73,7 +80,7 @@ __device__ __forceinline__ void q4_store_group(uint8_t *base, uint32_t row, uint
 // ---- q4 pack from the reference layout: one thread per (device row, 32-group)
 __global__ void q4_pack_kernel(uint8_t *dst, uint32_t dst_rows, uint32_t cols, const uint8_t *p0,
                                const float *s0, const uint8_t *p1, const float *s1, uint32_t group,
-                               int map)
+                               int map, uint32_t row0)
 {
     const uint32_t g32n = cols / 32;
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -92,18 +99,18 @@ __global__ void q4_pack_kernel(uint8_t *dst, uint32_t dst_rows, uint32_t cols, c
         q[2 * j + 1] = (int8_t)((int8_t)b >> 4);
     }
     const float scale = S[(size_t)srow * (cols / group) + (g32 * 32) / group];
-    q4_store_group(dst, row, g32, ceil_div(cols, 64), q, scale);
+    q4_store_group(dst, row0 + row, g32, ceil_div(cols, 64), q, scale);
 }
 
 // ---- q4 unpack to the reference layout (group 32)
 __global__ void q4_unpack_kernel(uint8_t *packed, float *scales, const uint8_t *src, uint32_t rows,
-                                 uint32_t cols, int map, int which)
+                                 uint32_t cols, int map, int which, uint32_t row0)
 {
     const uint32_t g32n = cols / 32;
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (uint64_t)rows * g32n) return;
     const uint32_t srow = (uint32_t)(idx / g32n), g32 = (uint32_t)(idx % g32n);
-    const uint32_t row = dev_row(map, (uint32_t)which, srow);
+    const uint32_t row = row0 + dev_row(map, (uint32_t)which, srow);
     const uint32_t kunits = ceil_div(cols, 64);
     uint8_t nib[32];
 #pragma unroll
@@ -124,7 +131,7 @@ __global__ void q4_unpack_kernel(uint8_t *packed, float *scales, const uint8_t *
 // ---- q4 synth: reference quantiser on generated groups. One thread per
 // (source, source row, 32-group).
 __global__ void q4_synth_kernel(uint8_t *dst, uint32_t dst_rows, uint32_t cols, uint64_t key0,
-                                uint64_t key1, float c, int map)
+                                uint64_t key1, float c, int map, uint32_t row0)
 {
     const uint32_t g32n = cols / 32;
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -153,7 +160,7 @@ __global__ void q4_synth_kernel(uint8_t *dst, uint32_t dst_rows, uint32_t cols, 
         r = r > 7 ? 7 : (r < -7 ? -7 : r);
         q[i] = (int8_t)r;
     }
-    q4_store_group(dst, dev_row(map, which, srow), g32, ceil_div(cols, 64), q, scale);
+    q4_store_group(dst, row0 + dev_row(map, which, srow), g32, ceil_div(cols, 64), q, scale);
 }
 
 // ---- q8 layout helpers
@@ -164,13 +171,13 @@ __device__ __forceinline__ size_t q8_byte_offset(uint32_t row, uint32_t col, uin
     const uint32_t t = (k & 15) >> 2, i = k & 3;
     const uint32_t lane = (r & 7) * 4 + t;
     const uint32_t reg = (k >> 4) * 2 + (r >> 3);
-    return ((size_t)tile * kunits + kb) * B2_Q8_UNIT_BYTES + lane * 16 + reg * 4 + i;
+    return unit_index(tile, kb, kunits) * B2_Q8_UNIT_BYTES + lane * 16 + reg * 4 + i;
 }
 
 // One thread per (device row, 32-col block).
 __global__ void q8_pack_kernel(uint8_t *dst, float *row_scale, uint32_t dst_rows, uint32_t cols,
                                const int8_t *v0, const float *s0, const int8_t *v1, const float *s1,
-                               int map)
+                               int map, uint32_t row0)
 {
     const uint32_t kbn = ceil_div(cols, 32);
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -182,25 +189,25 @@ __global__ void q8_pack_kernel(uint8_t *dst, float *row_scale, uint32_t dst_rows
     for (uint32_t k = 0; k < 32; ++k) {
         const uint32_t col = kb * 32 + k;
         const int8_t q = (col < cols) ? V[(size_t)srow * cols + col] : (int8_t)0;
-        dst[q8_byte_offset(row, col, kbn)] = (uint8_t)q;
+        dst[q8_byte_offset(row0 + row, col, kbn)] = (uint8_t)q;
     }
     if (kb == 0) row_scale[row] = (which ? s1 : s0)[srow];
 }
 
 __global__ void q8_unpack_kernel(int8_t *values, float *scales, const uint8_t *src, const float *row_scale,
-                                 uint32_t rows, uint32_t cols, int map, int which)
+                                 uint32_t rows, uint32_t cols, int map, int which, uint32_t row0)
 {
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (uint64_t)rows * cols) return;
     const uint32_t srow = (uint32_t)(idx / cols), col = (uint32_t)(idx % cols);
     const uint32_t row = dev_row(map, (uint32_t)which, srow);
-    values[idx] = (int8_t)src[q8_byte_offset(row, col, ceil_div(cols, 32))];
+    values[idx] = (int8_t)src[q8_byte_offset(row0 + row, col, ceil_div(cols, 32))];
     if (col == 0) scales[srow] = row_scale[row];
 }
 
 // q8 synth: one warp per source row (max over the row, then quantise).
 __global__ void q8_synth_kernel(uint8_t *dst, float *row_scale, uint32_t dst_rows, uint32_t cols,
-                                uint64_t key0, uint64_t key1, float c, int map)
+                                uint64_t key0, uint64_t key1, float c, int map, uint32_t row0)
 {
     const uint32_t lane = threadIdx.x & 31;
     const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -220,7 +227,7 @@ __global__ void q8_synth_kernel(uint8_t *dst, float *row_scale, uint32_t dst_row
     for (uint32_t k = lane; k < cols; k += 32) {
         long r = lroundf(__fdiv_rn(synth_normal(key, e0 + k, c), scale));
         r = r > 127 ? 127 : (r < -127 ? -127 : r);
-        dst[q8_byte_offset(row, k, kbn)] = (uint8_t)(int8_t)r;
+        dst[q8_byte_offset(row0 + row, k, kbn)] = (uint8_t)(int8_t)r;
     }
     if (lane == 0) row_scale[row] = scale;
 }
@@ -228,7 +235,8 @@ __global__ void q8_synth_kernel(uint8_t *dst, float *row_scale, uint32_t dst_row
 // q8 from device f32: one warp per device row; w (and w2 for the up half of
 // a gate/up interleave) hold [src_rows][cols], or [cols][src_rows] transposed.
 __global__ void q8_quantize_f32_kernel(uint8_t *dst, float *row_scale, uint32_t dst_rows, uint32_t cols,
-                                       const float *w0, const float *w1, int transposed, int map)
+                                       const float *w0, const float *w1, int transposed, int map,
+                                       uint32_t row0)
 {
     const uint32_t lane = threadIdx.x & 31;
     const uint64_t row = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -246,7 +254,7 @@ __global__ void q8_quantize_f32_kernel(uint8_t *dst, float *row_scale, uint32_t 
     for (uint32_t k = lane; k < cols; k += 32) {
         long r = lroundf(__fdiv_rn(at(k), scale));
         r = r > 127 ? 127 : (r < -127 ? -127 : r);
-        dst[q8_byte_offset((uint32_t)row, k, kbn)] = (uint8_t)(int8_t)r;
+        dst[q8_byte_offset(row0 + (uint32_t)row, k, kbn)] = (uint8_t)(int8_t)r;
     }
     if (lane == 0) row_scale[row] = scale;
 }
@@ -275,12 +283,12 @@ using namespace b2;
 
 extern "C" size_t b2_q4_bytes(uint32_t rows, uint32_t cols)
 {
-    return (size_t)ceil_div(rows, 16) * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
+    return (size_t)ceil_div(ceil_div(rows, 16), 16) * 16 * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
 }
 
 extern "C" size_t b2_q8_bytes(uint32_t rows, uint32_t cols)
 {
-    return (size_t)ceil_div(rows, 16) * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
+    return (size_t)ceil_div(ceil_div(rows, 16), 16) * 16 * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
 }
 
 static int check_launch()
@@ -296,10 +304,10 @@ extern "C" int b2_q4_pack(void *dst, uint32_t tile_offset, uint32_t dst_rows, ui
         (group != 32 && group != 64 && group != 128) || cols % group)
         return -1;
     if (map == B2_ROWS_GATEUP && (!packed2 || !scales2 || dst_rows % 16)) return -1;
-    uint8_t *base = (uint8_t *)dst + (size_t)tile_offset * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
+    uint8_t *base = (uint8_t *)dst;
     const uint64_t n = (uint64_t)dst_rows * (cols / 32);
     q4_pack_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(base, dst_rows, cols, packed, scales,
-                                                                       packed2, scales2, group, map);
+                                                                       packed2, scales2, group, map, tile_offset * 16);
     return check_launch();
 }
 
@@ -308,10 +316,10 @@ extern "C" int b2_q4_unpack(uint8_t *packed, float *scales, const void *src, uin
 {
     if (!packed || !scales || !src || rows == 0 || cols == 0 || cols % 32 || which < 0 || which > 1) return -1;
     if (map == B2_ROWS_GATEUP && rows % 8) return -1;
-    const uint8_t *base = (const uint8_t *)src + (size_t)tile_offset * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
+    const uint8_t *base = (const uint8_t *)src;
     const uint64_t n = (uint64_t)rows * (cols / 32);
     q4_unpack_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(packed, scales, base, rows, cols, map,
-                                                                         which);
+                                                                         which, tile_offset * 16);
     return check_launch();
 }
 
@@ -320,11 +328,11 @@ extern "C" int b2_q4_synth(void *dst, uint32_t tile_offset, uint32_t dst_rows, u
 {
     if (!dst || dst_rows == 0 || cols == 0 || cols % 32) return -1;
     if (map == B2_ROWS_GATEUP && dst_rows % 16) return -1;
-    uint8_t *base = (uint8_t *)dst + (size_t)tile_offset * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
+    uint8_t *base = (uint8_t *)dst;
     const float c = std * (1.0f / 131072.0f);
     const uint64_t n = (uint64_t)dst_rows * (cols / 32);
     q4_synth_kernel<<<grid_for(n, 128), 128, 0, (cudaStream_t)stream>>>(
-        base, dst_rows, cols, synth_key(seed, tensor_id), synth_key(seed, tensor_id2), c, map);
+        base, dst_rows, cols, synth_key(seed, tensor_id), synth_key(seed, tensor_id2), c, map, tile_offset * 16);
     return check_launch();
 }
 
@@ -334,10 +342,11 @@ extern "C" int b2_q8_pack(void *dst, float *row_scale, uint32_t tile_offset, uin
 {
     if (!dst || !row_scale || !values || !scales || dst_rows == 0 || cols == 0) return -1;
     if (map == B2_ROWS_GATEUP && (!values2 || !scales2 || dst_rows % 16)) return -1;
-    uint8_t *base = (uint8_t *)dst + (size_t)tile_offset * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
+    uint8_t *base = (uint8_t *)dst;
     const uint64_t n = (uint64_t)dst_rows * ceil_div(cols, 32);
     q8_pack_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        base, row_scale + (size_t)tile_offset * 16, dst_rows, cols, values, scales, values2, scales2, map);
+        base, row_scale + (size_t)tile_offset * 16, dst_rows, cols, values, scales, values2, scales2, map,
+        tile_offset * 16);
     return check_launch();
 }
 
@@ -346,10 +355,10 @@ extern "C" int b2_q8_unpack(int8_t *values, float *scales, const void *src, cons
 {
     if (!values || !scales || !src || !row_scale || rows == 0 || cols == 0 || which < 0 || which > 1) return -1;
     if (map == B2_ROWS_GATEUP && rows % 8) return -1;
-    const uint8_t *base = (const uint8_t *)src + (size_t)tile_offset * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
+    const uint8_t *base = (const uint8_t *)src;
     const uint64_t n = (uint64_t)rows * cols;
     q8_unpack_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        values, scales, base, row_scale + (size_t)tile_offset * 16, rows, cols, map, which);
+        values, scales, base, row_scale + (size_t)tile_offset * 16, rows, cols, map, which, tile_offset * 16);
     return check_launch();
 }
 
@@ -359,11 +368,11 @@ extern "C" int b2_q8_synth(void *dst, float *row_scale, uint32_t tile_offset, ui
 {
     if (!dst || !row_scale || dst_rows == 0 || cols == 0) return -1;
     if (map == B2_ROWS_GATEUP && dst_rows % 16) return -1;
-    uint8_t *base = (uint8_t *)dst + (size_t)tile_offset * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
+    uint8_t *base = (uint8_t *)dst;
     const float c = std * (1.0f / 131072.0f);
     q8_synth_kernel<<<grid_for((uint64_t)dst_rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
         base, row_scale + (size_t)tile_offset * 16, dst_rows, cols, synth_key(seed, tensor_id),
-        synth_key(seed, tensor_id2), c, map);
+        synth_key(seed, tensor_id2), c, map, tile_offset * 16);
     return check_launch();
 }
 
@@ -388,8 +397,8 @@ extern "C" int b2_q8_quantize_f32(void *dst, float *row_scale, uint32_t tile_off
 {
     if (!dst || !row_scale || !w || dst_rows == 0 || cols == 0) return -1;
     if (map == B2_ROWS_GATEUP && (!w2 || dst_rows % 16)) return -1;
-    uint8_t *base = (uint8_t *)dst + (size_t)tile_offset * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
+    uint8_t *base = (uint8_t *)dst;
     q8_quantize_f32_kernel<<<grid_for((uint64_t)dst_rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
-        base, row_scale + (size_t)tile_offset * 16, dst_rows, cols, w, w2, transposed, map);
+        base, row_scale + (size_t)tile_offset * 16, dst_rows, cols, w, w2, transposed, map, tile_offset * 16);
     return check_launch();
 }

@@ -32,7 +32,12 @@ extern "C" {
 /*
  * q4 "unit" layout: a matrix [rows][cols] is cut into 16-row tiles and
  * 64-column group pairs (two q4 groups of 32). Each (tile, pair) unit is 640
- * contiguous bytes, units ordered tile-major:
+ * contiguous bytes. Tiles are grouped into panels of 16 (256 rows; the last
+ * panel is padded with zero tiles) and units are ordered panel-major, then
+ * by column pair, then by tile, so the 16 units of one column pair of a
+ * panel (a "k-column", 10 KB) are contiguous:
+ *   unit(tile, pair) = ((tile / 16) * pairs + pair) * 16 + tile % 16
+ * Inside a unit:
  *   bytes [0,512):  32 lanes x 16 B; lane l = 4*r + t (r = row in tile mod 8)
  *                   holds words {row r g0, row r+8 g0, row r g1, row r+8 g1};
  *                   byte i of a word = nibble(col 4t+i) | nibble(col 16+4t+i)<<4
@@ -42,7 +47,8 @@ extern "C" {
  * Padding rows/columns hold zero nibbles and zero scales. The mapping is a
  * permutation of the reference's nibbles (b2_q4_unpack inverts it).
  *
- * q8 unit layout: (16-row tile, 32-column block) units of 512 bytes, lane l
+ * q8 unit layout: (16-row tile, 32-column block) units of 512 bytes in the
+ * same panel order, lane l
  * holds 16 int8 {row r k 4t..4t+3, row r+8 k 4t.., row r k 16+4t.., row r+8
  * k 16+4t..}; one f32 scale per row in a separate array [tiles*16].
  */
