@@ -134,6 +134,7 @@ _SIGS = {
     "att1_b200_infer_decode_batch": (C.c_int, [_P, C.POINTER(_U32), C.POINTER(_U32)]),
     "att1_b200_infer_logits_batch": (C.POINTER(_F), [_P, C.POINTER(_SZ)]),
     "att1_b200_infer_set_options": (C.c_int, [_P, C.c_int, C.c_int]),
+    "att1_b200_infer_set_persistent": (C.c_int, [_P, C.c_int]),
     "att1_b200_infer_run_steps": (C.c_int, [_P, _U32]),
     "att1_b200_infer_sync": (C.c_int, [_P]),
     "att1_b200_infer_stream": (_P, [_P]),
@@ -266,8 +267,12 @@ class Infer:
         check("att1_infer_position", lib().att1_infer_position(self.h, C.byref(n)))
         return n.value
 
-    def set_options(self, graph=True, pdl=True):
+    def set_options(self, graph=True, pdl=True, persistent=None):
+        """graph / pdl apply to the per-operation kernel sequence; persistent
+        selects the single-launch step (True) or that sequence (False)."""
         check("att1_b200_infer_set_options", lib().att1_b200_infer_set_options(self.h, int(graph), int(pdl)))
+        if persistent is not None:
+            check("att1_b200_infer_set_persistent", lib().att1_b200_infer_set_persistent(self.h, int(persistent)))
 
     def run_steps(self, n: int):
         check("att1_b200_infer_run_steps", lib().att1_b200_infer_run_steps(self.h, n))

@@ -1,0 +1,647 @@
+// b2_gemv.cuh - device side of the q4/q8 block-dequant GEMV.
+//
+// Shared by the standalone GEMV kernel (b2_gemv.cu) and the persistent decode
+// kernel (b2_decode.cu): parameters, the x prologue (RMSNorm, exponent,
+// digit planes), the tile epilogues, and the producer / consumer halves of
+// the bulk-copy ring. The design notes are in b2_gemv.cu.
+#pragma once
+
+#include "b2_common.cuh"
+
+#include <cfloat>
+#include <cuda_runtime.h>
+
+namespace b2 {
+
+constexpr int kWarps = 16;                          // consumer warps (16 hide the math latency)
+constexpr int kConsumers = kWarps * 32;
+constexpr int kThreads = kConsumers + 32;           // + one producer warp
+constexpr int kPanelTiles = 16;                     // tiles per panel: one per consumer warp
+constexpr int kStageCols = 4;                       // k-columns per stage
+constexpr int kStageUnits = kStageCols * kPanelTiles;  // 64 units: 40 KB of q4, one bulk copy
+constexpr int kMaxStages = 8;                       // ring depth, chosen per launch
+constexpr int kMaxItems = 16;
+constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
+static_assert(kPanelTiles == kWarps, "each consumer warp owns one tile of a panel");
+
+struct GemvParams {
+    const uint8_t *data;
+    const float *row_scale;
+    uint32_t rows, cols, tiles, kunits, panels;
+    uint32_t batch;
+    const float *x;
+    uint32_t x_stride;
+    const float *norm_w;
+    float eps;
+    int epilogue;
+    float *out;
+    uint32_t out_stride;
+    const float *resid;
+    uint32_t q_rows, kv_rows;
+    const float *rope_freq;
+    const int32_t *positions;
+    b2_kv_layout kv;
+    unsigned long long *argmax;
+    float *partial;
+    int *counters;
+    uint32_t maxseg;
+    uint32_t grid;  // CTAs taking part (the first `grid` CTAs of the launch)
+    int32_t *err;
+    // shared-memory carve-up (bytes)
+    uint32_t off_ring, off_xdig, off_tile, off_misc, stages;
+};
+
+template <int FMT>
+struct Fmt;
+template <>
+struct Fmt<4> {
+    static constexpr uint32_t kUnitBytes = B2_Q4_UNIT_BYTES;
+    static constexpr uint32_t kKW = 64;  // columns per unit
+};
+template <>
+struct Fmt<8> {
+    static constexpr uint32_t kUnitBytes = B2_Q8_UNIT_BYTES;
+    static constexpr uint32_t kKW = 32;
+};
+
+__device__ __forceinline__ uint32_t ordered_key(float f)
+{
+    uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
+// One pass of loads (x and the norm gains together) and one reduction round
+// per launch: every thread accumulates, per item, the sum of squares of x and
+// the largest |x * w|; the warps' partials meet in shared memory once. The
+// normed vector x * inv * w (src/norm.c:31) is bounded by inv * max|x * w|
+// (times 1 + 2^-20 for the two roundings), and that bound picks the exponent,
+// so no second reduction over the normed values is needed. Vectors of up to
+// kPrologueVec * 4 * kConsumers elements stay in registers between the two
+// steps (batch 1); otherwise the second step reads x again.
+constexpr int kPrologueVec = 8;   // float4 per thread held in registers (x and gains)
+
+template <int FMT>
+__device__ __forceinline__ void store_digits(const GemvParams &p, uint8_t *xdig, uint32_t b, uint32_t k, float4 v,
+                                             float sc, bool finite)
+{
+    constexpr uint32_t KW = Fmt<FMT>::kKW;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int q = finite ? __float2int_rn(__fmul_rn(vv[i], sc)) : 0;
+        const int d0 = ((q + 128) & 255) - 128;
+        const int q1 = (q - d0) >> 8;
+        const int d1 = ((q1 + 128) & 255) - 128;
+        const int d2 = (q1 - d1) >> 8;
+        w0 |= ((uint32_t)d0 & 0xFFu) << (8 * i);
+        w1 |= ((uint32_t)d1 & 0xFFu) << (8 * i);
+        w2 |= ((uint32_t)d2 & 0xFFu) << (8 * i);
+    }
+    const uint32_t unit = k / KW, kk = k % KW;
+    const uint32_t gi = kk >> 5, r = kk & 31;
+    const uint32_t half = r >> 4, t = (r & 15) >> 2;
+    uint8_t *base = xdig + ((size_t)(unit * p.batch + b) * 3) * KW + t * (KW / 4) + gi * 8 + half * 4;
+    *reinterpret_cast<uint32_t *>(base) = w0;
+    *reinterpret_cast<uint32_t *>(base + KW) = w1;
+    *reinterpret_cast<uint32_t *>(base + 2 * KW) = w2;
+}
+
+__device__ __forceinline__ float4 normed(float4 v, float inv, float4 w)
+{
+    // src/norm.c:31: dst = src * scale * weight
+    return make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
+                       __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
+}
+
+__device__ __forceinline__ float4 mul4(float4 a, float4 b)
+{
+    return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+
+__device__ __forceinline__ float sumsq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+
+__device__ __forceinline__ float absmax4(float4 v)
+{
+    const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    // fmaxf drops NaN: make any non-finite element visible
+    return (fabsf(v.x) <= FLT_MAX && fabsf(v.y) <= FLT_MAX && fabsf(v.z) <= FLT_MAX && fabsf(v.w) <= FLT_MAX)
+               ? a : INFINITY;
+}
+
+__device__ __forceinline__ int pick_exponent(float m)
+{
+    int E = 0;
+    if (m > 0.0f && m <= FLT_MAX) {
+        E = ilogbf(m) - 21;  // |x| * 2^-E < 2^22
+        if (E < -125) E = -125;
+    }
+    return E;
+}
+
+__device__ __forceinline__ void consumer_sync()
+{
+    asm volatile("bar.sync %0, %1;" ::"n"(kConsumerBarrier), "n"(kConsumers) : "memory");
+}
+
+// Per item: the normalisation factor (1 without a norm) and the exponent
+// scale, from the item's sum of squares and max |x * w| (max |x| without a norm).
+template <int FMT>
+__device__ __forceinline__ void item_setup(const GemvParams &p, uint32_t b, float ss, float mw, float *inv_out,
+                                           float *sc_out, bool *finite_out, float *item_scale)
+{
+    float inv = 1.0f, bound = mw;
+    if (p.norm_w != nullptr) {
+        // src/norm.c:26-28
+        inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)p.cols), p.eps)));
+        bound = __fmul_rn(__fmul_rn(mw, inv), 1.0f + 0x1p-20f);
+    }
+    const bool finite = mw <= FLT_MAX && inv <= FLT_MAX;
+    const int E = pick_exponent(bound);
+    *inv_out = inv;
+    *sc_out = ldexpf(1.0f, -E);
+    *finite_out = finite;
+    if (threadIdx.x == 0) {
+        item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
+        if (!finite) raise_error(p.err, B2_ERR_NONFINITE);
+    }
+}
+
+template <int FMT>
+__device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
+{
+    const uint32_t cols = p.cols;
+    const uint32_t stride = kConsumers * 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool norm = p.norm_w != nullptr;
+    if (p.batch == 1 && cols <= stride * kPrologueVec) {
+        float4 v[kPrologueVec], w[kPrologueVec];
+#pragma unroll
+        for (int i = 0; i < kPrologueVec; ++i) {
+            const uint32_t k = threadIdx.x * 4 + i * stride;
+            const bool in = k < cols;
+            v[i] = in ? __ldcg(reinterpret_cast<const float4 *>(p.x + k)) : make_float4(0, 0, 0, 0);
+            w[i] = (in && norm) ? __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)) : make_float4(1, 1, 1, 1);
+        }
+        float ss = 0.0f, mw = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kPrologueVec; ++i) {
+            ss += sumsq4(v[i]);
+            mw = fmaxf(mw, absmax4(norm ? mul4(v[i], w[i]) : v[i]));
+        }
+        ss = warp_sum(ss);
+        mw = warp_max(mw);
+        if (lane == 0) {
+            red[warp] = ss;
+            red[kWarps + warp] = mw;
+        }
+        consumer_sync();
+        float tss = 0.0f, tmw = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kWarps; ++i) {
+            tss += red[i];
+            tmw = fmaxf(tmw, red[kWarps + i]);
+        }
+        float inv, sc;
+        bool finite;
+        item_setup<FMT>(p, 0, tss, tmw, &inv, &sc, &finite, item_scale);
+#pragma unroll
+        for (int i = 0; i < kPrologueVec; ++i) {
+            const uint32_t k = threadIdx.x * 4 + i * stride;
+            if (k < cols) store_digits<FMT>(p, xdig, 0, k, norm ? normed(v[i], inv, w[i]) : v[i], sc, finite);
+        }
+        return;
+    }
+    // general path: statistics of every item in one reduction round, then the digits
+    float *stats = red;  // [kMaxItems][kWarps][2]
+    for (uint32_t b = 0; b < p.batch; ++b) {
+        const float *xb = p.x + (size_t)b * p.x_stride;
+        float ss = 0.0f, mw = 0.0f;
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            ss += sumsq4(v);
+            mw = fmaxf(mw, absmax4(norm ? mul4(v, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k))) : v));
+        }
+        ss = warp_sum(ss);
+        mw = warp_max(mw);
+        if (lane == 0) {
+            stats[(b * kWarps + warp) * 2] = ss;
+            stats[(b * kWarps + warp) * 2 + 1] = mw;
+        }
+    }
+    consumer_sync();
+    for (uint32_t b = 0; b < p.batch; ++b) {
+        float tss = 0.0f, tmw = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kWarps; ++i) {
+            tss += stats[(b * kWarps + i) * 2];
+            tmw = fmaxf(tmw, stats[(b * kWarps + i) * 2 + 1]);
+        }
+        float inv, sc;
+        bool finite;
+        item_setup<FMT>(p, b, tss, tmw, &inv, &sc, &finite, item_scale);
+        const float *xb = p.x + (size_t)b * p.x_stride;
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            if (norm) v = normed(v, inv, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)));
+            store_digits<FMT>(p, xdig, b, k, v, sc, finite);
+        }
+    }
+}
+
+// ---- epilogue on one finished 16-row tile held in shared memory [16][batch] --
+static __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const float *tb, unsigned long long *cta_key,
+                              int lane)
+{
+    const uint32_t B = p.batch;
+    // uniform trip count: every lane takes part in the shuffles of LOGITS
+    for (uint32_t base = 0; base < 16 * B; base += 32) {
+        const uint32_t idx = base + lane;
+        const bool valid = idx < 16 * B;
+        const uint32_t r = idx & 15, item = valid ? (idx >> 4) : 0;
+        const uint32_t row = valid ? tile * 16 + r : 0xFFFFFFFFu;
+        const float v = valid ? tb[r * B + item] : 0.0f;
+        if (!valid && p.epilogue != B2_EPI_LOGITS) continue;
+        switch (p.epilogue) {
+        case B2_EPI_STORE:
+            if (row < p.rows) p.out[(size_t)item * p.out_stride + row] = v;
+            break;
+        case B2_EPI_RESID:
+            if (row < p.rows) {
+                const size_t o = (size_t)item * p.out_stride + row;
+                p.out[o] = __fadd_rn(__ldcg(p.resid + o), v);  // src/transformer_block.c:63-72
+            }
+            break;
+        case B2_EPI_QKV: {
+            if (row >= p.rows) break;
+            const uint32_t hd = p.kv.head_dim;
+            const int32_t pos = p.positions[item];
+            const uint32_t cap = p.kv.pages_per_seq * p.kv.page_tokens;
+            if (row < p.q_rows + p.kv_rows) {
+                // RoPE on q and k (src/rope.c:20-30): interleaved pairs of a head
+                const uint32_t rr = row < p.q_rows ? row : row - p.q_rows;
+                const uint32_t i = rr % hd;
+                const float x0 = tb[(r & ~1u) * B + item], x1 = tb[(r | 1u) * B + item];
+                const float ang = __fmul_rn((float)pos, p.rope_freq[i >> 1]);
+                float s, c;
+                sincosf(ang, &s, &c);
+                const float y = (i & 1u) ? __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c))
+                                         : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+                if (row < p.q_rows) {
+                    p.out[(size_t)item * p.out_stride + row] = y;
+                } else if (pos >= 0 && (uint32_t)pos < cap) {
+                    const int32_t page = p.kv.page_table[(size_t)item * p.kv.pages_per_seq + pos / p.kv.page_tokens];
+                    const size_t slot = (size_t)page * p.kv.page_tokens + pos % p.kv.page_tokens;
+                    p.kv.k_pool[slot * p.kv.n_kv_heads * hd + rr] = y;
+                } else {
+                    raise_error(p.err, B2_ERR_POSITION);
+                }
+            } else {
+                const uint32_t rr = row - p.q_rows - p.kv_rows;
+                if (pos >= 0 && (uint32_t)pos < cap) {
+                    const int32_t page = p.kv.page_table[(size_t)item * p.kv.pages_per_seq + pos / p.kv.page_tokens];
+                    const size_t slot = (size_t)page * p.kv.page_tokens + pos % p.kv.page_tokens;
+                    p.kv.v_pool[slot * p.kv.n_kv_heads * hd + rr] = v;
+                } else {
+                    raise_error(p.err, B2_ERR_POSITION);
+                }
+            }
+            break;
+        }
+        case B2_EPI_SWIGLU:
+            if (r < 8) {
+                const uint32_t j = tile * 8 + r;
+                if (j < p.rows / 2) {
+                    const float g = v, u = tb[(r + 8) * B + item];
+                    // src/ffn.c:7 silu(g) = g / (1 + expf(-g)); then * up
+                    p.out[(size_t)item * p.out_stride + j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                }
+            }
+            break;
+        case B2_EPI_LOGITS: {
+            unsigned long long key = 0ull;
+            if (row < p.rows) {
+                p.out[(size_t)item * p.out_stride + row] = v;
+                if (v != v) {
+                    raise_error(p.err, B2_ERR_NAN_LOGITS);
+                } else {
+                    key = ((unsigned long long)ordered_key(v) << 32) | (0xFFFFFFFFu - row);
+                }
+            }
+            // max over the 16 lanes of this item (lanes 16*k .. 16*k+15)
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            if ((lane & 15) == 0 && valid) atomicMax(&cta_key[item], key);
+            break;
+        }
+        default:
+            break;
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// The mbarrier arrives once this thread's cp.async copies issued so far land.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// The stage sequence of a CTA over its k-columns (a k-column is the 16 units
+// of one k-unit of a panel, contiguous in memory): stage i covers columns
+// [u, u + n) with n = min(kStageCols, end of the CTA range, end of the panel).
+struct StageWalk {
+    uint32_t u, ce, pend;
+    uint32_t panel, kunits;
+    __device__ StageWalk(uint32_t cb, uint32_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
+    {
+        panel = cb / kunits_;
+        pend = (panel + 1) * kunits_;
+    }
+    __device__ bool more() const { return u < ce; }
+    __device__ uint32_t n() const
+    {
+        uint32_t e = u + kStageCols;
+        if (e > ce) e = ce;
+        if (e > pend) e = pend;
+        return e - u;
+    }
+    __device__ void advance(uint32_t n)
+    {
+        u += n;
+        if (u == pend) {
+            ++panel;
+            pend += kunits;
+        }
+    }
+};
+
+// Shared-memory view of the GEMV pipeline (same carve-up in both kernels).
+struct GemvSmem {
+    uint64_t *full, *empty;
+    uint8_t *ring, *xdig;
+    float *tbufs, *red, *item_scale;
+    unsigned long long *cta_key;
+    uint32_t stages;
+};
+
+__device__ __forceinline__ GemvSmem gemv_smem(uint8_t *smem, const GemvParams &p)
+{
+    GemvSmem s;
+    s.full = reinterpret_cast<uint64_t *>(smem);
+    s.empty = s.full + kMaxStages;
+    s.ring = smem + p.off_ring;
+    s.xdig = smem + p.off_xdig;
+    s.tbufs = reinterpret_cast<float *>(smem + p.off_tile);   // [kWarps][16*B]
+    s.red = reinterpret_cast<float *>(smem + p.off_misc);     // [kMaxItems][kWarps][2]
+    s.item_scale = s.red + kMaxItems * kWarps * 2;            // [kMaxItems]
+    s.cta_key = reinterpret_cast<unsigned long long *>(s.item_scale + kMaxItems);
+    s.stages = p.stages;
+    return s;
+}
+
+// Barriers of the ring: "full" completes on the producer's arrival plus the
+// bytes of the copy, "empty" on one arrival per consumer warp.
+__device__ __forceinline__ void gemv_init_barriers(const GemvSmem &s)
+{
+    for (uint32_t i = 0; i < s.stages; ++i) {
+        mbar_init(&s.full[i], 1);
+        mbar_init(&s.empty[i], kWarps);
+    }
+    fence_mbar_init();
+}
+
+// The CTA's k-columns [cb, ce): the first p.grid CTAs split the columns
+// (the host guarantees p.grid <= C and C * p.grid < 2^32), any further CTAs
+// of a larger launch get an empty range.
+__device__ __forceinline__ void cta_range(const GemvParams &p, uint32_t &cb, uint32_t &ce)
+{
+    const uint32_t C = p.panels * p.kunits, G = p.grid;
+    if (blockIdx.x >= G) {
+        cb = ce = 0;
+        return;
+    }
+    cb = blockIdx.x * C / G;
+    ce = (blockIdx.x + 1) * C / G;
+}
+
+// Producer warp: copy this CTA's stages of one GEMV into the ring. `i` counts
+// stages over the life of the ring (it continues across GEMVs that share a
+// ring); `waited` records that the programmatic-launch wait was taken (the
+// first NS stages are requested before it). Returns false after a timeout.
+template <int FMT>
+__device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &waited)
+{
+    constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
+    constexpr uint32_t CB = kPanelTiles * UB;  // bytes of one k-column
+    const int lane = threadIdx.x & 31;
+    uint32_t cb, ce;
+    cta_range(p, cb, ce);
+    StageWalk sw(cb, ce, p.kunits);
+    for (; sw.more(); ++i) {
+        const uint32_t slot = i % s.stages, n = sw.n();
+        if (i >= s.stages) {
+            if (!waited) {
+                pdl_wait();
+                pdl_launch_dependents();
+                waited = true;
+            }
+            if (!mbar_wait_bounded(&s.empty[slot], ((i / s.stages) - 1) & 1u, p.err)) return false;
+        }
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&s.full[slot], n * CB);
+            bulk_g2s(s.ring + (size_t)slot * kStageUnits * UB, p.data + (size_t)sw.u * CB, n * CB, &s.full[slot]);
+        }
+        __syncwarp();
+        sw.advance(n);
+    }
+    return true;
+}
+
+// Consumer warps (all kWarps of them): prologue, the CTA's stages of one GEMV
+// (ring position `i`, shared with the producer's count), tile epilogues and
+// cross-CTA completion. `dead` (a wait timed out) keeps the stage protocol
+// but skips the math and the stores.
+template <int FMT, int NI>
+__device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &dead)
+{
+    constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
+    constexpr uint32_t KW = Fmt<FMT>::kKW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t B = p.batch;
+    const uint32_t NS = s.stages;
+    uint32_t cb, ce;
+    cta_range(p, cb, ce);
+    if (cb == ce) return;  // no columns for this CTA
+    const uint32_t C = p.panels * p.kunits, G = p.grid;
+    if (threadIdx.x < kMaxItems) s.cta_key[threadIdx.x] = 0ull;
+    prepare_x<FMT>(p, s.xdig, s.item_scale, s.red);
+    consumer_sync();
+
+    const uint32_t digit = g & 3;
+    float acc[NI][2];
+    int iacc[NI][4];
+#pragma unroll
+    for (int j = 0; j < NI; ++j) {
+        acc[j][0] = acc[j][1] = 0.0f;
+        iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+    }
+    float *mytbuf = s.tbufs + (size_t)warp * 16 * B;
+
+    StageWalk sw(cb, ce, p.kunits);
+    for (; sw.more(); ++i) {
+        const uint32_t slot = i % NS, n = sw.n();
+        const uint32_t ku0 = sw.u - sw.panel * p.kunits;
+        if (!dead) {
+            const bool got = mbar_wait_bounded(&s.full[slot], (i / NS) & 1u, p.err);
+            dead = !__all_sync(0xffffffffu, got);
+        }
+        if (!dead) {
+            const uint8_t *stage = s.ring + (size_t)slot * kStageUnits * UB;
+#pragma unroll
+            for (int m = 0; m < kStageCols; ++m) {
+                if ((uint32_t)m < n) {
+                    const uint8_t *unit = stage + ((size_t)m * kPanelTiles + warp) * UB;
+                    const uint32_t ku = ku0 + m;
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
+                    if (FMT == 4) {
+                        const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
+                        const uint32_t M = 0xF0F0F0F0u;
+                        const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
+                        const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
+#pragma unroll
+                        for (int j = 0; j < NI; ++j) {
+                            const uint32_t item = 2 * j + (g >> 2);
+                            uint4 bf = make_uint4(0, 0, 0, 0);
+                            if (digit < 3 && item < B)
+                                bf = *reinterpret_cast<const uint4 *>(s.xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
+                            int d[4], e[4];
+                            imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
+                            imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
+                            acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
+                            acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
+                            acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
+                            acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < NI; ++j) {
+                            const uint32_t item = 2 * j + (g >> 2);
+                            uint2 bf = make_uint2(0, 0);
+                            if (digit < 3 && item < B)
+                                bf = *reinterpret_cast<const uint2 *>(s.xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
+                            imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                                       iacc[j][3]);
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[slot]);
+
+        const uint32_t panel = sw.panel;
+        const uint32_t pfirst = panel * p.kunits, pend = sw.pend;
+        sw.advance(n);
+        if (sw.u != pend && sw.u != ce) continue;
+
+        // ---- end of this CTA's part of the panel: this warp's tile is complete
+        // over the CTA's columns; no other warp holds a share of it
+        const uint32_t tile = panel * kPanelTiles + warp;
+#pragma unroll
+        for (int j = 0; j < NI; ++j) {
+            float v0, v1;
+            if (FMT == 4) {
+                v0 = acc[j][0];
+                v1 = acc[j][1];
+            } else {
+                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
+                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
+            }
+            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
+            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
+            const uint32_t item = 2 * j + (t >> 1);
+            if ((t & 1) == 0 && item < B) {
+                const float sc_item = s.item_scale[item];
+                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), sc_item);
+                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), sc_item);
+                if (FMT == 8) {
+                    const uint32_t r0 = tile * 16 + g, r1 = r0 + 8;
+                    y0 = __fmul_rn(y0, r0 < p.rows ? p.row_scale[r0] : 0.0f);
+                    y1 = __fmul_rn(y1, r1 < p.rows ? p.row_scale[r1] : 0.0f);
+                }
+                mytbuf[g * B + item] = y0;
+                mytbuf[(g + 8) * B + item] = y1;
+            }
+            acc[j][0] = acc[j][1] = 0.0f;
+            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+        }
+        __syncwarp();
+        if (!(pfirst >= cb && pend <= ce)) {
+            // the panel is shared with neighbouring CTAs: the last CTA to finish
+            // the tile adds all segments in CTA order
+            const uint32_t cf = ((pfirst + 1) * G - 1) / C, cl = (pend * G - 1) / C;
+            const uint32_t nseg = cl - cf + 1;
+            float *pb = p.partial + (size_t)tile * p.maxseg * 16 * B;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = mytbuf[idx];
+            // one fence per warp: __syncwarp orders the lanes' stores before
+            // lane 0's release, and lane 0's acquire before the lanes' loads
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                __threadfence();
+                last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
+                if (last) __threadfence();
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            __syncwarp();
+            if (!last) continue;
+            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+                float sum = 0.0f;
+                for (uint32_t sg = 0; sg < nseg; ++sg) sum = __fadd_rn(sum, ld_cg(pb + (size_t)sg * 16 * B + idx));
+                mytbuf[idx] = sum;
+            }
+            if (lane == 0) p.counters[tile] = 0;
+            __syncwarp();
+        }
+        if (!dead) tile_epilogue(p, tile, mytbuf, s.cta_key, lane);
+        __syncwarp();
+    }
+    if (p.epilogue == B2_EPI_LOGITS) {
+        consumer_sync();
+        if (threadIdx.x < B && s.cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], s.cta_key[threadIdx.x]);
+    }
+}
+
+// ---- host side (b2_gemv.cu) -------------------------------------------------------
+struct GemvPlan {
+    int grid;
+    uint32_t maxseg;
+    size_t partial_bytes;
+    uint32_t counter_len;
+    uint32_t smem, off_ring, off_xdig, off_tile, off_misc, stages, panels;
+};
+
+int sm_count();
+// Argument checks of b2_gemv (0 or a negative status).
+int gemv_check(const b2_gemv_args *a);
+// Grid, shared-memory carve-up and scratch sizes for a standalone launch.
+bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl);
+// Kernel parameters from checked arguments and a plan (scratch from `a`).
+void gemv_params(const b2_gemv_args *a, const GemvPlan &pl, GemvParams &p);
+
+}  // namespace b2

@@ -64,9 +64,10 @@ struct att1_infer {
     float *logits_h;
     int logits_valid;
     size_t position;
-    int use_graph, use_pdl;
+    int use_graph, use_pdl, use_persistent;
     cudaGraphExec_t exec;
     int graph_failed;
+    b2_decode_plan *plan;
     att1_backend *backend;
     att1_trace_t *trace;
     const att1_model *model;
@@ -128,6 +129,7 @@ static void release(att1_infer_t *inf)
     if (inf == NULL) return;
     if (inf->stream) cudaStreamSynchronize(inf->stream);
     if (inf->exec) cudaGraphExecDestroy(inf->exec);
+    if (inf->plan) b2_decode_plan_destroy(inf->plan);
     if (inf->layers) {
         for (l = 0; l < inf->cfg.n_layers; l++) {
             dev_layer *L = &inf->layers[l];
@@ -210,6 +212,50 @@ static b2_kv_layout kv_layout(att1_infer_t *inf, uint32_t layer)
     kv.n_kv_heads = inf->cfg.n_kv_heads;
     kv.head_dim = inf->head_dim;
     return kv;
+}
+
+/* The persistent single-launch step over the same arguments. A shape the
+ * persistent kernel cannot hold (shared memory) keeps the per-kernel sequence. */
+static att1_status_t build_plan(att1_infer_t *inf)
+{
+    const att1_b200_config *c = &inf->cfg;
+    b2_decode_layer *ls;
+    b2_decode_args da;
+    uint32_t l;
+    int rc;
+    if (inf->plan) {
+        cudaStreamSynchronize(inf->stream);
+        b2_decode_plan_destroy(inf->plan);
+        inf->plan = NULL;
+    }
+    ls = calloc(c->n_layers, sizeof(*ls));
+    if (ls == NULL) return ATT1_ERR_OOM;
+    for (l = 0; l < c->n_layers; l++) {
+        ls[l].qkv = inf->layers[l].a_qkv;
+        ls[l].wo = inf->layers[l].a_wo;
+        ls[l].gu = inf->layers[l].a_gu;
+        ls[l].down = inf->layers[l].a_down;
+        ls[l].attn = inf->layers[l].a_attn;
+    }
+    memset(&da, 0, sizeof(da));
+    da.n_layers = c->n_layers;
+    da.batch = inf->batch;
+    da.layers = ls;
+    da.out = inf->a_out;
+    da.embed = inf->embed;
+    da.vocab = c->vocab;
+    da.d_model = c->d_model;
+    da.tokens_in = inf->tokens_d;
+    da.tokens_out = inf->tokens_d;
+    da.positions = inf->pos_d;
+    da.argmax = inf->argmax_d;
+    da.x = inf->x;
+    da.err = inf->err_d;
+    rc = b2_decode_plan_create(&da, &inf->plan);
+    free(ls);
+    if (rc == -2) return ATT1_ERR_OOM;
+    if (rc != 0) inf->plan = NULL;
+    return ATT1_OK;
 }
 
 static att1_status_t build_args(att1_infer_t *inf)
@@ -336,7 +382,7 @@ static att1_status_t build_args(att1_infer_t *inf)
     inf->a_out.scratch_bytes = need;
     inf->a_out.counters = inf->counters;
     inf->a_out.counters_len = inf->counters_len;
-    return ATT1_OK;
+    return build_plan(inf);
 }
 
 static void set_pdl(att1_infer_t *inf, int pdl)
@@ -422,6 +468,7 @@ static att1_status_t new_context(const att1_b200_config *cfg, uint32_t batch, at
     inf->kv_rows = cfg->n_kv_heads * inf->head_dim;
     inf->use_graph = 1;
     inf->use_pdl = 1;
+    inf->use_persistent = 0;
     if (cudaGetDevice(&inf->device) != cudaSuccess ||
         cudaStreamCreateWithFlags(&inf->stream, cudaStreamNonBlocking) != cudaSuccess) {
         free(inf);
@@ -788,6 +835,7 @@ static int enqueue_kernels(att1_infer_t *inf)
 
 static int launch_step(att1_infer_t *inf)
 {
+    if (inf->use_persistent && inf->plan) return b2_decode_step(inf->plan, inf->stream);
     if (inf->use_graph && !inf->graph_failed) {
         if (inf->exec == NULL) {
             cudaGraph_t g = NULL;
@@ -822,6 +870,7 @@ static att1_status_t recover(att1_infer_t *inf, int32_t err)
     for (b = 0; b < inf->batch; b++) pos[b] = (int32_t)inf->position;
     cudaMemsetAsync(inf->err_d, 0, sizeof(int32_t), inf->stream);
     cudaMemsetAsync(inf->counters, 0, (size_t)inf->counters_len * sizeof(int32_t), inf->stream);
+    if (inf->plan) b2_decode_reset(inf->plan, inf->stream);
     cudaMemcpyAsync(inf->pos_d, pos, inf->batch * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream);
     cudaStreamSynchronize(inf->stream);
     if (err & B2_ERR_TIMEOUT) return ATT1_ERR_TIMEOUT;
@@ -1018,6 +1067,14 @@ att1_status_t att1_b200_infer_set_options(att1_infer_t *infer, int use_graph, in
     infer->use_graph = use_graph ? 1 : 0;
     set_pdl(infer, use_pdl ? 1 : 0);
     return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_set_persistent(att1_infer_t *infer, int on)
+{
+    if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    cudaStreamSynchronize(infer->stream);
+    infer->use_persistent = on ? 1 : 0;
+    return (on && infer->plan == NULL) ? ATT1_ERR_UNSUPPORTED : ATT1_OK;
 }
 
 att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps)

@@ -237,6 +237,9 @@ def run_b200(args, rank, world, local_rank):
     inf = b2.Infer.synth(cfg, args.seed, batch=args.batch)
     if args.no_graph:
         inf.set_options(graph=False, pdl=False)
+    persistent = args.persistent
+    if persistent:
+        inf.set_options(persistent=True)
     rng = np.random.default_rng(args.seed + rank)
     prompt = rng.integers(0, SHAPE["vocab"], size=(args.prompt, args.batch), dtype=np.int64)
     for t in prompt:
@@ -291,8 +294,20 @@ def run_b200(args, rank, world, local_rank):
     inf.close()
     peak, peak_kind = measured_peak()
     achieved = algo / (kms * 1e-3) / 1e9
-    traffic = load_traffic().get("gemv_q4_gateup_28672x4096")
+    traffics = load_traffic()
     bytes_step = step_bytes(pos_timed - args.steps // 2, args.batch)
+    gemv_line = {"kernel": "gemv_q4 gate/up 28672x4096 (RMSNorm+SwiGLU fused), standalone launches",
+                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                 "traffic": traffics.get("gemv_q4_gateup_28672x4096"), "algorithmic_bytes": algo, "launch_ms": kms}
+    if persistent:
+        # the step is one launch of the decode kernel: its algorithmic bytes are the step's
+        step_achieved = bytes_step / (ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "decode_kernel (whole step, one launch)", "achieved": step_achieved,
+                    "peak": peak, "unit": "GB/s", "frac": step_achieved / peak, "peak_kind": peak_kind,
+                    "traffic": traffics.get("decode_kernel_8b_step"), "algorithmic_bytes": bytes_step,
+                    "launch_ms": ms, "gemv": gemv_line}
+    else:
+        roofline = dict(gemv_line, bound="hbm", peak_kind=peak_kind)
     out = None
     if rank == 0:
         cpu = None
@@ -308,16 +323,14 @@ def run_b200(args, rank, world, local_rank):
             "config": {"workload": "llama3-8b-shape q4 decode", "global_batch": args.batch * (world if args.replicas else 1),
                        "seq_len": ctx, "context_at_timed_steps": pos_timed,
                        "parallelism": (f"replicas{world}" if args.replicas else f"tp{world}"),
+                       "step_launch": "one persistent kernel" if persistent else "kernel sequence (CUDA graph)",
                        "l2": "inputs larger than L2 (5.8 GB streamed per step)",
                        "step_bytes": bytes_step,
                        "step_hbm_frac": bytes_step / (ms * 1e-3) / (peak * 1e9)},
             "e2e": {"value": args.batch * 1000.0 / e2e_ms * (world if args.replicas else 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch + 4},
-            "gpu_launches": args.steps * (3 + 5 * args.layers),
-            "roofline": {"bound": "hbm", "kernel": "gemv_q4 gate/up 28672x4096 (RMSNorm+SwiGLU fused)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": traffic, "algorithmic_bytes": algo,
-                         "launch_ms": kms},
+            "gpu_launches": args.steps * (1 if persistent else 3 + 5 * args.layers),
+            "roofline": roofline,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
@@ -355,6 +368,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch kernels one by one without graph or PDL (for ncu launch lists)")
+    ap.add_argument("--persistent", action="store_true",
+                    help="run each step as one persistent launch instead of the per-operation kernel sequence")
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the dominant GEMV (gate/up shape) and print it (for ncu captures)")
     ap.add_argument("--layers", type=int, default=SHAPE["n_layers"],

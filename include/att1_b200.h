@@ -62,6 +62,10 @@ const float *att1_b200_infer_logits_batch(const att1_infer_t *infer, size_t *out
 /* use_graph: replay one captured CUDA graph per step (default 1);
  * use_pdl: programmatic dependent launch between kernels (default 1). */
 att1_status_t att1_b200_infer_set_options(att1_infer_t *infer, int use_graph, int use_pdl);
+/* Run each step as one persistent launch (on) or as the per-operation kernel
+ * sequence (off, the default). ATT1_ERR_UNSUPPORTED when the model's shape
+ * does not fit the persistent kernel (the sequence is used). */
+att1_status_t att1_b200_infer_set_persistent(att1_infer_t *infer, int on);
 
 /* Enqueue `steps` decode steps on the device, each feeding its greedy token
  * into the next, without host synchronisation (benchmark loop). The host

@@ -209,6 +209,44 @@ int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_model, const ui
 int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens,
                 int32_t *positions, int32_t *err, int pdl, void *stream);
 
+/* ---- the whole decode step as one persistent launch ------------------------ */
+/*
+ * One cooperative launch (one CTA per SM) runs the step of b2_step_begin, the
+ * per-layer b2_gemv / b2_attn sequence, the lm_head and b2_step_end, with a
+ * grid barrier between dependent operations; the weight stream of every
+ * GEMV is read ahead across those barriers. Numerically it is the same
+ * kernels' arithmetic. The plan owns its scratch, counters and the barrier
+ * words; the arguments' scratch, counters, grid and pdl fields are ignored.
+ */
+typedef struct b2_decode_layer {
+    b2_gemv_args qkv, wo, gu, down;  /* as for b2_gemv */
+    b2_attn_args attn;               /* as for b2_attn */
+} b2_decode_layer;
+
+typedef struct b2_decode_args {
+    uint32_t n_layers, batch;
+    const b2_decode_layer *layers;   /* host array [n_layers], read at plan creation */
+    b2_gemv_args out;                /* lm_head, B2_EPI_LOGITS */
+    const float *embed;              /* device [vocab][d_model] */
+    uint32_t vocab, d_model;
+    const uint32_t *tokens_in;       /* device [batch]: this step's tokens */
+    uint32_t *tokens_out;            /* device [batch]: greedy next tokens (may equal tokens_in) */
+    int32_t *positions;              /* device [batch]: advanced by one per step */
+    unsigned long long *argmax;      /* device [batch]: argmax keys (scratch) */
+    float *x;                        /* device [batch][d_model]: the residual stream */
+    int32_t *err;                    /* device error word */
+} b2_decode_args;
+
+typedef struct b2_decode_plan b2_decode_plan;
+/* Checks every operation as its own entry point does, plans one shared-memory
+ * carve-up for the step and uploads the operation list (allocates device memory). */
+int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **out);
+/* One decode step: one launch on `stream`. */
+int b2_decode_step(b2_decode_plan *p, void *stream);
+/* Zeroes the barrier words and counters (after a step that reported an error). */
+int b2_decode_reset(b2_decode_plan *p, void *stream);
+void b2_decode_plan_destroy(b2_decode_plan *p);
+
 /* ---- element ops (backend vtable on device buffers) ---------------------- */
 int b2_rmsnorm(float *dst, const float *src, const float *w, uint32_t n, float eps, void *stream);
 int b2_softmax(float *v, uint32_t n, void *stream);

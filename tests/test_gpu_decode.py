@@ -87,17 +87,40 @@ def test_long_context_crosses_pages(b2, orc):
 
 
 def test_graph_and_direct_launch_agree(b2, orc):
+    """The per-operation kernel sequence gives the same bits with or without
+    graph replay and programmatic dependent launch."""
     cfg = b2.Config.make(2000, 2, 4, 2, 128, 256, 32, dtype=4)
     outs = []
     for graph, pdl in ((True, True), (False, False), (False, True)):
         inf = b2.Infer.synth(cfg, 5)
-        inf.set_options(graph=graph, pdl=pdl)
+        inf.set_options(graph=graph, pdl=pdl, persistent=False)
         toks = [inf.decode(t) for t in (1, 2, 3, 4)]
         outs.append((toks, inf.logits()))
         inf.close()
     for toks, lg in outs[1:]:
         assert toks == outs[0][0]
         assert (lg == outs[0][1]).all()
+
+
+@pytest.mark.parametrize("dtype,batch", [(4, 1), (4, 3), (8, 2)])
+def test_persistent_step_matches_kernel_sequence(b2, orc, dtype, batch):
+    """The single-launch step runs the same arithmetic as the kernel sequence;
+    only the attention's split over positions differs (f32 reassociation)."""
+    cfg = b2.Config.make(3000, 3, 8, 2, 256, 512, 80, dtype=dtype)
+    rng = np.random.default_rng(11)
+    toks = rng.integers(0, 3000, size=(40, batch))
+    runs = []
+    for persistent in (True, False):
+        inf = b2.Infer.synth(cfg, 21, batch=batch)
+        inf.set_options(persistent=persistent)
+        lg = []
+        for t in toks:
+            inf.decode_batch(t)
+            lg.append(inf.logits())
+        runs.append(np.stack(lg))
+        inf.close()
+    a, b = runs
+    assert rel_err(a, b) <= 1e-5
 
 
 def test_kv_pages_hold_roped_keys(b2, orc):
