@@ -59,6 +59,14 @@ class KVLayout(C.Structure):
                 ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32)]
 
 
+class TpArgs(C.Structure):
+    """b2_tp (include/b2_kernels.h): tensor-parallel exchange of one kernel."""
+    _fields_ = [("rank", C.c_uint32), ("world", C.c_uint32), ("peer", C.c_void_p * 8), ("points", C.c_uint32),
+                ("slot_floats", C.c_uint32), ("logit_floats", C.c_uint32), ("epoch", C.c_void_p),
+                ("done", C.c_void_p), ("out_point", C.c_uint32), ("in_point", C.c_uint32),
+                ("in_resid", C.c_void_p), ("in_out", C.c_void_p), ("row_offset", C.c_uint32)]
+
+
 class GemvArgs(C.Structure):
     _fields_ = [("w", QWeight), ("batch", C.c_uint32), ("x", C.c_void_p), ("x_stride", C.c_uint32),
                 ("norm_w", C.c_void_p), ("eps", C.c_float), ("epilogue", C.c_int),
@@ -66,7 +74,8 @@ class GemvArgs(C.Structure):
                 ("q_rows", C.c_uint32), ("kv_rows", C.c_uint32), ("rope_freq", C.c_void_p),
                 ("positions", C.c_void_p), ("kv", KVLayout), ("argmax", C.c_void_p),
                 ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("counters", C.c_void_p),
-                ("counters_len", C.c_uint32), ("err", C.c_void_p), ("pdl", C.c_int), ("grid", C.c_int)]
+                ("counters_len", C.c_uint32), ("err", C.c_void_p), ("pdl", C.c_int), ("grid", C.c_int),
+                ("tp", TpArgs)]
 
 
 class AttnArgs(C.Structure):
@@ -129,6 +138,14 @@ _SIGS = {
     "att1_infer_set_backend": (C.c_int, [_P, _P]),
     # additions (att1_b200.h)
     "att1_b200_infer_create_synth": (C.c_int, [C.POINTER(Config), C.c_uint64, _U32, C.POINTER(_P)]),
+    "att1_b200_infer_create_synth_tp": (C.c_int, [C.POINTER(Config), C.c_uint64, _U32, _U32, _U32, C.POINTER(_P)]),
+    "att1_b200_infer_tp_handle": (C.c_int, [_P, _P]),
+    "att1_b200_infer_tp_connect": (C.c_int, [_P, _P]),
+    "att1_b200_infer_tp_connect_local": (C.c_int, [C.POINTER(_P), _U32]),
+    "att1_b200_infer_tp_disconnect": (C.c_int, [_P]),
+    "att1_b200_infer_step_async": (C.c_int, [_P, C.POINTER(_U32)]),
+    "att1_b200_infer_step_wait": (C.c_int, [_P, C.POINTER(_U32)]),
+    "att1_b200_set_device": (C.c_int, [C.c_int]),
     "att1_b200_infer_create_model": (C.c_int, [C.POINTER(Model), _U32, _F, _F, _F, C.POINTER(_P)]),
     "att1_b200_infer_batch": (_U32, [_P]),
     "att1_b200_infer_decode_batch": (C.c_int, [_P, C.POINTER(_U32), C.POINTER(_U32)]),
@@ -204,6 +221,9 @@ def lib() -> C.CDLL:
     return _lib
 
 
+TP_HANDLE_BYTES = 64
+
+
 def check(fn: str, rc: int) -> None:
     if rc != ATT1_OK:
         raise Att1Error(fn, rc)
@@ -232,6 +252,43 @@ class Infer:
         check("att1_b200_infer_create_synth",
               lib().att1_b200_infer_create_synth(C.byref(cfg), seed, batch, C.byref(h)))
         return cls(h.value, cfg.vocab, batch)
+
+    # ---- tensor parallelism (one context per GPU and rank) ----
+    @classmethod
+    def synth_tp(cls, cfg: Config, seed: int, rank: int, world: int, batch: int = 1, device: int = None) -> "Infer":
+        """This rank's shard of the synthetic model, on `device` (default: rank)."""
+        check("att1_b200_set_device", lib().att1_b200_set_device(rank if device is None else device))
+        h = C.c_void_p()
+        check("att1_b200_infer_create_synth_tp",
+              lib().att1_b200_infer_create_synth_tp(C.byref(cfg), seed, batch, rank, world, C.byref(h)))
+        return cls(h.value, cfg.vocab, batch)
+
+    def tp_handle(self) -> bytes:
+        buf = C.create_string_buffer(TP_HANDLE_BYTES)
+        check("att1_b200_infer_tp_handle", lib().att1_b200_infer_tp_handle(self.h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """handles: every rank's tp_handle() in rank order."""
+        blob = b"".join(handles)
+        check("att1_b200_infer_tp_connect", lib().att1_b200_infer_tp_connect(self.h, C.c_char_p(blob)))
+
+    def tp_disconnect(self) -> None:
+        check("att1_b200_infer_tp_disconnect", lib().att1_b200_infer_tp_disconnect(self.h))
+
+    @staticmethod
+    def tp_connect_local(ranks) -> None:
+        arr = (_P * len(ranks))(*[r.h.value for r in ranks])
+        check("att1_b200_infer_tp_connect_local", lib().att1_b200_infer_tp_connect_local(arr, len(ranks)))
+
+    def step_async(self, tokens) -> None:
+        t = (C.c_uint32 * self.batch)(*[int(x) for x in tokens])
+        check("att1_b200_infer_step_async", lib().att1_b200_infer_step_async(self.h, t))
+
+    def step_wait(self) -> np.ndarray:
+        o = (C.c_uint32 * self.batch)()
+        check("att1_b200_infer_step_wait", lib().att1_b200_infer_step_wait(self.h, o))
+        return np.array(o[:], np.uint32)
 
     def close(self):
         if self.h and self.h.value:

@@ -160,6 +160,69 @@ __device__ __forceinline__ float block_max(float v, float *red)
 // ---- loads that bypass L1 (data written by other SMs in the same kernel) -------
 __device__ __forceinline__ float ld_cg(const float *p) { return __ldcg(p); }
 
+// ---- tensor-parallel exchange region (layout in b2_kernels.h) ---------------------
+__device__ __forceinline__ uint64_t *tp_flag(uint8_t *region, uint32_t point, uint32_t src)
+{
+    return reinterpret_cast<uint64_t *>(region) + (size_t)point * B2_TP_MAX + src;
+}
+
+__device__ __forceinline__ uint64_t *tp_key(uint8_t *region, const b2_tp &tp, uint32_t src, uint32_t item)
+{
+    return reinterpret_cast<uint64_t *>(region) + (size_t)(tp.points + 1) * B2_TP_MAX + src * 16 + item;
+}
+
+__device__ __forceinline__ float *tp_slot(uint8_t *region, const b2_tp &tp, uint32_t point, uint32_t src)
+{
+    float *slots = reinterpret_cast<float *>(reinterpret_cast<uint64_t *>(region) + (size_t)(tp.points + 1) * B2_TP_MAX +
+                                             B2_TP_MAX * 16);
+    if (point < tp.points) return slots + ((size_t)point * B2_TP_MAX + src) * tp.slot_floats;
+    return slots + (size_t)tp.points * B2_TP_MAX * tp.slot_floats + (size_t)src * tp.logit_floats;
+}
+
+__device__ __forceinline__ void st_release_sys(uint64_t *p, uint64_t v)
+{
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t *p)
+{
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t tp_want(const b2_tp &tp)
+{
+    return (uint64_t)__ldcg(tp.epoch) + 1;
+}
+
+// Bounded wait (one thread) until every rank has set its flag of `point` in
+// this rank's region for this step; false (and B2_ERR_TIMEOUT) on timeout.
+__device__ __forceinline__ bool tp_wait(const b2_tp &tp, uint32_t point, int32_t *err)
+{
+    const uint64_t want = tp_want(tp);
+    uint8_t *own = tp.peer[tp.rank];
+    for (uint32_t s = 0; s < tp.world; ++s) {
+        uint32_t spins = 0;
+        while (ld_acquire_sys(tp_flag(own, point, s)) < want) {
+            if (++spins > (1u << 24)) {
+                raise_error(err, B2_ERR_TIMEOUT);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+// One thread: publish this rank's contribution to `point` (its stores to the
+// slots are ordered before by the caller's fence) to every rank.
+__device__ __forceinline__ void tp_signal(const b2_tp &tp, uint32_t point)
+{
+    const uint64_t v = tp_want(tp);
+    for (uint32_t s = 0; s < tp.world; ++s) st_release_sys(tp_flag(tp.peer[s], point, tp.rank), v);
+}
+
 // ---- seeded synthetic generator (bit-identical to or_synth_normal) -------------
 __host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x)
 {

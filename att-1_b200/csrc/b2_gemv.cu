@@ -167,14 +167,32 @@ static cudaError_t launch_t(const GemvParams &p, const GemvPlan &pl, int pdl, cu
     return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
+static int tp_check(const b2_tp &tp)
+{
+    if (tp.world < 2 || tp.world > B2_TP_MAX || tp.rank >= tp.world || tp.epoch == nullptr) return -1;
+    for (uint32_t s = 0; s < tp.world; ++s)
+        if (tp.peer[s] == nullptr || ((uintptr_t)tp.peer[s] & 15)) return -1;
+    if (tp.slot_floats % 4 || tp.logit_floats % 4) return -1;
+    return 0;
+}
+
 int gemv_check(const b2_gemv_args *a)
 {
-    if (a == nullptr || a->w.data == nullptr || a->x == nullptr || a->out == nullptr) return -1;
+    if (a == nullptr || a->w.data == nullptr) return -1;
+    const bool tp = a->tp.world > 1;
+    const bool tp_input = tp && a->tp.in_point != B2_TP_NONE;
+    if (tp && tp_check(a->tp) != 0) return -1;
+    if (tp_input && (a->tp.in_point >= a->tp.points || a->tp.in_resid == nullptr ||
+                     (size_t)a->w.cols * a->batch > a->tp.slot_floats || ((uintptr_t)a->tp.in_resid & 15) ||
+                     ((uintptr_t)a->tp.in_out & 15)))
+        return -1;
+    if (!tp_input && a->x == nullptr) return -1;
+    if (a->epilogue != B2_EPI_PUSH && a->out == nullptr) return -1;
     const b2_qweight &w = a->w;
     if ((w.format != 4 && w.format != 8) || (w.format == 8 && w.row_scale == nullptr)) return -1;
     if (a->batch == 0 || a->batch > kMaxItems || w.cols == 0 || w.cols % 32 || w.rows == 0) return -1;
     if (w.tiles != (w.rows + 15) / 16 || w.kunits != (w.format == 4 ? (w.cols + 63) / 64 : (w.cols + 31) / 32)) return -1;
-    if (a->x_stride < w.cols || (a->x_stride & 3) || ((uintptr_t)a->x & 15)) return -1;
+    if (!tp_input && (a->x_stride < w.cols || (a->x_stride & 3) || ((uintptr_t)a->x & 15))) return -1;
     if (a->norm_w != nullptr && (((uintptr_t)a->norm_w & 15) || !(a->eps > 0.0f))) return -1;
     if (((uintptr_t)w.data & 15)) return -1;
     switch (a->epilogue) {
@@ -182,6 +200,15 @@ int gemv_check(const b2_gemv_args *a)
     case B2_EPI_LOGITS:
         if (a->out_stride < w.rows) return -1;
         if (a->epilogue == B2_EPI_LOGITS && a->argmax == nullptr) return -1;
+        if (a->epilogue == B2_EPI_LOGITS && tp &&
+            (a->tp.out_point != a->tp.points || a->tp.done == nullptr ||
+             (size_t)w.rows * a->batch > a->tp.logit_floats))
+            return -1;
+        break;
+    case B2_EPI_PUSH:
+        if (!tp || a->tp.done == nullptr || a->tp.out_point >= a->tp.points ||
+            (size_t)w.rows * a->batch > a->tp.slot_floats)
+            return -1;
         break;
     case B2_EPI_RESID:
         if (a->out_stride < w.rows || a->resid == nullptr) return -1;
@@ -232,6 +259,7 @@ void gemv_params(const b2_gemv_args *a, const GemvPlan &pl, GemvParams &p)
     p.partial = (float *)a->scratch;
     p.counters = (int *)a->counters;
     p.maxseg = pl.maxseg;
+    p.tp = a->tp;
     p.grid = (uint32_t)pl.grid;
     p.err = a->err;
     p.off_ring = pl.off_ring;
@@ -286,6 +314,12 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
         else e = launch_t<8, 8>(p, pl, a->pdl, st);
     }
     return e == cudaSuccess ? 0 : -8;
+}
+
+extern "C" size_t b2_tp_region_bytes(uint32_t points, uint32_t slot_floats, uint32_t logit_floats)
+{
+    return ((size_t)(points + 1) * B2_TP_MAX + B2_TP_MAX * 16) * sizeof(uint64_t) +
+           ((size_t)points * B2_TP_MAX * slot_floats + (size_t)B2_TP_MAX * logit_floats) * sizeof(float);
 }
 
 // ---- GEMV without any allocation ------------------------------------------------

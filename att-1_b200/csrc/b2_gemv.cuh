@@ -47,9 +47,30 @@ struct GemvParams {
     uint32_t maxseg;
     uint32_t grid;  // CTAs taking part (the first `grid` CTAs of the launch)
     int32_t *err;
+    b2_tp tp;       // tensor-parallel exchange (world <= 1: none)
     // shared-memory carve-up (bytes)
     uint32_t off_ring, off_xdig, off_tile, off_misc, stages;
 };
+
+__device__ __forceinline__ bool tp_in(const GemvParams &p) { return p.tp.world > 1 && p.tp.in_point != B2_TP_NONE; }
+
+// Input element group k..k+3 of item b: x, or under tensor parallelism the
+// residual plus every rank's slot of the input point, added in rank order.
+__device__ __forceinline__ float4 load_x4(const GemvParams &p, uint32_t b, uint32_t k)
+{
+    if (!tp_in(p)) return __ldcg(reinterpret_cast<const float4 *>(p.x + (size_t)b * p.x_stride + k));
+    uint8_t *own = p.tp.peer[p.tp.rank];
+    const size_t o = (size_t)b * p.cols + k;
+    float4 v = __ldcg(reinterpret_cast<const float4 *>(tp_slot(own, p.tp, p.tp.in_point, 0) + o));
+    for (uint32_t s = 1; s < p.tp.world; ++s) {
+        const float4 w = __ldcg(reinterpret_cast<const float4 *>(tp_slot(own, p.tp, p.tp.in_point, s) + o));
+        v = make_float4(__fadd_rn(v.x, w.x), __fadd_rn(v.y, w.y), __fadd_rn(v.z, w.z), __fadd_rn(v.w, w.w));
+    }
+    const float4 r = __ldcg(reinterpret_cast<const float4 *>(p.tp.in_resid + o));
+    v = make_float4(__fadd_rn(r.x, v.x), __fadd_rn(r.y, v.y), __fadd_rn(r.z, v.z), __fadd_rn(r.w, v.w));
+    if (p.tp.in_out != nullptr && blockIdx.x == 0) *reinterpret_cast<float4 *>(p.tp.in_out + o) = v;
+    return v;
+}
 
 template <int FMT>
 struct Fmt;
@@ -175,13 +196,19 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
     const uint32_t stride = kConsumers * 4;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool norm = p.norm_w != nullptr;
+    if (tp_in(p)) {
+        // every rank's contribution to the input must have landed
+        int *ok = reinterpret_cast<int *>(red);
+        if (threadIdx.x == 0) *ok = tp_wait(p.tp, p.tp.in_point, p.err) ? 1 : 0;
+        consumer_sync();
+    }
     if (p.batch == 1 && cols <= stride * kPrologueVec) {
         float4 v[kPrologueVec], w[kPrologueVec];
 #pragma unroll
         for (int i = 0; i < kPrologueVec; ++i) {
             const uint32_t k = threadIdx.x * 4 + i * stride;
             const bool in = k < cols;
-            v[i] = in ? __ldcg(reinterpret_cast<const float4 *>(p.x + k)) : make_float4(0, 0, 0, 0);
+            v[i] = in ? load_x4(p, 0, k) : make_float4(0, 0, 0, 0);
             w[i] = (in && norm) ? __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)) : make_float4(1, 1, 1, 1);
         }
         float ss = 0.0f, mw = 0.0f;
@@ -216,10 +243,9 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
     // general path: statistics of every item in one reduction round, then the digits
     float *stats = red;  // [kMaxItems][kWarps][2]
     for (uint32_t b = 0; b < p.batch; ++b) {
-        const float *xb = p.x + (size_t)b * p.x_stride;
         float ss = 0.0f, mw = 0.0f;
         for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            const float4 v = load_x4(p, b, k);
             ss += sumsq4(v);
             mw = fmaxf(mw, absmax4(norm ? mul4(v, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k))) : v));
         }
@@ -241,9 +267,8 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
         float inv, sc;
         bool finite;
         item_setup<FMT>(p, b, tss, tmw, &inv, &sc, &finite, item_scale);
-        const float *xb = p.x + (size_t)b * p.x_stride;
         for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-            float4 v = __ldcg(reinterpret_cast<const float4 *>(xb + k));
+            float4 v = load_x4(p, b, k);
             if (norm) v = normed(v, inv, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)));
             store_digits<FMT>(p, xdig, b, k, v, sc, finite);
         }
@@ -319,14 +344,23 @@ static __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const f
                 }
             }
             break;
+        case B2_EPI_PUSH:
+            // tensor parallel partial: into this rank's slot on every rank
+            if (row < p.rows)
+                for (uint32_t s = 0; s < p.tp.world; ++s)
+                    tp_slot(p.tp.peer[s], p.tp, p.tp.out_point, p.tp.rank)[(size_t)item * p.rows + row] = v;
+            break;
         case B2_EPI_LOGITS: {
             unsigned long long key = 0ull;
             if (row < p.rows) {
                 p.out[(size_t)item * p.out_stride + row] = v;
+                if (p.tp.world > 1)  // all-gather of the vocabulary shards
+                    for (uint32_t s = 0; s < p.tp.world; ++s)
+                        tp_slot(p.tp.peer[s], p.tp, p.tp.out_point, p.tp.rank)[(size_t)item * p.rows + row] = v;
                 if (v != v) {
                     raise_error(p.err, B2_ERR_NAN_LOGITS);
                 } else {
-                    key = ((unsigned long long)ordered_key(v) << 32) | (0xFFFFFFFFu - row);
+                    key = ((unsigned long long)ordered_key(v) << 32) | (0xFFFFFFFFu - (p.tp.row_offset + row));
                 }
             }
             // max over the 16 lanes of this item (lanes 16*k .. 16*k+15)
@@ -620,10 +654,36 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
         }
         if (!dead) tile_epilogue(p, tile, mytbuf, s.cta_key, lane);
         __syncwarp();
+        if (p.epilogue == B2_EPI_PUSH && lane == 0) {
+            // the last tile of the GEMV on this rank publishes the point
+            __threadfence_system();
+            if (atomicAdd(p.tp.done, 1) == (int)(p.panels * kPanelTiles) - 1) {
+                *p.tp.done = 0;
+                __threadfence_system();
+                tp_signal(p.tp, p.tp.out_point);
+            }
+        }
     }
     if (p.epilogue == B2_EPI_LOGITS) {
         consumer_sync();
         if (threadIdx.x < B && s.cta_key[threadIdx.x] != 0ull) atomicMax(&p.argmax[threadIdx.x], s.cta_key[threadIdx.x]);
+        if (p.tp.world > 1) {
+            // the last CTA publishes this rank's logits and argmax keys
+            consumer_sync();
+            if (threadIdx.x == 0) {
+                __threadfence_system();
+                if (atomicAdd(p.tp.done, 1) == (int)p.grid - 1) {
+                    *p.tp.done = 0;
+                    __threadfence();
+                    for (uint32_t b = 0; b < B; ++b) {
+                        const uint64_t key = __ldcg(p.argmax + b);
+                        for (uint32_t q = 0; q < p.tp.world; ++q) *tp_key(p.tp.peer[q], p.tp, p.tp.rank, b) = key;
+                    }
+                    __threadfence_system();
+                    tp_signal(p.tp, p.tp.out_point);
+                }
+            }
+        }
     }
 }
 

@@ -64,6 +64,30 @@ __global__ void step_end_kernel(const unsigned long long *argmax, uint32_t batch
     positions[item] += 1;
 }
 
+// Tensor parallel: the greedy token is the largest key over every rank's
+// vocabulary shard (keys carry global ids); then positions and the epoch.
+__global__ void step_end_tp_kernel(const b2_tp tp, uint32_t batch, uint32_t *tokens, int32_t *positions, int32_t *err)
+{
+    __shared__ int ok;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) ok = tp_wait(tp, tp.points, err) ? 1 : 0;
+    __syncthreads();
+    const uint32_t item = threadIdx.x;
+    if (item < batch) {
+        unsigned long long key = 0ull;
+        for (uint32_t s = 0; s < tp.world; ++s) {
+            const unsigned long long k = __ldcg(tp_key(tp.peer[tp.rank], tp, s, item));
+            key = k > key ? k : key;
+        }
+        if (!ok || key == 0ull) raise_error(err, ok ? B2_ERR_NAN_LOGITS : B2_ERR_TIMEOUT);
+        else tokens[item] = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
+        positions[item] += 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *const_cast<uint32_t *>(tp.epoch) += 1;
+}
+
 __global__ void rmsnorm_kernel(float *dst, const float *src, const float *w, uint32_t n, float eps)
 {
     __shared__ float red[32];
@@ -185,6 +209,21 @@ extern "C" int b2_step_end(const unsigned long long *argmax, uint32_t batch, uin
     void *args[] = {(void *)&argmax, (void *)&batch, (void *)&tokens, (void *)&positions, (void *)&err};
     return launched(launch_pdl((const void *)step_end_kernel, dim3(1), dim3(((batch + 31) / 32) * 32), pdl,
                                (cudaStream_t)stream, args));
+}
+
+extern "C" int b2_step_end_tp(const b2_tp *tp, uint32_t batch, uint32_t *tokens, int32_t *positions, int32_t *err,
+                              int pdl, void *stream)
+{
+    if (tp == nullptr || tokens == nullptr || positions == nullptr || batch == 0 || batch > 16) return -1;
+    if (tp->world < 2 || tp->world > B2_TP_MAX || tp->rank >= tp->world || tp->epoch == nullptr ||
+        tp->peer[tp->rank] == nullptr)
+        return -1;
+    b2_tp t = *tp;
+    void *args[] = {&t, &batch, &tokens, &positions, &err};
+    return launch_pdl((const void *)step_end_tp_kernel, dim3(1), dim3(32), pdl, (cudaStream_t)stream, args) ==
+                   cudaSuccess
+               ? 0
+               : -8;
 }
 
 extern "C" int b2_rmsnorm(float *dst, const float *src, const float *w, uint32_t n, float eps, void *stream)

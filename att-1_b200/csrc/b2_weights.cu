@@ -131,7 +131,8 @@ __global__ void q4_unpack_kernel(uint8_t *packed, float *scales, const uint8_t *
 // ---- q4 synth: reference quantiser on generated groups. One thread per
 // (source, source row, 32-group).
 __global__ void q4_synth_kernel(uint8_t *dst, uint32_t dst_rows, uint32_t cols, uint64_t key0,
-                                uint64_t key1, float c, int map, uint32_t row0)
+                                uint64_t key1, float c, int map, uint32_t row0, uint32_t src_row0,
+                                uint32_t src_col0, uint32_t src_cols)
 {
     const uint32_t g32n = cols / 32;
     const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -144,7 +145,7 @@ __global__ void q4_synth_kernel(uint8_t *dst, uint32_t dst_rows, uint32_t cols, 
     const uint64_t key = which ? key1 : key0;
     float v[32];
     float max_abs = 0.0f;
-    const uint64_t e0 = (uint64_t)srow * cols + (uint64_t)g32 * 32;
+    const uint64_t e0 = (uint64_t)(src_row0 + srow) * src_cols + src_col0 + (uint64_t)g32 * 32;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
         v[i] = synth_normal(key, e0 + i, c);
@@ -207,7 +208,8 @@ __global__ void q8_unpack_kernel(int8_t *values, float *scales, const uint8_t *s
 
 // q8 synth: one warp per source row (max over the row, then quantise).
 __global__ void q8_synth_kernel(uint8_t *dst, float *row_scale, uint32_t dst_rows, uint32_t cols,
-                                uint64_t key0, uint64_t key1, float c, int map, uint32_t row0)
+                                uint64_t key0, uint64_t key1, float c, int map, uint32_t row0, uint32_t src_row0,
+                                uint32_t src_col0, uint32_t src_cols)
 {
     const uint32_t lane = threadIdx.x & 31;
     const uint64_t warp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -216,16 +218,17 @@ __global__ void q8_synth_kernel(uint8_t *dst, float *row_scale, uint32_t dst_row
     const uint32_t src_rows = dst_rows / srcs;
     const uint32_t which = (uint32_t)(warp / src_rows), srow = (uint32_t)(warp % src_rows);
     const uint64_t key = which ? key1 : key0;
-    const uint64_t e0 = (uint64_t)srow * cols;
+    // the scale comes from the whole source row, the values from its slice
+    const uint64_t e0 = (uint64_t)(src_row0 + srow) * src_cols;
     float m = 0.0f;
-    for (uint32_t k = lane; k < cols; k += 32) m = fmaxf(m, fabsf(synth_normal(key, e0 + k, c)));
+    for (uint32_t k = lane; k < src_cols; k += 32) m = fmaxf(m, fabsf(synth_normal(key, e0 + k, c)));
     m = warp_max(m);
     // src/quant.c:97-99
     const float scale = (m > 0.0f) ? __fdiv_rn(m, 127.0f) : 1.0f;
     const uint32_t row = dev_row(map, which, srow);
     const uint32_t kbn = ceil_div(cols, 32);
     for (uint32_t k = lane; k < cols; k += 32) {
-        long r = lroundf(__fdiv_rn(synth_normal(key, e0 + k, c), scale));
+        long r = lroundf(__fdiv_rn(synth_normal(key, e0 + src_col0 + k, c), scale));
         r = r > 127 ? 127 : (r < -127 ? -127 : r);
         dst[q8_byte_offset(row0 + row, k, kbn)] = (uint8_t)(int8_t)r;
     }
@@ -323,17 +326,26 @@ extern "C" int b2_q4_unpack(uint8_t *packed, float *scales, const void *src, uin
     return check_launch();
 }
 
-extern "C" int b2_q4_synth(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols, uint64_t seed,
-                           uint64_t tensor_id, uint64_t tensor_id2, float std, int map, void *stream)
+extern "C" int b2_q4_synth_part(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols, uint64_t seed,
+                                uint64_t tensor_id, uint64_t tensor_id2, float std, int map, uint32_t src_row0,
+                                uint32_t src_col0, uint32_t src_cols, void *stream)
 {
-    if (!dst || dst_rows == 0 || cols == 0 || cols % 32) return -1;
+    if (!dst || dst_rows == 0 || cols == 0 || cols % 32 || src_col0 % 32 || src_col0 + cols > src_cols) return -1;
     if (map == B2_ROWS_GATEUP && dst_rows % 16) return -1;
     uint8_t *base = (uint8_t *)dst;
     const float c = std * (1.0f / 131072.0f);
     const uint64_t n = (uint64_t)dst_rows * (cols / 32);
     q4_synth_kernel<<<grid_for(n, 128), 128, 0, (cudaStream_t)stream>>>(
-        base, dst_rows, cols, synth_key(seed, tensor_id), synth_key(seed, tensor_id2), c, map, tile_offset * 16);
+        base, dst_rows, cols, synth_key(seed, tensor_id), synth_key(seed, tensor_id2), c, map, tile_offset * 16,
+        src_row0, src_col0, src_cols);
     return check_launch();
+}
+
+extern "C" int b2_q4_synth(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols, uint64_t seed,
+                           uint64_t tensor_id, uint64_t tensor_id2, float std, int map, void *stream)
+{
+    return b2_q4_synth_part(dst, tile_offset, dst_rows, cols, seed, tensor_id, tensor_id2, std, map, 0, 0, cols,
+                            stream);
 }
 
 extern "C" int b2_q8_pack(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols,
@@ -362,18 +374,26 @@ extern "C" int b2_q8_unpack(int8_t *values, float *scales, const void *src, cons
     return check_launch();
 }
 
-extern "C" int b2_q8_synth(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols,
-                           uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2, float std, int map,
-                           void *stream)
+extern "C" int b2_q8_synth_part(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows,
+                                uint32_t cols, uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2, float std,
+                                int map, uint32_t src_row0, uint32_t src_col0, uint32_t src_cols, void *stream)
 {
-    if (!dst || !row_scale || dst_rows == 0 || cols == 0) return -1;
+    if (!dst || !row_scale || dst_rows == 0 || cols == 0 || src_col0 + cols > src_cols) return -1;
     if (map == B2_ROWS_GATEUP && dst_rows % 16) return -1;
     uint8_t *base = (uint8_t *)dst;
     const float c = std * (1.0f / 131072.0f);
     q8_synth_kernel<<<grid_for((uint64_t)dst_rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
         base, row_scale + (size_t)tile_offset * 16, dst_rows, cols, synth_key(seed, tensor_id),
-        synth_key(seed, tensor_id2), c, map, tile_offset * 16);
+        synth_key(seed, tensor_id2), c, map, tile_offset * 16, src_row0, src_col0, src_cols);
     return check_launch();
+}
+
+extern "C" int b2_q8_synth(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols,
+                           uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2, float std, int map,
+                           void *stream)
+{
+    return b2_q8_synth_part(dst, row_scale, tile_offset, dst_rows, cols, seed, tensor_id, tensor_id2, std, map, 0, 0,
+                            cols, stream);
 }
 
 extern "C" int b2_synth_f32(float *dst, size_t count, uint64_t seed, uint64_t tensor_id, float std, void *stream)

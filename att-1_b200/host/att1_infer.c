@@ -40,6 +40,17 @@ typedef struct dev_layer {
 struct att1_infer {
     att1_b200_config cfg;
     uint32_t head_dim, batch, q_rows, kv_rows;
+    /* tensor parallelism: this rank's shard (tp_world 1: the whole model) */
+    uint32_t tp_rank, tp_world;
+    uint32_t hq, hkv, ffl, vl, v_off;  /* query / KV heads, FFN rows, vocabulary rows and first id */
+    uint8_t *tp_region;                /* this rank's exchange region */
+    size_t tp_region_bytes;
+    uint8_t *tp_peer[B2_TP_MAX];       /* every rank's region as mapped here */
+    int tp_opened[B2_TP_MAX];          /* mapped through CUDA IPC (closed at release) */
+    uint32_t *tp_epoch;
+    int32_t *tp_done;
+    int tp_ready;
+    b2_tp tp_base;                     /* exchange description shared by the step's kernels */
     int device;
     cudaStream_t stream;
     dev_layer *layers;
@@ -65,6 +76,8 @@ struct att1_infer {
     int logits_valid;
     size_t position;
     int use_graph, use_pdl, use_persistent;
+    int step_pending;
+    uint64_t trace_t0;
     cudaGraphExec_t exec;
     int graph_failed;
     b2_decode_plan *plan;
@@ -127,6 +140,7 @@ static void release(att1_infer_t *inf)
 {
     uint32_t l;
     if (inf == NULL) return;
+    cudaSetDevice(inf->device);
     if (inf->stream) cudaStreamSynchronize(inf->stream);
     if (inf->exec) cudaGraphExecDestroy(inf->exec);
     if (inf->plan) b2_decode_plan_destroy(inf->plan);
@@ -166,6 +180,11 @@ static void release(att1_infer_t *inf)
     if (inf->err_h) cudaFreeHost(inf->err_h);
     if (inf->logits_h) cudaFreeHost(inf->logits_h);
     if (inf->backend) att1_backend_destroy(inf->backend);
+    for (l = 0; l < B2_TP_MAX; l++)
+        if (inf->tp_opened[l]) cudaIpcCloseMemHandle(inf->tp_peer[l]);
+    dfree(inf->tp_region);
+    dfree(inf->tp_epoch);
+    dfree(inf->tp_done);
     if (inf->stream) cudaStreamDestroy(inf->stream);
     free(inf);
 }
@@ -209,7 +228,7 @@ static b2_kv_layout kv_layout(att1_infer_t *inf, uint32_t layer)
     kv.page_table = inf->page_table;
     kv.page_tokens = inf->page_tokens;
     kv.pages_per_seq = inf->pages_per_seq;
-    kv.n_kv_heads = inf->cfg.n_kv_heads;
+    kv.n_kv_heads = inf->hkv;
     kv.head_dim = inf->head_dim;
     return kv;
 }
@@ -228,6 +247,7 @@ static att1_status_t build_plan(att1_infer_t *inf)
         b2_decode_plan_destroy(inf->plan);
         inf->plan = NULL;
     }
+    if (inf->tp_world > 1) return ATT1_OK; /* the persistent step has no exchange */
     ls = calloc(c->n_layers, sizeof(*ls));
     if (ls == NULL) return ATT1_ERR_OOM;
     for (l = 0; l < c->n_layers; l++) {
@@ -258,6 +278,61 @@ static att1_status_t build_plan(att1_infer_t *inf)
     return ATT1_OK;
 }
 
+/* Tensor parallelism (Megatron split, as proposed for ATT-1's shard
+ * metadata): QKV and gate/up hold this rank's heads / FFN rows, WO and down
+ * this rank's input columns; their partial outputs go to every rank's
+ * exchange slot (B2_EPI_PUSH) and the next GEMV's prologue adds the ranks'
+ * partials and the residual (x + WO, h1 + down) in rank order, so every rank
+ * carries the same residual stream. The lm_head holds this rank's vocabulary
+ * rows; logits and argmax keys are all-gathered and b2_step_end_tp takes the
+ * global greedy token. Exchange points: 2l = WO of layer l, 2l+1 = down of
+ * layer l, 2L = logits. */
+static void tp_wire(att1_infer_t *inf)
+{
+    const att1_b200_config *c = &inf->cfg;
+    b2_tp t;
+    uint32_t l, s;
+    memset(&t, 0, sizeof(t));
+    t.rank = inf->tp_rank;
+    t.world = inf->tp_world;
+    for (s = 0; s < inf->tp_world; s++) t.peer[s] = inf->tp_peer[s];
+    t.points = 2 * c->n_layers;
+    t.slot_floats = inf->batch * c->d_model;
+    t.logit_floats = inf->batch * inf->vl;
+    t.epoch = inf->tp_epoch;
+    t.done = inf->tp_done;
+    t.in_point = B2_TP_NONE;
+    t.out_point = B2_TP_NONE;
+    inf->tp_base = t;
+    for (l = 0; l < c->n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        L->a_wo.tp = t;
+        L->a_wo.epilogue = B2_EPI_PUSH;
+        L->a_wo.resid = NULL;
+        L->a_wo.tp.out_point = 2 * l;
+        L->a_gu.tp = t;
+        L->a_gu.tp.in_point = 2 * l;
+        L->a_gu.tp.in_resid = inf->x;
+        L->a_gu.tp.in_out = inf->h1;
+        L->a_down.tp = t;
+        L->a_down.epilogue = B2_EPI_PUSH;
+        L->a_down.resid = NULL;
+        L->a_down.tp.out_point = 2 * l + 1;
+        if (l > 0) {
+            L->a_qkv.tp = t;
+            L->a_qkv.tp.in_point = 2 * l - 1;
+            L->a_qkv.tp.in_resid = inf->h1;
+            L->a_qkv.tp.in_out = inf->x;
+        }
+    }
+    inf->a_out.tp = t;
+    inf->a_out.tp.out_point = t.points;
+    inf->a_out.tp.in_point = 2 * c->n_layers - 1;
+    inf->a_out.tp.in_resid = inf->h1;
+    inf->a_out.tp.row_offset = inf->v_off;
+    inf->tp_base.out_point = t.points;
+}
+
 static att1_status_t build_args(att1_infer_t *inf)
 {
     const att1_b200_config *c = &inf->cfg;
@@ -286,8 +361,8 @@ static att1_status_t build_args(att1_infer_t *inf)
 
         memset(&L->a_attn, 0, sizeof(L->a_attn));
         L->a_attn.batch = inf->batch;
-        L->a_attn.n_heads = c->n_heads;
-        L->a_attn.n_kv_heads = c->n_kv_heads;
+        L->a_attn.n_heads = inf->hq;
+        L->a_attn.n_kv_heads = inf->hkv;
         L->a_attn.head_dim = inf->head_dim;
         L->a_attn.q = inf->q;
         L->a_attn.kv = kv_layout(inf, l);
@@ -314,12 +389,12 @@ static att1_status_t build_args(att1_infer_t *inf)
         a->eps = c->eps;
         a->epilogue = B2_EPI_SWIGLU;
         a->out = inf->hs;
-        a->out_stride = c->d_ff;
+        a->out_stride = inf->ffl;
 
         a = &L->a_down;
         gemv_base(inf, a, &L->down);
         a->x = inf->hs;
-        a->x_stride = c->d_ff;
+        a->x_stride = inf->ffl;
         a->epilogue = B2_EPI_RESID;
         a->resid = inf->h1;
         a->out = inf->x;
@@ -334,9 +409,10 @@ static att1_status_t build_args(att1_infer_t *inf)
         a->eps = c->final_eps;
         a->epilogue = B2_EPI_LOGITS;
         a->out = inf->logits;
-        a->out_stride = c->vocab;
+        a->out_stride = inf->vl;
         a->argmax = inf->argmax_d;
     }
+    if (inf->tp_world > 1) tp_wire(inf);
     /* One partial-sum region and one counter array serve every kernel: they
      * run one after another and each leaves its counters at zero. */
     {
@@ -412,7 +488,7 @@ static att1_status_t alloc_common(att1_infer_t *inf)
     inf->page_tokens = c->max_seq < 64 ? c->max_seq : 64;
     inf->pages_per_seq = (c->max_seq + inf->page_tokens - 1) / inf->page_tokens;
     pages = (size_t)B * inf->pages_per_seq;
-    inf->layer_pool_elems = pages * inf->page_tokens * c->n_kv_heads * inf->head_dim;
+    inf->layer_pool_elems = pages * inf->page_tokens * inf->hkv * inf->head_dim;
     if ((st = dalloc(inf, (void **)&inf->k_pool, inf->layer_pool_elems * c->n_layers * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->v_pool, inf->layer_pool_elems * c->n_layers * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->page_table, pages * sizeof(int32_t))) ||
@@ -421,8 +497,8 @@ static att1_status_t alloc_common(att1_infer_t *inf)
         (st = dalloc(inf, (void **)&inf->h1, (size_t)B * c->d_model * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->q, (size_t)B * inf->q_rows * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->ctx, (size_t)B * inf->q_rows * sizeof(float))) ||
-        (st = dalloc(inf, (void **)&inf->hs, (size_t)B * c->d_ff * sizeof(float))) ||
-        (st = dalloc(inf, (void **)&inf->logits, (size_t)B * c->vocab * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->hs, (size_t)B * inf->ffl * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->logits, (size_t)B * inf->vl * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->tokens_d, 16 * sizeof(uint32_t))) ||
         (st = dalloc(inf, (void **)&inf->pos_d, 16 * sizeof(int32_t))) ||
         (st = dalloc(inf, (void **)&inf->argmax_d, 16 * sizeof(unsigned long long))) ||
@@ -450,22 +526,48 @@ static att1_status_t alloc_common(att1_infer_t *inf)
         cudaMallocHost((void **)&inf->err_h, sizeof(int32_t)) != cudaSuccess ||
         cudaMallocHost((void **)&inf->logits_h, (size_t)B * c->vocab * sizeof(float)) != cudaSuccess)
         return ATT1_ERR_OOM;
+    if (inf->tp_world > 1) {
+        inf->tp_region_bytes = b2_tp_region_bytes(2 * c->n_layers, B * c->d_model, B * inf->vl);
+        if ((st = dalloc(inf, (void **)&inf->tp_region, inf->tp_region_bytes)) ||
+            (st = dalloc(inf, (void **)&inf->tp_epoch, sizeof(uint32_t))) ||
+            (st = dalloc(inf, (void **)&inf->tp_done, sizeof(int32_t))))
+            return st;
+        inf->tp_peer[inf->tp_rank] = inf->tp_region;
+    }
     return ATT1_OK;
 }
 
-static att1_status_t new_context(const att1_b200_config *cfg, uint32_t batch, att1_infer_t **out)
+static att1_status_t new_context(const att1_b200_config *cfg, uint32_t batch, uint32_t rank, uint32_t world,
+                                 att1_infer_t **out)
 {
     att1_infer_t *inf;
+    uint32_t hd;
     att1_status_t st = check_config(cfg, batch);
     if (st != ATT1_OK) return st;
+    if (world == 0 || world > B2_TP_MAX || rank >= world) return ATT1_ERR_INVALID_ARG;
+    hd = cfg->d_model / cfg->n_heads;
+    if (world > 1) {
+        /* whole heads, whole 32-column groups and a whole 16-row gate/up tile per rank */
+        if (cfg->n_heads % world || cfg->n_kv_heads % world || cfg->d_ff % world || cfg->vocab % world)
+            return ATT1_ERR_SHAPE;
+        if ((cfg->n_heads / world) * hd % 32 || (cfg->d_ff / world) % 32) return ATT1_ERR_UNSUPPORTED;
+    }
     inf = calloc(1, sizeof(*inf));
     if (inf == NULL) return ATT1_ERR_OOM;
     inf->cfg = *cfg;
     if (inf->cfg.group == 0) inf->cfg.group = 32;
     inf->batch = batch;
-    inf->head_dim = cfg->d_model / cfg->n_heads;
-    inf->q_rows = cfg->n_heads * inf->head_dim;
-    inf->kv_rows = cfg->n_kv_heads * inf->head_dim;
+    inf->tp_rank = rank;
+    inf->tp_world = world;
+    inf->hq = cfg->n_heads / world;
+    inf->hkv = cfg->n_kv_heads / world;
+    inf->ffl = cfg->d_ff / world;
+    inf->vl = cfg->vocab / world;
+    inf->v_off = rank * inf->vl;
+    inf->tp_ready = world == 1;
+    inf->head_dim = hd;
+    inf->q_rows = inf->hq * hd;
+    inf->kv_rows = inf->hkv * hd;
     inf->use_graph = 1;
     inf->use_pdl = 1;
     inf->use_persistent = 0;
@@ -492,13 +594,13 @@ static att1_status_t alloc_weights(att1_infer_t *inf, uint32_t fmt)
         dev_layer *L = &inf->layers[l];
         if ((st = mat_alloc(inf, &L->qkv, fmt, inf->q_rows + 2 * inf->kv_rows, c->d_model)) ||
             (st = mat_alloc(inf, &L->wo, fmt, c->d_model, inf->q_rows)) ||
-            (st = mat_alloc(inf, &L->gu, fmt, 2 * c->d_ff, c->d_model)) ||
-            (st = mat_alloc(inf, &L->down, fmt, c->d_model, c->d_ff)) ||
+            (st = mat_alloc(inf, &L->gu, fmt, 2 * inf->ffl, c->d_model)) ||
+            (st = mat_alloc(inf, &L->down, fmt, c->d_model, inf->ffl)) ||
             (st = dalloc(inf, (void **)&L->attn_norm, c->d_model * sizeof(float))) ||
             (st = dalloc(inf, (void **)&L->ffn_norm, c->d_model * sizeof(float))))
             return st;
     }
-    if ((st = mat_alloc(inf, &inf->output, fmt, c->vocab, c->d_model)) ||
+    if ((st = mat_alloc(inf, &inf->output, fmt, inf->vl, c->d_model)) ||
         (st = dalloc(inf, (void **)&inf->embed, (size_t)c->vocab * c->d_model * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->out_norm, c->d_model * sizeof(float))))
         return st;
@@ -533,16 +635,21 @@ static att1_status_t finish_create(att1_infer_t *inf)
 #define T_EMBED 0x7F000000ull
 #define T_OUTPUT 0x7F000002ull
 
+/* rows [row0, row0 + rows) x columns [col0, col0 + cols) of a source tensor
+ * with src_cols columns */
 static int synth_mat(att1_infer_t *inf, b2_dev_mat *m, uint32_t tile_off, uint32_t rows, uint32_t cols,
-                     uint64_t seed, uint64_t tid, uint64_t tid2, int map)
+                     uint64_t seed, uint64_t tid, uint64_t tid2, int map, uint32_t row0, uint32_t col0,
+                     uint32_t src_cols)
 {
     if (m->w.format == 4)
-        return b2_q4_synth(m->data, tile_off, rows, cols, seed, tid, tid2, 0.02f, map, inf->stream);
-    return b2_q8_synth(m->data, m->row_scale, tile_off, rows, cols, seed, tid, tid2, 0.02f, map, inf->stream);
+        return b2_q4_synth_part(m->data, tile_off, rows, cols, seed, tid, tid2, 0.02f, map, row0, col0, src_cols,
+                                inf->stream);
+    return b2_q8_synth_part(m->data, m->row_scale, tile_off, rows, cols, seed, tid, tid2, 0.02f, map, row0, col0,
+                            src_cols, inf->stream);
 }
 
-att1_status_t att1_b200_infer_create_synth(const att1_b200_config *cfg, uint64_t seed, uint32_t batch,
-                                           att1_infer_t **out_infer)
+static att1_status_t create_synth(const att1_b200_config *cfg, uint64_t seed, uint32_t batch, uint32_t rank,
+                                  uint32_t world, att1_infer_t **out_infer)
 {
     att1_infer_t *inf = NULL;
     att1_status_t st;
@@ -551,37 +658,140 @@ att1_status_t att1_b200_infer_create_synth(const att1_b200_config *cfg, uint64_t
 
     if (out_infer == NULL) return ATT1_ERR_INVALID_ARG;
     *out_infer = NULL;
-    st = new_context(cfg, batch, &inf);
+    st = new_context(cfg, batch, rank, world, &inf);
     if (st != ATT1_OK) return st;
     if ((st = alloc_weights(inf, cfg->dtype)) || (st = alloc_common(inf))) goto fail;
     for (l = 0; l < cfg->n_layers && rc == 0; l++) {
         dev_layer *L = &inf->layers[l];
         const uint64_t b = (uint64_t)l * T_PER_LAYER;
-        rc |= synth_mat(inf, &L->qkv, 0, inf->q_rows, cfg->d_model, seed, b + ATT1_B200_WQ, 0, B2_ROWS_PLAIN);
-        rc |= synth_mat(inf, &L->qkv, inf->q_rows / 16, inf->kv_rows, cfg->d_model, seed, b + ATT1_B200_WK, 0,
-                        B2_ROWS_PLAIN);
-        rc |= synth_mat(inf, &L->qkv, (inf->q_rows + inf->kv_rows) / 16, inf->kv_rows, cfg->d_model, seed,
-                        b + ATT1_B200_WV, 0, B2_ROWS_PLAIN);
-        rc |= synth_mat(inf, &L->wo, 0, cfg->d_model, inf->q_rows, seed, b + ATT1_B200_WO, 0, B2_ROWS_PLAIN);
-        rc |= synth_mat(inf, &L->gu, 0, 2 * cfg->d_ff, cfg->d_model, seed, b + ATT1_B200_GATE, b + ATT1_B200_UP,
-                        B2_ROWS_GATEUP);
-        rc |= synth_mat(inf, &L->down, 0, cfg->d_model, cfg->d_ff, seed, b + ATT1_B200_DOWN, 0, B2_ROWS_PLAIN);
+        const uint32_t d = cfg->d_model, qr = inf->q_rows, kr = inf->kv_rows, fl = inf->ffl, r = rank;
+        rc |= synth_mat(inf, &L->qkv, 0, qr, d, seed, b + ATT1_B200_WQ, 0, B2_ROWS_PLAIN, r * qr, 0, d);
+        rc |= synth_mat(inf, &L->qkv, qr / 16, kr, d, seed, b + ATT1_B200_WK, 0, B2_ROWS_PLAIN, r * kr, 0, d);
+        rc |= synth_mat(inf, &L->qkv, (qr + kr) / 16, kr, d, seed, b + ATT1_B200_WV, 0, B2_ROWS_PLAIN, r * kr, 0, d);
+        rc |= synth_mat(inf, &L->wo, 0, d, qr, seed, b + ATT1_B200_WO, 0, B2_ROWS_PLAIN, 0, r * qr, world * qr);
+        rc |= synth_mat(inf, &L->gu, 0, 2 * fl, d, seed, b + ATT1_B200_GATE, b + ATT1_B200_UP, B2_ROWS_GATEUP, r * fl,
+                        0, d);
+        rc |= synth_mat(inf, &L->down, 0, d, fl, seed, b + ATT1_B200_DOWN, 0, B2_ROWS_PLAIN, 0, r * fl, world * fl);
         rc |= b2_fill_f32(L->attn_norm, cfg->d_model, 1.0f, inf->stream);
         rc |= b2_fill_f32(L->ffn_norm, cfg->d_model, 1.0f, inf->stream);
     }
-    rc |= synth_mat(inf, &inf->output, 0, cfg->vocab, cfg->d_model, seed, T_OUTPUT, 0, B2_ROWS_PLAIN);
+    rc |= synth_mat(inf, &inf->output, 0, inf->vl, cfg->d_model, seed, T_OUTPUT, 0, B2_ROWS_PLAIN, inf->v_off, 0,
+                    cfg->d_model);
     rc |= b2_synth_f32(inf->embed, (size_t)cfg->vocab * cfg->d_model, seed, T_EMBED, 0.02f, inf->stream);
     rc |= b2_fill_f32(inf->out_norm, cfg->d_model, 1.0f, inf->stream);
     if (rc != 0) {
         st = ATT1_ERR_STATE;
         goto fail;
     }
-    if ((st = finish_create(inf)) != ATT1_OK) goto fail;
+    /* a tensor-parallel rank is finished when it is connected to its peers */
+    if (world > 1) {
+        cudaError_t e = cudaStreamSynchronize(inf->stream);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if ((st = b2_cuda_status(e)) != ATT1_OK) goto fail;
+    } else if ((st = finish_create(inf)) != ATT1_OK) {
+        goto fail;
+    }
     *out_infer = inf;
     return ATT1_OK;
 fail:
     release(inf);
     return st;
+}
+
+att1_status_t att1_b200_infer_create_synth(const att1_b200_config *cfg, uint64_t seed, uint32_t batch,
+                                           att1_infer_t **out_infer)
+{
+    return create_synth(cfg, seed, batch, 0, 1, out_infer);
+}
+
+att1_status_t att1_b200_infer_create_synth_tp(const att1_b200_config *cfg, uint64_t seed, uint32_t batch,
+                                              uint32_t rank, uint32_t world, att1_infer_t **out_infer)
+{
+    if (world < 2) return ATT1_ERR_INVALID_ARG;
+    return create_synth(cfg, seed, batch, rank, world, out_infer);
+}
+
+att1_status_t att1_b200_infer_tp_handle(const att1_infer_t *infer, void *handle)
+{
+    cudaIpcMemHandle_t h;
+    if (infer == NULL || handle == NULL || infer->tp_world < 2) return ATT1_ERR_INVALID_ARG;
+    if (cudaIpcGetMemHandle(&h, infer->tp_region) != cudaSuccess) return ATT1_ERR_UNSUPPORTED;
+    memcpy(handle, &h, sizeof(h));
+    return ATT1_OK;
+}
+
+static att1_status_t tp_finish(att1_infer_t *inf)
+{
+    att1_status_t st;
+    cudaError_t e;
+    if ((st = build_args(inf)) != ATT1_OK) return st;
+    e = cudaStreamSynchronize(inf->stream);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if ((st = b2_cuda_status(e)) != ATT1_OK) return st;
+    inf->tp_ready = 1;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_tp_connect(att1_infer_t *infer, const void *handles)
+{
+    uint32_t s;
+    if (infer == NULL || handles == NULL || infer->tp_world < 2 || infer->tp_ready) return ATT1_ERR_INVALID_ARG;
+    for (s = 0; s < infer->tp_world; s++) {
+        cudaIpcMemHandle_t h;
+        void *p = NULL;
+        if (s == infer->tp_rank) continue;
+        memcpy(&h, (const uint8_t *)handles + (size_t)s * ATT1_B200_TP_HANDLE_BYTES, sizeof(h));
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            return ATT1_ERR_UNSUPPORTED;
+        }
+        infer->tp_peer[s] = p;
+        infer->tp_opened[s] = 1;
+    }
+    return tp_finish(infer);
+}
+
+att1_status_t att1_b200_infer_tp_disconnect(att1_infer_t *infer)
+{
+    uint32_t s;
+    if (infer == NULL || infer->tp_world < 2) return ATT1_ERR_INVALID_ARG;
+    cudaSetDevice(infer->device);
+    cudaStreamSynchronize(infer->stream);
+    for (s = 0; s < B2_TP_MAX; s++) {
+        if (infer->tp_opened[s]) cudaIpcCloseMemHandle(infer->tp_peer[s]);
+        infer->tp_opened[s] = 0;
+        if (s != infer->tp_rank) infer->tp_peer[s] = NULL;
+    }
+    infer->tp_ready = 0;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_tp_connect_local(att1_infer_t *const *infers, uint32_t world)
+{
+    uint32_t r, s;
+    att1_status_t st;
+    if (infers == NULL || world < 2 || world > B2_TP_MAX) return ATT1_ERR_INVALID_ARG;
+    for (r = 0; r < world; r++)
+        if (infers[r] == NULL || infers[r]->tp_world != world || infers[r]->tp_rank != r || infers[r]->tp_ready)
+            return ATT1_ERR_INVALID_ARG;
+    for (r = 0; r < world; r++) {
+        int dev = infers[r]->device;
+        if (cudaSetDevice(dev) != cudaSuccess) return ATT1_ERR_STATE;
+        for (s = 0; s < world; s++) {
+            int ok = 0;
+            if (infers[s]->device == dev) continue;
+            if (cudaDeviceCanAccessPeer(&ok, dev, infers[s]->device) != cudaSuccess || !ok) return ATT1_ERR_UNSUPPORTED;
+            if (cudaDeviceEnablePeerAccess(infers[s]->device, 0) != cudaSuccess) {
+                if (cudaGetLastError() != cudaErrorPeerAccessAlreadyEnabled) return ATT1_ERR_UNSUPPORTED;
+            }
+        }
+        for (s = 0; s < world; s++) infers[r]->tp_peer[s] = infers[s]->tp_region;
+    }
+    for (r = 0; r < world; r++) {
+        if (cudaSetDevice(infers[r]->device) != cudaSuccess) return ATT1_ERR_STATE;
+        if ((st = tp_finish(infers[r])) != ATT1_OK) return st;
+    }
+    return ATT1_OK;
 }
 
 /* ---- model from a .att1 file ------------------------------------------------------------------------ */
@@ -755,7 +965,7 @@ att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dty
     if (c.vocab == 0 || c.n_layers == 0 || c.n_heads == 0 || c.d_model == 0 || c.d_ff == 0 || c.max_seq == 0 ||
         c.d_model % c.n_heads || ((c.d_model / c.n_heads) % 2))
         return ATT1_ERR_INVALID_ARG;
-    st = new_context(&c, 1, &inf);
+    st = new_context(&c, 1, 0, 1, &inf);
     if (st != ATT1_OK) return st;
     inf->model = model;
     if ((st = alloc_weights(inf, dtype)) || (st = alloc_common(inf)) ||
@@ -829,12 +1039,16 @@ static int enqueue_kernels(att1_infer_t *inf)
         rc |= b2_gemv(&L->a_down, st);
     }
     if (rc == 0) rc = b2_gemv(&inf->a_out, st);
-    if (rc == 0) rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
-    return rc;
+    if (rc != 0) return rc;
+    if (inf->tp_world > 1)
+        return b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    return b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
 }
 
 static int launch_step(att1_infer_t *inf)
 {
+    /* contexts of several GPUs may be driven from one thread */
+    if (cudaSetDevice(inf->device) != cudaSuccess) return -8;
     if (inf->use_persistent && inf->plan) return b2_decode_step(inf->plan, inf->stream);
     if (inf->use_graph && !inf->graph_failed) {
         if (inf->exec == NULL) {
@@ -878,19 +1092,20 @@ static att1_status_t recover(att1_infer_t *inf, int32_t err)
     return ATT1_ERR_STATE;
 }
 
-static att1_status_t step(att1_infer_t *inf, const uint32_t *tokens, uint32_t *out_tokens)
+/* First half of a step: token upload, the step's kernels and the read-back
+ * copies, all queued on the context's stream. */
+static att1_status_t step_launch(att1_infer_t *inf, const uint32_t *tokens)
 {
     const att1_b200_config *c = &inf->cfg;
-    uint64_t t0 = 0;
     uint32_t b;
-    cudaError_t e;
 
+    if (!inf->tp_ready) return ATT1_ERR_STATE;
     if (inf->position >= c->max_seq) return ATT1_ERR_INVALID_ARG;
     for (b = 0; b < inf->batch; b++) {
         if (tokens[b] >= c->vocab) return ATT1_ERR_INVALID_ARG;
         inf->tokens_h[b] = tokens[b];
     }
-    if (inf->trace) t0 = att1_trace_now_us();
+    if (inf->trace) inf->trace_t0 = att1_trace_now_us();
     if (inf->position == 0) {
         int32_t zero[16] = {0};
         if (cudaMemcpyAsync(inf->pos_d, zero, inf->batch * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream) !=
@@ -903,6 +1118,19 @@ static att1_status_t step(att1_infer_t *inf, const uint32_t *tokens, uint32_t *o
     if (launch_step(inf) != 0) return ATT1_ERR_STATE;
     cudaMemcpyAsync(inf->out_h, inf->tokens_d, inf->batch * sizeof(uint32_t), cudaMemcpyDeviceToHost, inf->stream);
     cudaMemcpyAsync(inf->err_h, inf->err_d, sizeof(int32_t), cudaMemcpyDeviceToHost, inf->stream);
+    inf->step_pending = 1;
+    return ATT1_OK;
+}
+
+/* Second half: wait for the step and take its tokens. */
+static att1_status_t step_finish(att1_infer_t *inf, uint32_t *out_tokens)
+{
+    const att1_b200_config *c = &inf->cfg;
+    const uint64_t t0 = inf->trace_t0;
+    uint32_t b;
+    cudaError_t e;
+    if (!inf->step_pending) return ATT1_ERR_STATE;
+    inf->step_pending = 0;
     e = cudaStreamSynchronize(inf->stream);
     if (e != cudaSuccess) return b2_cuda_status(e);
     inf->logits_valid = 0;
@@ -918,6 +1146,13 @@ static att1_status_t step(att1_infer_t *inf, const uint32_t *tokens, uint32_t *o
     }
     inf->position++;
     return ATT1_OK;
+}
+
+static att1_status_t step(att1_infer_t *inf, const uint32_t *tokens, uint32_t *out_tokens)
+{
+    att1_status_t st = step_launch(inf, tokens);
+    if (st != ATT1_OK) return st;
+    return step_finish(inf, out_tokens);
 }
 
 static int backend_ok(const att1_infer_t *inf)
@@ -938,6 +1173,19 @@ att1_status_t att1_infer_decode_token(att1_infer_t *infer, uint32_t token_id, ui
     if (token_id >= infer->cfg.vocab || infer->position >= infer->cfg.max_seq) return ATT1_ERR_INVALID_ARG;
     if (!backend_ok(infer)) return ATT1_ERR_STATE;
     return step(infer, &token_id, out_token);
+}
+
+att1_status_t att1_b200_infer_step_async(att1_infer_t *infer, const uint32_t *tokens)
+{
+    if (infer == NULL || tokens == NULL || infer->step_pending) return ATT1_ERR_INVALID_ARG;
+    if (!backend_ok(infer)) return ATT1_ERR_STATE;
+    return step_launch(infer, tokens);
+}
+
+att1_status_t att1_b200_infer_step_wait(att1_infer_t *infer, uint32_t *out_tokens)
+{
+    if (infer == NULL || out_tokens == NULL) return ATT1_ERR_INVALID_ARG;
+    return step_finish(infer, out_tokens);
 }
 
 att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *tokens, uint32_t *out_tokens)
@@ -984,8 +1232,24 @@ static const float *logits_host(const att1_infer_t *cinfer, size_t *out_count, s
         return NULL;
     }
     if (!infer->logits_valid) {
-        if (cudaMemcpy(infer->logits_h, infer->logits, (size_t)infer->batch * infer->cfg.vocab * sizeof(float),
-                       cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaError_t e = cudaSetDevice(infer->device);
+        if (infer->tp_world > 1) {
+            /* every rank's vocabulary rows, all-gathered into this rank's region */
+            const size_t V = infer->cfg.vocab, vl = infer->vl;
+            uint32_t s;
+            for (s = 0; s < infer->tp_world && e == cudaSuccess; s++) {
+                const float *src = (const float *)(infer->tp_region + b2_tp_region_bytes(2 * infer->cfg.n_layers,
+                                                                                          infer->batch * infer->cfg.d_model,
+                                                                                          0)) +
+                                   (size_t)s * infer->batch * vl;
+                e = cudaMemcpy2D(infer->logits_h + (size_t)s * vl, V * sizeof(float), src, vl * sizeof(float),
+                                 vl * sizeof(float), infer->batch, cudaMemcpyDeviceToHost);
+            }
+        } else {
+            e = cudaMemcpy(infer->logits_h, infer->logits, (size_t)infer->batch * infer->cfg.vocab * sizeof(float),
+                           cudaMemcpyDeviceToHost);
+        }
+        if (e != cudaSuccess) {
             if (out_count) *out_count = 0;
             return NULL;
         }
@@ -1077,10 +1341,17 @@ att1_status_t att1_b200_infer_set_persistent(att1_infer_t *infer, int on)
     return (on && infer->plan == NULL) ? ATT1_ERR_UNSUPPORTED : ATT1_OK;
 }
 
+att1_status_t att1_b200_set_device(int device)
+{
+    return cudaSetDevice(device) == cudaSuccess ? ATT1_OK : ATT1_ERR_INVALID_ARG;
+}
+
 att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps)
 {
     uint32_t i;
     if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    if (!infer->tp_ready) return ATT1_ERR_STATE;
+    if (cudaSetDevice(infer->device) != cudaSuccess) return ATT1_ERR_STATE;
     if (infer->position + steps > infer->cfg.max_seq) return ATT1_ERR_INVALID_ARG;
     if (infer->position == 0) {
         int32_t zero[16] = {0};

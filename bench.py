@@ -234,7 +234,16 @@ def run_b200(args, rank, world, local_rank):
     e2e_steps = max(args.steps, 8)
     cfg = b2.Config.make(SHAPE["vocab"], args.layers, SHAPE["n_heads"], SHAPE["n_kv_heads"],
                          SHAPE["d_model"], SHAPE["d_ff"], ctx, dtype=4, eps=SHAPE["eps"], theta=SHAPE["theta"])
-    inf = b2.Infer.synth(cfg, args.seed, batch=args.batch)
+    if world > 1 and not args.replicas:
+        # tensor parallel: this rank's shard; ranks exchange their exchange-region
+        # handles (CUDA IPC) over the process group, then connect
+        inf = b2.Infer.synth_tp(cfg, args.seed, rank, world, batch=args.batch, device=local_rank)
+        handles = [None] * world
+        dist.all_gather_object(handles, inf.tp_handle())
+        inf.tp_connect(handles)
+    else:
+        b2.lib().att1_b200_set_device(local_rank)
+        inf = b2.Infer.synth(cfg, args.seed, batch=args.batch)
     if args.no_graph:
         inf.set_options(graph=False, pdl=False)
     persistent = args.persistent
@@ -290,8 +299,11 @@ def run_b200(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
 
-    algo, kms = time_dominant_gemv(b2, torch, reps=4 if args.no_graph else 30)
+    if dist and not args.replicas:
+        inf.tp_disconnect()  # unmap the peers' regions before any rank frees its own
+        dist.barrier()
     inf.close()
+    algo, kms = time_dominant_gemv(b2, torch, reps=4 if args.no_graph else 30)
     peak, peak_kind = measured_peak()
     achieved = algo / (kms * 1e-3) / 1e9
     traffics = load_traffic()
@@ -326,7 +338,7 @@ def run_b200(args, rank, world, local_rank):
                        "step_launch": "one persistent kernel" if persistent else "kernel sequence (CUDA graph)",
                        "l2": "inputs larger than L2 (5.8 GB streamed per step)",
                        "step_bytes": bytes_step,
-                       "step_hbm_frac": bytes_step / (ms * 1e-3) / (peak * 1e9)},
+                       "step_hbm_frac": bytes_step / (ms * 1e-3) / (peak * 1e9 * (1 if args.replicas else world))},
             "e2e": {"value": args.batch * 1000.0 / e2e_ms * (world if args.replicas else 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch + 4},
             "gpu_launches": args.steps * (1 if persistent else 3 + 5 * args.layers),
@@ -368,6 +380,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch kernels one by one without graph or PDL (for ncu launch lists)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with several GPUs: independent replicas instead of one tensor-parallel model")
     ap.add_argument("--persistent", action="store_true",
                     help="run each step as one persistent launch instead of the per-operation kernel sequence")
     ap.add_argument("--kernel-only", action="store_true",
@@ -378,7 +392,7 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    args.replicas = world > 1
+    args.replicas = args.replicas and world > 1
     if args.kernel_only:
         import torch
         import att1_b200 as b2

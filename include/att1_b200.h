@@ -54,6 +54,35 @@ att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dty
 uint32_t att1_b200_infer_batch(const att1_infer_t *infer);
 
 /* One step for all sequences: tokens[batch] in, greedy next tokens out. */
+/* ---- tensor parallelism over GPUs ----------------------------------------------
+ * One context per GPU and rank, holding that rank's shard (query / KV heads,
+ * FFN rows, vocabulary rows; WO and down by input columns); the ranks
+ * exchange partial results through each other's device memory inside the
+ * step's kernels. Create every rank, then connect them: across processes
+ * with CUDA IPC handles (exchanged by the caller, e.g. over
+ * torch.distributed), or inside one process with peer access. Every rank
+ * must then run the same steps with the same tokens; logits (all vocabulary
+ * rows) and tokens are the same on every rank. */
+#define ATT1_B200_TP_HANDLE_BYTES 64
+/* Device for the contexts created next by this thread (the library's own CUDA
+ * runtime state; a context keeps its device for all later calls). */
+att1_status_t att1_b200_set_device(int device);
+att1_status_t att1_b200_infer_create_synth_tp(const att1_b200_config *cfg, uint64_t seed, uint32_t batch,
+                                              uint32_t rank, uint32_t world, att1_infer_t **out_infer);
+/* This rank's exchange-region handle (ATT1_B200_TP_HANDLE_BYTES bytes). */
+att1_status_t att1_b200_infer_tp_handle(const att1_infer_t *infer, void *handle);
+/* handles: world * ATT1_B200_TP_HANDLE_BYTES bytes, rank order (own entry ignored). */
+att1_status_t att1_b200_infer_tp_connect(att1_infer_t *infer, const void *handles);
+/* Unmaps the other ranks' regions (IPC): every rank disconnects, the caller
+ * synchronises the ranks, then each destroys its context. */
+att1_status_t att1_b200_infer_tp_disconnect(att1_infer_t *infer);
+/* All ranks of one process (rank r on its own device), connected by peer access. */
+att1_status_t att1_b200_infer_tp_connect_local(att1_infer_t *const *infers, uint32_t world);
+/* A step in two halves, so one thread can drive several ranks: queue the
+ * step on every rank, then wait for each. */
+att1_status_t att1_b200_infer_step_async(att1_infer_t *infer, const uint32_t *tokens);
+att1_status_t att1_b200_infer_step_wait(att1_infer_t *infer, uint32_t *out_tokens);
+
 att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *tokens,
                                            uint32_t *out_tokens);
 /* Host copy of the last step's logits [batch][vocab]. */

@@ -90,6 +90,19 @@ int b2_q4_synth(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t col
                 uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2, float std,
                 int map, void *stream);
 
+/* A shard of a generated tensor (tensor parallelism): device row i takes
+ * source row src_row0 + i (of each source for GATEUP) and device column j
+ * source column src_col0 + j of rows src_cols long. q4 groups stay the
+ * reference's 32-column groups (src_col0 % 32 == 0); a q8 row keeps the
+ * scale of its whole source row. */
+int b2_q4_synth_part(void *dst, uint32_t tile_offset, uint32_t dst_rows, uint32_t cols,
+                     uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2, float std, int map,
+                     uint32_t src_row0, uint32_t src_col0, uint32_t src_cols, void *stream);
+int b2_q8_synth_part(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows,
+                     uint32_t cols, uint64_t seed, uint64_t tensor_id, uint64_t tensor_id2,
+                     float std, int map, uint32_t src_row0, uint32_t src_col0, uint32_t src_cols,
+                     void *stream);
+
 int b2_q8_pack(void *dst, float *row_scale, uint32_t tile_offset, uint32_t dst_rows,
                uint32_t cols, const int8_t *values, const float *scales,
                const int8_t *values2, const float *scales2, int map, void *stream);
@@ -121,8 +134,42 @@ enum b2_epilogue {
     B2_EPI_RESID = 1,   /* out[b][r] = resid[b][r] + y */
     B2_EPI_QKV = 2,     /* q rows -> out (RoPE); k rows -> K cache (RoPE); v rows -> V cache */
     B2_EPI_SWIGLU = 3,  /* gate/up rows -> out[b][j] = silu(gate) * up */
-    B2_EPI_LOGITS = 4   /* out[b][r] = y and greedy argmax key per item */
+    B2_EPI_LOGITS = 4,  /* out[b][r] = y and greedy argmax key per item */
+    B2_EPI_PUSH = 5     /* tensor parallel: y to every rank's exchange slot (b2_tp) */
 };
+
+/* ---- tensor parallelism: partial results exchanged over peer memory ------- */
+/*
+ * Each rank owns one exchange region (b2_tp_region_bytes) in its device
+ * memory that every rank can store to (NVLink peer access or CUDA IPC
+ * mappings). Layout: flags [points+1][B2_TP_MAX] u64 | argmax keys
+ * [B2_TP_MAX][16] u64 | slots [points][B2_TP_MAX][slot_floats] f32 | logits
+ * slots [B2_TP_MAX][logit_floats] f32. Rank s contributes to point p by
+ * storing into slot (p, s) of every rank and then setting flag (p, s) of
+ * every rank to the step epoch + 1; a consumer waits for all flags of p and
+ * adds the slots in rank order, so every rank computes the same sum. Point
+ * `points` is the logits all-gather (rank s's vocabulary rows in logits slot
+ * s, its argmax key in keys[s]).
+ */
+#define B2_TP_MAX 8
+#define B2_TP_NONE 0xFFFFFFFFu
+
+typedef struct b2_tp {
+    uint32_t rank, world;         /* world 0 or 1: no exchange */
+    uint8_t *peer[B2_TP_MAX];     /* every rank's region as mapped on this device; peer[rank] = own */
+    uint32_t points;              /* regular exchange points in the region */
+    uint32_t slot_floats;         /* floats per regular slot (batch * d_model) */
+    uint32_t logit_floats;        /* floats per logits slot (batch * local vocab rows) */
+    const uint32_t *epoch;        /* device step counter, equal on every rank (b2_step_end_tp advances it) */
+    int32_t *done;                /* device completion counter of this kernel: zero, left zero */
+    uint32_t out_point;           /* B2_EPI_PUSH: point this GEMV contributes to (LOGITS: the logits point) */
+    uint32_t in_point;            /* prologue input x = in_resid + sum over ranks of slot (in_point, r); or B2_TP_NONE */
+    const float *in_resid;        /* [batch][cols] residual added by that prologue */
+    float *in_out;                /* [batch][cols]: the prologue stores the summed input here, may be NULL */
+    uint32_t row_offset;          /* LOGITS: vocabulary id of local row 0 */
+} b2_tp;
+
+size_t b2_tp_region_bytes(uint32_t points, uint32_t slot_floats, uint32_t logit_floats);
 
 typedef struct b2_kv_layout {
     float *k_pool, *v_pool;       /* page pools of one layer */
@@ -160,6 +207,7 @@ typedef struct b2_gemv_args {
     int32_t *err;                 /* device error word */
     int pdl;                      /* launch with programmatic dependent launch */
     int grid;                     /* 0 = one CTA per SM */
+    b2_tp tp;                     /* tensor parallel exchange (zero = none) */
 } b2_gemv_args;
 
 size_t b2_gemv_scratch_bytes(const b2_gemv_args *a);
@@ -208,6 +256,11 @@ int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_model, const ui
 /* tokens[b] = argmax index; positions[b] += 1. */
 int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens,
                 int32_t *positions, int32_t *err, int pdl, void *stream);
+/* Tensor parallel step end: waits for every rank's logits flag, takes the
+ * largest argmax key over the ranks (the global greedy token), advances the
+ * positions and the epoch (tp->epoch is written through a cast). */
+int b2_step_end_tp(const b2_tp *tp, uint32_t batch, uint32_t *tokens, int32_t *positions, int32_t *err,
+                   int pdl, void *stream);
 
 /* ---- the whole decode step as one persistent launch ------------------------ */
 /*
