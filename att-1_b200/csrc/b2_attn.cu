@@ -2,71 +2,303 @@
 //
 // Replaces the per-head host loops of src/attention.c:508-541 (scores =
 // q.k * 1/sqrt(hd), softmax of src/norm.c:36-71, context = sum p * v) for one
-// decoded token per sequence. The KV pages use the KV-MMU page layout
-// [token_in_page][head][head_dim] (src/kv_mmu.c:95-101) with n_kv_heads heads;
-// the H/Hkv query heads of a KV head share every K/V read (grouped-query
-// attention; the reference reaches the same numbers with expanded heads).
+// decoded token per sequence. The KV cache is paged like the reference's
+// KV-MMU (src/kv_mmu.c:95-101: fixed-size pages, a page table per sequence),
+// with n_kv_heads heads; inside a page the heads come first
+// ([head][token_in_page][head_dim]) so that one KV head's tokens are
+// contiguous runs in HBM. The H/Hkv query heads of a KV head share every K/V
+// read (grouped-query attention; the reference reaches the same numbers with
+// expanded heads).
 //
-// Work split: CTA (chunk, kv head, item) covers kChunk positions; eight warps
-// take four positions at a time (all K/V loads of the four issued together)
-// and keep an online softmax per query head. Each CTA writes its
-// (max, sum, weighted V) partial; the last CTA of a (item, kv head) to arrive
-// combines the partials in chunk order (deterministic) and writes the context.
+// Work split: CTA (split, KV head, item) owns a contiguous range of one KV
+// head's positions, about one CTA per SM over the step. A KV head's rows are
+// contiguous inside a page, so the range streams through kBufs shared-memory
+// buffers with 1-D bulk copies (the TMA engine, completion on an mbarrier);
+// the scores of the query heads that share the KV head, an online softmax
+// and the weighted V sum are computed from shared memory. Each CTA writes
+// its (max, sum, weighted V) partial; the last CTA of an (item, KV head) to
+// arrive combines the partials in split order (deterministic) and writes the
+// context.
 #include "b2_attn.cuh"
 
 namespace b2 {
 
-constexpr int kAttnWarps = 8;
+constexpr int kAttnWarps = 16;     // consumer warps
+constexpr int kAttnThreads = kAttnWarps * 32 + 32;  // + one producer warp
+constexpr uint32_t kSub = 32;       // positions per sub-tile
+constexpr uint32_t kBufs = 6;       // sub-tile buffers (ring stages)
+constexpr int kCtasPerSm = 1;       // resident CTAs per SM the split count aims at
 
-struct CtaSync {
-    __device__ void operator()() const { __syncthreads(); }
+struct ConsumerWarps {
+    __device__ void operator()() const { asm volatile("bar.sync 1, %0;" ::"n"(kAttnWarps * 32) : "memory"); }
 };
 
-template <int DPL>  // dims per lane = ceil(head_dim / 32)
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(const AttnParams p)
+__host__ __device__ constexpr size_t attn_ring_smem(uint32_t hd)
 {
-    const uint32_t chunk = blockIdx.x, kvh = blockIdx.y, item = blockIdx.z;
-    __shared__ __align__(16) uint8_t smem[attn_smem_bytes(DPL, kAttnWarps, kMaxGroup)];
+    // full / empty mbarriers | kBufs sub-tile buffers of K and V | combine flag
+    return 2 * kBufs * 8 + 2 * (size_t)kBufs * kSub * hd * sizeof(float) + 16;
+}
+
+// Merge two online-softmax states (m, l, o) of one query head.
+__device__ __forceinline__ void soft_merge4(float &m, float &l, float4 &o, float m2, float l2, float4 o2)
+{
+    const float M = fmaxf(m, m2);
+    if (M == -INFINITY) return;  // both empty
+    const float f1 = expf(m - M), f2 = expf(m2 - M);
+    l = fmaf(l, f1, l2 * f2);
+    o = make_float4(fmaf(o.x, f1, o2.x * f2), fmaf(o.y, f1, o2.y * f2), fmaf(o.z, f1, o2.z * f2),
+                    fmaf(o.w, f1, o2.w * f2));
+    m = M;
+}
+
+// CTA (split, KV head, item) owns a contiguous range of one KV head's
+// positions (about one CTA per SM over the step). Inside a page a KV head's
+// rows are contiguous, so a producer warp streams the range through a ring of
+// kBufs shared-memory sub-tiles with 1-D bulk copies (TMA; "full" mbarrier
+// per stage, counted in bytes). Sixteen consumer warps take positions of each
+// sub-tile (LP lanes per position, four dimensions per lane), compute the
+// scores of the query heads that share the KV head with a halving exchange
+// (each step hands half of the heads to the partner lane), keep an online
+// softmax and the weighted V sum per lane, and release the stage on its
+// "empty" mbarrier, so warps never wait for one another while streaming.
+// At the end the lane groups and the warps are merged.
+template <int LP, int MG>  // lanes per position (attn_lanes), query heads per KV head (bound)
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnParams p)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int PPW = 32 / LP;
+    const uint32_t split = blockIdx.x, S = gridDim.x, kvh = blockIdx.y, item = blockIdx.z;
+    const uint32_t hd = p.head_dim, G = p.group;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);   // [kBufs]
+    uint64_t *empty = full + kBufs;                          // [kBufs]
+    float *Kb = reinterpret_cast<float *>(smem + 2 * kBufs * 8);  // [kBufs][kSub][hd]
+    float *Vb = Kb + kBufs * kSub * hd;                             // [kBufs][kSub][hd]
+    int *last = reinterpret_cast<int *>(Vb + kBufs * kSub * hd);
+
     pdl_wait();
     pdl_launch_dependents();
-    // positions beyond max_ctx would need more chunks than the grid has
     const int32_t pos = p.positions[item];
     if (pos < 0 || (uint32_t)pos >= p.max_ctx) {
-        if (threadIdx.x == 0 && chunk == 0 && kvh == 0) raise_error(p.err, B2_ERR_POSITION);
+        if (threadIdx.x == 0 && split == 0 && kvh == 0) raise_error(p.err, B2_ERR_POSITION);
         return;
     }
     const uint32_t len = (uint32_t)pos + 1;
-    const uint32_t nactive = (len + kChunk - 1) / kChunk;
-    if (chunk >= nactive) return;
-    const uint32_t p0 = chunk * kChunk, p1 = min(p0 + kChunk, len);
-    attn_chunk<DPL, kAttnWarps>(p, attn_smem<DPL, kAttnWarps>(smem, kMaxGroup), item, kvh, chunk, nactive, p0, p1, CtaSync());
+    const uint32_t nactive = min(S, len);
+    if (split >= nactive) return;
+    const uint32_t p0 = (uint32_t)((uint64_t)split * len / nactive);
+    const uint32_t n = (uint32_t)((uint64_t)(split + 1) * len / nactive) - p0;
+    const uint32_t ntiles = (n + kSub - 1) / kSub;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t b = 0; b < kBufs; ++b) {
+            mbar_init(&full[b], 1);
+            mbar_init(&empty[b], kAttnWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kAttnWarps) {
+        // producer: sub-tile t of the range into stage t % kBufs (page pieces are contiguous)
+        const uint32_t rowb = hd * sizeof(float);
+        for (uint32_t t = 0; t < ntiles; ++t) {
+            const uint32_t buf = t % kBufs;
+            if (t >= kBufs && !mbar_wait_bounded(&empty[buf], ((t / kBufs) - 1) & 1u, p.err)) break;
+            if (lane == 0) {
+                const uint32_t r0 = t * kSub, nt = min(kSub, n - r0);
+                mbar_arrive_expect_tx(&full[buf], 2 * nt * rowb);
+                for (uint32_t r = 0; r < nt;) {
+                    const uint32_t ps = p0 + r0 + r, run = min(nt - r, p.kv.page_tokens - ps % p.kv.page_tokens);
+                    bulk_g2s(Kb + ((size_t)buf * kSub + r) * hd, kv_row(p.kv, p.kv.k_pool, item, ps, kvh), run * rowb,
+                             &full[buf]);
+                    bulk_g2s(Vb + ((size_t)buf * kSub + r) * hd, kv_row(p.kv, p.kv.v_pool, item, ps, kvh), run * rowb,
+                             &full[buf]);
+                    r += run;
+                }
+            }
+            __syncwarp();
+        }
+        return;
+    }
+
+    // ---- consumers ----
+    const int sub = lane / LP, sl = lane % LP;
+    const uint32_t d0 = 4 * sl;
+    const bool dval = d0 < hd;
+    float4 qv[MG];
+#pragma unroll
+    for (int gq = 0; gq < MG; ++gq) {
+        qv[gq] = make_float4(0, 0, 0, 0);
+        if (gq < (int)G && dval)
+            qv[gq] = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)item * p.n_heads * hd +
+                                                             (size_t)(kvh * G + gq) * hd + d0));
+    }
+    float m[MG], l[MG];
+    float4 o[MG];
+#pragma unroll
+    for (int gq = 0; gq < MG; ++gq) {
+        m[gq] = -INFINITY;
+        l[gq] = 0.0f;
+        o[gq] = make_float4(0, 0, 0, 0);
+    }
+    bool ok = true;
+    for (uint32_t t = 0; t < ntiles; ++t) {
+        const uint32_t buf = t % kBufs, nt = min(kSub, n - t * kSub);
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[buf], (t / kBufs) & 1u, p.err));
+        const float *K = Kb + (size_t)buf * kSub * hd, *V = Vb + (size_t)buf * kSub * hd;
+        // this warp's positions of the sub-tile, two at a time (warp-uniform trip count)
+        constexpr uint32_t kStride = kAttnWarps * PPW;
+        for (uint32_t wb = warp * PPW; wb < nt; wb += 2 * kStride) {
+            const uint32_t ra = wb + sub, rb = ra + kStride;
+            const bool va = ok && ra < nt, vb = ok && rb < nt;
+            float4 k4[2], v4[2];
+            k4[0] = (va && dval) ? *reinterpret_cast<const float4 *>(K + ra * hd + d0) : make_float4(0, 0, 0, 0);
+            v4[0] = (va && dval) ? *reinterpret_cast<const float4 *>(V + ra * hd + d0) : make_float4(0, 0, 0, 0);
+            k4[1] = (vb && dval) ? *reinterpret_cast<const float4 *>(K + rb * hd + d0) : make_float4(0, 0, 0, 0);
+            v4[1] = (vb && dval) ? *reinterpret_cast<const float4 *>(V + rb * hd + d0) : make_float4(0, 0, 0, 0);
+            float mine[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float dot[MG];
+#pragma unroll
+                for (int gq = 0; gq < MG; ++gq)
+                    dot[gq] = qv[gq].x * k4[j].x + qv[gq].y * k4[j].y + qv[gq].z * k4[j].z + qv[gq].w * k4[j].w;
+                // sum over the LP lanes of the position: while more than one head
+                // is left each exchange hands half of them to the partner lane
+                // (the upper lane keeps the upper half), then plain exchanges;
+                // lane sl ends with head (top log2 MG bits of sl)
+#pragma unroll
+                for (int cnt = MG, off = LP / 2; off > 0; off >>= 1) {
+                    if (cnt > 1) {
+                        const bool upper = (sl & off) != 0;
+#pragma unroll
+                        for (int i = 0; i < cnt / 2; ++i) {
+                            const float send = upper ? dot[i] : dot[i + cnt / 2];
+                            const float keep = upper ? dot[i + cnt / 2] : dot[i];
+                            dot[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                        }
+                        cnt /= 2;
+                    } else {
+                        dot[0] += __shfl_xor_sync(0xffffffffu, dot[0], off);
+                    }
+                }
+                mine[j] = __fmul_rn(dot[0], p.inv_sqrt);  // src/attention.c:521-523
+            }
+            // online softmax over both positions at once, per query head
+#pragma unroll
+            for (int gq = 0; gq < MG; ++gq) {
+                if (gq < (int)G) {
+                    const int src = (sub * LP) | (gq * (LP / MG));  // a lane holding head gq
+                    const float sa = __shfl_sync(0xffffffffu, mine[0], src);
+                    const float sb = __shfl_sync(0xffffffffu, mine[1], src);
+                    if (va) {
+                        const float nm = fmaxf(m[gq], vb ? fmaxf(sa, sb) : sa);
+                        const float corr = __expf(m[gq] - nm);
+                        const float pa = __expf(sa - nm), pb = vb ? __expf(sb - nm) : 0.0f;
+                        l[gq] = fmaf(l[gq], corr, pa + pb);
+                        o[gq] = make_float4(fmaf(o[gq].x, corr, fmaf(pa, v4[0].x, pb * v4[1].x)),
+                                            fmaf(o[gq].y, corr, fmaf(pa, v4[0].y, pb * v4[1].y)),
+                                            fmaf(o[gq].z, corr, fmaf(pa, v4[0].z, pb * v4[1].z)),
+                                            fmaf(o[gq].w, corr, fmaf(pa, v4[0].w, pb * v4[1].w)));
+                        m[gq] = nm;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[buf]);
+    }
+    // merge the lane groups of the warp (positions differ, dimensions match)
+#pragma unroll
+    for (int off = LP; off < 32; off <<= 1) {
+#pragma unroll
+        for (int gq = 0; gq < MG; ++gq) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m[gq], off);
+            const float l2 = __shfl_xor_sync(0xffffffffu, l[gq], off);
+            float4 o2;
+            o2.x = __shfl_xor_sync(0xffffffffu, o[gq].x, off);
+            o2.y = __shfl_xor_sync(0xffffffffu, o[gq].y, off);
+            o2.z = __shfl_xor_sync(0xffffffffu, o[gq].z, off);
+            o2.w = __shfl_xor_sync(0xffffffffu, o[gq].w, off);
+            soft_merge4(m[gq], l[gq], o[gq], m2, l2, o2);
+        }
+    }
+    // merge the warps: state in shared memory (the ring is drained)
+    ConsumerWarps SYNC;
+    SYNC();
+    float *wm = Kb, *wl = Kb + kAttnWarps * MG, *wo = Kb + 2 * kAttnWarps * MG;  // wo [warps][MG][hd]
+#pragma unroll
+    for (int gq = 0; gq < MG; ++gq) {
+        if (gq < (int)G && sub == 0) {
+            if (sl == 0) {
+                wm[warp * MG + gq] = m[gq];
+                wl[warp * MG + gq] = l[gq];
+            }
+            if (dval) *reinterpret_cast<float4 *>(wo + ((size_t)warp * MG + gq) * hd + d0) = o[gq];
+        }
+    }
+    SYNC();
+    float *part_base = p.partial + ((size_t)(item * p.n_kv_heads + kvh) * p.nchunks_max) * G * (hd + 2);
+    float *part = part_base + (size_t)split * G * (hd + 2);
+    const uint32_t nthreads = kAttnWarps * 32;
+    for (uint32_t i = threadIdx.x; i < G * (hd + 2); i += nthreads) {
+        const uint32_t gq = i / (hd + 2), d = i % (hd + 2);
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * MG + gq]);
+        float v = 0.0f;
+        if (d == 0) {
+            v = M;
+        } else {
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float wmv = wm[w * MG + gq];
+                if (wmv == -INFINITY) continue;  // warp saw no position
+                v = fmaf(d == 1 ? wl[w * MG + gq] : wo[((size_t)w * MG + gq) * hd + d - 2], expf(wmv - M), v);
+            }
+        }
+        part[i] = v;
+    }
+    attn_publish(p, Kb + 2 * kAttnWarps * MG + (size_t)kAttnWarps * MG * hd, last, item, kvh, nactive, part_base,
+                 nthreads, SYNC);
 }
 
 static cudaError_t launch_attn(const AttnParams &p, dim3 grid, int pdl, cudaStream_t st)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kAttnWarps * 32);
+    cfg.blockDim = dim3(kAttnThreads);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const uint32_t dpl = (p.head_dim + 31) / 32;
-    switch (dpl) {
-    case 1: return cudaLaunchKernelEx(&cfg, attn_kernel<1>, p);
-    case 2: return cudaLaunchKernelEx(&cfg, attn_kernel<2>, p);
-    case 3: return cudaLaunchKernelEx(&cfg, attn_kernel<3>, p);
-    case 4: return cudaLaunchKernelEx(&cfg, attn_kernel<4>, p);
-    default: return cudaErrorInvalidValue;
+    const int mg = p.group <= 4 ? 4 : 8;
+    cfg.dynamicSmemBytes = attn_ring_smem(p.head_dim);
+    const void *fn;
+    switch (attn_lanes(p.head_dim) * 10 + mg) {
+    case 84: fn = (const void *)attn_ring_kernel<8, 4>; break;
+    case 88: fn = (const void *)attn_ring_kernel<8, 8>; break;
+    case 164: fn = (const void *)attn_ring_kernel<16, 4>; break;
+    case 168: fn = (const void *)attn_ring_kernel<16, 8>; break;
+    case 324: fn = (const void *)attn_ring_kernel<32, 4>; break;
+    default: fn = (const void *)attn_ring_kernel<32, 8>; break;
     }
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+    if (e != cudaSuccess) return e;
+    void *args[] = {const_cast<AttnParams *>(&p)};
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 
+// Splits per (item, KV head): about kCtasPerSm CTAs per SM over the grid,
+// at least one position each at the longest context.
 static void attn_sizes(const b2_attn_args *a, uint32_t &nchunks, size_t &partial, uint32_t &counters)
 {
-    nchunks = (a->max_ctx + kChunk - 1) / kChunk;
+    const uint32_t heads = a->batch * a->n_kv_heads;
+    nchunks = (uint32_t)(kCtasPerSm * sm_count()) / heads;
+    if (nchunks < 1) nchunks = 1;
+    if (nchunks > a->max_ctx) nchunks = a->max_ctx;
     const uint32_t G = a->n_heads / a->n_kv_heads;
     partial = (size_t)a->batch * a->n_kv_heads * nchunks * G * (a->head_dim + 2) * sizeof(float);
     partial = (partial + 255) & ~(size_t)255;
@@ -87,8 +319,14 @@ int attn_check(const b2_attn_args *a)
         return -1;
     // the chunk combine stages (max, sum) of every chunk and query head in the
     // warp-state area of the standalone kernel
-    const uint32_t nchunks = (a->max_ctx + kChunk - 1) / kChunk, dpl = (a->head_dim + 31) / 32;
-    if (2ull * nchunks * G > 8ull * kMaxGroup * 32 * dpl) return -9;
+    // the split combine stages (max, sum) of every split in the sub-tile buffers
+    uint32_t nchunks, cl;
+    size_t pb;
+    attn_sizes(a, nchunks, pb, cl);
+    // warp states and the combine staging share the drained ring
+    if (2ull * kAttnWarps * kMaxGroup + (uint64_t)kAttnWarps * kMaxGroup * a->head_dim + 2ull * nchunks * G >
+        2ull * kBufs * kSub * a->head_dim)
+        return -9;
     return 0;
 }
 

@@ -14,6 +14,9 @@
 
 namespace b2 {
 
+// SMs of the current device (host; defined in b2_gemv.cu).
+int sm_count();
+
 // ---- error word ------------------------------------------------------------
 __device__ __forceinline__ void raise_error(int32_t *err, int32_t bit)
 {
@@ -62,6 +65,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Bounded wait: gives up after ~`limit` polls (each poll may suspend for a

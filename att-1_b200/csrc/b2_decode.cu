@@ -52,7 +52,7 @@ struct GridBar {
 
 struct DecodeParams {
     const DecodeOp *ops;
-    uint32_t nops, batch, d_model, vocab, dpl, attn_chunks;
+    uint32_t nops, batch, d_model, vocab, lp, attn_chunks;
     const float *embed;
     const uint32_t *tokens_in;
     uint32_t *tokens_out;
@@ -135,12 +135,12 @@ __device__ void op_end(const DecodeParams &dp)
     if (threadIdx.x == 0) atomicAdd(&dp.bar->epoch, 1ull);
 }
 
-template <int DPL>
+template <int LP, int MG>
 __device__ void attn_items(const AttnParams &a, const DecodeParams &dp, uint8_t *sbase)
 {
     const uint32_t NC = dp.attn_chunks;  // chunks per (item, KV head), at most
     const uint32_t nwork = a.batch * a.n_kv_heads * NC;
-    const AttnSmem sm = attn_smem<DPL, kWarps>(sbase, a.group);
+    const AttnSmem sm = attn_smem<LP, kWarps>(sbase, a.group);
     for (uint32_t w = blockIdx.x; w < nwork; w += gridDim.x) {
         const uint32_t item = w / (a.n_kv_heads * NC), kvh = (w / NC) % a.n_kv_heads, c = w % NC;
         const int32_t pos = a.positions[item];
@@ -153,7 +153,7 @@ __device__ void attn_items(const AttnParams &a, const DecodeParams &dp, uint8_t 
         if (nc > NC) nc = NC;
         if (c >= nc) continue;
         const uint32_t p0 = (uint32_t)((uint64_t)c * len / nc), p1 = (uint32_t)((uint64_t)(c + 1) * len / nc);
-        attn_chunk<DPL, kWarps>(a, sm, item, kvh, c, nc, p0, p1, ConsumerSync());
+        attn_chunk<LP, MG, kWarps>(a, sm, item, kvh, c, nc, p0, p1, ConsumerSync());
     }
 }
 
@@ -215,12 +215,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             break;
         case OP_ATTN:
             if (dead) break;
-            switch (dp.dpl) {
-            case 1: attn_items<1>(op->a, dp, s.xdig); break;
-            case 2: attn_items<2>(op->a, dp, s.xdig); break;
-            case 3: attn_items<3>(op->a, dp, s.xdig); break;
-            default: attn_items<4>(op->a, dp, s.xdig); break;
-            }
+            // the plan admits at most four query heads per KV head here
+            if (dp.lp == 8) attn_items<8, 4>(op->a, dp, s.xdig);
+            else if (dp.lp == 16) attn_items<16, 4>(op->a, dp, s.xdig);
+            else attn_items<32, 4>(op->a, dp, s.xdig);
             break;
         default:
             if (!dead) op_end(dp);
@@ -347,10 +345,11 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
             const int rc = attn_check(t);
             if (rc != 0) return rc;
             if (t->batch != B) return -1;
-            const uint32_t d = (t->head_dim + 31) / 32;
+            const uint32_t d = (uint32_t)attn_lanes(t->head_dim);
             if (dpl != 0 && d != dpl) return -1;
             dpl = d;
             const uint32_t G = t->n_heads / t->n_kv_heads;
+            if (G > 4) return -9;  // register budget of the persistent kernel
             const size_t need = attn_smem_bytes((int)d, kWarps, G);
             if (need > shared_need) shared_need = need;
             if (t->batch * t->n_kv_heads > counters) counters = t->batch * t->n_kv_heads;
@@ -447,7 +446,7 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
     dp.batch = B;
     dp.d_model = a->d_model;
     dp.vocab = a->vocab;
-    dp.dpl = dpl;
+    dp.lp = dpl;
     dp.attn_chunks = attn_chunks;
     dp.embed = a->embed;
     dp.tokens_in = a->tokens_in;

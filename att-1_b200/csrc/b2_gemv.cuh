@@ -317,8 +317,8 @@ static __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const f
                     p.out[(size_t)item * p.out_stride + row] = y;
                 } else if (pos >= 0 && (uint32_t)pos < cap) {
                     const int32_t page = p.kv.page_table[(size_t)item * p.kv.pages_per_seq + pos / p.kv.page_tokens];
-                    const size_t slot = (size_t)page * p.kv.page_tokens + pos % p.kv.page_tokens;
-                    p.kv.k_pool[slot * p.kv.n_kv_heads * hd + rr] = y;
+                    p.kv.k_pool[(((size_t)page * p.kv.n_kv_heads + rr / hd) * p.kv.page_tokens +
+                                 pos % p.kv.page_tokens) * hd + rr % hd] = y;
                 } else {
                     raise_error(p.err, B2_ERR_POSITION);
                 }
@@ -326,8 +326,8 @@ static __device__ void tile_epilogue(const GemvParams &p, uint32_t tile, const f
                 const uint32_t rr = row - p.q_rows - p.kv_rows;
                 if (pos >= 0 && (uint32_t)pos < cap) {
                     const int32_t page = p.kv.page_table[(size_t)item * p.kv.pages_per_seq + pos / p.kv.page_tokens];
-                    const size_t slot = (size_t)page * p.kv.page_tokens + pos % p.kv.page_tokens;
-                    p.kv.v_pool[slot * p.kv.n_kv_heads * hd + rr] = v;
+                    p.kv.v_pool[(((size_t)page * p.kv.n_kv_heads + rr / hd) * p.kv.page_tokens +
+                                 pos % p.kv.page_tokens) * hd + rr % hd] = v;
                 } else {
                     raise_error(p.err, B2_ERR_POSITION);
                 }
@@ -389,10 +389,6 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // The stage sequence of a CTA over its k-columns (a k-column is the 16 units
 // of one k-unit of a panel, contiguous in memory): stage i covers columns
@@ -696,7 +692,6 @@ struct GemvPlan {
     uint32_t smem, off_ring, off_xdig, off_tile, off_misc, stages, panels;
 };
 
-int sm_count();
 // Argument checks of b2_gemv (0 or a negative status).
 int gemv_check(const b2_gemv_args *a);
 // Grid, shared-memory carve-up and scratch sizes for a standalone launch.

@@ -1477,7 +1477,7 @@ out:
 att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item, uint32_t layer, size_t count,
                                         float *keys, float *values)
 {
-    const size_t row = (size_t)infer->cfg.n_kv_heads * infer->head_dim;
+    const size_t row = (size_t)infer->hkv * infer->head_dim;
     size_t p;
     if (infer == NULL || keys == NULL || values == NULL || item >= infer->batch || layer >= infer->cfg.n_layers ||
         count > infer->cfg.max_seq)
@@ -1485,11 +1485,15 @@ att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item
     if (cudaStreamSynchronize(infer->stream) != cudaSuccess) return ATT1_ERR_STATE;
     for (p = 0; p < count; p++) {
         /* identity page table: sequence item's pages are contiguous */
+        /* page = [head][token][dim]: one head_dim run per head, page_tokens rows apart */
         const size_t page = (size_t)item * infer->pages_per_seq + p / infer->page_tokens;
-        const size_t slot = page * infer->page_tokens + p % infer->page_tokens;
-        const size_t off = (size_t)layer * infer->layer_pool_elems + slot * row;
-        if (cudaMemcpy(keys + p * row, infer->k_pool + off, row * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess ||
-            cudaMemcpy(values + p * row, infer->v_pool + off, row * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        const size_t off = (size_t)layer * infer->layer_pool_elems +
+                           (page * infer->hkv * infer->page_tokens + p % infer->page_tokens) * infer->head_dim;
+        const size_t hd = infer->head_dim, pitch = (size_t)infer->page_tokens * hd * sizeof(float);
+        if (cudaMemcpy2D(keys + p * row, hd * sizeof(float), infer->k_pool + off, pitch, hd * sizeof(float), infer->hkv,
+                         cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemcpy2D(values + p * row, hd * sizeof(float), infer->v_pool + off, pitch, hd * sizeof(float),
+                         infer->hkv, cudaMemcpyDeviceToHost) != cudaSuccess)
             return ATT1_ERR_STATE;
     }
     return ATT1_OK;

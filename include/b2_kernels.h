@@ -176,7 +176,8 @@ typedef struct b2_kv_layout {
     const int32_t *page_table;    /* [batch][pages_per_seq] physical page ids */
     uint32_t page_tokens;         /* tokens per page */
     uint32_t pages_per_seq;
-    uint32_t n_kv_heads, head_dim;/* page = [page_tokens][n_kv_heads][head_dim] f32 */
+    uint32_t n_kv_heads, head_dim;/* page = [n_kv_heads][page_tokens][head_dim] f32: a head's
+                                     tokens contiguous (32 KB runs at 64 tokens x 128 dims) */
 } b2_kv_layout;
 
 typedef struct b2_gemv_args {
