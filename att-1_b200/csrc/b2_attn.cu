@@ -76,10 +76,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
     float *Vb = Kb + kBufs * kSub * hd;                             // [kBufs][kSub][hd]
     int *last = reinterpret_cast<int *>(Vb + kBufs * kSub * hd);
 
-    pdl_wait();
-    pdl_launch_dependents();
-    const int32_t pos = p.positions[item];
+    // The KV rows before this step's position were written by earlier steps
+    // and the position itself by the previous step's step end, so the ring
+    // starts filling before the programmatic-launch wait; only the sub-tile
+    // holding this step's K/V row (written by the QKV GEMV just before) and
+    // q wait for it.
+    const int32_t pos = __ldcg(p.positions + item);
     if (pos < 0 || (uint32_t)pos >= p.max_ctx) {
+        pdl_wait();
         if (threadIdx.x == 0 && split == 0 && kvh == 0) raise_error(p.err, B2_ERR_POSITION);
         return;
     }
@@ -102,9 +106,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
     if (warp == kAttnWarps) {
         // producer: sub-tile t of the range into stage t % kBufs (page pieces are contiguous)
         const uint32_t rowb = hd * sizeof(float);
+        bool waited = false;
         for (uint32_t t = 0; t < ntiles; ++t) {
             const uint32_t buf = t % kBufs;
             if (t >= kBufs && !mbar_wait_bounded(&empty[buf], ((t / kBufs) - 1) & 1u, p.err)) break;
+            if (!waited && split == nactive - 1 && t == ntiles - 1) {  // this sub-tile holds position len - 1
+                pdl_wait();
+                waited = true;
+            }
             if (lane == 0) {
                 const uint32_t r0 = t * kSub, nt = min(kSub, n - r0);
                 mbar_arrive_expect_tx(&full[buf], 2 * nt * rowb);
@@ -119,10 +128,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
             }
             __syncwarp();
         }
+        if (!waited) pdl_wait();
+        pdl_launch_dependents();
         return;
     }
 
     // ---- consumers ----
+    pdl_wait();
+    pdl_launch_dependents();
     const int sub = lane / LP, sl = lane % LP;
     const uint32_t d0 = 4 * sl;
     const bool dval = d0 < hd;
