@@ -21,9 +21,9 @@
 // error word; after a timeout the consumers keep the ring protocol (so the
 // producer finishes) and skip the rest of the work.
 //
-// Partial sums (GEMV panels shared between CTAs, attention chunks) use one
-// scratch region and one counter array: operations are separated by grid
-// barriers and each leaves its counters at zero.
+// Attention partial sums use one scratch region and one counter array:
+// operations are separated by grid barriers and each leaves its counters at
+// zero. (A GEMV keeps its partial sums inside the CTA.)
 #include "b2_attn.cuh"
 #include "b2_gemv.cuh"
 
@@ -61,7 +61,7 @@ struct DecodeParams {
     float *x;
     GridBar *bar;
     int32_t *err;
-    uint32_t off_ring, off_shared, off_tile, off_misc, off_ops, stages;
+    uint32_t off_ring, off_shared, off_tile, off_parts, off_misc, off_ops, stages;
 };
 
 struct ConsumerSync {
@@ -167,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     s.ring = smem + dp.off_ring;
     s.xdig = smem + dp.off_shared;
     s.tbufs = reinterpret_cast<float *>(smem + dp.off_tile);
+    s.parts = reinterpret_cast<float *>(smem + dp.off_parts);
     s.red = reinterpret_cast<float *>(smem + dp.off_misc);
     s.item_scale = s.red + kMaxItems * kWarps * 2;
     s.cta_key = reinterpret_cast<unsigned long long *>(s.item_scale + kMaxItems);
@@ -371,6 +372,9 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
     if (attn_partial > scratch) scratch = attn_partial;
 
     const uint32_t tbuf = kWarps * 16 * B * 4;
+    // per-warp tile sums: rounds of up to 16 tiles in every GEMV of the step
+    const uint32_t per_tile = kWarps * 16 * B * 4, round_cap = 16;
+    const uint32_t parts = round_cap * per_tile;
     const uint32_t misc = (kMaxItems * kWarps * 2 + kMaxItems) * 4 + kMaxItems * 8 + 16;
     const uint32_t opslots = (uint32_t)((2 * sizeof(DecodeOp) + 15) & ~(size_t)15);
     const uint32_t limit = 227u * 1024u;
@@ -378,7 +382,7 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
     off = (off + 127) & ~127u;
     const uint32_t off_ring = off;
     const uint32_t stage_b = kStageUnits * B2_Q4_UNIT_BYTES;
-    const uint32_t fixed = off_ring + (uint32_t)((shared_need + 127) & ~(size_t)127) + tbuf + 32 + misc + opslots;
+    const uint32_t fixed = off_ring + (uint32_t)((shared_need + 127) & ~(size_t)127) + tbuf + parts + 32 + misc + opslots;
     if (fixed + 2 * stage_b > limit) return -9;
     uint32_t ns = (limit - fixed) / stage_b;
     if (ns > (uint32_t)kMaxStages) ns = kMaxStages;
@@ -387,6 +391,8 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
     off += (uint32_t)((shared_need + 127) & ~(size_t)127);
     const uint32_t off_tile = off;
     off += tbuf;
+    const uint32_t off_parts = off;
+    off += parts;
     off = (off + 15) & ~15u;
     const uint32_t off_misc = off;
     off += misc;
@@ -425,6 +431,8 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
             o.g.off_ring = off_ring;
             o.g.off_xdig = off_shared;
             o.g.off_tile = off_tile;
+            o.g.off_parts = off_parts;
+            if (o.g.round_tiles > round_cap) o.g.round_tiles = round_cap;
             o.g.off_misc = off_misc;
             o.g.stages = ns;
         } else if (kinds[k] == OP_ATTN) {
@@ -459,6 +467,7 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
     dp.off_ring = off_ring;
     dp.off_shared = off_shared;
     dp.off_tile = off_tile;
+    dp.off_parts = off_parts;
     dp.off_misc = off_misc;
     dp.off_ops = off_ops;
     dp.stages = ns;

@@ -23,33 +23,34 @@
 // and in the 2^-22 relative quantisation of x, far inside the 1e-3 logits
 // tolerance of the parity tests.
 //
-// Streaming. Weights sit in the panel/unit layout of b2_kernels.h: a panel
-// is 16 row tiles, stored k-column by k-column (the 16 units of one column
-// pair, contiguous). Each CTA owns a contiguous range of k-columns (stream-K
-// over panel-major columns, balanced to one column across the grid), so at
-// any moment the GPU reads ~one compact window per CTA. The range is cut into
-// stages of up to kStageCols columns that never straddle a panel. One
-// producer lane copies each stage into a shared-memory ring of up to
-// kMaxStages stages with a single 1-D bulk copy (cp.async.bulk, completion
-// counted in bytes on the stage's "full" mbarrier). Consumer warp w owns tile
-// w of every panel: it multiplies unit (column, w) of each staged column,
-// keeps the tile's sums in registers across stages, and releases each stage
-// on its "empty" mbarrier, so the warps never meet at a CTA barrier and never
-// add each other's partial sums. When the CTA's part of a panel ends, each
-// warp finishes its own tile; a panel shared with neighbouring CTAs is added
-// by the last CTA to finish each tile (per-tile arrival counter), in CTA
-// order, so results are deterministic. The producer requests the first
-// stages before griddepcontrol.wait, so under programmatic dependent launch
-// the weight fetch overlaps the previous kernel.
+// Streaming. Weights sit in the tile-major unit layout of b2_kernels.h. Each
+// CTA owns whole 16-row tiles (a contiguous range of the unit stream; at most
+// one tile more than the lightest CTA), so no partial sum leaves the CTA.
+// One producer lane copies the range into a shared-memory ring of up to
+// kMaxStages stages of kStageUnits units with single 1-D bulk copies
+// (cp.async.bulk, completion counted in bytes on the stage's "full"
+// mbarrier). Consumer warp w multiplies units w, w + 16, ... of every stage,
+// keeps one tile's sums in registers and, when its units move on to the next
+// tile, stores them in its own slot of the round's per-warp tile sums; it
+// releases each stage on its "empty" mbarrier, so the warps never meet at a
+// CTA barrier while streaming. At the end of a round (the CTA's tiles, or a
+// share of them when shared memory is short) one CTA barrier, then the warps
+// add each tile's slots in warp order (deterministic) and run the tile
+// epilogues, one warp per tile. The producer requests the first stages
+// before griddepcontrol.wait, so under programmatic dependent launch the
+// weight fetch overlaps the previous kernel.
 //
-// Measured alternatives, slower: tile-major units split by k between the 16
-// warps (every tile then needs a cross-warp reduction in shared memory, and
-// the warp doing it lags and holds back the ring: half the speed of this
-// layout at 4096 columns); small bulk copies (an SM completes roughly one
-// bulk copy per 0.4-0.6 us almost whatever its size, so tens of KB per copy
-// are needed); per-warp contiguous ranges read with register prefetch
-// (~2400 small streams over HBM, under 2.5 TB/s without arithmetic); a ring
-// refilled by 16-byte cp.async from one warp.
+// Measured alternatives, slower: splitting the k range of tiles between CTAs
+// (stream-K) balances the CTAs exactly but every shared tile costs a global
+// partial, a fence and an atomic ticket, and the last CTA of each tile adds
+// the partials: those round trips made the end of every launch 3-7 us long;
+// a cross-warp reduction per tile at the moment the tile ends (the last warp
+// adds sixteen partials while the ring waits for it: half the speed); small
+// bulk copies (an SM completes roughly one bulk copy per 0.4-0.6 us almost
+// whatever its size, so tens of KB per copy are needed); per-warp contiguous
+// ranges read with register prefetch (~2400 small streams over HBM, under
+// 2.5 TB/s without arithmetic); a ring refilled by 16-byte cp.async from one
+// warp.
 #include "b2_gemv.cuh"
 
 #include <cfloat>
@@ -102,49 +103,56 @@ bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     const uint32_t fmt = a->w.format;
     const uint32_t UB = fmt == 4 ? B2_Q4_UNIT_BYTES : B2_Q8_UNIT_BYTES;
     const uint32_t KW = fmt == 4 ? 64u : 32u;
-    const uint32_t panels = (a->w.tiles + kPanelTiles - 1) / kPanelTiles;
-    const uint64_t C = (uint64_t)panels * a->w.kunits;  // k-columns
-    if (C == 0) return false;
-    pl.panels = panels;
+    const uint32_t T = a->w.tiles;
+    if (T == 0 || a->w.kunits == 0) return false;
+    // one CTA per SM, whole tiles per CTA
+    int grid = a->grid > 0 ? a->grid : sm_count();
+    if ((uint32_t)grid > T) grid = (int)T;
+    if (grid < 1) grid = 1;
+    if ((uint64_t)T * (uint64_t)grid >= (1ull << 32)) return false;  // 32-bit index arithmetic in the kernel
+    if ((uint64_t)T * a->w.kunits >= (1ull << 32)) return false;
+    pl.grid = grid;
+    const uint32_t per_cta = (T + grid - 1) / grid;
     // shared memory: mbarriers | stage ring | digit planes | per-warp tile
-    // buffers | misc; the ring takes what the rest leaves, up to kMaxStages
+    // buffers | per-warp tile sums of a round | misc. Prefer kPreferStages ring
+    // stages, then as many tiles per round as fit (rounds of fewer tiles add a CTA
+    // barrier each), then the ring takes what is left, up to kMaxStages.
     const uint32_t xdig = a->w.kunits * a->batch * 3 * KW;
     const uint32_t tbuf = kWarps * 16 * a->batch * 4;
     const uint32_t misc = (kMaxItems * kWarps * 2 + kMaxItems) * 4 + kMaxItems * 8;
-    const uint32_t fixed = 2 * kMaxStages * 8 + 128 + xdig + 128 + tbuf + 16 + misc;
-    const uint32_t per_stage = kStageUnits * UB;
+    const uint32_t fixed = 2 * kMaxStages * 8 + 128 + xdig + 128 + tbuf + 16 + misc + 16;
+    const uint32_t per_tile = kWarps * 16 * a->batch * 4;
+    const uint32_t stage = kStageUnits * UB;
     const uint32_t limit = 227u * 1024u;
-    if (fixed + 2 * per_stage > limit) return false;
-    uint32_t ns = (limit - fixed) / per_stage;
+    if (fixed + 2 * stage + per_tile > limit) return false;
+    uint32_t rt = 0;
+    for (uint32_t want = kPreferStages; want >= 2 && rt == 0; --want)
+        if (fixed + want * stage + per_tile <= limit) rt = (limit - fixed - want * stage) / per_tile;
+    if (rt > per_cta) rt = per_cta;
+    if (rt < 1) rt = 1;
+    uint32_t ns = (limit - fixed - rt * per_tile) / stage;
     if (ns > kMaxStages) ns = kMaxStages;
+    pl.round_tiles = rt;
     pl.stages = ns;
     uint32_t off = 2 * kMaxStages * 8;
     off = (off + 127) & ~127u;
     pl.off_ring = off;
-    off += ns * kStageUnits * UB;
+    off += ns * stage;
     pl.off_xdig = off;
     off += xdig;
     off = (off + 127) & ~127u;
     pl.off_tile = off;
     off += tbuf;
+    pl.off_parts = off;
+    off += rt * per_tile;
     off = (off + 15) & ~15u;
     pl.off_misc = off;
     off += misc;
     pl.smem = off;
-    // one CTA per SM, at least one k-column per CTA
-    int grid = a->grid > 0 ? a->grid : sm_count();
-    if ((uint64_t)grid > C) grid = (int)C;
-    if (grid < 1) grid = 1;
-    if (C * (uint64_t)grid >= (1ull << 32)) return false;  // 32-bit index arithmetic in the kernel
-    pl.grid = grid;
-    // CTAs sharing one panel: each holds at least minc of its kunits columns
-    const uint64_t minc = C / (uint64_t)grid;
-    uint64_t maxseg = (a->w.kunits + minc - 1) / minc + 1;
-    if (maxseg > a->w.kunits) maxseg = a->w.kunits;
-    pl.maxseg = (uint32_t)maxseg;
-    pl.partial_bytes = (size_t)panels * kPanelTiles * maxseg * 16 * a->batch * sizeof(float);
-    pl.partial_bytes = (pl.partial_bytes + 255) & ~(size_t)255;
-    pl.counter_len = panels * kPanelTiles;
+    // no partial sums leave the CTA: the scratch and counters of the ABI are
+    // not used (a minimal size keeps callers that allocate them working)
+    pl.partial_bytes = 256;
+    pl.counter_len = 1;
     return true;
 }
 
@@ -240,7 +248,7 @@ void gemv_params(const b2_gemv_args *a, const GemvPlan &pl, GemvParams &p)
     p.cols = w.cols;
     p.tiles = w.tiles;
     p.kunits = w.kunits;
-    p.panels = pl.panels;
+    p.round_tiles = pl.round_tiles;
     p.batch = a->batch;
     p.x = a->x;
     p.x_stride = a->x_stride;
@@ -256,9 +264,6 @@ void gemv_params(const b2_gemv_args *a, const GemvPlan &pl, GemvParams &p)
     p.positions = a->positions;
     p.kv = a->kv;
     p.argmax = a->argmax;
-    p.partial = (float *)a->scratch;
-    p.counters = (int *)a->counters;
-    p.maxseg = pl.maxseg;
     p.tp = a->tp;
     p.grid = (uint32_t)pl.grid;
     p.err = a->err;
@@ -266,6 +271,7 @@ void gemv_params(const b2_gemv_args *a, const GemvPlan &pl, GemvParams &p)
     p.stages = pl.stages;
     p.off_xdig = pl.off_xdig;
     p.off_tile = pl.off_tile;
+    p.off_parts = pl.off_parts;
     p.off_misc = pl.off_misc;
 }
 
@@ -373,9 +379,12 @@ extern "C" int b2_gemv_noalloc(const b2_gemv_args *a, void *stream)
     b2_gemv_args c = *a;
     c.scratch = nullptr;
     c.counters = nullptr;
-    const size_t need = b2_gemv_scratch_bytes(&c);
-    const uint32_t ncnt = b2_gemv_counters_len(&c);
-    if (need == 0 || ncnt == 0) return -1;
+    const int rc = gemv_check(&c);
+    if (rc != 0 && c.x != nullptr) return rc;
+    GemvPlan pl;
+    if (c.batch == 0 || !plan_gemv(&c, pl)) return rc != 0 ? rc : -9;
+    const size_t need = pl.partial_bytes;
+    const uint32_t ncnt = pl.counter_len;
     const size_t cnt_bytes = ((size_t)ncnt * sizeof(int32_t) + 255) & ~(size_t)255;
     if (cnt_bytes + need > (size_t)B2_NOALLOC_SCRATCH_BYTES) return -9;
     c.counters = reinterpret_cast<int32_t *>(base);

@@ -16,18 +16,17 @@ namespace b2 {
 constexpr int kWarps = 16;                          // consumer warps (16 hide the math latency)
 constexpr int kConsumers = kWarps * 32;
 constexpr int kThreads = kConsumers + 32;           // + one producer warp
-constexpr int kPanelTiles = 16;                     // tiles per panel: one per consumer warp
-constexpr int kStageCols = 4;                       // k-columns per stage
-constexpr int kStageUnits = kStageCols * kPanelTiles;  // 64 units: 40 KB of q4, one bulk copy
+constexpr int kStageUnits = 64;                     // units per stage: 40 KB of q4, one bulk copy
 constexpr int kMaxStages = 8;                       // ring depth, chosen per launch
+constexpr uint32_t kPreferStages = 5;               // ring depth kept before tile sums get more room
 constexpr int kMaxItems = 16;
 constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
-static_assert(kPanelTiles == kWarps, "each consumer warp owns one tile of a panel");
 
 struct GemvParams {
     const uint8_t *data;
     const float *row_scale;
-    uint32_t rows, cols, tiles, kunits, panels;
+    uint32_t rows, cols, tiles, kunits;
+    uint32_t round_tiles;  // tiles reduced together in shared memory (a round)
     uint32_t batch;
     const float *x;
     uint32_t x_stride;
@@ -42,14 +41,11 @@ struct GemvParams {
     const int32_t *positions;
     b2_kv_layout kv;
     unsigned long long *argmax;
-    float *partial;
-    int *counters;
-    uint32_t maxseg;
     uint32_t grid;  // CTAs taking part (the first `grid` CTAs of the launch)
     int32_t *err;
     b2_tp tp;       // tensor-parallel exchange (world <= 1: none)
     // shared-memory carve-up (bytes)
-    uint32_t off_ring, off_xdig, off_tile, off_misc, stages;
+    uint32_t off_ring, off_xdig, off_tile, off_parts, off_misc, stages;
 };
 
 __device__ __forceinline__ bool tp_in(const GemvParams &p) { return p.tp.world > 1 && p.tp.in_point != B2_TP_NONE; }
@@ -390,32 +386,40 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t *bar)
 }
 
 
-// The stage sequence of a CTA over its k-columns (a k-column is the 16 units
-// of one k-unit of a panel, contiguous in memory): stage i covers columns
-// [u, u + n) with n = min(kStageCols, end of the CTA range, end of the panel).
+// Tiles of at least kSplitStageUnits units end a stage (a stage then holds
+// one tile's units); narrower tiles share stages.
+constexpr uint32_t kSplitStageUnits = 16;
+
+// The stage sequence of a CTA over its units (whole tiles [t0, t1), each
+// tile's k-units contiguous): stage i covers units [u, u + n) with
+// n = min(kStageUnits, end of the current round of round-tiles tiles, end of
+// the tile when tiles are at least kSplitStageUnits units).
 struct StageWalk {
-    uint32_t u, ce, pend;
-    uint32_t panel, kunits;
-    __device__ StageWalk(uint32_t cb, uint32_t ce_, uint32_t kunits_) : u(cb), ce(ce_), kunits(kunits_)
+    uint32_t u, ce, rend, kunits, rtiles, tend;
+    __device__ StageWalk(uint32_t t0, uint32_t t1, uint32_t kunits_, uint32_t rtiles_)
+        : u(t0 * kunits_), ce(t1 * kunits_), kunits(kunits_), rtiles(rtiles_)
     {
-        panel = cb / kunits_;
-        pend = (panel + 1) * kunits_;
+        rend = min(t1, t0 + rtiles_) * kunits_;
+        tend = u + kunits_;
     }
     __device__ bool more() const { return u < ce; }
     __device__ uint32_t n() const
     {
-        uint32_t e = u + kStageCols;
-        if (e > ce) e = ce;
-        if (e > pend) e = pend;
+        uint32_t e = u + kStageUnits;
+        if (e > rend) e = rend;
+        if (kunits >= kSplitStageUnits && e > tend) e = tend;
         return e - u;
     }
-    __device__ void advance(uint32_t n)
+    // advance; true at the end of a round
+    __device__ bool advance(uint32_t n)
     {
         u += n;
-        if (u == pend) {
-            ++panel;
-            pend += kunits;
+        if (u == tend) tend += kunits;
+        if (u == rend) {
+            rend = min(ce, rend + rtiles * kunits);
+            return true;
         }
+        return false;
     }
 };
 
@@ -424,6 +428,7 @@ struct GemvSmem {
     uint64_t *full, *empty;
     uint8_t *ring, *xdig;
     float *tbufs, *red, *item_scale;
+    float *parts;  // [round tiles][kWarps][16 * batch] per-warp tile sums
     unsigned long long *cta_key;
     uint32_t stages;
 };
@@ -436,6 +441,7 @@ __device__ __forceinline__ GemvSmem gemv_smem(uint8_t *smem, const GemvParams &p
     s.ring = smem + p.off_ring;
     s.xdig = smem + p.off_xdig;
     s.tbufs = reinterpret_cast<float *>(smem + p.off_tile);   // [kWarps][16*B]
+    s.parts = reinterpret_cast<float *>(smem + p.off_parts);  // [round_tiles][kWarps][16*B]
     s.red = reinterpret_cast<float *>(smem + p.off_misc);     // [kMaxItems][kWarps][2]
     s.item_scale = s.red + kMaxItems * kWarps * 2;            // [kMaxItems]
     s.cta_key = reinterpret_cast<unsigned long long *>(s.item_scale + kMaxItems);
@@ -454,18 +460,18 @@ __device__ __forceinline__ void gemv_init_barriers(const GemvSmem &s)
     fence_mbar_init();
 }
 
-// The CTA's k-columns [cb, ce): the first p.grid CTAs split the columns
-// (the host guarantees p.grid <= C and C * p.grid < 2^32), any further CTAs
-// of a larger launch get an empty range.
-__device__ __forceinline__ void cta_range(const GemvParams &p, uint32_t &cb, uint32_t &ce)
+// The CTA's tiles [t0, t1): the first p.grid CTAs split the tiles (the
+// host guarantees p.grid <= tiles and tiles * p.grid < 2^32), any further
+// CTAs of a larger launch get none.
+__device__ __forceinline__ void cta_range(const GemvParams &p, uint32_t &t0, uint32_t &t1)
 {
-    const uint32_t C = p.panels * p.kunits, G = p.grid;
+    const uint32_t T = p.tiles, G = p.grid;
     if (blockIdx.x >= G) {
-        cb = ce = 0;
+        t0 = t1 = 0;
         return;
     }
-    cb = blockIdx.x * C / G;
-    ce = (blockIdx.x + 1) * C / G;
+    t0 = blockIdx.x * T / G;
+    t1 = (blockIdx.x + 1) * T / G;
 }
 
 // Producer warp: copy this CTA's stages of one GEMV into the ring. `i` counts
@@ -476,11 +482,11 @@ template <int FMT>
 __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &waited)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
-    constexpr uint32_t CB = kPanelTiles * UB;  // bytes of one k-column
     const int lane = threadIdx.x & 31;
-    uint32_t cb, ce;
-    cta_range(p, cb, ce);
-    StageWalk sw(cb, ce, p.kunits);
+    uint32_t t0, t1;
+    cta_range(p, t0, t1);
+    if (t0 == t1) return true;
+    StageWalk sw(t0, t1, p.kunits, p.round_tiles);
     for (; sw.more(); ++i) {
         const uint32_t slot = i % s.stages, n = sw.n();
         if (i >= s.stages) {
@@ -492,8 +498,8 @@ __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i
             if (!mbar_wait_bounded(&s.empty[slot], ((i / s.stages) - 1) & 1u, p.err)) return false;
         }
         if (lane == 0) {
-            mbar_arrive_expect_tx(&s.full[slot], n * CB);
-            bulk_g2s(s.ring + (size_t)slot * kStageUnits * UB, p.data + (size_t)sw.u * CB, n * CB, &s.full[slot]);
+            mbar_arrive_expect_tx(&s.full[slot], n * UB);
+            bulk_g2s(s.ring + (size_t)slot * kStageUnits * UB, p.data + (size_t)sw.u * UB, n * UB, &s.full[slot]);
         }
         __syncwarp();
         sw.advance(n);
@@ -502,9 +508,13 @@ __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i
 }
 
 // Consumer warps (all kWarps of them): prologue, the CTA's stages of one GEMV
-// (ring position `i`, shared with the producer's count), tile epilogues and
-// cross-CTA completion. `dead` (a wait timed out) keeps the stage protocol
-// but skips the math and the stores.
+// (ring position `i`, shared with the producer's count), per-tile sums and
+// epilogues. Warp w multiplies units w, w + kWarps, ... of every stage and
+// keeps one tile's sums in registers; when its units move to the next tile it
+// stores them in its slot of the round's per-warp tile sums. At the end of a
+// round (round_tiles tiles) the warps add the slots of each tile in warp
+// order (deterministic) and run the tile epilogues, one warp per tile. `dead`
+// (a wait timed out) keeps the stage protocol but skips the math and stores.
 template <int FMT, int NI>
 __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &dead)
 {
@@ -512,13 +522,14 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
     constexpr uint32_t KW = Fmt<FMT>::kKW;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const uint32_t B = p.batch;
+    const uint32_t B = p.batch, K = p.kunits, SB = 16 * B;
     const uint32_t NS = s.stages;
-    uint32_t cb, ce;
-    cta_range(p, cb, ce);
-    if (cb == ce) return;  // no columns for this CTA
-    const uint32_t C = p.panels * p.kunits, G = p.grid;
+    uint32_t t0, t1;
+    cta_range(p, t0, t1);
+    if (t0 == t1) return;  // no tiles for this CTA
     if (threadIdx.x < kMaxItems) s.cta_key[threadIdx.x] = 0ull;
+    const uint32_t parts_n = p.round_tiles * kWarps * SB;
+    for (uint32_t k = threadIdx.x; k < parts_n; k += kConsumers) s.parts[k] = 0.0f;
     prepare_x<FMT>(p, s.xdig, s.item_scale, s.red);
     consumer_sync();
 
@@ -530,23 +541,68 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
         acc[j][0] = acc[j][1] = 0.0f;
         iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
     }
-    float *mytbuf = s.tbufs + (size_t)warp * 16 * B;
+    float *mytbuf = s.tbufs + (size_t)warp * SB;
+    uint32_t round_t0 = t0;       // first tile of the current round
+    uint32_t cur = 0xFFFFFFFFu;   // tile whose sums this warp holds
 
-    StageWalk sw(cb, ce, p.kunits);
+    // store this warp's sums of tile `cur` into its slot and clear them
+    auto flush = [&]() {
+#pragma unroll
+        for (int j = 0; j < NI; ++j) {
+            float v0, v1;
+            if (FMT == 4) {
+                v0 = acc[j][0];
+                v1 = acc[j][1];
+            } else {
+                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
+                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
+            }
+            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
+            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
+            const uint32_t item = 2 * j + (t >> 1);
+            if ((t & 1) == 0 && item < B && cur != 0xFFFFFFFFu) {
+                float *slot = s.parts + ((size_t)(cur - round_t0) * kWarps + warp) * SB;
+                const float sc_item = s.item_scale[item];
+                slot[g * B + item] = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), sc_item);
+                slot[(g + 8) * B + item] = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), sc_item);
+            }
+            acc[j][0] = acc[j][1] = 0.0f;
+            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
+        }
+    };
+
+    StageWalk sw(t0, t1, K, p.round_tiles);
     for (; sw.more(); ++i) {
         const uint32_t slot = i % NS, n = sw.n();
-        const uint32_t ku0 = sw.u - sw.panel * p.kunits;
+        const uint32_t tile0 = sw.u / K, ku0 = sw.u - tile0 * K;
+        const bool one_tile = K >= kSplitStageUnits;  // the stage holds units of tile0 only
         if (!dead) {
             const bool got = mbar_wait_bounded(&s.full[slot], (i / NS) & 1u, p.err);
             dead = !__all_sync(0xffffffffu, got);
         }
+        if (one_tile && tile0 != cur && (uint32_t)warp < n) {
+            flush();
+            cur = tile0;
+        }
         if (!dead) {
             const uint8_t *stage = s.ring + (size_t)slot * kStageUnits * UB;
 #pragma unroll
-            for (int m = 0; m < kStageCols; ++m) {
-                if ((uint32_t)m < n) {
-                    const uint8_t *unit = stage + ((size_t)m * kPanelTiles + warp) * UB;
-                    const uint32_t ku = ku0 + m;
+            for (int m = 0; m < kStageUnits / kWarps; ++m) {
+                const uint32_t k = warp + m * kWarps;
+                if (k < n) {
+                    uint32_t ku = ku0 + k;
+                    if (!one_tile) {
+                        uint32_t tile = tile0;
+                        while (ku >= K) {
+                            ku -= K;
+                            ++tile;
+                        }
+                        if (tile != cur) {
+                            flush();
+                            cur = tile;
+                        }
+                    }
+                    const uint8_t *unit = stage + (size_t)k * UB;
                     const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
                     if (FMT == 4) {
                         const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
@@ -583,82 +639,43 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.empty[slot]);
+        if (!sw.advance(n)) continue;
 
-        const uint32_t panel = sw.panel;
-        const uint32_t pfirst = panel * p.kunits, pend = sw.pend;
-        sw.advance(n);
-        if (sw.u != pend && sw.u != ce) continue;
-
-        // ---- end of this CTA's part of the panel: this warp's tile is complete
-        // over the CTA's columns; no other warp holds a share of it
-        const uint32_t tile = panel * kPanelTiles + warp;
-#pragma unroll
-        for (int j = 0; j < NI; ++j) {
-            float v0, v1;
-            if (FMT == 4) {
-                v0 = acc[j][0];
-                v1 = acc[j][1];
-            } else {
-                v0 = __fadd_rn((float)iacc[j][0], __fmul_rn(256.0f, (float)iacc[j][1]));
-                v1 = __fadd_rn((float)iacc[j][2], __fmul_rn(256.0f, (float)iacc[j][3]));
-            }
-            const float h0 = __shfl_down_sync(0xffffffffu, v0, 1);
-            const float h1 = __shfl_down_sync(0xffffffffu, v1, 1);
-            const uint32_t item = 2 * j + (t >> 1);
-            if ((t & 1) == 0 && item < B) {
-                const float sc_item = s.item_scale[item];
-                float y0 = __fmul_rn(__fadd_rn(v0, __fmul_rn(65536.0f, h0)), sc_item);
-                float y1 = __fmul_rn(__fadd_rn(v1, __fmul_rn(65536.0f, h1)), sc_item);
-                if (FMT == 8) {
-                    const uint32_t r0 = tile * 16 + g, r1 = r0 + 8;
-                    y0 = __fmul_rn(y0, r0 < p.rows ? p.row_scale[r0] : 0.0f);
-                    y1 = __fmul_rn(y1, r1 < p.rows ? p.row_scale[r1] : 0.0f);
-                }
-                mytbuf[g * B + item] = y0;
-                mytbuf[(g + 8) * B + item] = y1;
-            }
-            acc[j][0] = acc[j][1] = 0.0f;
-            iacc[j][0] = iacc[j][1] = iacc[j][2] = iacc[j][3] = 0;
-        }
-        __syncwarp();
-        if (!(pfirst >= cb && pend <= ce)) {
-            // the panel is shared with neighbouring CTAs: the last CTA to finish
-            // the tile adds all segments in CTA order
-            const uint32_t cf = ((pfirst + 1) * G - 1) / C, cl = (pend * G - 1) / C;
-            const uint32_t nseg = cl - cf + 1;
-            float *pb = p.partial + (size_t)tile * p.maxseg * 16 * B;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) pb[(blockIdx.x - cf) * 16 * B + idx] = mytbuf[idx];
-            // one fence per warp: __syncwarp orders the lanes' stores before
-            // lane 0's release, and lane 0's acquire before the lanes' loads
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) {
-                __threadfence();
-                last = (atomicAdd(&p.counters[tile], 1) == (int)nseg - 1);
-                if (last) __threadfence();
-            }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            __syncwarp();
-            if (!last) continue;
-            for (uint32_t idx = lane; idx < 16 * B; idx += 32) {
+        // ---- end of a round: the warps' tile sums are complete
+        flush();
+        cur = 0xFFFFFFFFu;
+        consumer_sync();
+        const uint32_t round_t1 = min(t1, round_t0 + p.round_tiles);
+        for (uint32_t tile = round_t0 + warp; tile < round_t1; tile += kWarps) {
+            const float *sl = s.parts + (size_t)(tile - round_t0) * kWarps * SB;
+            for (uint32_t idx = lane; idx < SB; idx += 32) {
                 float sum = 0.0f;
-                for (uint32_t sg = 0; sg < nseg; ++sg) sum = __fadd_rn(sum, ld_cg(pb + (size_t)sg * 16 * B + idx));
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) sum = __fadd_rn(sum, sl[w * SB + idx]);
+                if (FMT == 8) {
+                    const uint32_t row = tile * 16 + idx / B;
+                    sum = __fmul_rn(sum, row < p.rows ? p.row_scale[row] : 0.0f);
+                }
                 mytbuf[idx] = sum;
             }
-            if (lane == 0) p.counters[tile] = 0;
             __syncwarp();
-        }
-        if (!dead) tile_epilogue(p, tile, mytbuf, s.cta_key, lane);
-        __syncwarp();
-        if (p.epilogue == B2_EPI_PUSH && lane == 0) {
-            // the last tile of the GEMV on this rank publishes the point
-            __threadfence_system();
-            if (atomicAdd(p.tp.done, 1) == (int)(p.panels * kPanelTiles) - 1) {
-                *p.tp.done = 0;
+            if (!dead) tile_epilogue(p, tile, mytbuf, s.cta_key, lane);
+            __syncwarp();
+            if (p.epilogue == B2_EPI_PUSH && lane == 0) {
+                // the last tile of the GEMV on this rank publishes the point
                 __threadfence_system();
-                tp_signal(p.tp, p.tp.out_point);
+                if (atomicAdd(p.tp.done, 1) == (int)p.tiles - 1) {
+                    *p.tp.done = 0;
+                    __threadfence_system();
+                    tp_signal(p.tp, p.tp.out_point);
+                }
             }
         }
+        consumer_sync();
+        for (uint32_t k = threadIdx.x; k < parts_n; k += kConsumers) s.parts[k] = 0.0f;
+        round_t0 = round_t1;
+        // the next round's slots are cleared before any warp stores into them
+        consumer_sync();
     }
     if (p.epilogue == B2_EPI_LOGITS) {
         consumer_sync();
@@ -686,10 +703,10 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
 // ---- host side (b2_gemv.cu) -------------------------------------------------------
 struct GemvPlan {
     int grid;
-    uint32_t maxseg;
-    size_t partial_bytes;
-    uint32_t counter_len;
-    uint32_t smem, off_ring, off_xdig, off_tile, off_misc, stages, panels;
+    size_t partial_bytes;   // scratch the caller provides (unused by the kernel; kept for the ABI)
+    uint32_t counter_len;   // counters the caller provides (likewise)
+    uint32_t round_tiles;
+    uint32_t smem, off_ring, off_xdig, off_tile, off_parts, off_misc, stages;
 };
 
 // Argument checks of b2_gemv (0 or a negative status).

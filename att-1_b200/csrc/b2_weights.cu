@@ -34,11 +34,10 @@ __device__ __forceinline__ uint32_t dev_row(int map, uint32_t which, uint32_t sr
     return src_row;
 }
 
-// Index of unit (tile, k-unit): panels of 16 tiles, k-unit-major inside a
-// panel, so the 16 units of one k-unit of a panel are contiguous.
+// Index of unit (tile, k-unit): tile-major, a tile's k-units contiguous.
 __device__ __forceinline__ size_t unit_index(uint32_t tile, uint32_t ku, uint32_t kunits)
 {
-    return ((size_t)(tile >> 4) * kunits + ku) * 16 + (tile & 15);
+    return (size_t)tile * kunits + ku;
 }
 
 // Byte offset of the nibble word for (device row, 32-col group, t) inside the
@@ -286,12 +285,12 @@ using namespace b2;
 
 extern "C" size_t b2_q4_bytes(uint32_t rows, uint32_t cols)
 {
-    return (size_t)ceil_div(ceil_div(rows, 16), 16) * 16 * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
+    return (size_t)ceil_div(rows, 16) * ceil_div(cols, 64) * B2_Q4_UNIT_BYTES;
 }
 
 extern "C" size_t b2_q8_bytes(uint32_t rows, uint32_t cols)
 {
-    return (size_t)ceil_div(ceil_div(rows, 16), 16) * 16 * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
+    return (size_t)ceil_div(rows, 16) * ceil_div(cols, 32) * B2_Q8_UNIT_BYTES;
 }
 
 static int check_launch()

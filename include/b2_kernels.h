@@ -32,12 +32,8 @@ extern "C" {
 /*
  * q4 "unit" layout: a matrix [rows][cols] is cut into 16-row tiles and
  * 64-column group pairs (two q4 groups of 32). Each (tile, pair) unit is 640
- * contiguous bytes. Tiles are grouped into panels of 16 (256 rows; the last
- * panel is padded with zero tiles) and units are ordered panel-major, then
- * by column pair, then by tile, so the 16 units of one column pair of a
- * panel (a "k-column", 10 KB) are contiguous:
- *   unit(tile, pair) = ((tile / 16) * pairs + pair) * 16 + tile % 16
- * Inside a unit:
+ * contiguous bytes, units ordered tile-major (a tile's column pairs are
+ * contiguous): unit(tile, pair) = tile * pairs + pair. Inside a unit:
  *   bytes [0,512):  32 lanes x 16 B; lane l = 4*r + t (r = row in tile mod 8)
  *                   holds words {row r g0, row r+8 g0, row r g1, row r+8 g1};
  *                   byte i of a word = nibble(col 4t+i) | nibble(col 16+4t+i)<<4
@@ -48,7 +44,7 @@ extern "C" {
  * permutation of the reference's nibbles (b2_q4_unpack inverts it).
  *
  * q8 unit layout: (16-row tile, 32-column block) units of 512 bytes in the
- * same panel order, lane l
+ * same tile-major order, lane l
  * holds 16 int8 {row r k 4t..4t+3, row r+8 k 4t.., row r k 16+4t.., row r+8
  * k 16+4t..}; one f32 scale per row in a separate array [tiles*16].
  */
@@ -198,11 +194,11 @@ typedef struct b2_gemv_args {
     b2_kv_layout kv;
     /* B2_EPI_LOGITS */
     unsigned long long *argmax;   /* [batch] packed (ordered value, ~index) keys */
-    /* scratch: partial sums of tiles split between warps (any contents) */
+    /* scratch and counters (b2_gemv_scratch_bytes / b2_gemv_counters_len):
+     * reserved; a CTA owns whole tiles, so partial sums stay in shared memory.
+     * Counters are zeroed once by the caller and left zero. */
     void *scratch;
     size_t scratch_bytes;
-    /* per-tile arrival counters: zeroed once by the caller, every launch
-     * leaves them zero again; may be shared by kernels that run in order */
     int32_t *counters;
     uint32_t counters_len;
     int32_t *err;                 /* device error word */
