@@ -661,17 +661,20 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
             __syncwarp();
             if (!dead) tile_epilogue(p, tile, mytbuf, s.cta_key, lane);
             __syncwarp();
-            if (p.epilogue == B2_EPI_PUSH && lane == 0) {
-                // the last tile of the GEMV on this rank publishes the point
-                __threadfence_system();
-                if (atomicAdd(p.tp.done, 1) == (int)p.tiles - 1) {
-                    *p.tp.done = 0;
-                    __threadfence_system();
-                    tp_signal(p.tp, p.tp.out_point);
-                }
-            }
         }
         consumer_sync();
+        if (p.epilogue == B2_EPI_PUSH && threadIdx.x == 0) {
+            // one system fence per CTA round (the barrier above orders every
+            // warp's peer stores before it); the last round of the GEMV on
+            // this rank publishes the point
+            __threadfence_system();
+            const int n_round = (int)(round_t1 - round_t0);
+            if (atomicAdd(p.tp.done, n_round) == (int)p.tiles - n_round) {
+                *p.tp.done = 0;
+                __threadfence_system();
+                tp_signal(p.tp, p.tp.out_point);
+            }
+        }
         for (uint32_t k = threadIdx.x; k < parts_n; k += kConsumers) s.parts[k] = 0.0f;
         round_t0 = round_t1;
         // the next round's slots are cleared before any warp stores into them
