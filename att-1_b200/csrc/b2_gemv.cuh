@@ -586,54 +586,62 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
         }
         if (!dead) {
             const uint8_t *stage = s.ring + (size_t)slot * kStageUnits * UB;
+            // one unit: weights and scales from the stage, digits of k-unit ku
+            auto unit_math = [&](uint32_t k, uint32_t ku) {
+                const uint8_t *unit = stage + (size_t)k * UB;
+                const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
+                if (FMT == 4) {
+                    const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
+                    const uint32_t M = 0xF0F0F0F0u;
+                    const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
+                    const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
 #pragma unroll
-            for (int m = 0; m < kStageUnits / kWarps; ++m) {
-                const uint32_t k = warp + m * kWarps;
-                if (k < n) {
-                    uint32_t ku = ku0 + k;
-                    if (!one_tile) {
-                        uint32_t tile = tile0;
-                        while (ku >= K) {
-                            ku -= K;
-                            ++tile;
-                        }
-                        if (tile != cur) {
-                            flush();
-                            cur = tile;
-                        }
+                    for (int j = 0; j < NI; ++j) {
+                        const uint32_t item = 2 * j + (g >> 2);
+                        uint4 bf = make_uint4(0, 0, 0, 0);
+                        if (digit < 3 && item < B)
+                            bf = *reinterpret_cast<const uint4 *>(s.xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
+                        int d[4], e[4];
+                        imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
+                        imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
+                        acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
+                        acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
+                        acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
+                        acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
                     }
-                    const uint8_t *unit = stage + (size_t)k * UB;
-                    const uint4 wv = *reinterpret_cast<const uint4 *>(unit + lane * 16);
-                    if (FMT == 4) {
-                        const float4 sc = *reinterpret_cast<const float4 *>(unit + 512 + g * 16);
-                        const uint32_t M = 0xF0F0F0F0u;
-                        const uint32_t a00 = (wv.x << 4) & M, a01 = (wv.y << 4) & M, a02 = wv.x & M, a03 = wv.y & M;
-                        const uint32_t a10 = (wv.z << 4) & M, a11 = (wv.w << 4) & M, a12 = wv.z & M, a13 = wv.w & M;
+                } else {
 #pragma unroll
-                        for (int j = 0; j < NI; ++j) {
-                            const uint32_t item = 2 * j + (g >> 2);
-                            uint4 bf = make_uint4(0, 0, 0, 0);
-                            if (digit < 3 && item < B)
-                                bf = *reinterpret_cast<const uint4 *>(s.xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 16);
-                            int d[4], e[4];
-                            imma_16832(d, a00, a01, a02, a03, bf.x, bf.y, 0, 0, 0, 0);
-                            imma_16832(e, a10, a11, a12, a13, bf.z, bf.w, 0, 0, 0, 0);
-                            acc[j][0] = fmaf((float)(d[0] + 256 * d[1]), sc.x, acc[j][0]);
-                            acc[j][1] = fmaf((float)(d[2] + 256 * d[3]), sc.z, acc[j][1]);
-                            acc[j][0] = fmaf((float)(e[0] + 256 * e[1]), sc.y, acc[j][0]);
-                            acc[j][1] = fmaf((float)(e[2] + 256 * e[3]), sc.w, acc[j][1]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < NI; ++j) {
-                            const uint32_t item = 2 * j + (g >> 2);
-                            uint2 bf = make_uint2(0, 0);
-                            if (digit < 3 && item < B)
-                                bf = *reinterpret_cast<const uint2 *>(s.xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
-                            imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
-                                       iacc[j][3]);
-                        }
+                    for (int j = 0; j < NI; ++j) {
+                        const uint32_t item = 2 * j + (g >> 2);
+                        uint2 bf = make_uint2(0, 0);
+                        if (digit < 3 && item < B)
+                            bf = *reinterpret_cast<const uint2 *>(s.xdig + ((size_t)(ku * B + item) * 3 + digit) * KW + t * 8);
+                        imma_16832(iacc[j], wv.x, wv.y, wv.z, wv.w, bf.x, bf.y, iacc[j][0], iacc[j][1], iacc[j][2],
+                                   iacc[j][3]);
                     }
+                }
+            };
+            if (one_tile) {
+#pragma unroll
+                for (int m = 0; m < kStageUnits / kWarps; ++m) {
+                    const uint32_t k = warp + m * kWarps;
+                    if (k < n) unit_math(k, ku0 + k);
+                }
+            } else {
+                // narrow tiles share the stage (small matrices): the tile of
+                // each unit, kept out of the unrolled hot loop above
+#pragma unroll 1
+                for (uint32_t k = warp; k < n; k += kWarps) {
+                    uint32_t tile = tile0, ku = ku0 + k;
+                    while (ku >= K) {
+                        ku -= K;
+                        ++tile;
+                    }
+                    if (tile != cur) {
+                        flush();
+                        cur = tile;
+                    }
+                    unit_math(k, ku);
                 }
             }
         }

@@ -211,6 +211,52 @@ def time_dominant_gemv(b2, torch, reps=30):
     return algo, ms
 
 
+def time_attention(b2, torch, reps=30, ctx=4096, layers=8):
+    """Single-query attention of the 8B shape at context `ctx`: 8 layers of KV
+    pools (268 MB at 4096, larger than L2) used in turn, back-to-back launches."""
+    import ctypes as C
+    L = b2.lib()
+    H, HKV = SHAPE["n_heads"], SHAPE["n_kv_heads"]
+    hd = SHAPE["d_model"] // H
+    pt = 64
+    pages = (ctx + pt - 1) // pt
+    kp = [torch.randn(pages * HKV * pt * hd, device="cuda") * 0.1 for _ in range(layers)]
+    vp = [torch.randn(pages * HKV * pt * hd, device="cuda") for _ in range(layers)]
+    ptab = torch.arange(pages, dtype=torch.int32, device="cuda")
+    q = torch.randn(H * hd, device="cuda")
+    out = torch.zeros(H * hd, device="cuda")
+    pos = torch.tensor([ctx - 1], dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = []
+    for layer in range(layers):
+        a = b2.AttnArgs()
+        a.batch, a.n_heads, a.n_kv_heads, a.head_dim = 1, H, HKV, hd
+        a.q, a.ctx, a.positions, a.max_ctx, a.err = q.data_ptr(), out.data_ptr(), pos.data_ptr(), ctx, err.data_ptr()
+        a.kv = b2.KVLayout(kp[layer].data_ptr(), vp[layer].data_ptr(), ptab.data_ptr(), pt, pages, HKV, hd)
+        args.append(a)
+    need, ncnt = L.b2_attn_scratch_bytes(C.byref(args[0])), L.b2_attn_counters_len(C.byref(args[0]))
+    scr = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    cnt = torch.zeros(ncnt, dtype=torch.int32, device="cuda")
+    for a in args:
+        a.scratch, a.scratch_bytes, a.counters, a.counters_len = scr.data_ptr(), need, cnt.data_ptr(), ncnt
+    stream = torch.cuda.Stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(8):
+            assert L.b2_attn(C.byref(args[i % layers]), sp) == 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            L.b2_attn(C.byref(args[i % layers]), sp)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ms = e0.elapsed_time(e1) / reps
+    algo = 2 * HKV * ctx * hd * 4 + 2 * H * hd * 4
+    return algo, ms
+
+
 def load_traffic():
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -384,8 +430,8 @@ def main():
                     help="with several GPUs: independent replicas instead of one tensor-parallel model")
     ap.add_argument("--persistent", action="store_true",
                     help="run each step as one persistent launch instead of the per-operation kernel sequence")
-    ap.add_argument("--kernel-only", action="store_true",
-                    help="time only the dominant GEMV (gate/up shape) and print it (for ncu captures)")
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "attn"],
+                    help="time only one kernel and print it (for ncu captures): the gate/up GEMV (default) or the attention at context 4096")
     ap.add_argument("--layers", type=int, default=SHAPE["n_layers"],
                     help="decoder depth (profiling runs only; the metric is defined at 32)")
     args = ap.parse_args()
@@ -397,8 +443,13 @@ def main():
         import torch
         import att1_b200 as b2
         torch.cuda.set_device(local_rank)
-        algo, kms = time_dominant_gemv(b2, torch, reps=args.steps)
-        print(json.dumps({"kernel": "gemv_q4 gate/up 28672x4096", "launch_ms": kms,
+        if args.kernel_only == "attn":
+            algo, kms = time_attention(b2, torch, reps=args.steps)
+            name = "attention 8B shape, context 4096 (32 query / 8 KV heads, hd 128)"
+        else:
+            algo, kms = time_dominant_gemv(b2, torch, reps=args.steps)
+            name = "gemv_q4 gate/up 28672x4096"
+        print(json.dumps({"kernel": name, "launch_ms": kms,
                           "algorithmic_bytes": algo, "GB/s": algo / (kms * 1e-3) / 1e9}), flush=True)
         return
     out = run_reference(args, rank) if args.impl == "reference" else run_b200(args, rank, world, local_rank)
