@@ -78,6 +78,14 @@ class GemvArgs(C.Structure):
                 ("tp", TpArgs)]
 
 
+class GemmArgs(C.Structure):
+    """b2_gemm_args (include/b2_kernels.h): dequant GEMM on the tensor cores."""
+    _fields_ = [("w", QWeight), ("xs", C.c_void_p), ("m", C.c_uint32), ("epilogue", C.c_uint32),
+                ("out", C.c_void_p), ("out_stride", C.c_uint32), ("resid", C.c_void_p),
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("splits", C.c_uint32),
+                ("err", C.c_void_p), ("pdl", C.c_int)]
+
+
 class AttnArgs(C.Structure):
     _fields_ = [("batch", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
                 ("head_dim", C.c_uint32), ("q", C.c_void_p), ("kv", KVLayout),
@@ -149,6 +157,7 @@ _SIGS = {
     "att1_b200_infer_create_model": (C.c_int, [C.POINTER(Model), _U32, _F, _F, _F, C.POINTER(_P)]),
     "att1_b200_infer_batch": (_U32, [_P]),
     "att1_b200_infer_decode_batch": (C.c_int, [_P, C.POINTER(_U32), C.POINTER(_U32)]),
+    "att1_b200_infer_prefill": (C.c_int, [_P, C.POINTER(_U32), _SZ, C.POINTER(_U32)]),
     "att1_b200_infer_logits_batch": (C.POINTER(_F), [_P, C.POINTER(_SZ)]),
     "att1_b200_infer_set_options": (C.c_int, [_P, C.c_int, C.c_int]),
     "att1_b200_infer_set_persistent": (C.c_int, [_P, C.c_int]),
@@ -192,6 +201,10 @@ _SIGS = {
     "b2_attn_counters_len": (_U32, [C.POINTER(AttnArgs)]),
     "b2_gemv": (C.c_int, [C.POINTER(GemvArgs), _P]),
     "b2_gemv_noalloc": (C.c_int, [C.POINTER(GemvArgs), _P]),
+    "b2_gemm_xs_bytes": (_SZ, [_U32, _U32]),
+    "b2_gemm_prep": (C.c_int, [_P, _U32, _U32, _U32, _P, _F, _P, _P, _P]),
+    "b2_gemm_scratch_bytes": (_SZ, [C.POINTER(GemmArgs)]),
+    "b2_gemm": (C.c_int, [C.POINTER(GemmArgs), _P]),
     "b2_attn_scratch_bytes": (_SZ, [C.POINTER(AttnArgs)]),
     "b2_attn": (C.c_int, [C.POINTER(AttnArgs), _P]),
     "b2_rmsnorm": (C.c_int, [_P, _P, _P, _U32, _F, _P]),
@@ -304,6 +317,22 @@ class Infer:
     def decode(self, token: int) -> int:
         out = C.c_uint32(0)
         check("att1_infer_decode_token", lib().att1_infer_decode_token(self.h, int(token), C.byref(out)))
+        return int(out.value)
+
+    def generate(self, prompt: bytes, count: int) -> np.ndarray:
+        """att1_infer_generate: greedy continuation of a byte prompt."""
+        out = (C.c_uint32 * max(count, 1))()
+        n = C.c_size_t(0)
+        check("att1_infer_generate", lib().att1_infer_generate(self.h, bytes(prompt), len(prompt), count, out,
+                                                                 count, C.byref(n)))
+        return np.array(out[:n.value], np.uint32)
+
+    def prefill(self, tokens) -> int:
+        """att1_b200_infer_prefill: the prompt in one pass; returns the greedy next token."""
+        ids = np.ascontiguousarray(np.asarray(tokens, np.uint32))
+        out = C.c_uint32(0)
+        check("att1_b200_infer_prefill", lib().att1_b200_infer_prefill(
+            self.h, ids.ctypes.data_as(C.POINTER(C.c_uint32)), ids.size, C.byref(out)))
         return int(out.value)
 
     def decode_batch(self, tokens) -> np.ndarray:

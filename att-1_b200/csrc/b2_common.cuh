@@ -23,6 +23,15 @@ __device__ __forceinline__ void raise_error(int32_t *err, int32_t bit)
     if (err != nullptr) atomicOr(err, bit);
 }
 
+// Greedy-sampler key of a logit: the float's order as an unsigned integer
+// (-0 and +0 equal); the high word of an argmax key whose low word is
+// 0xFFFFFFFF - id, so the largest key is the largest logit with the lowest id.
+__device__ __forceinline__ uint32_t ordered_key(float f)
+{
+    uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // ---- shared-memory addressing --------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
 {

@@ -1,0 +1,617 @@
+// b2_gemm.cu - q4/q8 dequant GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Replaces att1_matmul_q4xf32 (src/quant.c:340-393) and att1_matmul_q8xf32
+// (src/matmul_q8.c:3-40) when many input rows share one pass over the weights:
+// prompt prefill (the reference feeds the prompt through the decode step one
+// token at a time, src/infer.c:905-912) and decode batches too large for the
+// GEMV's on-chip digit planes. Y[m][o] = sum_k X[m][k] * W[o][k].
+//
+// Precision. The reference accumulates f32 products x * (q * scale). Here every
+// f32 operand v is split into two bf16 numbers v = hi + lo (hi = bf16(v),
+// lo = bf16(v - hi), 16 significant bits together) and the product is
+//   x.w ~= x_hi w_hi + x_lo w_hi + x_hi w_lo     (q4: w = q * group scale)
+//   x.w ~= (x_hi q + x_lo q) * row scale          (q8: q is exact in bf16)
+// three (two) bf16 MMAs with f32 accumulation in tensor memory; the dropped
+// terms are below 2^-16 relative, the same order as the GEMV's 2^-22 fixed
+// point plus f32 summation, far inside the 1e-3 logits tolerance.
+//
+// Work split. CTA (row block, token tile, k split) computes a 128-row x BN-token
+// tile of Y over a range of 64-column k steps:
+//   warp 0      allocates tensor memory and streams the prepared X tile of each
+//               k step (b2_gemm_prep writes it in the MMA operand layout, so one
+//               1-D bulk copy per stage) into a ring of shared-memory stages;
+//   warp 1      one thread issues tcgen05.mma (M=128, N=BN, K=16) for every
+//               k step, then tcgen05.commit releases the stage;
+//   warps 2..5  read the weight units of the 8 row tiles with 16-byte loads
+//               (each lane's 16 bytes are one fixed set of 32 weights), scale,
+//               split into bf16 hi/lo and store them in the operand layout;
+//               after the k loop they read the accumulator out of tensor memory
+//               (warp w reads TMEM lanes 32*(w%4)..: one output row per thread)
+//               and write Y, or the split's partial sums.
+// Operands are K-major without swizzle: 8-row x 16-byte core matrices,
+// element (r, k) of a tile with R rows at byte
+//   (k / 8) * (R * 16) + (r / 8) * 128 + (r % 8) * 16 + (k % 8) * 2,
+// so the descriptor's stride between 8-row groups is 128 bytes and the
+// stride between 8-column chunks is R * 16 bytes.
+// Every wait is bounded and reports B2_ERR_TIMEOUT; tensor memory is freed by
+// the allocating warp after the whole CTA has passed the epilogue.
+#include "b2_common.cuh"
+
+#include <cuda_bf16.h>
+
+namespace b2 {
+
+constexpr uint32_t kGemmBM = 128;          // output rows per CTA (8 tiles of 16)
+constexpr uint32_t kGemmBK = 64;           // columns per k step
+constexpr uint32_t kGemmMaxBN = 256;       // tokens per CTA tile
+constexpr int kGemmThreads = 192;          // 6 warps
+constexpr uint32_t kGemmMaxStages = 4;
+constexpr uint32_t kGemmMaxSplits = 16;
+constexpr uint32_t kGemmSmemLimit = 227u * 1024u;
+
+__host__ __device__ constexpr uint32_t gemm_x_stage_bytes(uint32_t bn) { return bn * kGemmBK * 2 * 2; }
+__host__ __device__ constexpr uint32_t gemm_w_stage_bytes(uint32_t fmt)
+{
+    return kGemmBM * kGemmBK * 2 * (fmt == 4 ? 2 : 1);
+}
+
+// Token tiling shared by b2_gemm_prep and b2_gemm: as few tiles of at most
+// 256 tokens as possible, equal sizes rounded up to 16 (the MMA's N step).
+__host__ __device__ inline void gemm_token_tiles(uint32_t m, uint32_t &ntiles, uint32_t &bn)
+{
+    ntiles = (m + kGemmMaxBN - 1) / kGemmMaxBN;
+    if (ntiles == 0) ntiles = 1;
+    const uint32_t per = (m + ntiles - 1) / ntiles;
+    bn = (per + 15) / 16 * 16;
+    if (bn < 16) bn = 16;
+}
+
+struct GemmParams {
+    const uint8_t *w;
+    const float *row_scale;
+    uint32_t fmt, rows, cols, tiles, kunits;
+    uint32_t ksteps;        // ceil(cols / 64)
+    const uint8_t *xs;
+    uint32_t m, bn, ntiles;
+    float *out;
+    uint32_t out_stride;
+    const float *resid;
+    uint32_t epilogue;
+    float *part;            // [splits][m][rows] when splits > 1
+    uint32_t splits, ksplit;  // k steps per split
+    uint32_t stages;
+    uint32_t off_x, off_w, tmem_cols;
+    int32_t *err;
+};
+
+// ---- tcgen05 wrappers ------------------------------------------------------------
+
+// Shared-memory matrix descriptor: K-major, no swizzle (layout type 0),
+// version 1 (bits 46-47), base offset 0. Addresses and offsets in 16-byte units.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A and B bf16, both K-major,
+// N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(uint32_t m, uint32_t n)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05 operation issued so far by this thread is complete.
+__device__ __forceinline__ void umma_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t cols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// 32 lanes x 16 columns of 32 bits: thread i gets lane (base + i), columns col..col+15.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16])
+{
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- operand packing ----------------------------------------------------------------
+
+// bf16 hi/lo split of four consecutive values, packed as two bf16x2 words each.
+__device__ __forceinline__ void split4(const float (&v)[4], uint2 &hi, uint2 &lo)
+{
+    const __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+    const __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+    const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+    const __nv_bfloat162 l0 = __floats2bfloat162_rn(v[0] - f0.x, v[1] - f0.y);
+    const __nv_bfloat162 l1 = __floats2bfloat162_rn(v[2] - f1.x, v[3] - f1.y);
+    hi = make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+    lo = make_uint2(*reinterpret_cast<const uint32_t *>(&l0), *reinterpret_cast<const uint32_t *>(&l1));
+}
+
+// Byte offset of element (r, k) in a K-major core-matrix tile of R rows x 64 columns.
+__host__ __device__ __forceinline__ uint32_t op_off(uint32_t r, uint32_t k, uint32_t R)
+{
+    return (k >> 3) * (R * 16) + (r >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
+}
+
+// ---- X preparation: optional RMSNorm, bf16 hi/lo split, operand layout -------------------
+
+// One CTA per padded token row n (ntiles * bn rows; rows >= m are zero).
+// Output block (tile, k step) = [hi: bn x 64][lo: bn x 64] bf16 in op_off order.
+__global__ void __launch_bounds__(256) gemm_prep_kernel(const float *__restrict__ x, uint32_t x_stride, uint32_t m,
+                                                        uint32_t cols, const float *__restrict__ norm_w, float eps,
+                                                        uint32_t bn, uint32_t ksteps, uint8_t *__restrict__ xs,
+                                                        int32_t *err)
+{
+    __shared__ float red[32];
+    const uint32_t n = blockIdx.x;
+    const uint32_t tile = n / bn, nr = n % bn;
+    const bool live = n < m;
+    const float *row = x + (size_t)n * x_stride;
+    float inv = 1.0f;
+    if (norm_w != nullptr && live) {
+        float ss = 0.0f;
+        for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(row + k);
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+        ss = block_sum(ss, red);
+        inv = 1.0f / sqrtf(ss / (float)cols + eps);
+    }
+    const uint32_t xstage = gemm_x_stage_bytes(bn);
+    bool finite = true;
+    // each thread writes one 8-column chunk (16 bytes of hi, 16 of lo)
+    for (uint32_t c = threadIdx.x; c < ksteps * 8; c += blockDim.x) {
+        const uint32_t k0 = c * 8;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        if (live && k0 < cols) {  // cols % 32 == 0: a chunk is all in or all out
+            const float4 a = *reinterpret_cast<const float4 *>(row + k0);
+            const float4 b = *reinterpret_cast<const float4 *>(row + k0 + 4);
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+            if (norm_w != nullptr) {
+                const float4 wa = *reinterpret_cast<const float4 *>(norm_w + k0);
+                const float4 wb = *reinterpret_cast<const float4 *>(norm_w + k0 + 4);
+                const float w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * w8[i];
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) finite = finite && isfinite(v[i]);
+        }
+        uint2 h0, l0, h1, l1;
+        const float a4[4] = {v[0], v[1], v[2], v[3]}, b4[4] = {v[4], v[5], v[6], v[7]};
+        split4(a4, h0, l0);
+        split4(b4, h1, l1);
+        uint8_t *blk = xs + (size_t)(tile * ksteps + k0 / kGemmBK) * xstage;
+        const uint32_t off = op_off(nr, k0 % kGemmBK, bn);
+        *reinterpret_cast<uint4 *>(blk + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+        *reinterpret_cast<uint4 *>(blk + xstage / 2 + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+    }
+    if (!finite) raise_error(err, B2_ERR_NONFINITE);
+}
+
+// ---- the GEMM ----------------------------------------------------------------------------
+
+struct GemmSmem {
+    uint64_t *x_full, *w_full, *empty, *acc_full;
+    uint32_t *tmem_slot;
+    uint8_t *x, *w;
+};
+
+__device__ __forceinline__ GemmSmem gemm_smem(uint8_t *smem, const GemmParams &p)
+{
+    GemmSmem s;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    s.x_full = bars;
+    s.w_full = bars + kGemmMaxStages;
+    s.empty = bars + 2 * kGemmMaxStages;
+    s.acc_full = bars + 3 * kGemmMaxStages;
+    s.tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * kGemmMaxStages + 1);
+    s.x = smem + p.off_x;
+    s.w = smem + p.off_w;
+    return s;
+}
+
+// Dequantise one k step of the CTA's 8 row tiles into the W stage (hi at 0, lo
+// at 16 KB for q4). Warp d (0..3) takes tiles 2d and 2d+1.
+template <int FMT>
+__device__ __forceinline__ void dequant_step(const GemmParams &p, uint8_t *wst, uint32_t rb, uint32_t ks, uint32_t d,
+                                             uint32_t lane)
+{
+    const uint32_t r = lane >> 2, t = lane & 3;
+    constexpr uint32_t kLo = kGemmBM * kGemmBK * 2;  // byte offset of the lo half (q4)
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+        const uint32_t tl = 2 * d + h;  // tile within the row block
+        const uint32_t T = rb * 8 + tl;
+        if constexpr (FMT == 4) {
+            uint4 q = make_uint4(0, 0, 0, 0);
+            float4 sc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (T < p.tiles) {
+                const uint8_t *u = p.w + ((size_t)T * p.kunits + ks) * B2_Q4_UNIT_BYTES;
+                q = __ldg(reinterpret_cast<const uint4 *>(u) + lane);
+                sc = __ldg(reinterpret_cast<const float4 *>(u + 512) + r);
+            }
+            // words: {row r g0, row r+8 g0, row r g1, row r+8 g1}; scales {s(r,g0), s(r,g1), s(r+8,g0), s(r+8,g1)}
+            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+            const float ws[4] = {sc.x, sc.z, sc.y, sc.w};
+#pragma unroll
+            for (uint32_t j = 0; j < 4; ++j) {
+                const uint32_t row = tl * 16 + r + (j & 1) * 8;
+                const uint32_t g = j >> 1;
+#pragma unroll
+                for (uint32_t half = 0; half < 2; ++half) {  // low nibbles: k 4t..; high nibbles: k 16+4t..
+                    float v[4];
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i) {
+                        const int qv = (int)((wd[j] << (28 - 8 * i - 4 * half))) >> 28;
+                        v[i] = (float)qv * ws[j];
+                    }
+                    uint2 hi, lo;
+                    split4(v, hi, lo);
+                    const uint32_t k = 32 * g + 16 * half + 4 * t;
+                    const uint32_t off = op_off(row, k, kGemmBM);
+                    *reinterpret_cast<uint2 *>(wst + off) = hi;
+                    *reinterpret_cast<uint2 *>(wst + kLo + off) = lo;
+                }
+            }
+        } else {
+            // q8: two 32-column units per k step; bf16 holds the int8 values exactly
+#pragma unroll
+            for (uint32_t uh = 0; uh < 2; ++uh) {
+                const uint32_t ku = 2 * ks + uh;
+                uint4 q = make_uint4(0, 0, 0, 0);
+                if (T < p.tiles && ku < p.kunits)
+                    q = __ldg(reinterpret_cast<const uint4 *>(p.w + ((size_t)T * p.kunits + ku) * B2_Q8_UNIT_BYTES) +
+                              lane);
+                // bytes: {row r k 4t.., row r+8 k 4t.., row r k 16+4t.., row r+8 k 16+4t..}
+                const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (uint32_t j = 0; j < 4; ++j) {
+                    const uint32_t row = tl * 16 + r + (j & 1) * 8;
+                    const uint32_t k = 32 * uh + 16 * (j >> 1) + 4 * t;
+                    float v[4];
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i) v[i] = (float)((int)(wd[j] << (24 - 8 * i)) >> 24);
+                    const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+                    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+                    *reinterpret_cast<uint2 *>(wst + op_off(row, k, kGemmBM)) =
+                        make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+                }
+            }
+        }
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams p)
+{
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const GemmSmem s = gemm_smem(smem, p);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rb = blockIdx.x, nt = blockIdx.y, split = blockIdx.z;
+    const uint32_t k0 = split * p.ksplit;
+    const uint32_t k1 = min(p.ksteps, k0 + p.ksplit);
+    const uint32_t nk = k1 > k0 ? k1 - k0 : 0;
+    const uint32_t xstage = gemm_x_stage_bytes(p.bn);
+    constexpr uint32_t wstage = gemm_w_stage_bytes(FMT);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < kGemmMaxStages; ++i) {
+            mbar_init(&s.x_full[i], 1);
+            mbar_init(&s.w_full[i], 128);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(s.acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(s.tmem_slot, p.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s.tmem_slot;
+    pdl_wait();
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (uint32_t i = 0; i < nk; ++i) {
+                const uint32_t st = i % p.stages, pass = i / p.stages;
+                if (pass > 0) mbar_wait_bounded(&s.empty[st], (pass - 1) & 1, p.err);
+                mbar_arrive_expect_tx(&s.x_full[st], xstage);
+                bulk_g2s(s.x + st * xstage, p.xs + (size_t)(nt * p.ksteps + k0 + i) * xstage, xstage, &s.x_full[st]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_bf16(kGemmBM, p.bn);
+            const uint32_t xb = smem_u32(s.x), wb = smem_u32(s.w);
+            for (uint32_t i = 0; i < nk; ++i) {
+                const uint32_t st = i % p.stages, pass = i / p.stages;
+                mbar_wait_bounded(&s.x_full[st], pass & 1, p.err);
+                mbar_wait_bounded(&s.w_full[st], pass & 1, p.err);
+                tc_fence_after();
+                const uint32_t xa = xb + st * xstage, wa = wb + st * wstage;
+#pragma unroll
+                for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
+                    // 16 columns = two 8-column chunks
+                    const uint64_t a_hi = umma_desc(wa + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                    const uint64_t b_hi = umma_desc(xa + kk * 2 * (p.bn * 16), p.bn * 16, 128);
+                    const uint64_t b_lo = umma_desc(xa + xstage / 2 + kk * 2 * (p.bn * 16), p.bn * 16, 128);
+                    umma_bf16(tmem, a_hi, b_hi, idesc, (i | kk) != 0);
+                    umma_bf16(tmem, a_hi, b_lo, idesc, 1);
+                    if constexpr (FMT == 4) {
+                        const uint64_t a_lo =
+                            umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                        umma_bf16(tmem, a_lo, b_hi, idesc, 1);
+                    }
+                }
+                umma_commit(&s.empty[st]);
+            }
+            umma_commit(s.acc_full);
+            // the accumulator must be complete before tensor memory is freed
+            mbar_wait_bounded(s.acc_full, 0, p.err);
+        }
+    } else {
+        const uint32_t d = warp - 2;
+        for (uint32_t i = 0; i < nk; ++i) {
+            const uint32_t st = i % p.stages, pass = i / p.stages;
+            if (pass > 0) mbar_wait_bounded(&s.empty[st], (pass - 1) & 1, p.err);
+            dequant_step<FMT>(p, s.w + st * wstage, rb, k0 + i, d, lane);
+            fence_proxy_async();
+            mbar_arrive(&s.w_full[st]);
+        }
+        // epilogue: TMEM lane = output row, column = token
+        const uint32_t q = warp & 3;
+        const uint32_t o = rb * kGemmBM + q * 32 + lane;
+        const bool ok = nk == 0 || mbar_wait_bounded(s.acc_full, 0, p.err);
+        tc_fence_after();
+        const float rs = (FMT == 8 && o < p.rows) ? __ldg(p.row_scale + o) : 1.0f;
+        for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+            float v[16];
+            if (nk > 0) {
+                tmem_ld16(tmem + ((q * 32) << 16) + c0, v);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+            }
+            if (!ok || o >= p.rows) continue;
+#pragma unroll
+            for (uint32_t j = 0; j < 16; ++j) {
+                const uint32_t n = nt * p.bn + c0 + j;
+                if (n >= p.m) break;
+                const float y = v[j] * rs;
+                if (p.splits > 1) {
+                    p.part[((size_t)split * p.m + n) * p.rows + o] = y;
+                } else {
+                    const size_t at = (size_t)n * p.out_stride + o;
+                    p.out[at] = p.epilogue == B2_EPI_RESID ? p.resid[at] + y : y;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_free(tmem, p.tmem_cols);
+    }
+}
+
+// Sum of the k splits in split order (+ residual).
+__global__ void gemm_reduce_kernel(const float *__restrict__ part, uint32_t splits, uint32_t m, uint32_t rows,
+                                   float *out, uint32_t out_stride, const float *resid, uint32_t epilogue)
+{
+    const size_t total = (size_t)m * rows;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t n = (uint32_t)(i / rows), o = (uint32_t)(i % rows);
+        float y = 0.0f;
+        for (uint32_t s = 0; s < splits; ++s) y += part[(size_t)s * total + i];
+        const size_t at = (size_t)n * out_stride + o;
+        out[at] = epilogue == B2_EPI_RESID ? resid[at] + y : y;
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+
+struct GemmPlan {
+    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, smem, off_x, off_w, tmem_cols;
+};
+
+static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
+{
+    const b2_qweight &w = a->w;
+    gemm_token_tiles(a->m, pl.ntiles, pl.bn);
+    pl.row_blocks = (w.tiles + 7) / 8;
+    pl.ksteps = (w.cols + kGemmBK - 1) / kGemmBK;
+    const uint32_t xst = gemm_x_stage_bytes(pl.bn), wst = gemm_w_stage_bytes(w.format);
+    const uint32_t head = 1024;  // mbarriers + TMEM slot, then 1 KB-aligned stages
+    uint32_t st = (kGemmSmemLimit - head) / (xst + wst);
+    if (st > kGemmMaxStages) st = kGemmMaxStages;
+    if (st < 2) return false;
+    pl.stages = st;
+    pl.off_x = head;
+    pl.off_w = head + st * xst;
+    pl.smem = pl.off_w + st * wst;
+    uint32_t tc = 32;
+    while (tc < pl.bn) tc <<= 1;
+    pl.tmem_cols = tc;
+    // k splits: fill the SMs when row blocks x token tiles do not, at least 4 k steps each
+    uint32_t splits = a->splits;
+    if (splits == 0) {
+        const uint32_t ctas = pl.row_blocks * pl.ntiles;
+        splits = (uint32_t)sm_count() / (ctas ? ctas : 1);
+        const uint32_t most = pl.ksteps / 4;
+        if (splits > most) splits = most;
+        if (splits > kGemmMaxSplits) splits = kGemmMaxSplits;
+        if (splits < 1) splits = 1;
+    }
+    if (splits > pl.ksteps) splits = pl.ksteps;
+    pl.ksplit = (pl.ksteps + splits - 1) / splits;
+    pl.splits = (pl.ksteps + pl.ksplit - 1) / pl.ksplit;
+    return true;
+}
+
+static int gemm_check(const b2_gemm_args *a)
+{
+    if (a == nullptr || a->w.data == nullptr || a->xs == nullptr || a->out == nullptr) return -1;
+    const b2_qweight &w = a->w;
+    if ((w.format != 4 && w.format != 8) || (w.format == 8 && w.row_scale == nullptr)) return -1;
+    if (a->m == 0 || w.rows == 0 || w.cols == 0 || w.cols % 32) return -1;
+    if (w.tiles != (w.rows + 15) / 16 || w.kunits != (w.format == 4 ? (w.cols + 63) / 64 : (w.cols + 31) / 32))
+        return -1;
+    if (((uintptr_t)w.data & 15) || ((uintptr_t)a->xs & 15)) return -1;
+    if (a->out_stride < w.rows) return -1;
+    if (a->epilogue != B2_EPI_STORE && a->epilogue != B2_EPI_RESID) return -1;
+    if (a->epilogue == B2_EPI_RESID && a->resid == nullptr) return -1;
+    if ((uint64_t)w.tiles * w.kunits >= (1ull << 32)) return -1;
+    return 0;
+}
+
+template <int FMT>
+static cudaError_t launch_gemm(const GemmParams &p, const GemmPlan &pl, int pdl, cudaStream_t st)
+{
+    auto fn = gemm_kernel<FMT>;
+    // the whole shared-memory window (one CTA per SM either way): operand reads
+    // of the tensor cores stay inside the CTA's allocation whatever the stage count
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemLimit);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.row_blocks, pl.ntiles, pl.splits);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = kGemmSmemLimit;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, p);
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" size_t b2_gemm_xs_bytes(uint32_t m, uint32_t cols)
+{
+    uint32_t ntiles, bn;
+    gemm_token_tiles(m, ntiles, bn);
+    const size_t ksteps = (cols + kGemmBK - 1) / kGemmBK;
+    return (size_t)ntiles * ksteps * gemm_x_stage_bytes(bn);
+}
+
+extern "C" int b2_gemm_prep(const float *x, uint32_t x_stride, uint32_t m, uint32_t cols, const float *norm_w,
+                            float eps, void *xs, int32_t *err, void *stream)
+{
+    if (x == nullptr || xs == nullptr || m == 0 || cols == 0 || cols % 32 || x_stride < cols || (x_stride & 3) ||
+        ((uintptr_t)x & 15) || ((uintptr_t)xs & 15))
+        return -1;
+    if (norm_w != nullptr && (((uintptr_t)norm_w & 15) || !(eps > 0.0f))) return -1;
+    uint32_t ntiles, bn;
+    gemm_token_tiles(m, ntiles, bn);
+    const uint32_t ksteps = (cols + kGemmBK - 1) / kGemmBK;
+    gemm_prep_kernel<<<ntiles * bn, 256, 0, (cudaStream_t)stream>>>(x, x_stride, m, cols, norm_w, eps, bn, ksteps,
+                                                                     (uint8_t *)xs, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -8;
+}
+
+extern "C" size_t b2_gemm_scratch_bytes(const b2_gemm_args *a)
+{
+    GemmPlan pl;
+    if (a == nullptr || gemm_check(a) != 0 || !plan_gemm(a, pl)) return 0;
+    return pl.splits > 1 ? (size_t)pl.splits * a->m * a->w.rows * sizeof(float) : 16;
+}
+
+extern "C" int b2_gemm(const b2_gemm_args *a, void *stream)
+{
+    const int rc = gemm_check(a);
+    if (rc != 0) return rc;
+    GemmPlan pl;
+    if (!plan_gemm(a, pl)) return -9;
+    const size_t need = pl.splits > 1 ? (size_t)pl.splits * a->m * a->w.rows * sizeof(float) : 0;
+    if (need > 0 && (a->scratch == nullptr || a->scratch_bytes < need || ((uintptr_t)a->scratch & 15))) return -1;
+    GemmParams p = {};
+    p.w = (const uint8_t *)a->w.data;
+    p.row_scale = a->w.row_scale;
+    p.fmt = a->w.format;
+    p.rows = a->w.rows;
+    p.cols = a->w.cols;
+    p.tiles = a->w.tiles;
+    p.kunits = a->w.kunits;
+    p.ksteps = pl.ksteps;
+    p.xs = (const uint8_t *)a->xs;
+    p.m = a->m;
+    p.bn = pl.bn;
+    p.ntiles = pl.ntiles;
+    p.out = a->out;
+    p.out_stride = a->out_stride;
+    p.resid = a->resid;
+    p.epilogue = a->epilogue;
+    p.part = (float *)a->scratch;
+    p.splits = pl.splits;
+    p.ksplit = pl.ksplit;
+    p.stages = pl.stages;
+    p.off_x = pl.off_x;
+    p.off_w = pl.off_w;
+    p.tmem_cols = pl.tmem_cols;
+    p.err = a->err;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = a->w.format == 4 ? launch_gemm<4>(p, pl, a->pdl, st) : launch_gemm<8>(p, pl, a->pdl, st);
+    if (e != cudaSuccess) return -8;
+    if (pl.splits > 1) {
+        const size_t total = (size_t)a->m * a->w.rows;
+        uint32_t blocks = (uint32_t)((total + 255) / 256);
+        const uint32_t cap = (uint32_t)sm_count() * 8;
+        if (blocks > cap) blocks = cap;
+        gemm_reduce_kernel<<<blocks, 256, 0, st>>>((const float *)a->scratch, pl.splits, a->m, a->w.rows, a->out,
+                                                    a->out_stride, a->resid, a->epilogue);
+        if (cudaGetLastError() != cudaSuccess) return -8;
+    }
+    return 0;
+}

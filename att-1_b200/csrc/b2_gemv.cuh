@@ -81,12 +81,6 @@ struct Fmt<8> {
     static constexpr uint32_t kKW = 32;
 };
 
-__device__ __forceinline__ uint32_t ordered_key(float f)
-{
-    uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-
 // ---- prologue: per item, optional RMSNorm, exponent choice, digit planes ----
 // One pass of loads (x and the norm gains together) and one reduction round
 // per launch: every thread accumulates, per item, the sum of squares of x and

@@ -76,6 +76,20 @@ struct att1_infer {
     int logits_valid;
     size_t position;
     int use_graph, use_pdl, use_persistent;
+    /* decode through the tensor-core GEMM (batches the GEMVs cannot hold) */
+    int use_dense;
+    float *y_qkv, *y_gu;
+    void *xs, *gscratch;
+    size_t xs_bytes, gscratch_bytes;
+    /* prompt prefill buffers for up to pf_cap tokens (allocated on first use) */
+    uint32_t pf_cap;
+    float *pf_x, *pf_h, *pf_q, *pf_ctx, *pf_hs, *pf_yqkv, *pf_ygu;
+    uint32_t *pf_tok;
+    int32_t *pf_pos, *pf_pt, *pf_counters;
+    unsigned long long *pf_keys;
+    void *pf_xs, *pf_gscratch, *pf_ascratch;
+    size_t pf_xs_bytes, pf_gscratch_bytes, pf_ascratch_bytes;
+    uint32_t pf_counters_len;
     int step_pending;
     uint64_t trace_t0;
     cudaGraphExec_t exec;
@@ -86,6 +100,8 @@ struct att1_infer {
     const att1_model *model;
     size_t device_bytes;
 };
+
+static att1_status_t dense_alloc(att1_infer_t *inf);
 
 /* ---- allocation ------------------------------------------------------------ */
 
@@ -136,6 +152,26 @@ static void mat_free(b2_dev_mat *m)
     memset(m, 0, sizeof(*m));
 }
 
+static void free_prefill(att1_infer_t *inf)
+{
+    dfree(inf->pf_x);
+    dfree(inf->pf_h);
+    dfree(inf->pf_q);
+    dfree(inf->pf_ctx);
+    dfree(inf->pf_hs);
+    dfree(inf->pf_yqkv);
+    dfree(inf->pf_ygu);
+    dfree(inf->pf_tok);
+    dfree(inf->pf_pos);
+    dfree(inf->pf_pt);
+    dfree(inf->pf_counters);
+    dfree(inf->pf_keys);
+    dfree(inf->pf_xs);
+    dfree(inf->pf_gscratch);
+    dfree(inf->pf_ascratch);
+    inf->pf_cap = 0;
+}
+
 static void release(att1_infer_t *inf)
 {
     uint32_t l;
@@ -175,6 +211,11 @@ static void release(att1_infer_t *inf)
     dfree(inf->err_d);
     dfree(inf->scratch);
     dfree(inf->counters);
+    dfree(inf->y_qkv);
+    dfree(inf->y_gu);
+    dfree(inf->xs);
+    dfree(inf->gscratch);
+    free_prefill(inf);
     if (inf->tokens_h) cudaFreeHost(inf->tokens_h);
     if (inf->out_h) cudaFreeHost(inf->out_h);
     if (inf->err_h) cudaFreeHost(inf->err_h);
@@ -194,7 +235,7 @@ static void release(att1_infer_t *inf)
 static att1_status_t check_config(const att1_b200_config *c, uint32_t batch)
 {
     uint32_t hd;
-    if (c == NULL || batch == 0 || batch > 16) return ATT1_ERR_INVALID_ARG;
+    if (c == NULL || batch == 0 || batch > ATT1_B200_MAX_BATCH) return ATT1_ERR_INVALID_ARG;
     if (c->vocab == 0 || c->n_layers == 0 || c->n_heads == 0 || c->n_kv_heads == 0 || c->d_model == 0 ||
         c->d_ff == 0 || c->max_seq == 0)
         return ATT1_ERR_INVALID_ARG;
@@ -415,6 +456,7 @@ static att1_status_t build_args(att1_infer_t *inf)
     if (inf->tp_world > 1) tp_wire(inf);
     /* One partial-sum region and one counter array serve every kernel: they
      * run one after another and each leaves its counters at zero. */
+    inf->use_dense = inf->batch > 16;
     {
         uint32_t cmax = 0, cl;
         for (l = 0; l < c->n_layers; l++) {
@@ -423,12 +465,14 @@ static att1_status_t build_args(att1_infer_t *inf)
             int k;
             for (k = 0; k < 4; k++) {
                 if ((s = b2_gemv_scratch_bytes(g[k])) > need) need = s;
+                if (s == 0) inf->use_dense = 1; /* x's digit planes do not fit on chip */
                 if ((cl = b2_gemv_counters_len(g[k])) > cmax) cmax = cl;
             }
             if ((s = b2_attn_scratch_bytes(&L->a_attn)) > need) need = s;
             if ((cl = b2_attn_counters_len(&L->a_attn)) > cmax) cmax = cl;
         }
         if ((s = b2_gemv_scratch_bytes(&inf->a_out)) > need) need = s;
+        if (s == 0) inf->use_dense = 1;
         if ((cl = b2_gemv_counters_len(&inf->a_out)) > cmax) cmax = cl;
         dfree(inf->scratch);
         dfree(inf->counters);
@@ -458,6 +502,11 @@ static att1_status_t build_args(att1_infer_t *inf)
     inf->a_out.scratch_bytes = need;
     inf->a_out.counters = inf->counters;
     inf->a_out.counters_len = inf->counters_len;
+    if (inf->use_dense) {
+        /* the tensor-parallel exchange lives in the GEMV epilogues */
+        if (inf->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
+        return dense_alloc(inf);
+    }
     return build_plan(inf);
 }
 
@@ -499,9 +548,9 @@ static att1_status_t alloc_common(att1_infer_t *inf)
         (st = dalloc(inf, (void **)&inf->ctx, (size_t)B * inf->q_rows * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->hs, (size_t)B * inf->ffl * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->logits, (size_t)B * inf->vl * sizeof(float))) ||
-        (st = dalloc(inf, (void **)&inf->tokens_d, 16 * sizeof(uint32_t))) ||
-        (st = dalloc(inf, (void **)&inf->pos_d, 16 * sizeof(int32_t))) ||
-        (st = dalloc(inf, (void **)&inf->argmax_d, 16 * sizeof(unsigned long long))) ||
+        (st = dalloc(inf, (void **)&inf->tokens_d, ATT1_B200_MAX_BATCH * sizeof(uint32_t))) ||
+        (st = dalloc(inf, (void **)&inf->pos_d, ATT1_B200_MAX_BATCH * sizeof(int32_t))) ||
+        (st = dalloc(inf, (void **)&inf->argmax_d, ATT1_B200_MAX_BATCH * sizeof(unsigned long long))) ||
         (st = dalloc(inf, (void **)&inf->err_d, sizeof(int32_t))))
         return st;
     /* page table: sequence b owns pages [b*pages_per_seq, (b+1)*pages_per_seq) */
@@ -521,8 +570,8 @@ static att1_status_t alloc_common(att1_infer_t *inf)
     free(pt);
     free(freq);
     if (e != cudaSuccess) return b2_cuda_status(e);
-    if (cudaMallocHost((void **)&inf->tokens_h, 16 * sizeof(uint32_t)) != cudaSuccess ||
-        cudaMallocHost((void **)&inf->out_h, 16 * sizeof(uint32_t)) != cudaSuccess ||
+    if (cudaMallocHost((void **)&inf->tokens_h, ATT1_B200_MAX_BATCH * sizeof(uint32_t)) != cudaSuccess ||
+        cudaMallocHost((void **)&inf->out_h, ATT1_B200_MAX_BATCH * sizeof(uint32_t)) != cudaSuccess ||
         cudaMallocHost((void **)&inf->err_h, sizeof(int32_t)) != cudaSuccess ||
         cudaMallocHost((void **)&inf->logits_h, (size_t)B * c->vocab * sizeof(float)) != cudaSuccess)
         return ATT1_ERR_OOM;
@@ -1023,6 +1072,203 @@ void *att1_b200_infer_stream(const att1_infer_t *infer)
 
 /* ---- the decode step ------------------------------------------------------------------------------------- */
 
+/* ---- the tensor-core route: GEMM + row epilogues ------------------------------------------------ */
+
+/* Buffers of one pass of m rows (a decode batch, or a prompt chunk). */
+typedef struct dense_bufs {
+    uint32_t m;
+    float *x, *h, *q, *ctx, *hs, *y_qkv, *y_gu;
+    const int32_t *positions, *page_table;
+    void *xs, *gscratch, *ascratch;
+    size_t xs_bytes, gscratch_bytes, ascratch_bytes;
+    int32_t *acounters;
+    uint32_t acounters_len;
+} dense_bufs;
+
+static void gemm_init(att1_infer_t *inf, b2_gemm_args *g, const b2_dev_mat *w, const dense_bufs *b)
+{
+    memset(g, 0, sizeof(*g));
+    g->w = w->w;
+    g->xs = b->xs;
+    g->m = b->m;
+    g->scratch = b->gscratch;
+    g->scratch_bytes = b->gscratch_bytes;
+    g->err = inf->err_d;
+    g->pdl = inf->use_pdl;
+}
+
+/* x (optionally RMS-normed) times W^T: prep + GEMM (+ split reduction). */
+static int dense_gemm(att1_infer_t *inf, const dense_bufs *b, const b2_dev_mat *w, const float *x, uint32_t x_stride,
+                      const float *norm_w, float eps, uint32_t epilogue, float *out, uint32_t out_stride,
+                      const float *resid, cudaStream_t st)
+{
+    b2_gemm_args g;
+    int rc = b2_gemm_prep(x, x_stride, b->m, w->w.cols, norm_w, eps, b->xs, inf->err_d, st);
+    if (rc != 0) return rc;
+    gemm_init(inf, &g, w, b);
+    g.epilogue = epilogue;
+    g.out = out;
+    g.out_stride = out_stride;
+    g.resid = resid;
+    return b2_gemm(&g, st);
+}
+
+/* One transformer block (src/transformer_block.c:417-557) over b->m rows. */
+static int dense_layer(att1_infer_t *inf, uint32_t l, const dense_bufs *b, cudaStream_t st)
+{
+    const att1_b200_config *c = &inf->cfg;
+    dev_layer *L = &inf->layers[l];
+    const uint32_t d = c->d_model, qkv = inf->q_rows + 2 * inf->kv_rows;
+    b2_rows_args r;
+    b2_attn_args at;
+    int rc = dense_gemm(inf, b, &L->qkv, b->x, d, L->attn_norm, c->eps, B2_EPI_STORE, b->y_qkv, qkv, NULL, st);
+    if (rc != 0) return rc;
+    memset(&r, 0, sizeof(r));
+    r.epilogue = B2_EPI_QKV;
+    r.m = b->m;
+    r.y = b->y_qkv;
+    r.y_stride = qkv;
+    r.rows = qkv;
+    r.out = b->q;
+    r.out_stride = inf->q_rows;
+    r.q_rows = inf->q_rows;
+    r.kv_rows = inf->kv_rows;
+    r.rope_freq = inf->rope_freq;
+    r.positions = b->positions;
+    r.kv = kv_layout(inf, l);
+    r.kv.page_table = b->page_table;
+    r.err = inf->err_d;
+    r.pdl = inf->use_pdl;
+    if ((rc = b2_rows_epilogue(&r, st)) != 0) return rc;
+    at = L->a_attn;
+    at.batch = b->m;
+    at.q = b->q;
+    at.kv.page_table = b->page_table;
+    at.positions = b->positions;
+    at.ctx = b->ctx;
+    at.scratch = b->ascratch;
+    at.scratch_bytes = b->ascratch_bytes;
+    at.counters = b->acounters;
+    at.counters_len = b->acounters_len;
+    at.pdl = inf->use_pdl;
+    if ((rc = b2_attn(&at, st)) != 0) return rc;
+    if ((rc = dense_gemm(inf, b, &L->wo, b->ctx, inf->q_rows, NULL, 0.0f, B2_EPI_RESID, b->h, d, b->x, st)) != 0)
+        return rc;
+    if ((rc = dense_gemm(inf, b, &L->gu, b->h, d, L->ffn_norm, c->eps, B2_EPI_STORE, b->y_gu, 2 * inf->ffl, NULL,
+                         st)) != 0)
+        return rc;
+    memset(&r, 0, sizeof(r));
+    r.epilogue = B2_EPI_SWIGLU;
+    r.m = b->m;
+    r.y = b->y_gu;
+    r.y_stride = 2 * inf->ffl;
+    r.rows = 2 * inf->ffl;
+    r.out = b->hs;
+    r.out_stride = inf->ffl;
+    r.err = inf->err_d;
+    r.pdl = inf->use_pdl;
+    if ((rc = b2_rows_epilogue(&r, st)) != 0) return rc;
+    return dense_gemm(inf, b, &L->down, b->hs, inf->ffl, NULL, 0.0f, B2_EPI_RESID, b->x, d, b->h, st);
+}
+
+/* Scratch of the GEMMs of one m-row pass (the largest k-split partials). */
+static size_t dense_gscratch(att1_infer_t *inf, uint32_t m)
+{
+    /* every layer has the shapes of layer 0 */
+    const b2_dev_mat *ws[4] = {&inf->layers[0].qkv, &inf->layers[0].wo, &inf->layers[0].gu, &inf->layers[0].down};
+    b2_gemm_args g;
+    size_t need = 16, s;
+    uint32_t k;
+    for (k = 0; k < 4; k++) {
+        memset(&g, 0, sizeof(g));
+        g.w = ws[k]->w;
+        g.xs = inf->embed; /* any aligned non-null pointer: only the plan is asked for */
+        g.out = inf->embed;
+        g.out_stride = ws[k]->w.rows;
+        g.m = m;
+        if ((s = b2_gemm_scratch_bytes(&g)) > need) need = s;
+    }
+    memset(&g, 0, sizeof(g));
+    g.w = inf->output.w;
+    g.xs = inf->embed;
+    g.out = inf->embed;
+    g.out_stride = inf->output.w.rows;
+    g.m = m;
+    if ((s = b2_gemm_scratch_bytes(&g)) > need) need = s;
+    return need;
+}
+
+static size_t dense_xs(att1_infer_t *inf, uint32_t m)
+{
+    size_t a = b2_gemm_xs_bytes(m, inf->cfg.d_model), b = b2_gemm_xs_bytes(m, inf->q_rows),
+           f = b2_gemm_xs_bytes(m, inf->ffl);
+    if (b > a) a = b;
+    return f > a ? f : a;
+}
+
+/* Decode through the GEMM: buffers for the context's batch. */
+static att1_status_t dense_alloc(att1_infer_t *inf)
+{
+    const uint32_t B = inf->batch;
+    att1_status_t st;
+    dfree(inf->y_qkv);
+    dfree(inf->y_gu);
+    dfree(inf->xs);
+    dfree(inf->gscratch);
+    inf->y_qkv = inf->y_gu = NULL;
+    inf->xs = inf->gscratch = NULL;
+    inf->xs_bytes = dense_xs(inf, B);
+    inf->gscratch_bytes = dense_gscratch(inf, B);
+    if ((st = dalloc(inf, (void **)&inf->y_qkv, (size_t)B * (inf->q_rows + 2 * inf->kv_rows) * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->y_gu, (size_t)B * 2 * inf->ffl * sizeof(float))) ||
+        (st = dalloc(inf, &inf->xs, inf->xs_bytes)) || (st = dalloc(inf, &inf->gscratch, inf->gscratch_bytes)))
+        return st;
+    return ATT1_OK;
+}
+
+static void decode_bufs(att1_infer_t *inf, dense_bufs *b)
+{
+    memset(b, 0, sizeof(*b));
+    b->m = inf->batch;
+    b->x = inf->x;
+    b->h = inf->h1;
+    b->q = inf->q;
+    b->ctx = inf->ctx;
+    b->hs = inf->hs;
+    b->y_qkv = inf->y_qkv;
+    b->y_gu = inf->y_gu;
+    b->positions = inf->pos_d;
+    b->page_table = inf->page_table;
+    b->xs = inf->xs;
+    b->xs_bytes = inf->xs_bytes;
+    b->gscratch = inf->gscratch;
+    b->gscratch_bytes = inf->gscratch_bytes;
+    b->ascratch = inf->scratch;
+    b->ascratch_bytes = inf->scratch_bytes;
+    b->acounters = inf->counters;
+    b->acounters_len = inf->counters_len;
+}
+
+/* Final RMSNorm + lm_head + argmax keys for b->m rows of x. */
+static int dense_head(att1_infer_t *inf, const dense_bufs *b, cudaStream_t st)
+{
+    b2_rows_args r;
+    int rc = dense_gemm(inf, b, &inf->output, b->x, inf->cfg.d_model, inf->out_norm, inf->cfg.final_eps, B2_EPI_STORE,
+                        inf->logits, inf->vl, NULL, st);
+    if (rc != 0) return rc;
+    memset(&r, 0, sizeof(r));
+    r.epilogue = B2_EPI_LOGITS;
+    r.m = b->m;
+    r.y = inf->logits;
+    r.y_stride = inf->vl;
+    r.rows = inf->vl;
+    r.argmax = inf->argmax_d;
+    r.row_offset = inf->v_off;
+    r.err = inf->err_d;
+    r.pdl = inf->use_pdl;
+    return b2_rows_epilogue(&r, st);
+}
+
 static int enqueue_kernels(att1_infer_t *inf)
 {
     const att1_b200_config *c = &inf->cfg;
@@ -1030,6 +1276,14 @@ static int enqueue_kernels(att1_infer_t *inf)
     uint32_t l;
     int rc = b2_step_begin(inf->embed, c->vocab, c->d_model, inf->tokens_d, inf->batch, inf->x, inf->argmax_d,
                            inf->err_d, inf->use_pdl, st);
+    if (inf->use_dense) {
+        dense_bufs b;
+        decode_bufs(inf, &b);
+        for (l = 0; l < c->n_layers && rc == 0; l++) rc = dense_layer(inf, l, &b, st);
+        if (rc == 0) rc = dense_head(inf, &b, st);
+        if (rc != 0) return rc;
+        return b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    }
     for (l = 0; l < c->n_layers && rc == 0; l++) {
         dev_layer *L = &inf->layers[l];
         rc |= b2_gemv(&L->a_qkv, st);
@@ -1079,7 +1333,7 @@ static int launch_step(att1_infer_t *inf)
  * scratch, and put the device position back to the host position. */
 static att1_status_t recover(att1_infer_t *inf, int32_t err)
 {
-    int32_t pos[16];
+    int32_t pos[ATT1_B200_MAX_BATCH];
     uint32_t b;
     for (b = 0; b < inf->batch; b++) pos[b] = (int32_t)inf->position;
     cudaMemsetAsync(inf->err_d, 0, sizeof(int32_t), inf->stream);
@@ -1107,7 +1361,7 @@ static att1_status_t step_launch(att1_infer_t *inf, const uint32_t *tokens)
     }
     if (inf->trace) inf->trace_t0 = att1_trace_now_us();
     if (inf->position == 0) {
-        int32_t zero[16] = {0};
+        int32_t zero[ATT1_B200_MAX_BATCH] = {0};
         if (cudaMemcpyAsync(inf->pos_d, zero, inf->batch * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream) !=
             cudaSuccess)
             return ATT1_ERR_STATE;
@@ -1195,6 +1449,164 @@ att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *
     return step(infer, tokens, out_tokens);
 }
 
+/* ---- prompt prefill ------------------------------------------------------------------------------ */
+
+#define PREFILL_CHUNK 512u
+
+/* Buffers for prompt chunks of up to `cap` tokens: every row of a chunk is a
+ * position of sequence 0, so the chunk's page-table rows all repeat
+ * sequence 0's row. Sizes are the largest over chunk lengths 1..cap (the
+ * split choices depend on the length). */
+static att1_status_t prefill_alloc(att1_infer_t *inf, uint32_t cap)
+{
+    const att1_b200_config *c = &inf->cfg;
+    const uint32_t pps = inf->pages_per_seq;
+    att1_status_t st;
+    b2_attn_args at;
+    int32_t *pt;
+    uint32_t m, i;
+    size_t s;
+    cudaError_t e;
+    if (inf->pf_cap >= cap) return ATT1_OK;
+    free_prefill(inf);
+    at = inf->layers[0].a_attn;
+    inf->pf_xs_bytes = inf->pf_gscratch_bytes = inf->pf_ascratch_bytes = 0;
+    for (m = 1; m <= cap; m++) {
+        if ((s = dense_xs(inf, m)) > inf->pf_xs_bytes) inf->pf_xs_bytes = s;
+        if ((s = dense_gscratch(inf, m)) > inf->pf_gscratch_bytes) inf->pf_gscratch_bytes = s;
+        at.batch = m;
+        if ((s = b2_attn_scratch_bytes(&at)) > inf->pf_ascratch_bytes) inf->pf_ascratch_bytes = s;
+    }
+    at.batch = cap;
+    inf->pf_counters_len = b2_attn_counters_len(&at);
+    if ((st = dalloc(inf, (void **)&inf->pf_x, (size_t)cap * c->d_model * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_h, (size_t)cap * c->d_model * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_q, (size_t)cap * inf->q_rows * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_ctx, (size_t)cap * inf->q_rows * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_hs, (size_t)cap * inf->ffl * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_yqkv, (size_t)cap * (inf->q_rows + 2 * inf->kv_rows) * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_ygu, (size_t)cap * 2 * inf->ffl * sizeof(float))) ||
+        (st = dalloc(inf, (void **)&inf->pf_tok, (size_t)cap * sizeof(uint32_t))) ||
+        (st = dalloc(inf, (void **)&inf->pf_pos, (size_t)cap * sizeof(int32_t))) ||
+        (st = dalloc(inf, (void **)&inf->pf_pt, (size_t)cap * pps * sizeof(int32_t))) ||
+        (st = dalloc(inf, (void **)&inf->pf_counters, (size_t)inf->pf_counters_len * sizeof(int32_t))) ||
+        (st = dalloc(inf, (void **)&inf->pf_keys, (size_t)cap * sizeof(unsigned long long))) ||
+        (st = dalloc(inf, &inf->pf_xs, inf->pf_xs_bytes)) ||
+        (st = dalloc(inf, &inf->pf_gscratch, inf->pf_gscratch_bytes)) ||
+        (st = dalloc(inf, &inf->pf_ascratch, inf->pf_ascratch_bytes))) {
+        free_prefill(inf);
+        return st;
+    }
+    pt = malloc((size_t)cap * pps * sizeof(int32_t));
+    if (pt == NULL) {
+        free_prefill(inf);
+        return ATT1_ERR_OOM;
+    }
+    e = cudaMemcpy(pt, inf->page_table, pps * sizeof(int32_t), cudaMemcpyDeviceToHost);
+    for (i = 1; i < cap; i++) memcpy(pt + (size_t)i * pps, pt, pps * sizeof(int32_t));
+    if (e == cudaSuccess) e = cudaMemcpy(inf->pf_pt, pt, (size_t)cap * pps * sizeof(int32_t), cudaMemcpyHostToDevice);
+    free(pt);
+    if (e != cudaSuccess) {
+        free_prefill(inf);
+        return b2_cuda_status(e);
+    }
+    inf->pf_cap = cap;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_prefill(att1_infer_t *inf, const uint32_t *tokens, size_t n, uint32_t *out_token)
+{
+    const att1_b200_config *c;
+    cudaStream_t st;
+    int32_t *pos_h;
+    size_t done = 0, i;
+    uint32_t cap, m = 0;
+    att1_status_t s;
+    int rc = 0;
+    if (inf == NULL || tokens == NULL || out_token == NULL || n == 0) return ATT1_ERR_INVALID_ARG;
+    c = &inf->cfg;
+    if (inf->batch != 1 || inf->step_pending || !backend_ok(inf)) return ATT1_ERR_STATE;
+    if (inf->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
+    if (n > c->max_seq || inf->position + n > c->max_seq) return ATT1_ERR_INVALID_ARG;
+    for (i = 0; i < n; i++)
+        if (tokens[i] >= c->vocab) return ATT1_ERR_INVALID_ARG;
+    if (cudaSetDevice(inf->device) != cudaSuccess) return ATT1_ERR_STATE;
+    cap = n < PREFILL_CHUNK ? (uint32_t)n : PREFILL_CHUNK;
+    if ((s = prefill_alloc(inf, cap)) != ATT1_OK) return s;
+    pos_h = malloc((size_t)cap * sizeof(int32_t));
+    if (pos_h == NULL) return ATT1_ERR_OOM;
+    st = inf->stream;
+    while (done < n && rc == 0) {
+        dense_bufs b;
+        uint32_t l;
+        m = (uint32_t)((n - done) < cap ? (n - done) : cap);
+        for (i = 0; i < m; i++) pos_h[i] = (int32_t)(inf->position + done + i);
+        /* pageable sources: each copy has left the buffer when it returns */
+        if (cudaMemcpyAsync(inf->pf_tok, tokens + done, m * sizeof(uint32_t), cudaMemcpyHostToDevice, st) !=
+                cudaSuccess ||
+            cudaMemcpyAsync(inf->pf_pos, pos_h, m * sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            rc = -8;
+            break;
+        }
+        memset(&b, 0, sizeof(b));
+        b.m = m;
+        b.x = inf->pf_x;
+        b.h = inf->pf_h;
+        b.q = inf->pf_q;
+        b.ctx = inf->pf_ctx;
+        b.hs = inf->pf_hs;
+        b.y_qkv = inf->pf_yqkv;
+        b.y_gu = inf->pf_ygu;
+        b.positions = inf->pf_pos;
+        b.page_table = inf->pf_pt;
+        b.xs = inf->pf_xs;
+        b.xs_bytes = inf->pf_xs_bytes;
+        b.gscratch = inf->pf_gscratch;
+        b.gscratch_bytes = inf->pf_gscratch_bytes;
+        b.ascratch = inf->pf_ascratch;
+        b.ascratch_bytes = inf->pf_ascratch_bytes;
+        b.acounters = inf->pf_counters;
+        b.acounters_len = inf->pf_counters_len;
+        rc = b2_step_begin(inf->embed, c->vocab, c->d_model, inf->pf_tok, m, inf->pf_x, inf->pf_keys, inf->err_d, 0, st);
+        for (l = 0; l < c->n_layers && rc == 0; l++) rc = dense_layer(inf, l, &b, st);
+        done += m;
+    }
+    free(pos_h);
+    if (rc == 0) {
+        /* the last prompt token's row finishes like a decode step: final norm,
+         * lm_head, greedy sampler, position = prompt end */
+        const int32_t last = (int32_t)(inf->position + n - 1);
+        if (cudaMemcpyAsync(inf->x, inf->pf_x + (size_t)(m - 1) * c->d_model, c->d_model * sizeof(float),
+                            cudaMemcpyDeviceToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(inf->pos_d, &last, sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemsetAsync(inf->argmax_d, 0, sizeof(unsigned long long), st) != cudaSuccess)
+            rc = -8;
+    }
+    if (rc == 0) {
+        if (inf->use_dense) {
+            dense_bufs b;
+            decode_bufs(inf, &b);
+            rc = dense_head(inf, &b, st);
+        } else {
+            rc = b2_gemv(&inf->a_out, st);
+        }
+    }
+    if (rc == 0) rc = b2_step_end(inf->argmax_d, 1, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    if (rc != 0) {
+        cudaStreamSynchronize(st);
+        cudaGetLastError();
+        return ATT1_ERR_STATE;
+    }
+    cudaMemcpyAsync(inf->out_h, inf->tokens_d, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(inf->err_h, inf->err_d, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return ATT1_ERR_STATE;
+    inf->logits_valid = 0;
+    if (*inf->err_h != 0) return recover(inf, *inf->err_h);
+    inf->position += n;
+    *out_token = inf->out_h[0];
+    return ATT1_OK;
+}
+
 att1_status_t att1_infer_generate(att1_infer_t *infer, const unsigned char *prompt, size_t prompt_bytes,
                                   size_t generated_token_count, uint32_t *out_tokens, size_t out_token_capacity,
                                   size_t *out_token_count)
@@ -1205,11 +1617,22 @@ att1_status_t att1_infer_generate(att1_infer_t *infer, const unsigned char *prom
     /* same contract as src/infer.c:882-928 */
     if (infer == NULL || prompt == NULL || out_tokens == NULL || out_token_count == NULL) return ATT1_ERR_INVALID_ARG;
     if (prompt_bytes == 0 || out_token_capacity < generated_token_count) return ATT1_ERR_INVALID_ARG;
-    for (i = 0; i < prompt_bytes; i++) {
-        uint32_t next = 0;
-        st = att1_infer_decode_token(infer, (uint32_t)prompt[i], &next);
+    if (infer->batch == 1 && infer->tp_world == 1) {
+        /* the prompt in one pass over the weights per chunk (same results as
+         * the token-by-token loop of the reference) */
+        uint32_t *ids = malloc(prompt_bytes * sizeof(uint32_t));
+        if (ids == NULL) return ATT1_ERR_OOM;
+        for (i = 0; i < prompt_bytes; i++) ids[i] = prompt[i];
+        st = att1_b200_infer_prefill(infer, ids, prompt_bytes, &token);
+        free(ids);
         if (st != ATT1_OK) return st;
-        token = next;
+    } else {
+        for (i = 0; i < prompt_bytes; i++) {
+            uint32_t next = 0;
+            st = att1_infer_decode_token(infer, (uint32_t)prompt[i], &next);
+            if (st != ATT1_OK) return st;
+            token = next;
+        }
     }
     for (i = 0; i < generated_token_count; i++) {
         uint32_t next = 0;
@@ -1354,7 +1777,7 @@ att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps)
     if (cudaSetDevice(infer->device) != cudaSuccess) return ATT1_ERR_STATE;
     if (infer->position + steps > infer->cfg.max_seq) return ATT1_ERR_INVALID_ARG;
     if (infer->position == 0) {
-        int32_t zero[16] = {0};
+        int32_t zero[ATT1_B200_MAX_BATCH] = {0};
         if (cudaMemcpyAsync(infer->pos_d, zero, infer->batch * sizeof(int32_t), cudaMemcpyHostToDevice,
                             infer->stream) != cudaSuccess)
             return ATT1_ERR_STATE;

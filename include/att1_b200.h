@@ -41,6 +41,11 @@ enum {
     ATT1_B200_GATE = 6, ATT1_B200_UP = 7, ATT1_B200_DOWN = 8, ATT1_B200_OUTPUT = 9
 };
 
+/* Sequences one context decodes together. Up to 16 whose activation digit
+ * planes fit the GEMVs' shared memory go through the fused GEMVs; larger
+ * batches (and shapes the GEMVs cannot tile) through the tensor-core GEMM. */
+#define ATT1_B200_MAX_BATCH 64
+
 /* Synthetic model on the current device: every matrix N(0, 0.02) from
  * (seed, tensor id) quantised by the reference rule, norm gains 1.0,
  * embedding N(0, 0.02) in f32. `batch` sequences decode together. */
@@ -82,6 +87,12 @@ att1_status_t att1_b200_infer_tp_connect_local(att1_infer_t *const *infers, uint
  * step on every rank, then wait for each. */
 att1_status_t att1_b200_infer_step_async(att1_infer_t *infer, const uint32_t *tokens);
 att1_status_t att1_b200_infer_step_wait(att1_infer_t *infer, uint32_t *out_tokens);
+
+/* Prompt prefill (batch-1 contexts, one GPU): the same result as feeding
+ * tokens[0..n) through att1_infer_decode_token one by one (KV cache, position,
+ * logits of the last token, greedy next token in *out_token), computed with
+ * the tensor-core GEMM over up to 512 prompt tokens at a time. */
+att1_status_t att1_b200_infer_prefill(att1_infer_t *infer, const uint32_t *tokens, size_t n, uint32_t *out_token);
 
 att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *tokens,
                                            uint32_t *out_tokens);

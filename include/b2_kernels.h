@@ -297,6 +297,59 @@ int b2_decode_step(b2_decode_plan *p, void *stream);
 int b2_decode_reset(b2_decode_plan *p, void *stream);
 void b2_decode_plan_destroy(b2_decode_plan *p);
 
+/* ---- dequant GEMM on the tensor cores (prefill, large decode batches) ---- */
+/*
+ * out[n][o] (= resid[n][o] +) sum_k x[n][k] * W[o][k] for n < m rows of x,
+ * W in the unit layout above. Replaces att1_matmul_q4xf32 / _q8xf32
+ * (src/quant.c:340-393, src/matmul_q8.c:3-40) when many rows of x share one
+ * pass over W (tcgen05.mma, bf16 hi/lo operand splits, f32 accumulation).
+ * x is first prepared by b2_gemm_prep (optional RMSNorm of each row with
+ * norm_w, as src/norm.c:5-34, then the split into the MMA operand layout)
+ * into a buffer of b2_gemm_xs_bytes(m, cols). When the k range is split over
+ * CTAs the partial sums need scratch of b2_gemm_scratch_bytes(args).
+ */
+typedef struct b2_gemm_args {
+    b2_qweight w;
+    const void *xs;        /* device, b2_gemm_prep output for m rows, w.cols columns */
+    uint32_t m;            /* rows of x (tokens) */
+    uint32_t epilogue;     /* B2_EPI_STORE or B2_EPI_RESID */
+    float *out;            /* device [m][out_stride] */
+    uint32_t out_stride;
+    const float *resid;    /* B2_EPI_RESID: device [m][out_stride] (may equal out) */
+    void *scratch;         /* device, b2_gemm_scratch_bytes */
+    size_t scratch_bytes;
+    uint32_t splits;       /* k splits; 0 = choose */
+    int32_t *err;          /* device error word (timeouts) */
+    int pdl;
+} b2_gemm_args;
+
+size_t b2_gemm_xs_bytes(uint32_t m, uint32_t cols);
+int b2_gemm_prep(const float *x, uint32_t x_stride, uint32_t m, uint32_t cols, const float *norm_w, float eps,
+                 void *xs, int32_t *err, void *stream);
+size_t b2_gemm_scratch_bytes(const b2_gemm_args *a);
+int b2_gemm(const b2_gemm_args *a, void *stream);
+
+/* The GEMV epilogues (QKV: RoPE + KV append; SWIGLU over interleaved gate/up
+ * rows; LOGITS: greedy argmax keys) applied to a dense [m][rows] result y,
+ * e.g. of b2_gemm. Row n of y is item n: positions[n] and page-table row n. */
+typedef struct b2_rows_args {
+    uint32_t epilogue;             /* B2_EPI_QKV, B2_EPI_SWIGLU or B2_EPI_LOGITS */
+    uint32_t m;                    /* rows of y */
+    const float *y;                /* device [m][y_stride] */
+    uint32_t y_stride, rows;       /* rows: logical device rows of the weight (q|k|v, gate/up, vocab) */
+    float *out;                    /* QKV: q [m][out_stride]; SWIGLU: [m][out_stride]; LOGITS: copy or NULL */
+    uint32_t out_stride;
+    uint32_t q_rows, kv_rows;      /* QKV */
+    const float *rope_freq;
+    const int32_t *positions;      /* [m] */
+    b2_kv_layout kv;
+    unsigned long long *argmax;    /* LOGITS: [m] keys, max-combined (reset by b2_step_begin) */
+    uint32_t row_offset;           /* LOGITS: global id of row 0 */
+    int32_t *err;
+    int pdl;
+} b2_rows_args;
+int b2_rows_epilogue(const b2_rows_args *a, void *stream);
+
 /* ---- element ops (backend vtable on device buffers) ---------------------- */
 int b2_rmsnorm(float *dst, const float *src, const float *w, uint32_t n, float eps, void *stream);
 int b2_softmax(float *v, uint32_t n, void *stream);
