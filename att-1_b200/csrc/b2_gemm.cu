@@ -17,17 +17,24 @@
 //
 // Work split. CTA (row block, token tile, k split) computes a 128-row x BN-token
 // tile of Y over a range of 64-column k steps:
-//   warp 0      allocates tensor memory and streams the prepared X tile of each
-//               k step (b2_gemm_prep writes it in the MMA operand layout, so one
-//               1-D bulk copy per stage) into a ring of shared-memory stages;
+//   warp 0      allocates tensor memory and streams the prepared X tiles
+//               (b2_gemm_prep writes them in the MMA operand layout, k steps of
+//               a token tile contiguous) into two slots of xk k steps each, one
+//               1-D bulk copy of ~32 KB per slot (an SM completes bulk copies at
+//               a bounded rate whatever their size);
 //   warp 1      one thread issues tcgen05.mma (M=128, N=BN, K=16) for every
-//               k step, then tcgen05.commit releases the stage;
-//   warps 2..5  read the weight units of the 8 row tiles with 16-byte loads
-//               (each lane's 16 bytes are one fixed set of 32 weights), scale,
-//               split into bf16 hi/lo and store them in the operand layout;
-//               after the k loop they read the accumulator out of tensor memory
-//               (warp w reads TMEM lanes 32*(w%4)..: one output row per thread)
-//               and write Y, or the split's partial sums.
+//               k step, then tcgen05.commit releases the W stage (and the X
+//               slot after its last k step). Each MMA has a fixed cost of
+//               roughly the read of its 4 KB weight operand, so for small BN
+//               (decode batches) this thread, not the dequant, sets the pace;
+//   warps 2..9  one per 16-row tile: read the tile's weight unit of each k
+//               step with 16-byte loads issued two k steps ahead (each lane's
+//               16 bytes are one fixed set of 32 weights), scale, split into
+//               bf16 hi/lo and store them in the operand layout; after the k
+//               loop they read the accumulator out of tensor memory (warp w
+//               reads TMEM lanes 32*(w%4)..: one output row per thread, the two
+//               warps of a lane quarter alternate 16-column chunks) and write Y,
+//               or the split's partial sums.
 // Operands are K-major without swizzle: 8-row x 16-byte core matrices,
 // element (r, k) of a tile with R rows at byte
 //   (k / 8) * (R * 16) + (r / 8) * 128 + (r % 8) * 16 + (k % 8) * 2,
@@ -44,8 +51,11 @@ namespace b2 {
 constexpr uint32_t kGemmBM = 128;          // output rows per CTA (8 tiles of 16)
 constexpr uint32_t kGemmBK = 64;           // columns per k step
 constexpr uint32_t kGemmMaxBN = 256;       // tokens per CTA tile
-constexpr int kGemmThreads = 192;          // 6 warps
-constexpr uint32_t kGemmMaxStages = 4;
+constexpr int kGemmDequantWarps = 8;      // one 16-row tile each
+constexpr int kGemmThreads = 64 + 32 * kGemmDequantWarps;  // + TMEM/X-copy warp + MMA warp
+constexpr uint32_t kGemmMaxStages = 6;      // W ring
+constexpr uint32_t kGemmXSlots = 2;         // X ring
+constexpr uint32_t kGemmXCopy = 32768;      // target bytes per X bulk copy
 constexpr uint32_t kGemmMaxSplits = 16;
 constexpr uint32_t kGemmSmemLimit = 227u * 1024u;
 
@@ -79,7 +89,8 @@ struct GemmParams {
     uint32_t epilogue;
     float *part;            // [splits][m][rows] when splits > 1
     uint32_t splits, ksplit;  // k steps per split
-    uint32_t stages;
+    uint32_t stages;        // W ring stages (one k step each)
+    uint32_t xk;            // k steps per X slot (one bulk copy)
     uint32_t off_x, off_w, tmem_cols;
     int32_t *err;
 };
@@ -238,7 +249,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float *__restrict_
 // ---- the GEMM ----------------------------------------------------------------------------
 
 struct GemmSmem {
-    uint64_t *x_full, *w_full, *empty, *acc_full;
+    uint64_t *x_full, *x_empty, *w_full, *w_empty, *acc_full;
     uint32_t *tmem_slot;
     uint8_t *x, *w;
 };
@@ -248,81 +259,127 @@ __device__ __forceinline__ GemmSmem gemm_smem(uint8_t *smem, const GemmParams &p
     GemmSmem s;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     s.x_full = bars;
-    s.w_full = bars + kGemmMaxStages;
-    s.empty = bars + 2 * kGemmMaxStages;
-    s.acc_full = bars + 3 * kGemmMaxStages;
-    s.tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * kGemmMaxStages + 1);
+    s.x_empty = bars + kGemmXSlots;
+    s.w_full = bars + 2 * kGemmXSlots;
+    s.w_empty = bars + 2 * kGemmXSlots + kGemmMaxStages;
+    s.acc_full = bars + 2 * kGemmXSlots + 2 * kGemmMaxStages;
+    s.tmem_slot = reinterpret_cast<uint32_t *>(s.acc_full + 1);
     s.x = smem + p.off_x;
     s.w = smem + p.off_w;
     return s;
 }
 
-// Dequantise one k step of the CTA's 8 row tiles into the W stage (hi at 0, lo
-// at 16 KB for q4). Warp d (0..3) takes tiles 2d and 2d+1.
+// The weight bytes one dequant lane needs for one k step of its tile: q4 one
+// unit (16 bytes of nibbles + the float4 of its row's scales), q8 two units.
+struct RawStep {
+    uint4 q0, q1;
+    float4 sc;
+};
+
 template <int FMT>
-__device__ __forceinline__ void dequant_step(const GemmParams &p, uint8_t *wst, uint32_t rb, uint32_t ks, uint32_t d,
-                                             uint32_t lane)
+__device__ __forceinline__ RawStep load_step(const GemmParams &p, uint32_t T, uint32_t ks, uint32_t lane)
+{
+    RawStep r;
+    r.q0 = r.q1 = make_uint4(0, 0, 0, 0);
+    r.sc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (T >= p.tiles) return r;
+    if constexpr (FMT == 4) {
+        const uint8_t *u = p.w + ((size_t)T * p.kunits + ks) * B2_Q4_UNIT_BYTES;
+        r.q0 = __ldg(reinterpret_cast<const uint4 *>(u) + lane);
+        r.sc = __ldg(reinterpret_cast<const float4 *>(u + 512) + (lane >> 2));
+    } else {
+        const uint32_t ku = 2 * ks;
+        const uint8_t *u = p.w + ((size_t)T * p.kunits + ku) * B2_Q8_UNIT_BYTES;
+        r.q0 = __ldg(reinterpret_cast<const uint4 *>(u) + lane);
+        if (ku + 1 < p.kunits) r.q1 = __ldg(reinterpret_cast<const uint4 *>(u + B2_Q8_UNIT_BYTES) + lane);
+    }
+    return r;
+}
+
+// Conversions (I2F, F2F) issue at a fraction of the ALU rate, so the weights
+// are decoded with bit operations and exact f32 additions instead:
+//   * a 4-bit field u (0..15) at bit p <= 19 of a word, OR-ed into the bits of
+//     2^23, is the float 2^23 + u 2^p; subtracting 2^23 + 8 2^p (exact) leaves
+//     (u - 8) 2^p, and the word was XOR-ed with 0x8888.. so u - 8 is the
+//     signed nibble q; times (s 2^-p) this is fl(q s), the reference's product
+//     bit for bit (s 2^-p is exact for every normal scale);
+//   * the split keeps hi = v with the low 16 bits cleared (truncation: bf16's 8
+//     significant bits) and lo = bf16_rn(v - hi) (v - hi is exact in f32): the
+//     pair represents v within 2^-16 relative, one conversion per two values.
+__device__ __forceinline__ float field_f(uint32_t w, uint32_t mask) { return __uint_as_float((w & mask) | 0x4B000000u); }
+// 2^23 + 8 * 2^p and 2^23 + 128 * 2^p (exact in f32 for the bit positions used)
+__host__ __device__ constexpr float nib_off(int p) { return 8388608.0f + 8.0f * (float)(1u << p); }
+__host__ __device__ constexpr float byte_off(int p) { return 8388608.0f + 128.0f * (float)(1u << p); }
+static_assert(nib_off(0) == 8388616.0f && nib_off(4) == 8388736.0f && nib_off(8) == 8390656.0f &&
+                  nib_off(12) == 8421376.0f && nib_off(16) == 8912896.0f,
+              "nibble offsets");
+static_assert(byte_off(0) == 8388736.0f && byte_off(8) == 8421376.0f, "byte offsets");
+
+__device__ __forceinline__ void split_pair(float v0, float v1, uint32_t &hi, uint32_t &lo)
+{
+    const uint32_t b0 = __float_as_uint(v0) & 0xFFFF0000u, b1 = __float_as_uint(v1) & 0xFFFF0000u;
+    hi = __byte_perm(b0, b1, 0x7632);  // upper halves: element 0 low, element 1 high
+    const __nv_bfloat162 l = __floats2bfloat162_rn(v0 - __uint_as_float(b0), v1 - __uint_as_float(b1));
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// Dequantise one k step of tile tl (0..7 within the row block) into the W
+// stage (bf16, hi at 0 and, for q4, lo at 16 KB).
+template <int FMT>
+__device__ __forceinline__ void dequant_store(const RawStep &raw, uint8_t *wst, uint32_t tl, uint32_t lane)
 {
     const uint32_t r = lane >> 2, t = lane & 3;
     constexpr uint32_t kLo = kGemmBM * kGemmBK * 2;  // byte offset of the lo half (q4)
+    if constexpr (FMT == 4) {
+        // words: {row r g0, row r+8 g0, row r g1, row r+8 g1}; scales {s(r,g0), s(r,g1), s(r+8,g0), s(r+8,g1)}
+        const uint32_t wd[4] = {raw.q0.x, raw.q0.y, raw.q0.z, raw.q0.w};
+        const float ws[4] = {raw.sc.x, raw.sc.z, raw.sc.y, raw.sc.w};
 #pragma unroll
-    for (uint32_t h = 0; h < 2; ++h) {
-        const uint32_t tl = 2 * d + h;  // tile within the row block
-        const uint32_t T = rb * 8 + tl;
-        if constexpr (FMT == 4) {
-            uint4 q = make_uint4(0, 0, 0, 0);
-            float4 sc = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (T < p.tiles) {
-                const uint8_t *u = p.w + ((size_t)T * p.kunits + ks) * B2_Q4_UNIT_BYTES;
-                q = __ldg(reinterpret_cast<const uint4 *>(u) + lane);
-                sc = __ldg(reinterpret_cast<const float4 *>(u + 512) + r);
+        for (uint32_t j = 0; j < 4; ++j) {
+            const uint32_t row = tl * 16 + r + (j & 1) * 8;
+            const uint32_t g = j >> 1;
+            const uint32_t w = wd[j] ^ 0x88888888u, w12 = w >> 12;
+            const float s0 = ws[j], s4 = s0 * 0x1p-4f, s8 = s0 * 0x1p-8f, s12 = s0 * 0x1p-12f, s16 = s0 * 0x1p-16f;
+            // byte i: low nibble (bit 8i) = column 4t+i, high nibble (bit 8i+4) = column 16+4t+i
+            float v[8];
+            v[0] = (field_f(w, 0xFu) - nib_off(0)) * s0;              // bit 0
+            v[1] = (field_f(w, 0xF00u) - nib_off(8)) * s8;            // bit 8
+            v[2] = (field_f(w, 0xF0000u) - nib_off(16)) * s16;        // bit 16
+            v[3] = (field_f(w12, 0xF000u) - nib_off(12)) * s12;       // bit 24 (12 after the shift)
+            v[4] = (field_f(w, 0xF0u) - nib_off(4)) * s4;             // bit 4
+            v[5] = (field_f(w, 0xF000u) - nib_off(12)) * s12;         // bit 12
+            v[6] = (field_f(w12, 0xF00u) - nib_off(8)) * s8;          // bit 20 (8 after the shift)
+            v[7] = (field_f(w12, 0xF0000u) - nib_off(16)) * s16;      // bit 28 (16 after the shift)
+#pragma unroll
+            for (uint32_t half = 0; half < 2; ++half) {
+                uint32_t h0, h1, l0, l1;
+                split_pair(v[4 * half + 0], v[4 * half + 1], h0, l0);
+                split_pair(v[4 * half + 2], v[4 * half + 3], h1, l1);
+                const uint32_t off = op_off(row, 32 * g + 16 * half + 4 * t, kGemmBM);
+                *reinterpret_cast<uint2 *>(wst + off) = make_uint2(h0, h1);
+                *reinterpret_cast<uint2 *>(wst + kLo + off) = make_uint2(l0, l1);
             }
-            // words: {row r g0, row r+8 g0, row r g1, row r+8 g1}; scales {s(r,g0), s(r,g1), s(r+8,g0), s(r+8,g1)}
+        }
+    } else {
+        // two 32-column units; bytes {row r k 4t.., row r+8 k 4t.., row r k 16+4t.., row r+8 k 16+4t..};
+        // bf16 holds the int8 values exactly: byte u = q + 128 at bit p gives
+        // 2^23 + u 2^p, minus 2^23 + 128 2^p is q 2^p, whose upper half is bf16(q 2^p)
+#pragma unroll
+        for (uint32_t uh = 0; uh < 2; ++uh) {
+            const uint4 q = uh ? raw.q1 : raw.q0;
             const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-            const float ws[4] = {sc.x, sc.z, sc.y, sc.w};
 #pragma unroll
             for (uint32_t j = 0; j < 4; ++j) {
                 const uint32_t row = tl * 16 + r + (j & 1) * 8;
-                const uint32_t g = j >> 1;
-#pragma unroll
-                for (uint32_t half = 0; half < 2; ++half) {  // low nibbles: k 4t..; high nibbles: k 16+4t..
-                    float v[4];
-#pragma unroll
-                    for (uint32_t i = 0; i < 4; ++i) {
-                        const int qv = (int)((wd[j] << (28 - 8 * i - 4 * half))) >> 28;
-                        v[i] = (float)qv * ws[j];
-                    }
-                    uint2 hi, lo;
-                    split4(v, hi, lo);
-                    const uint32_t k = 32 * g + 16 * half + 4 * t;
-                    const uint32_t off = op_off(row, k, kGemmBM);
-                    *reinterpret_cast<uint2 *>(wst + off) = hi;
-                    *reinterpret_cast<uint2 *>(wst + kLo + off) = lo;
-                }
-            }
-        } else {
-            // q8: two 32-column units per k step; bf16 holds the int8 values exactly
-#pragma unroll
-            for (uint32_t uh = 0; uh < 2; ++uh) {
-                const uint32_t ku = 2 * ks + uh;
-                uint4 q = make_uint4(0, 0, 0, 0);
-                if (T < p.tiles && ku < p.kunits)
-                    q = __ldg(reinterpret_cast<const uint4 *>(p.w + ((size_t)T * p.kunits + ku) * B2_Q8_UNIT_BYTES) +
-                              lane);
-                // bytes: {row r k 4t.., row r+8 k 4t.., row r k 16+4t.., row r+8 k 16+4t..}
-                const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (uint32_t j = 0; j < 4; ++j) {
-                    const uint32_t row = tl * 16 + r + (j & 1) * 8;
-                    const uint32_t k = 32 * uh + 16 * (j >> 1) + 4 * t;
-                    float v[4];
-#pragma unroll
-                    for (uint32_t i = 0; i < 4; ++i) v[i] = (float)((int)(wd[j] << (24 - 8 * i)) >> 24);
-                    const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
-                    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
-                    *reinterpret_cast<uint2 *>(wst + op_off(row, k, kGemmBM)) =
-                        make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
-                }
+                const uint32_t k = 32 * uh + 16 * (j >> 1) + 4 * t;
+                const uint32_t w = wd[j] ^ 0x80808080u, w16 = w >> 16;
+                const float v0 = field_f(w, 0xFFu) - byte_off(0);
+                const float v1 = (field_f(w, 0xFF00u) - byte_off(8)) * 0x1p-8f;
+                const float v2 = field_f(w16, 0xFFu) - byte_off(0);
+                const float v3 = (field_f(w16, 0xFF00u) - byte_off(8)) * 0x1p-8f;
+                const uint32_t a = __byte_perm(__float_as_uint(v0), __float_as_uint(v1), 0x7632);
+                const uint32_t b = __byte_perm(__float_as_uint(v2), __float_as_uint(v3), 0x7632);
+                *reinterpret_cast<uint2 *>(wst + op_off(row, k, kGemmBM)) = make_uint2(a, b);
             }
         }
     }
@@ -342,10 +399,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
     constexpr uint32_t wstage = gemm_w_stage_bytes(FMT);
 
     if (threadIdx.x == 0) {
-        for (uint32_t i = 0; i < kGemmMaxStages; ++i) {
+        for (uint32_t i = 0; i < kGemmXSlots; ++i) {
             mbar_init(&s.x_full[i], 1);
-            mbar_init(&s.w_full[i], 128);
-            mbar_init(&s.empty[i], 1);
+            mbar_init(&s.x_empty[i], 1);
+        }
+        for (uint32_t i = 0; i < kGemmMaxStages; ++i) {
+            mbar_init(&s.w_full[i], 32 * kGemmDequantWarps);
+            mbar_init(&s.w_empty[i], 1);
         }
         mbar_init(s.acc_full, 1);
         fence_mbar_init();
@@ -360,11 +420,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
 
     if (warp == 0) {
         if (lane == 0) {
-            for (uint32_t i = 0; i < nk; ++i) {
-                const uint32_t st = i % p.stages, pass = i / p.stages;
-                if (pass > 0) mbar_wait_bounded(&s.empty[st], (pass - 1) & 1, p.err);
-                mbar_arrive_expect_tx(&s.x_full[st], xstage);
-                bulk_g2s(s.x + st * xstage, p.xs + (size_t)(nt * p.ksteps + k0 + i) * xstage, xstage, &s.x_full[st]);
+            // X slot j holds k steps [j*xk, j*xk + xk): consecutive k steps of a
+            // token tile are contiguous in the prepared buffer, one copy per slot
+            const uint32_t nslots = (nk + p.xk - 1) / p.xk;
+            for (uint32_t j = 0; j < nslots; ++j) {
+                const uint32_t xs = j % kGemmXSlots, pass = j / kGemmXSlots;
+                const uint32_t steps = min(p.xk, nk - j * p.xk);
+                if (pass > 0) mbar_wait_bounded(&s.x_empty[xs], (pass - 1) & 1, p.err);
+                mbar_arrive_expect_tx(&s.x_full[xs], steps * xstage);
+                bulk_g2s(s.x + xs * p.xk * xstage, p.xs + (size_t)(nt * p.ksteps + k0 + j * p.xk) * xstage,
+                         steps * xstage, &s.x_full[xs]);
             }
         }
     } else if (warp == 1) {
@@ -373,10 +438,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
             const uint32_t xb = smem_u32(s.x), wb = smem_u32(s.w);
             for (uint32_t i = 0; i < nk; ++i) {
                 const uint32_t st = i % p.stages, pass = i / p.stages;
-                mbar_wait_bounded(&s.x_full[st], pass & 1, p.err);
+                const uint32_t j = i / p.xk, xs = j % kGemmXSlots, xi = i % p.xk;
+                if (xi == 0) mbar_wait_bounded(&s.x_full[xs], (j / kGemmXSlots) & 1, p.err);
                 mbar_wait_bounded(&s.w_full[st], pass & 1, p.err);
                 tc_fence_after();
-                const uint32_t xa = xb + st * xstage, wa = wb + st * wstage;
+                const uint32_t xa = xb + (xs * p.xk + xi) * xstage, wa = wb + st * wstage;
 #pragma unroll
                 for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
                     // 16 columns = two 8-column chunks
@@ -391,28 +457,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
                         umma_bf16(tmem, a_lo, b_hi, idesc, 1);
                     }
                 }
-                umma_commit(&s.empty[st]);
+                umma_commit(&s.w_empty[st]);
+                if (xi + 1 == p.xk || i + 1 == nk) umma_commit(&s.x_empty[xs]);
             }
             umma_commit(s.acc_full);
             // the accumulator must be complete before tensor memory is freed
             mbar_wait_bounded(s.acc_full, 0, p.err);
         }
     } else {
+        // dequant warp d owns tile d of the row block; its loads run two k
+        // steps ahead of the stores
         const uint32_t d = warp - 2;
+        const uint32_t T = rb * 8 + d;
+        RawStep r0 = load_step<FMT>(p, T, k0, lane);
+        RawStep r1 = nk > 1 ? load_step<FMT>(p, T, k0 + 1, lane) : r0;
         for (uint32_t i = 0; i < nk; ++i) {
             const uint32_t st = i % p.stages, pass = i / p.stages;
-            if (pass > 0) mbar_wait_bounded(&s.empty[st], (pass - 1) & 1, p.err);
-            dequant_step<FMT>(p, s.w + st * wstage, rb, k0 + i, d, lane);
+            const RawStep cur = r0;
+            r0 = r1;
+            if (i + 2 < nk) r1 = load_step<FMT>(p, T, k0 + i + 2, lane);
+            if (pass > 0) mbar_wait_bounded(&s.w_empty[st], (pass - 1) & 1, p.err);
+            dequant_store<FMT>(cur, s.w + st * wstage, d, lane);
             fence_proxy_async();
             mbar_arrive(&s.w_full[st]);
         }
         // epilogue: TMEM lane = output row, column = token
-        const uint32_t q = warp & 3;
+        // (two warps per TMEM lane quarter take alternate 16-column chunks)
+        const uint32_t q = warp & 3, part = d >> 2;
         const uint32_t o = rb * kGemmBM + q * 32 + lane;
         const bool ok = nk == 0 || mbar_wait_bounded(s.acc_full, 0, p.err);
         tc_fence_after();
         const float rs = (FMT == 8 && o < p.rows) ? __ldg(p.row_scale + o) : 1.0f;
-        for (uint32_t c0 = 0; c0 < p.bn; c0 += 16) {
+        for (uint32_t c0 = 16 * part; c0 < p.bn; c0 += 32) {
             float v[16];
             if (nk > 0) {
                 tmem_ld16(tmem + ((q * 32) << 16) + c0, v);
@@ -460,7 +536,7 @@ __global__ void gemm_reduce_kernel(const float *__restrict__ part, uint32_t spli
 // ---- host side ------------------------------------------------------------------------------
 
 struct GemmPlan {
-    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, smem, off_x, off_w, tmem_cols;
+    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, xk, smem, off_x, off_w, tmem_cols;
 };
 
 static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
@@ -470,13 +546,26 @@ static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
     pl.row_blocks = (w.tiles + 7) / 8;
     pl.ksteps = (w.cols + kGemmBK - 1) / kGemmBK;
     const uint32_t xst = gemm_x_stage_bytes(pl.bn), wst = gemm_w_stage_bytes(w.format);
-    const uint32_t head = 1024;  // mbarriers + TMEM slot, then 1 KB-aligned stages
-    uint32_t st = (kGemmSmemLimit - head) / (xst + wst);
+    const uint32_t head = 1024;  // mbarriers + TMEM slot, then 1 KB-aligned rings
+    // X: two slots of xk k steps (about kGemmXCopy bytes per bulk copy: an SM
+    // completes bulk copies at a bounded rate whatever their size); W: the rest
+    uint32_t xk = kGemmXCopy / xst;
+    if (xk < 1) xk = 1;
+    if (xk > 8) xk = 8;
+    uint32_t st = 0;
+    for (;; xk = xk > 1 ? xk / 2 : 0) {
+        if (xk == 0) return false;
+        const uint32_t xbytes = kGemmXSlots * xk * xst;
+        if (head + xbytes + 2 * wst <= kGemmSmemLimit) {
+            st = (kGemmSmemLimit - head - xbytes) / wst;
+            break;
+        }
+    }
     if (st > kGemmMaxStages) st = kGemmMaxStages;
-    if (st < 2) return false;
     pl.stages = st;
+    pl.xk = xk;
     pl.off_x = head;
-    pl.off_w = head + st * xst;
+    pl.off_w = head + kGemmXSlots * xk * xst;
     pl.smem = pl.off_w + st * wst;
     uint32_t tc = 32;
     while (tc < pl.bn) tc <<= 1;
@@ -597,6 +686,7 @@ extern "C" int b2_gemm(const b2_gemm_args *a, void *stream)
     p.splits = pl.splits;
     p.ksplit = pl.ksplit;
     p.stages = pl.stages;
+    p.xk = pl.xk;
     p.off_x = pl.off_x;
     p.off_w = pl.off_w;
     p.tmem_cols = pl.tmem_cols;
