@@ -63,7 +63,8 @@ template <int FMT, int NI>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    const GemvSmem s = gemv_smem(smem, p);
+    GemvSmem s = gemv_smem(smem, p);
+    s.xready = s.full + 2 * kMaxStages;  // after the ring's full / empty barriers
     if (threadIdx.x == 0) gemv_init_barriers(s);
     __syncthreads();
     uint32_t i = 0;
@@ -134,7 +135,7 @@ bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
     if (ns > kMaxStages) ns = kMaxStages;
     pl.round_tiles = rt;
     pl.stages = ns;
-    uint32_t off = 2 * kMaxStages * 8;
+    uint32_t off = 2 * kMaxStages * 8 + 8;  // full / empty barriers, x-ready barrier
     off = (off + 127) & ~127u;
     pl.off_ring = off;
     off += ns * stage;

@@ -19,6 +19,7 @@ constexpr int kThreads = kConsumers + 32;           // + one producer warp
 constexpr int kStageUnits = 64;                     // units per stage: 40 KB of q4, one bulk copy
 constexpr int kMaxStages = 8;                       // ring depth, chosen per launch
 constexpr uint32_t kPreferStages = 5;               // ring depth kept before tile sums get more room
+constexpr uint32_t kEarlyStages = 2;                // weight stages requested before x's digits are ready
 constexpr int kMaxItems = 16;
 constexpr int kConsumerBarrier = 1;                 // named barrier of the consumer warps
 
@@ -424,6 +425,7 @@ struct GemvSmem {
     float *tbufs, *red, *item_scale;
     float *parts;  // [round tiles][kWarps][16 * batch] per-warp tile sums
     unsigned long long *cta_key;
+    uint64_t *xready;  // arrives when x's digit planes are in place (null: no gate)
     uint32_t stages;
 };
 
@@ -439,6 +441,7 @@ __device__ __forceinline__ GemvSmem gemv_smem(uint8_t *smem, const GemvParams &p
     s.red = reinterpret_cast<float *>(smem + p.off_misc);     // [kMaxItems][kWarps][2]
     s.item_scale = s.red + kMaxItems * kWarps * 2;            // [kMaxItems]
     s.cta_key = reinterpret_cast<unsigned long long *>(s.item_scale + kMaxItems);
+    s.xready = nullptr;
     s.stages = p.stages;
     return s;
 }
@@ -451,6 +454,7 @@ __device__ __forceinline__ void gemv_init_barriers(const GemvSmem &s)
         mbar_init(&s.full[i], 1);
         mbar_init(&s.empty[i], kWarps);
     }
+    if (s.xready != nullptr) mbar_init(s.xready, 1);
     fence_mbar_init();
 }
 
@@ -471,7 +475,11 @@ __device__ __forceinline__ void cta_range(const GemvParams &p, uint32_t &t0, uin
 // Producer warp: copy this CTA's stages of one GEMV into the ring. `i` counts
 // stages over the life of the ring (it continues across GEMVs that share a
 // ring); `waited` records that the programmatic-launch wait was taken (the
-// first NS stages are requested before it). Returns false after a timeout.
+// first NS stages are requested before it). With an x-ready gate only the
+// first kEarlyStages stages go out before the consumers have x's digit planes:
+// the prologue's loads of x (L2 hits) otherwise queue behind a ring's worth of
+// weight requests (HBM) and the prologue takes microseconds. Returns false
+// after a timeout.
 template <int FMT>
 __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &waited)
 {
@@ -481,15 +489,20 @@ __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i
     cta_range(p, t0, t1);
     if (t0 == t1) return true;
     StageWalk sw(t0, t1, p.kunits, p.round_tiles);
-    for (; sw.more(); ++i) {
+    bool gated = s.xready != nullptr;
+    for (uint32_t own = 0; sw.more(); ++i, ++own) {
         const uint32_t slot = i % s.stages, n = sw.n();
-        if (i >= s.stages) {
+        if (i >= s.stages || (gated && own >= kEarlyStages)) {
             if (!waited) {
                 pdl_wait();
                 pdl_launch_dependents();
                 waited = true;
             }
-            if (!mbar_wait_bounded(&s.empty[slot], ((i / s.stages) - 1) & 1u, p.err)) return false;
+            if (gated) {
+                if (!mbar_wait_bounded(s.xready, 0, p.err)) return false;
+                gated = false;
+            }
+            if (i >= s.stages && !mbar_wait_bounded(&s.empty[slot], ((i / s.stages) - 1) & 1u, p.err)) return false;
         }
         if (lane == 0) {
             mbar_arrive_expect_tx(&s.full[slot], n * UB);
@@ -526,6 +539,7 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
     for (uint32_t k = threadIdx.x; k < parts_n; k += kConsumers) s.parts[k] = 0.0f;
     prepare_x<FMT>(p, s.xdig, s.item_scale, s.red);
     consumer_sync();
+    if (s.xready != nullptr && threadIdx.x == 0) mbar_arrive(s.xready);
 
     const uint32_t digit = g & 3;
     float acc[NI][2];
