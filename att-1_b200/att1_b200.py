@@ -119,6 +119,13 @@ class TraceCounters(C.Structure):
         "kv_appends", "kv_key_reads", "kv_value_reads", "tile_layer_executions")]
 
 
+class TileCounters(C.Structure):
+    """att1_cluster_tile_counters (include/att1_cluster_infer.h)."""
+    _fields_ = [("activations_received", C.c_uint64), ("activations_sent", C.c_uint64),
+                ("layers_run", C.c_uint64), ("logits_sent", C.c_uint64), ("layer_start", C.c_uint32),
+                ("layer_end", C.c_uint32)]
+
+
 class ClusterConfig(C.Structure):
     _fields_ = [("tile_count", C.c_size_t), ("fabric_queue_capacity", C.c_size_t),
                 ("fabric_max_payload_bytes", C.c_size_t), ("shard_plan_mode", C.c_int)]
@@ -185,6 +192,9 @@ _SIGS = {
     "att1_cluster_infer_destroy": (None, [_P]),
     "att1_cluster_infer_decode_token": (C.c_int, [_P, _U32, C.POINTER(_U32)]),
     "att1_cluster_infer_logits": (C.POINTER(_F), [_P, C.POINTER(_SZ)]),
+    "att1_cluster_infer_get_tile_counters": (C.c_int, [_P, _U32, C.POINTER(TileCounters)]),
+    "att1_cluster_infer_position": (C.c_int, [_P, C.POINTER(_SZ)]),
+    "att1_b200_infer_create_model_tp": (C.c_int, [C.POINTER(Model), _U32, _F, _F, _F, _U32, _U32, C.POINTER(_P)]),
     # kernel ABI (b2_kernels.h)
     "b2_q4_bytes": (_SZ, [_U32, _U32]),
     "b2_q8_bytes": (_SZ, [_U32, _U32]),

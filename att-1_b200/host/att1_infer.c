@@ -931,7 +931,138 @@ static att1_status_t upload_f32(att1_infer_t *inf, float *dst, const att1_model_
     return b2_cuda_status(cudaMemcpyAsync(dst, t->data, t->nbytes, cudaMemcpyHostToDevice, inf->stream));
 }
 
-/* Validate (src/model_view.c:221-366) and upload one precision's weights. */
+/* ---- tensor-parallel shards of file tensors --------------------------------------------------- */
+
+/* Host copy of rows [r0, r0 + nr) x columns [c0, c0 + nc) of a q4 or q8 file
+ * tensor, in the tensor's own layout (q4: packed nibbles then group scales;
+ * q8: int8 values then one scale per row, the whole source row's), described
+ * by `view`. Shards keep whole q4 groups, so the bytes equal those of the
+ * reference's quantisation of the full matrix. */
+static att1_status_t slice_quant(const att1_model_tensor *t, uint64_t r0, uint64_t nr, uint64_t c0, uint64_t nc,
+                                 att1_model_tensor *view, uint8_t **buf)
+{
+    const uint64_t cols = t->shape[1];
+    const uint8_t *src = (const uint8_t *)t->data;
+    uint8_t *out;
+    uint64_t r;
+    *buf = NULL;
+    *view = *t;
+    if (t->dtype == ATT1_MODEL_DTYPE_Q4) {
+        const uint64_t g = q4_group_of(t), rows = t->shape[0];
+        const float *sc = (const float *)(src + rows * cols / 2);
+        float *os;
+        if (c0 % g || nc % g) return ATT1_ERR_UNSUPPORTED;
+        out = malloc(nr * nc / 2 + nr * (nc / g) * sizeof(float));
+        if (out == NULL) return ATT1_ERR_OOM;
+        for (r = 0; r < nr; r++) memcpy(out + r * nc / 2, src + (r0 + r) * cols / 2 + c0 / 2, nc / 2);
+        os = (float *)(out + nr * nc / 2);
+        for (r = 0; r < nr; r++)
+            memcpy(os + r * (nc / g), sc + (r0 + r) * (cols / g) + c0 / g, (nc / g) * sizeof(float));
+        view->nbytes = nr * nc / 2 + nr * (nc / g) * sizeof(float);
+    } else {
+        const uint64_t rows = t->shape[0];
+        const float *sc = (const float *)(src + rows * cols);
+        out = malloc(nr * nc + nr * sizeof(float));
+        if (out == NULL) return ATT1_ERR_OOM;
+        for (r = 0; r < nr; r++) memcpy(out + r * nc, src + (r0 + r) * cols + c0, nc);
+        memcpy(out + nr * nc, sc + r0, nr * sizeof(float));
+        view->nbytes = nr * nc + nr * sizeof(float);
+    }
+    view->shape[0] = nr;
+    view->shape[1] = nc;
+    view->data = out;
+    *buf = out;
+    return ATT1_OK;
+}
+
+/* Host copy of output columns [o0, o0 + no) of an f32 tensor stored [in][out]. */
+static att1_status_t slice_f32_out(const att1_model_tensor *t, uint64_t o0, uint64_t no, att1_model_tensor *view,
+                                   uint8_t **buf)
+{
+    const uint64_t in = t->shape[0], outd = t->shape[1];
+    const float *src = (const float *)t->data;
+    float *out = malloc(in * no * sizeof(float));
+    uint64_t i;
+    *buf = (uint8_t *)out;
+    if (out == NULL) return ATT1_ERR_OOM;
+    for (i = 0; i < in; i++) memcpy(out + i * no, src + i * outd + o0, no * sizeof(float));
+    *view = *t;
+    view->shape[1] = no;
+    view->nbytes = in * no * sizeof(float);
+    view->data = out;
+    return ATT1_OK;
+}
+
+/* q8 from an f32 [in][out] tensor, input rows [i0, i0 + ni) of every output
+ * row: the whole matrix is quantised on the device (each row's scale from all
+ * of its inputs, src/quant.c:61-116) and this shard's 32-column units copied. */
+static att1_status_t load_q8_f32_cols(att1_infer_t *inf, b2_dev_mat *m, const att1_model_tensor *t, uint64_t i0,
+                                      uint64_t ni)
+{
+    const uint32_t in = (uint32_t)t->shape[0], outr = (uint32_t)t->shape[1], tiles = (outr + 15) / 16;
+    const size_t ku_all = in / 32, ku0 = i0 / 32, nku = ni / 32;
+    void *d0 = NULL, *units = NULL;
+    float *rs = NULL;
+    att1_status_t st;
+    cudaError_t e;
+    if (in % 32 || i0 % 32 || ni % 32) return ATT1_ERR_UNSUPPORTED;
+    if ((st = upload_tmp(inf, t, &d0)) != ATT1_OK) goto out;
+    if ((e = cudaMalloc(&units, b2_q8_bytes(outr, in))) != cudaSuccess ||
+        (e = cudaMalloc((void **)&rs, (size_t)tiles * 16 * sizeof(float))) != cudaSuccess) {
+        st = b2_cuda_status(e);
+        goto out;
+    }
+    if (b2_q8_quantize_f32(units, rs, 0, outr, in, (const float *)d0, NULL, 1, B2_ROWS_PLAIN, inf->stream) != 0) {
+        st = ATT1_ERR_STATE;
+        goto out;
+    }
+    e = cudaMemcpy2DAsync(m->data, nku * B2_Q8_UNIT_BYTES, (const uint8_t *)units + ku0 * B2_Q8_UNIT_BYTES,
+                          ku_all * B2_Q8_UNIT_BYTES, nku * B2_Q8_UNIT_BYTES, tiles, cudaMemcpyDeviceToDevice,
+                          inf->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->row_scale, rs, (size_t)tiles * 16 * sizeof(float), cudaMemcpyDeviceToDevice,
+                            inf->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(inf->stream);
+    st = b2_cuda_status(e);
+out:
+    if (d0) cudaFree(d0);
+    if (units) cudaFree(units);
+    if (rs) cudaFree(rs);
+    return st;
+}
+
+/* One matrix (or the gate/up pair) of this rank: rows [r0, r0 + nr) when
+ * `by_rows`, else input columns [r0, r0 + nr); the whole tensor at world 1. */
+static att1_status_t load_shard(att1_infer_t *inf, uint32_t fmt, b2_dev_mat *m, uint32_t tile_off,
+                                const att1_model_tensor *t0, const att1_model_tensor *t1, int by_rows, uint64_t r0,
+                                uint64_t nr)
+{
+    att1_model_tensor v0, v1;
+    uint8_t *b0 = NULL, *b1 = NULL;
+    att1_status_t st;
+    const int f32 = t0->dtype == ATT1_MODEL_DTYPE_F32;
+    if (inf->tp_world == 1) return (fmt == 4 ? load_q4 : load_q8)(inf, m, tile_off, t0, t1);
+    if (f32 && !by_rows) {
+        if (t1 != NULL) return ATT1_ERR_UNSUPPORTED;
+        return load_q8_f32_cols(inf, m, t0, r0, nr);
+    }
+    if (f32) {
+        st = slice_f32_out(t0, r0, nr, &v0, &b0);
+        if (st == ATT1_OK && t1 != NULL) st = slice_f32_out(t1, r0, nr, &v1, &b1);
+    } else if (by_rows) {
+        st = slice_quant(t0, r0, nr, 0, t0->shape[1], &v0, &b0);
+        if (st == ATT1_OK && t1 != NULL) st = slice_quant(t1, r0, nr, 0, t1->shape[1], &v1, &b1);
+    } else {
+        st = slice_quant(t0, 0, t0->shape[0], r0, nr, &v0, &b0);
+    }
+    if (st == ATT1_OK) st = (fmt == 4 ? load_q4 : load_q8)(inf, m, tile_off, &v0, t1 ? &v1 : NULL);
+    free(b0);
+    free(b1);
+    return st;
+}
+
+/* Validate (src/model_view.c:221-366) and upload one precision's weights
+ * (this rank's shard under tensor parallelism). */
 static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, uint32_t fmt)
 {
     const att1_model_config *mc = &m->config;
@@ -973,24 +1104,25 @@ static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, 
         }
         {
             dev_layer *L = &inf->layers[l];
-            att1_status_t (*load)(att1_infer_t *, b2_dev_mat *, uint32_t, const att1_model_tensor *,
-                                  const att1_model_tensor *) = fmt == 4 ? load_q4 : load_q8;
-            if ((st = load(inf, &L->qkv, 0, t[0], NULL)) || (st = load(inf, &L->qkv, inf->q_rows / 16, t[1], NULL)) ||
-                (st = load(inf, &L->qkv, (inf->q_rows + inf->kv_rows) / 16, t[2], NULL)) ||
-                (st = load(inf, &L->wo, 0, t[3], NULL)) || (st = load(inf, &L->gu, 0, t[4], t[5])) ||
-                (st = load(inf, &L->down, 0, t[6], NULL)) || (st = upload_f32(inf, L->attn_norm, an)) ||
-                (st = upload_f32(inf, L->ffn_norm, fn)))
+            const uint64_t r = inf->tp_rank, qr = inf->q_rows, kr = inf->kv_rows, fl = inf->ffl;
+            if ((st = load_shard(inf, fmt, &L->qkv, 0, t[0], NULL, 1, r * qr, qr)) ||
+                (st = load_shard(inf, fmt, &L->qkv, inf->q_rows / 16, t[1], NULL, 1, r * kr, kr)) ||
+                (st = load_shard(inf, fmt, &L->qkv, (inf->q_rows + inf->kv_rows) / 16, t[2], NULL, 1, r * kr, kr)) ||
+                (st = load_shard(inf, fmt, &L->wo, 0, t[3], NULL, 0, r * qr, qr)) ||
+                (st = load_shard(inf, fmt, &L->gu, 0, t[4], t[5], 1, r * fl, fl)) ||
+                (st = load_shard(inf, fmt, &L->down, 0, t[6], NULL, 0, r * fl, fl)) ||
+                (st = upload_f32(inf, L->attn_norm, an)) || (st = upload_f32(inf, L->ffn_norm, fn)))
                 return st;
         }
     }
-    if ((st = (fmt == 4 ? load_q4 : load_q8)(inf, &inf->output, 0, outw, NULL)) ||
+    if ((st = load_shard(inf, fmt, &inf->output, 0, outw, NULL, 1, inf->v_off, inf->vl)) ||
         (st = upload_f32(inf, inf->embed, emb)) || (st = upload_f32(inf, inf->out_norm, onorm)))
         return st;
     return b2_cuda_status(cudaStreamSynchronize(inf->stream));
 }
 
-att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dtype, float eps, float final_eps,
-                                           float theta, att1_infer_t **out_infer)
+static att1_status_t create_model(const att1_model *model, uint32_t dtype, float eps, float final_eps, float theta,
+                                  uint32_t rank, uint32_t world, att1_infer_t **out_infer)
 {
     att1_b200_config c;
     att1_infer_t *inf = NULL;
@@ -1014,17 +1146,37 @@ att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dty
     if (c.vocab == 0 || c.n_layers == 0 || c.n_heads == 0 || c.d_model == 0 || c.d_ff == 0 || c.max_seq == 0 ||
         c.d_model % c.n_heads || ((c.d_model / c.n_heads) % 2))
         return ATT1_ERR_INVALID_ARG;
-    st = new_context(&c, 1, 0, 1, &inf);
+    st = new_context(&c, 1, rank, world, &inf);
     if (st != ATT1_OK) return st;
     inf->model = model;
-    if ((st = alloc_weights(inf, dtype)) || (st = alloc_common(inf)) ||
-        (st = load_model_weights(inf, model, dtype)) || (st = finish_create(inf)))
+    if ((st = alloc_weights(inf, dtype)) || (st = alloc_common(inf)) || (st = load_model_weights(inf, model, dtype)))
         goto fail;
+    /* a tensor-parallel rank is finished when it is connected to its peers */
+    if (world > 1) {
+        cudaError_t e = cudaStreamSynchronize(inf->stream);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        st = b2_cuda_status(e);
+    } else {
+        st = finish_create(inf);
+    }
+    if (st != ATT1_OK) goto fail;
     *out_infer = inf;
     return ATT1_OK;
 fail:
     release(inf);
     return st;
+}
+
+att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dtype, float eps, float final_eps,
+                                           float theta, att1_infer_t **out_infer)
+{
+    return create_model(model, dtype, eps, final_eps, theta, 0, 1, out_infer);
+}
+
+att1_status_t att1_b200_infer_create_model_tp(const att1_model *model, uint32_t dtype, float eps, float final_eps,
+                                              float theta, uint32_t rank, uint32_t world, att1_infer_t **out_infer)
+{
+    return create_model(model, dtype, eps, final_eps, theta, rank, world, out_infer);
 }
 
 att1_status_t att1_infer_create_q4(const att1_model *model, att1_infer_t **out_infer)

@@ -56,6 +56,13 @@ att1_status_t att1_b200_infer_create_synth(const att1_b200_config *cfg, uint64_t
 att1_status_t att1_b200_infer_create_model(const att1_model *model, uint32_t dtype, float eps,
                                            float final_eps, float theta,
                                            att1_infer_t **out_infer);
+/* Rank `rank` of `world` tensor-parallel shards of a loaded .att1 model (the
+ * split of att1_b200_infer_create_synth_tp; q4 and q8 tensors are sliced
+ * byte for byte, f32 tensors quantised per whole output row first). Connect
+ * the ranks before the first step. */
+att1_status_t att1_b200_infer_create_model_tp(const att1_model *model, uint32_t dtype, float eps,
+                                              float final_eps, float theta, uint32_t rank,
+                                              uint32_t world, att1_infer_t **out_infer);
 uint32_t att1_b200_infer_batch(const att1_infer_t *infer);
 
 /* One step for all sequences: tokens[batch] in, greedy next tokens out. */

@@ -116,3 +116,59 @@ def test_tp2_two_processes_ipc_matches_oracle(orc, tmp_path):
         clog, _ = om.decode(int(t))
         for r in range(2):
             assert rel_err(res[r]["logits"][s], clog) <= LOGITS_RTOL
+
+
+def _cluster_vs_single(b2, orc, tmp_path, dtype):
+    """att1_cluster_infer_* with tile_count 2 on a .att1 file against the
+    single-device context of the same file: same tokens, logits within the
+    parity tolerance, per-tile counters advanced."""
+    import ctypes as C
+    import att1file
+    path = str(tmp_path / f"m_{dtype}.att1")
+    att1file.synth_model_file(path, orc, 512, 2, 4, 128, 256, 64, dtype, 21)
+    L = b2.lib()
+    m = b2.Model()
+    assert L.att1_model_load(path.encode(), C.byref(m)) == 0
+    single, cl = C.c_void_p(), C.c_void_p()
+    create = L.att1_infer_create_q4 if dtype == "q4" else L.att1_infer_create
+    ccreate = L.att1_cluster_infer_create_q4 if dtype == "q4" else L.att1_cluster_infer_create
+    assert create(C.byref(m), C.byref(single)) == 0
+    cfg = b2.ClusterConfig(2, 0, 0, 0)
+    assert ccreate(C.byref(m), C.byref(cfg), C.byref(cl)) == 0
+    try:
+        toks = orc.synth_tokens(9, 12, 512)
+        for t in toks:
+            a, b = C.c_uint32(), C.c_uint32()
+            assert L.att1_infer_decode_token(single, int(t), C.byref(a)) == 0
+            assert L.att1_cluster_infer_decode_token(cl, int(t), C.byref(b)) == 0
+            n1, n2 = C.c_size_t(), C.c_size_t()
+            l1 = np.ctypeslib.as_array(L.att1_infer_logits(single, C.byref(n1)), (512,)).copy()
+            l2 = np.ctypeslib.as_array(L.att1_cluster_infer_logits(cl, C.byref(n2)), (512,)).copy()
+            assert n1.value == n2.value == 512
+            assert rel_err(l2, l1) <= LOGITS_RTOL
+            top2 = np.sort(l1)[-2:]
+            if (top2[1] - top2[0]) / np.abs(l1).max() > 2 * LOGITS_RTOL:
+                assert a.value == b.value
+        pos = C.c_size_t()
+        assert L.att1_cluster_infer_position(cl, C.byref(pos)) == 0 and pos.value == 12
+        for tile in range(2):
+            k = b2.TileCounters()
+            assert L.att1_cluster_infer_get_tile_counters(cl, tile, C.byref(k)) == 0
+            assert k.layers_run == 12 * 2 and k.activations_sent == 12 * 2 * 2
+            assert (k.layer_start, k.layer_end) == (0, 2)
+    finally:
+        L.att1_cluster_infer_destroy(cl)
+        L.att1_infer_destroy(single)
+        L.att1_model_free(C.byref(m))
+
+
+@need2
+def test_cluster_two_tiles_q4_file(b2, orc, tmp_path):
+    _cluster_vs_single(b2, orc, tmp_path, "q4")
+
+
+@need2
+def test_cluster_two_tiles_f32_file_q8(b2, orc, tmp_path):
+    """f32 file through att1_cluster_infer_create: q8 weights quantised per
+    whole output row before the row-parallel split."""
+    _cluster_vs_single(b2, orc, tmp_path, "f32")

@@ -131,3 +131,19 @@ def test_no_device_is_reported_cleanly(b2):
     h = C.c_void_p()
     assert L.att1_b200_infer_create_synth(C.byref(cfg), 1, 1, C.byref(h)) != 0
     assert not h.value
+
+
+def test_cluster_rejects_bad_tile_counts(b2, orc, tmp_path):
+    """tile_count 0 is an argument error; more tiles than GPUs (or than the
+    eight of one box) is unsupported: checked before any device work."""
+    path = str(tmp_path / "m.att1")
+    att1file.synth_model_file(path, orc, 64, 1, 2, 32, 64, 8, "q4", 1)
+    L = b2.lib()
+    m = b2.Model()
+    assert L.att1_model_load(path.encode(), C.byref(m)) == 0
+    h = C.c_void_p()
+    assert L.att1_cluster_infer_create_q4(C.byref(m), C.byref(b2.ClusterConfig(0, 0, 0, 0)), C.byref(h)) == -1
+    assert L.att1_cluster_infer_create_q4(C.byref(m), C.byref(b2.ClusterConfig(16, 0, 0, 0)), C.byref(h)) == -9
+    assert L.att1_cluster_infer_create_q4(C.byref(m), C.byref(b2.ClusterConfig(1, 0, 0, 1)), C.byref(h)) == -9
+    assert not h.value
+    L.att1_model_free(C.byref(m))
