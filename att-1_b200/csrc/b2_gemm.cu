@@ -65,6 +65,15 @@ __host__ __device__ constexpr uint32_t gemm_w_stage_bytes(uint32_t fmt)
     return kGemmBM * kGemmBK * 2 * (fmt == 4 ? 2 : 1);
 }
 
+// Token tiles of at most 128 rows keep x's hi and lo halves as ONE operand of
+// 2*bn rows (hi rows, then lo rows, in every 8-column chunk): one MMA then
+// multiplies w_hi with both halves, so a k step needs two MMAs for q4
+// (w_hi [x_hi; x_lo], w_lo x_hi) and one for q8 instead of three and two. At
+// small bn every MMA costs about the read of its 4 KB weight operand whatever
+// N is, so fewer, wider MMAs are faster. Larger tiles (N would pass 256) keep
+// hi and lo as separate operands.
+__host__ __device__ constexpr bool gemm_stacked(uint32_t bn) { return bn <= 128; }
+
 // Token tiling shared by b2_gemm_prep and b2_gemm: as few tiles of at most
 // 256 tokens as possible, equal sizes rounded up to 16 (the MMA's N step).
 __host__ __device__ inline void gemm_token_tiles(uint32_t m, uint32_t &ntiles, uint32_t &bn)
@@ -188,7 +197,8 @@ __host__ __device__ __forceinline__ uint32_t op_off(uint32_t r, uint32_t k, uint
 // ---- X preparation: optional RMSNorm, bf16 hi/lo split, operand layout -------------------
 
 // One CTA per padded token row n (ntiles * bn rows; rows >= m are zero).
-// Output block (tile, k step) = [hi: bn x 64][lo: bn x 64] bf16 in op_off order.
+// Output block (tile, k step): stacked tiles one 2*bn x 64 operand (row n hi,
+// row bn + n lo), else [hi: bn x 64][lo: bn x 64], bf16 in op_off order.
 __global__ void __launch_bounds__(256) gemm_prep_kernel(const float *__restrict__ x, uint32_t x_stride, uint32_t m,
                                                         uint32_t cols, const float *__restrict__ norm_w, float eps,
                                                         uint32_t bn, uint32_t ksteps, uint8_t *__restrict__ xs,
@@ -239,9 +249,12 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(const float *__restrict_
         split4(a4, h0, l0);
         split4(b4, h1, l1);
         uint8_t *blk = xs + (size_t)(tile * ksteps + k0 / kGemmBK) * xstage;
-        const uint32_t off = op_off(nr, k0 % kGemmBK, bn);
-        *reinterpret_cast<uint4 *>(blk + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
-        *reinterpret_cast<uint4 *>(blk + xstage / 2 + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+        const uint32_t kc = k0 % kGemmBK;
+        const bool stk = gemm_stacked(bn);
+        const uint32_t off_hi = stk ? op_off(nr, kc, 2 * bn) : op_off(nr, kc, bn);
+        const uint32_t off_lo = stk ? op_off(bn + nr, kc, 2 * bn) : xstage / 2 + op_off(nr, kc, bn);
+        *reinterpret_cast<uint4 *>(blk + off_hi) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+        *reinterpret_cast<uint4 *>(blk + off_lo) = make_uint4(l0.x, l0.y, l1.x, l1.y);
     }
     if (!finite) raise_error(err, B2_ERR_NONFINITE);
 }
@@ -434,7 +447,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            const bool stk = gemm_stacked(p.bn);
             const uint32_t idesc = umma_idesc_bf16(kGemmBM, p.bn);
+            const uint32_t idesc2 = umma_idesc_bf16(kGemmBM, 2 * p.bn);  // stacked: hi and lo rows
             const uint32_t xb = smem_u32(s.x), wb = smem_u32(s.w);
             for (uint32_t i = 0; i < nk; ++i) {
                 const uint32_t st = i % p.stages, pass = i / p.stages;
@@ -443,6 +458,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
                 mbar_wait_bounded(&s.w_full[st], pass & 1, p.err);
                 tc_fence_after();
                 const uint32_t xa = xb + (xs * p.xk + xi) * xstage, wa = wb + st * wstage;
+                if (stk) {
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
+                        const uint64_t a_hi = umma_desc(wa + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                        // rows 0..bn-1 of this descriptor are x_hi, bn..2bn-1 x_lo
+                        const uint64_t b = umma_desc(xa + kk * 2 * (2 * p.bn * 16), 2 * p.bn * 16, 128);
+                        umma_bf16(tmem, a_hi, b, idesc2, (i | kk) != 0);
+                        if constexpr (FMT == 4) {
+                            const uint64_t a_lo =
+                                umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                            umma_bf16(tmem, a_lo, b, idesc, 1);  // N = bn: the x_hi rows only
+                        }
+                    }
+                } else {
 #pragma unroll
                 for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
                     // 16 columns = two 8-column chunks
@@ -456,6 +485,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
                             umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
                         umma_bf16(tmem, a_lo, b_hi, idesc, 1);
                     }
+                }
                 }
                 umma_commit(&s.w_empty[st]);
                 if (xi + 1 == p.xk || i + 1 == nk) umma_commit(&s.x_empty[xs]);
@@ -488,10 +518,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams 
         const bool ok = nk == 0 || mbar_wait_bounded(s.acc_full, 0, p.err);
         tc_fence_after();
         const float rs = (FMT == 8 && o < p.rows) ? __ldg(p.row_scale + o) : 1.0f;
+        const bool stk = gemm_stacked(p.bn);
         for (uint32_t c0 = 16 * part; c0 < p.bn; c0 += 32) {
             float v[16];
             if (nk > 0) {
                 tmem_ld16(tmem + ((q * 32) << 16) + c0, v);
+                if (stk) {  // + the x_lo columns
+                    float v2[16];
+                    tmem_ld16(tmem + ((q * 32) << 16) + p.bn + c0, v2);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] += v2[j];
+                }
             } else {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) v[j] = 0.0f;
@@ -568,7 +605,7 @@ static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
     pl.off_w = head + kGemmXSlots * xk * xst;
     pl.smem = pl.off_w + st * wst;
     uint32_t tc = 32;
-    while (tc < pl.bn) tc <<= 1;
+    while (tc < (gemm_stacked(pl.bn) ? 2 * pl.bn : pl.bn)) tc <<= 1;
     pl.tmem_cols = tc;
     // k splits: fill the SMs when row blocks x token tiles do not, at least 4 k steps each
     uint32_t splits = a->splits;
