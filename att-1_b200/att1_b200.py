@@ -119,6 +119,22 @@ class TraceCounters(C.Structure):
         "kv_appends", "kv_key_reads", "kv_value_reads", "tile_layer_executions")]
 
 
+class KvMmuConfig(C.Structure):
+    """att1_kv_mmu_config (include/att1_kv_mmu.h)."""
+    _fields_ = [(n, C.c_size_t) for n in ("max_sessions", "max_pages", "num_layers", "num_heads", "head_dim",
+                                          "page_tokens", "max_positions")]
+
+
+class KvMmuCounters(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("page_hits", "page_misses", "page_allocations", "append_ops",
+                                          "read_ops", "range_copy_ops", "errors")]
+
+
+class KvMmuPageRef(C.Structure):
+    _fields_ = [("physical_page", C.c_uint64), ("session_id", C.c_uint64), ("layer_id", C.c_size_t),
+                ("logical_page", C.c_size_t), ("page_tokens", C.c_size_t)]
+
+
 class TileCounters(C.Structure):
     """att1_cluster_tile_counters (include/att1_cluster_infer.h)."""
     _fields_ = [("activations_received", C.c_uint64), ("activations_sent", C.c_uint64),
@@ -195,6 +211,18 @@ _SIGS = {
     "att1_cluster_infer_get_tile_counters": (C.c_int, [_P, _U32, C.POINTER(TileCounters)]),
     "att1_cluster_infer_position": (C.c_int, [_P, C.POINTER(_SZ)]),
     "att1_b200_infer_create_model_tp": (C.c_int, [C.POINTER(Model), _U32, _F, _F, _F, _U32, _U32, C.POINTER(_P)]),
+    # KV-MMU (att1_kv_mmu.h)
+    "att1_kv_mmu_create": (C.c_int, [C.POINTER(KvMmuConfig), C.POINTER(_P)]),
+    "att1_kv_mmu_destroy": (None, [_P]),
+    "att1_kv_mmu_create_session": (C.c_int, [_P, C.c_uint64]),
+    "att1_kv_mmu_destroy_session": (C.c_int, [_P, C.c_uint64]),
+    "att1_kv_mmu_append": (C.c_int, [_P, C.c_uint64, _SZ, _SZ, _P, _P]),
+    "att1_kv_mmu_read": (C.c_int, [_P, C.c_uint64, _SZ, _SZ, _SZ, _P, _P]),
+    "att1_kv_mmu_copy_range": (C.c_int, [_P, C.c_uint64, _SZ, _SZ, _SZ, _SZ, _P, _P]),
+    "att1_kv_mmu_lookup_page": (C.c_int, [_P, C.c_uint64, _SZ, _SZ, C.POINTER(KvMmuPageRef)]),
+    "att1_kv_mmu_get_counters": (None, [_P, C.POINTER(KvMmuCounters)]),
+    "att1_kv_mmu_reset_counters": (None, [_P]),
+    "att1_b200_kv_mmu_layout": (C.c_int, [_P, C.c_uint64, _SZ, C.POINTER(KVLayout)]),
     # kernel ABI (b2_kernels.h)
     "b2_q4_bytes": (_SZ, [_U32, _U32]),
     "b2_q8_bytes": (_SZ, [_U32, _U32]),

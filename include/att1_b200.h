@@ -17,7 +17,9 @@
 #define ATT1_B200_H
 
 #include "att1_infer.h"
+#include "att1_kv_mmu.h"
 #include "att1_status.h"
+#include "b2_kernels.h"
 
 #include <stddef.h>
 #include <stdint.h>
@@ -133,6 +135,14 @@ att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item
                                         size_t count, float *keys, float *values);
 /* Device bytes held by the context (weights, KV pages, buffers). */
 size_t att1_b200_infer_device_bytes(const att1_infer_t *infer);
+
+/* One session's layer of a KV-MMU (att1_kv_mmu.h) as the kernels of
+ * b2_kernels.h address KV: the device page pools, that session and layer's
+ * device page-table row (batch item 0) and the page geometry. Valid until the
+ * session is destroyed; positions the session has appended are readable by
+ * b2_attn, and the QKV epilogue may append the next one. */
+att1_status_t att1_b200_kv_mmu_layout(const att1_kv_mmu *mmu, uint64_t session_id, size_t layer_id,
+                                      b2_kv_layout *out);
 
 #ifdef __cplusplus
 }
