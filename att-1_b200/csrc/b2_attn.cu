@@ -56,13 +56,15 @@ __device__ __forceinline__ void soft_merge4(float &m, float &l, float4 &o, float
 // rows are contiguous, so a producer warp streams the range through a ring of
 // kBufs shared-memory sub-tiles with 1-D bulk copies (TMA; "full" mbarrier
 // per stage, counted in bytes). Sixteen consumer warps take positions of each
-// sub-tile (LP lanes per position, four dimensions per lane), compute the
+// sub-tile (LP lanes per position, 4*V4 dimensions per lane: float4 chunk v of
+// lane sl holds dimensions 4*(sl + v*LP)..+3, so a lane group's loads of one
+// chunk are contiguous), compute the
 // scores of the query heads that share the KV head with a halving exchange
 // (each step hands half of the heads to the partner lane), keep an online
 // softmax and the weighted V sum per lane, and release the stage on its
 // "empty" mbarrier, so warps never wait for one another while streaming.
 // At the end the lane groups and the warps are merged.
-template <int LP, int MG>  // lanes per position (attn_lanes), query heads per KV head (bound)
+template <int LP, int MG, int V4>  // lanes per position, query heads per KV head (bound), float4s per lane
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -137,46 +139,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
     pdl_wait();
     pdl_launch_dependents();
     const int sub = lane / LP, sl = lane % LP;
-    const uint32_t d0 = 4 * sl;
-    const bool dval = d0 < hd;
-    float4 qv[MG];
+    uint32_t dv[V4];
+    bool dval[V4];
 #pragma unroll
-    for (int gq = 0; gq < MG; ++gq) {
-        qv[gq] = make_float4(0, 0, 0, 0);
-        if (gq < (int)G && dval)
-            qv[gq] = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)item * p.n_heads * hd +
-                                                             (size_t)(kvh * G + gq) * hd + d0));
+    for (int v = 0; v < V4; ++v) {
+        dv[v] = 4 * (sl + v * LP);
+        dval[v] = dv[v] < hd;
     }
+    float4 qv[MG][V4];
+#pragma unroll
+    for (int gq = 0; gq < MG; ++gq)
+#pragma unroll
+        for (int v = 0; v < V4; ++v) {
+            qv[gq][v] = make_float4(0, 0, 0, 0);
+            if (gq < (int)G && dval[v])
+                qv[gq][v] = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)item * p.n_heads * hd +
+                                                                    (size_t)(kvh * G + gq) * hd + dv[v]));
+        }
     float m[MG], l[MG];
-    float4 o[MG];
+    float4 o[MG][V4];
 #pragma unroll
     for (int gq = 0; gq < MG; ++gq) {
         m[gq] = -INFINITY;
         l[gq] = 0.0f;
-        o[gq] = make_float4(0, 0, 0, 0);
+#pragma unroll
+        for (int v = 0; v < V4; ++v) o[gq][v] = make_float4(0, 0, 0, 0);
     }
     bool ok = true;
     for (uint32_t t = 0; t < ntiles; ++t) {
         const uint32_t buf = t % kBufs, nt = min(kSub, n - t * kSub);
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[buf], (t / kBufs) & 1u, p.err));
         const float *K = Kb + (size_t)buf * kSub * hd, *V = Vb + (size_t)buf * kSub * hd;
-        // this warp's positions of the sub-tile, two at a time (warp-uniform trip count)
+        // this warp's positions of the sub-tile (warp-uniform trip count); a lane
+        // group takes two at a time only when the warps' groups cannot cover
+        // the sub-tile in one pass (NP = 1: the second would always be empty)
         constexpr uint32_t kStride = kAttnWarps * PPW;
-        for (uint32_t wb = warp * PPW; wb < nt; wb += 2 * kStride) {
+        constexpr int NP = kStride < kSub ? 2 : 1;
+        for (uint32_t wb = warp * PPW; wb < nt; wb += NP * kStride) {
             const uint32_t ra = wb + sub, rb = ra + kStride;
-            const bool va = ok && ra < nt, vb = ok && rb < nt;
-            float4 k4[2], v4[2];
-            k4[0] = (va && dval) ? *reinterpret_cast<const float4 *>(K + ra * hd + d0) : make_float4(0, 0, 0, 0);
-            v4[0] = (va && dval) ? *reinterpret_cast<const float4 *>(V + ra * hd + d0) : make_float4(0, 0, 0, 0);
-            k4[1] = (vb && dval) ? *reinterpret_cast<const float4 *>(K + rb * hd + d0) : make_float4(0, 0, 0, 0);
-            v4[1] = (vb && dval) ? *reinterpret_cast<const float4 *>(V + rb * hd + d0) : make_float4(0, 0, 0, 0);
-            float mine[2];
+            const bool va = ok && ra < nt, vb = NP == 2 && ok && rb < nt;
+            float4 k4[NP][V4], v4[NP][V4];
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
+            for (int v = 0; v < V4; ++v) {
+                const float4 z = make_float4(0, 0, 0, 0);
+                k4[0][v] = (va && dval[v]) ? *reinterpret_cast<const float4 *>(K + ra * hd + dv[v]) : z;
+                v4[0][v] = (va && dval[v]) ? *reinterpret_cast<const float4 *>(V + ra * hd + dv[v]) : z;
+                if constexpr (NP == 2) {
+                    k4[NP - 1][v] = vb && dval[v] ? *reinterpret_cast<const float4 *>(K + rb * hd + dv[v]) : z;
+                    v4[NP - 1][v] = vb && dval[v] ? *reinterpret_cast<const float4 *>(V + rb * hd + dv[v]) : z;
+                }
+            }
+            float mine[NP];
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
                 float dot[MG];
 #pragma unroll
-                for (int gq = 0; gq < MG; ++gq)
-                    dot[gq] = qv[gq].x * k4[j].x + qv[gq].y * k4[j].y + qv[gq].z * k4[j].z + qv[gq].w * k4[j].w;
+                for (int gq = 0; gq < MG; ++gq) {
+                    dot[gq] = 0.0f;
+#pragma unroll
+                    for (int v = 0; v < V4; ++v)
+                        dot[gq] += qv[gq][v].x * k4[j][v].x + qv[gq][v].y * k4[j][v].y + qv[gq][v].z * k4[j][v].z +
+                                   qv[gq][v].w * k4[j][v].w;
+                }
                 // sum over the LP lanes of the position: while more than one head
                 // is left each exchange hands half of them to the partner lane
                 // (the upper lane keeps the upper half), then plain exchanges;
@@ -204,16 +228,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
                 if (gq < (int)G) {
                     const int src = (sub * LP) | (gq * (LP / MG));  // a lane holding head gq
                     const float sa = __shfl_sync(0xffffffffu, mine[0], src);
-                    const float sb = __shfl_sync(0xffffffffu, mine[1], src);
+                    const float sb = NP == 2 ? __shfl_sync(0xffffffffu, mine[NP - 1], src) : 0.0f;
                     if (va) {
                         const float nm = fmaxf(m[gq], vb ? fmaxf(sa, sb) : sa);
                         const float corr = __expf(m[gq] - nm);
                         const float pa = __expf(sa - nm), pb = vb ? __expf(sb - nm) : 0.0f;
                         l[gq] = fmaf(l[gq], corr, pa + pb);
-                        o[gq] = make_float4(fmaf(o[gq].x, corr, fmaf(pa, v4[0].x, pb * v4[1].x)),
-                                            fmaf(o[gq].y, corr, fmaf(pa, v4[0].y, pb * v4[1].y)),
-                                            fmaf(o[gq].z, corr, fmaf(pa, v4[0].z, pb * v4[1].z)),
-                                            fmaf(o[gq].w, corr, fmaf(pa, v4[0].w, pb * v4[1].w)));
+#pragma unroll
+                        for (int v = 0; v < V4; ++v) {
+                            float4 w = make_float4(pa * v4[0][v].x, pa * v4[0][v].y, pa * v4[0][v].z, pa * v4[0][v].w);
+                            if constexpr (NP == 2)
+                                w = make_float4(fmaf(pb, v4[NP - 1][v].x, w.x), fmaf(pb, v4[NP - 1][v].y, w.y),
+                                                fmaf(pb, v4[NP - 1][v].z, w.z), fmaf(pb, v4[NP - 1][v].w, w.w));
+                            o[gq][v] = make_float4(fmaf(o[gq][v].x, corr, w.x), fmaf(o[gq][v].y, corr, w.y),
+                                                   fmaf(o[gq][v].z, corr, w.z), fmaf(o[gq][v].w, corr, w.w));
+                        }
                         m[gq] = nm;
                     }
                 }
@@ -229,12 +258,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
         for (int gq = 0; gq < MG; ++gq) {
             const float m2 = __shfl_xor_sync(0xffffffffu, m[gq], off);
             const float l2 = __shfl_xor_sync(0xffffffffu, l[gq], off);
-            float4 o2;
-            o2.x = __shfl_xor_sync(0xffffffffu, o[gq].x, off);
-            o2.y = __shfl_xor_sync(0xffffffffu, o[gq].y, off);
-            o2.z = __shfl_xor_sync(0xffffffffu, o[gq].z, off);
-            o2.w = __shfl_xor_sync(0xffffffffu, o[gq].w, off);
-            soft_merge4(m[gq], l[gq], o[gq], m2, l2, o2);
+            float4 o2[V4];
+#pragma unroll
+            for (int v = 0; v < V4; ++v) {
+                o2[v].x = __shfl_xor_sync(0xffffffffu, o[gq][v].x, off);
+                o2[v].y = __shfl_xor_sync(0xffffffffu, o[gq][v].y, off);
+                o2[v].z = __shfl_xor_sync(0xffffffffu, o[gq][v].z, off);
+                o2[v].w = __shfl_xor_sync(0xffffffffu, o[gq][v].w, off);
+            }
+            // the chunks share one (m, l): merge them with the same factors
+            const float M = fmaxf(m[gq], m2);
+            if (M != -INFINITY) {
+                const float f1 = expf(m[gq] - M), f2 = expf(m2 - M);
+                l[gq] = fmaf(l[gq], f1, l2 * f2);
+#pragma unroll
+                for (int v = 0; v < V4; ++v)
+                    o[gq][v] = make_float4(fmaf(o[gq][v].x, f1, o2[v].x * f2), fmaf(o[gq][v].y, f1, o2[v].y * f2),
+                                           fmaf(o[gq][v].z, f1, o2[v].z * f2), fmaf(o[gq][v].w, f1, o2[v].w * f2));
+                m[gq] = M;
+            }
         }
     }
     // merge the warps: state in shared memory (the ring is drained)
@@ -248,7 +290,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
                 wm[warp * MG + gq] = m[gq];
                 wl[warp * MG + gq] = l[gq];
             }
-            if (dval) *reinterpret_cast<float4 *>(wo + ((size_t)warp * MG + gq) * hd + d0) = o[gq];
+#pragma unroll
+            for (int v = 0; v < V4; ++v)
+                if (dval[v]) *reinterpret_cast<float4 *>(wo + ((size_t)warp * MG + gq) * hd + dv[v]) = o[gq][v];
         }
     }
     SYNC();
@@ -289,13 +333,16 @@ static cudaError_t launch_attn(const AttnParams &p, dim3 grid, int pdl, cudaStre
     const int mg = p.group <= 4 ? 4 : 8;
     cfg.dynamicSmemBytes = attn_ring_smem(p.head_dim);
     const void *fn;
+    // one float4 of dimensions per lane: 8, 16 or 32 lanes per position (16
+    // lanes x 8 dimensions for head_dim 128 measured slower in the decode step:
+    // 2.37 vs 2.29 ms, at the 96-register limit of 17 warps)
     switch (attn_lanes(p.head_dim) * 10 + mg) {
-    case 84: fn = (const void *)attn_ring_kernel<8, 4>; break;
-    case 88: fn = (const void *)attn_ring_kernel<8, 8>; break;
-    case 164: fn = (const void *)attn_ring_kernel<16, 4>; break;
-    case 168: fn = (const void *)attn_ring_kernel<16, 8>; break;
-    case 324: fn = (const void *)attn_ring_kernel<32, 4>; break;
-    default: fn = (const void *)attn_ring_kernel<32, 8>; break;
+    case 84: fn = (const void *)attn_ring_kernel<8, 4, 1>; break;
+    case 88: fn = (const void *)attn_ring_kernel<8, 8, 1>; break;
+    case 164: fn = (const void *)attn_ring_kernel<16, 4, 1>; break;
+    case 168: fn = (const void *)attn_ring_kernel<16, 8, 1>; break;
+    case 324: fn = (const void *)attn_ring_kernel<32, 4, 1>; break;
+    default: fn = (const void *)attn_ring_kernel<32, 8, 1>; break;
     }
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
     if (e != cudaSuccess) return e;
