@@ -208,6 +208,16 @@ __device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t *p)
     return v;
 }
 
+// Acquire-release atomic add at system scope: this thread's earlier writes
+// (and, after a CTA barrier, the CTA's) are performed before the add, and the
+// adds it reads from are visible to it afterwards.
+__device__ __forceinline__ int atom_add_acq_rel_sys(int *p, int v)
+{
+    int old;
+    asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ uint64_t tp_want(const b2_tp &tp)
 {
     return (uint64_t)__ldcg(tp.epoch) + 1;
@@ -232,8 +242,9 @@ __device__ __forceinline__ bool tp_wait(const b2_tp &tp, uint32_t point, int32_t
     return true;
 }
 
-// One thread: publish this rank's contribution to `point` (its stores to the
-// slots are ordered before by the caller's fence) to every rank.
+// One thread: publish this rank's contribution to `point` to every rank with
+// system-scope release stores (the CTAs' stores to the slots were ordered
+// before them by the acquire-release adds that chain the CTAs).
 __device__ __forceinline__ void tp_signal(const b2_tp &tp, uint32_t point)
 {
     const uint64_t v = tp_want(tp);

@@ -680,14 +680,13 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
         }
         consumer_sync();
         if (p.epilogue == B2_EPI_PUSH && threadIdx.x == 0) {
-            // one system fence per CTA round (the barrier above orders every
-            // warp's peer stores before it); the last round of the GEMV on
-            // this rank publishes the point
-            __threadfence_system();
+            // one system-scope acquire-release add per CTA round (the barrier
+            // above orders every warp's peer stores before it); the round that
+            // completes the GEMV on this rank has acquired all the others and
+            // publishes the point with a release store (no further fence)
             const int n_round = (int)(round_t1 - round_t0);
-            if (atomicAdd(p.tp.done, n_round) == (int)p.tiles - n_round) {
+            if (atom_add_acq_rel_sys(p.tp.done, n_round) == (int)p.tiles - n_round) {
                 *p.tp.done = 0;
-                __threadfence_system();
                 tp_signal(p.tp, p.tp.out_point);
             }
         }
@@ -703,16 +702,13 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
             // the last CTA publishes this rank's logits and argmax keys
             consumer_sync();
             if (threadIdx.x == 0) {
-                __threadfence_system();
-                if (atomicAdd(p.tp.done, 1) == (int)p.grid - 1) {
+                if (atom_add_acq_rel_sys(p.tp.done, 1) == (int)p.grid - 1) {
                     *p.tp.done = 0;
-                    __threadfence();
                     for (uint32_t b = 0; b < B; ++b) {
                         const uint64_t key = __ldcg(p.argmax + b);
                         for (uint32_t q = 0; q < p.tp.world; ++q) *tp_key(p.tp.peer[q], p.tp, p.tp.rank, b) = key;
                     }
-                    __threadfence_system();
-                    tp_signal(p.tp, p.tp.out_point);
+                    tp_signal(p.tp, p.tp.out_point);  // release stores: the keys are ordered before
                 }
             }
         }
