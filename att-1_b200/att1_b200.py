@@ -223,6 +223,7 @@ _SIGS = {
     "att1_kv_mmu_get_counters": (None, [_P, C.POINTER(KvMmuCounters)]),
     "att1_kv_mmu_reset_counters": (None, [_P]),
     "att1_b200_kv_mmu_layout": (C.c_int, [_P, C.c_uint64, _SZ, C.POINTER(KVLayout)]),
+    "att1_b200_infer_use_kv_mmu": (C.c_int, [_P, _P, C.POINTER(C.c_uint64)]),
     # kernel ABI (b2_kernels.h)
     "b2_q4_bytes": (_SZ, [_U32, _U32]),
     "b2_q8_bytes": (_SZ, [_U32, _U32]),

@@ -76,6 +76,11 @@ struct att1_infer {
     int logits_valid;
     size_t position;
     int use_graph, use_pdl, use_persistent;
+    /* KV in the sessions of a KV-MMU (att1_b200_infer_use_kv_mmu): item b is the
+     * session in slot mmu_slot0 + b; NULL: the context's own page pools */
+    att1_kv_mmu *mmu;
+    uint64_t mmu_sid0;
+    size_t mmu_slot0;
     /* decode through the tensor-core GEMM (batches the GEMVs cannot hold) */
     int use_dense;
     float *y_qkv, *y_gu;
@@ -264,6 +269,7 @@ static void gemv_base(att1_infer_t *inf, b2_gemv_args *a, const b2_dev_mat *m)
 static b2_kv_layout kv_layout(att1_infer_t *inf, uint32_t layer)
 {
     b2_kv_layout kv;
+    if (inf->mmu != NULL && att1_b200_kv_mmu_layout(inf->mmu, inf->mmu_sid0, layer, &kv) == ATT1_OK) return kv;
     kv.k_pool = inf->k_pool + (size_t)layer * inf->layer_pool_elems;
     kv.v_pool = inf->v_pool + (size_t)layer * inf->layer_pool_elems;
     kv.page_table = inf->page_table;
@@ -1288,14 +1294,14 @@ static int dense_layer(att1_infer_t *inf, uint32_t l, const dense_bufs *b, cudaS
     r.rope_freq = inf->rope_freq;
     r.positions = b->positions;
     r.kv = kv_layout(inf, l);
-    r.kv.page_table = b->page_table;
+    if (b->page_table != NULL) r.kv.page_table = b->page_table;
     r.err = inf->err_d;
     r.pdl = inf->use_pdl;
     if ((rc = b2_rows_epilogue(&r, st)) != 0) return rc;
     at = L->a_attn;
     at.batch = b->m;
     at.q = b->q;
-    at.kv.page_table = b->page_table;
+    at.kv = r.kv;
     at.positions = b->positions;
     at.ctx = b->ctx;
     at.scratch = b->ascratch;
@@ -1390,7 +1396,7 @@ static void decode_bufs(att1_infer_t *inf, dense_bufs *b)
     b->y_qkv = inf->y_qkv;
     b->y_gu = inf->y_gu;
     b->positions = inf->pos_d;
-    b->page_table = inf->page_table;
+    b->page_table = NULL; /* each layer's own table rows (kv_layout) */
     b->xs = inf->xs;
     b->xs_bytes = inf->xs_bytes;
     b->gscratch = inf->gscratch;
@@ -1518,6 +1524,11 @@ static att1_status_t step_launch(att1_infer_t *inf, const uint32_t *tokens)
             cudaSuccess)
             return ATT1_ERR_STATE;
     }
+    if (inf->mmu != NULL) { /* pages for this position in every session, before the kernels append there */
+        att1_status_t st;
+        for (b = 0; b < inf->batch; b++)
+            if ((st = b2_kv_mmu_reserve(inf->mmu, inf->mmu_slot0 + b, inf->position, 1)) != ATT1_OK) return st;
+    }
     if (cudaMemcpyAsync(inf->tokens_d, inf->tokens_h, inf->batch * sizeof(uint32_t), cudaMemcpyHostToDevice,
                         inf->stream) != cudaSuccess)
         return ATT1_ERR_STATE;
@@ -1550,6 +1561,8 @@ static att1_status_t step_finish(att1_infer_t *inf, uint32_t *out_tokens)
         att1_trace_record_logits(inf->trace, 0, (uint64_t)c->vocab * sizeof(float));
         att1_trace_record_token(inf->trace, us);
     }
+    if (inf->mmu != NULL)
+        for (b = 0; b < inf->batch; b++) b2_kv_mmu_advance(inf->mmu, inf->mmu_slot0 + b, 1);
     inf->position++;
     return ATT1_OK;
 }
@@ -1678,7 +1691,7 @@ att1_status_t att1_b200_infer_prefill(att1_infer_t *inf, const uint32_t *tokens,
     if (inf == NULL || tokens == NULL || out_token == NULL || n == 0) return ATT1_ERR_INVALID_ARG;
     c = &inf->cfg;
     if (inf->batch != 1 || inf->step_pending || !backend_ok(inf)) return ATT1_ERR_STATE;
-    if (inf->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
+    if (inf->tp_world > 1 || inf->mmu != NULL) return ATT1_ERR_UNSUPPORTED;
     if (n > c->max_seq || inf->position + n > c->max_seq) return ATT1_ERR_INVALID_ARG;
     for (i = 0; i < n; i++)
         if (tokens[i] >= c->vocab) return ATT1_ERR_INVALID_ARG;
@@ -1769,7 +1782,7 @@ att1_status_t att1_infer_generate(att1_infer_t *infer, const unsigned char *prom
     /* same contract as src/infer.c:882-928 */
     if (infer == NULL || prompt == NULL || out_tokens == NULL || out_token_count == NULL) return ATT1_ERR_INVALID_ARG;
     if (prompt_bytes == 0 || out_token_capacity < generated_token_count) return ATT1_ERR_INVALID_ARG;
-    if (infer->batch == 1 && infer->tp_world == 1) {
+    if (infer->batch == 1 && infer->tp_world == 1 && infer->mmu == NULL) {
         /* the prompt in one pass over the weights per chunk (same results as
          * the token-by-token loop of the reference) */
         uint32_t *ids = malloc(prompt_bytes * sizeof(uint32_t));
@@ -1921,6 +1934,49 @@ att1_status_t att1_b200_set_device(int device)
     return cudaSetDevice(device) == cudaSuccess ? ATT1_OK : ATT1_ERR_INVALID_ARG;
 }
 
+/* Batch item b keeps its KV in KV-MMU session session_ids[b] (pages mapped on
+ * demand as positions advance; the MMU's lengths and append counters follow
+ * the steps). Sessions must sit in consecutive slots in batch order (create
+ * them one after another), be empty, and match the context's layers, KV
+ * heads and head_dim, with max_positions >= max_seq. NULL mmu returns to the
+ * context's own pools. Only at position 0, one GPU. */
+att1_status_t att1_b200_infer_use_kv_mmu(att1_infer_t *infer, att1_kv_mmu *mmu, const uint64_t *session_ids)
+{
+    const att1_kv_mmu_config *mc;
+    size_t slot0 = 0, slot, l;
+    uint32_t b;
+    att1_status_t st;
+    if (infer == NULL || (mmu != NULL && session_ids == NULL)) return ATT1_ERR_INVALID_ARG;
+    if (infer->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
+    if (infer->position != 0 || infer->step_pending) return ATT1_ERR_STATE;
+    if (mmu != NULL) {
+        mc = b2_kv_mmu_config(mmu);
+        if (mc->num_layers != infer->cfg.n_layers || mc->num_heads != infer->hkv || mc->head_dim != infer->head_dim ||
+            mc->max_positions < infer->cfg.max_seq)
+            return ATT1_ERR_SHAPE;
+        for (b = 0; b < infer->batch; b++) {
+            if (!b2_kv_mmu_session_slot(mmu, session_ids[b], &slot)) return ATT1_ERR_NOT_FOUND;
+            if (b == 0) slot0 = slot;
+            if (slot != slot0 + b) return ATT1_ERR_UNSUPPORTED;
+            for (l = 0; l < mc->num_layers; l++)
+                if (b2_kv_mmu_length(mmu, slot, l) != 0) return ATT1_ERR_STATE;
+        }
+    }
+    if (cudaSetDevice(infer->device) != cudaSuccess) return ATT1_ERR_STATE;
+    cudaStreamSynchronize(infer->stream);
+    infer->mmu = mmu;
+    infer->mmu_sid0 = mmu != NULL ? session_ids[0] : 0;
+    infer->mmu_slot0 = slot0;
+    /* the kernels' arguments name the KV pools: rebuild them and the step graph */
+    if (infer->exec) {
+        cudaGraphExecDestroy(infer->exec);
+        infer->exec = NULL;
+    }
+    infer->graph_failed = 0;
+    if ((st = build_args(infer)) != ATT1_OK) return st;
+    return b2_cuda_status(cudaStreamSynchronize(infer->stream));
+}
+
 att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps)
 {
     uint32_t i;
@@ -1934,8 +1990,19 @@ att1_status_t att1_b200_infer_run_steps(att1_infer_t *infer, uint32_t steps)
                             infer->stream) != cudaSuccess)
             return ATT1_ERR_STATE;
     }
+    if (infer->mmu != NULL) {
+        uint32_t b;
+        att1_status_t st;
+        for (b = 0; b < infer->batch; b++)
+            if ((st = b2_kv_mmu_reserve(infer->mmu, infer->mmu_slot0 + b, infer->position, steps)) != ATT1_OK)
+                return st;
+    }
     for (i = 0; i < steps; i++) {
         if (launch_step(infer) != 0) return ATT1_ERR_STATE;
+    }
+    if (infer->mmu != NULL) {
+        uint32_t b;
+        for (b = 0; b < infer->batch; b++) b2_kv_mmu_advance(infer->mmu, infer->mmu_slot0 + b, steps);
     }
     infer->position += steps;
     infer->logits_valid = 0;
@@ -2054,6 +2121,7 @@ att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item
 {
     const size_t row = (size_t)infer->hkv * infer->head_dim;
     size_t p;
+    if (infer != NULL && infer->mmu != NULL) return ATT1_ERR_UNSUPPORTED; /* read through att1_kv_mmu_copy_range */
     if (infer == NULL || keys == NULL || values == NULL || item >= infer->batch || layer >= infer->cfg.n_layers ||
         count > infer->cfg.max_seq)
         return ATT1_ERR_INVALID_ARG;

@@ -8,7 +8,9 @@
  * and rejections need no device round trip; the K/V data and the page table
  * the kernels read live on the device:
  *   k_pool, v_pool   [max_pages][num_heads][page_tokens][head_dim] f32
- *   page_table       [max_sessions][num_layers][pages_per_seq] int32
+ *   page_table       [num_layers][max_sessions][pages_per_seq] int32 (layer-major:
+ *                    the rows of sessions in consecutive slots are consecutive, as
+ *                    the kernels index a batch's rows)
  * Appends write one position of every head with one strided copy; range copies
  * move the contiguous run of a head inside each page with one copy per page.
  */
@@ -91,6 +93,36 @@ static int find_slot(const att1_kv_mmu *mmu, uint64_t session_id, size_t *slot)
 static int32_t *mirror(att1_kv_mmu *mmu, size_t slot, size_t layer)
 {
     return mmu->table + (slot * mmu->config.num_layers + layer) * mmu->pages_per_seq;
+}
+
+/* Offset of (slot, layer, logical page) in the device page table. */
+static size_t dev_index(const att1_kv_mmu *mmu, size_t slot, size_t layer, size_t lp)
+{
+    return (layer * mmu->config.max_sessions + slot) * mmu->pages_per_seq + lp;
+}
+
+/* Map logical page lp of (slot, layer) to the lowest free physical page:
+ * bookkeeping, device table entry, allocation counter. -1 when none is free. */
+static int32_t map_page(att1_kv_mmu *mmu, size_t slot, size_t layer, size_t lp)
+{
+    const att1_kv_mmu_config *c = &mmu->config;
+    int32_t pp;
+    size_t p;
+    for (p = 0; p < c->max_pages && mmu->owner[p].active; p++) {
+    }
+    if (p == c->max_pages) return -1;
+    pp = (int32_t)p;
+    if (cudaSetDevice(mmu->device) != cudaSuccess ||
+        cudaMemcpy(mmu->page_table + dev_index(mmu, slot, layer, lp), &pp, sizeof(int32_t), cudaMemcpyHostToDevice) !=
+            cudaSuccess)
+        return -2;
+    mmu->owner[p].active = 1;
+    mmu->owner[p].slot = slot;
+    mmu->owner[p].layer = layer;
+    mmu->owner[p].logical_page = lp;
+    mirror(mmu, slot, layer)[lp] = pp;
+    mmu->counters.page_allocations++;
+    return pp;
 }
 
 /* src/kv_mmu.c:263-285 */
@@ -260,26 +292,11 @@ att1_status_t att1_kv_mmu_append(att1_kv_mmu *mmu, uint64_t session_id, size_t l
     pp = lookup_counted(mmu, slot, layer_id, position);
     if (pp < 0) {
         /* a new logical page: the lowest free physical page (src/kv_mmu.c:158-191) */
-        size_t p, lp = position / c->page_tokens;
-        for (p = 0; p < c->max_pages && mmu->owner[p].active; p++) {
-        }
-        if (p == c->max_pages) {
+        pp = map_page(mmu, slot, layer_id, position / c->page_tokens);
+        if (pp < 0) {
             count_error(mmu);
-            return ATT1_ERR_OOM;
+            return pp == -1 ? ATT1_ERR_OOM : ATT1_ERR_STATE;
         }
-        pp = (int32_t)p;
-        if (cudaSetDevice(mmu->device) != cudaSuccess ||
-            cudaMemcpy(mmu->page_table + (slot * c->num_layers + layer_id) * mmu->pages_per_seq + lp, &pp,
-                       sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess) {
-            count_error(mmu);
-            return ATT1_ERR_STATE;
-        }
-        mmu->owner[p].active = 1;
-        mmu->owner[p].slot = slot;
-        mmu->owner[p].layer = layer_id;
-        mmu->owner[p].logical_page = lp;
-        mirror(mmu, slot, layer_id)[lp] = pp;
-        mmu->counters.page_allocations++;
     }
     /* one position of every head: head h at (h * page_tokens + t) * head_dim */
     hd = c->head_dim;
@@ -462,10 +479,55 @@ att1_status_t att1_b200_kv_mmu_layout(const att1_kv_mmu *mmu, uint64_t session_i
         return ATT1_ERR_UNSUPPORTED;
     out->k_pool = mmu->k_pool;
     out->v_pool = mmu->v_pool;
-    out->page_table = mmu->page_table + (slot * mmu->config.num_layers + layer_id) * mmu->pages_per_seq;
+    out->page_table = mmu->page_table + dev_index(mmu, slot, layer_id, 0);
     out->page_tokens = (uint32_t)mmu->config.page_tokens;
     out->pages_per_seq = (uint32_t)mmu->pages_per_seq;
     out->n_kv_heads = (uint32_t)mmu->config.num_heads;
     out->head_dim = (uint32_t)mmu->config.head_dim;
     return ATT1_OK;
+}
+
+/* ---- hooks for a decode context whose batch items are KV-MMU sessions ---------------------------- */
+
+int b2_kv_mmu_session_slot(const att1_kv_mmu *mmu, uint64_t session_id, size_t *slot)
+{
+    return mmu != NULL && find_slot(mmu, session_id, slot);
+}
+
+size_t b2_kv_mmu_length(const att1_kv_mmu *mmu, size_t slot, size_t layer)
+{
+    return mmu->length[slot * mmu->config.num_layers + layer];
+}
+
+const att1_kv_mmu_config *b2_kv_mmu_config(const att1_kv_mmu *mmu)
+{
+    return &mmu->config;
+}
+
+/* Pages for positions [first, first + count) of (slot, every layer), mapped
+ * before the kernels append there. */
+att1_status_t b2_kv_mmu_reserve(att1_kv_mmu *mmu, size_t slot, size_t first, size_t count)
+{
+    const size_t T = mmu->config.page_tokens;
+    size_t l, lp;
+    if (count == 0) return ATT1_OK;
+    if (first + count > mmu->config.max_positions) return ATT1_ERR_INVALID_ARG;
+    for (l = 0; l < mmu->config.num_layers; l++)
+        for (lp = first / T; lp <= (first + count - 1) / T; lp++)
+            if (mirror(mmu, slot, l)[lp] < 0) {
+                const int32_t pp = map_page(mmu, slot, l, lp);
+                if (pp < 0) {
+                    count_error(mmu);
+                    return pp == -1 ? ATT1_ERR_OOM : ATT1_ERR_STATE;
+                }
+            }
+    return ATT1_OK;
+}
+
+/* The kernels appended `count` positions of (slot, every layer). */
+void b2_kv_mmu_advance(att1_kv_mmu *mmu, size_t slot, size_t count)
+{
+    size_t l;
+    for (l = 0; l < mmu->config.num_layers; l++) mmu->length[slot * mmu->config.num_layers + l] += count;
+    mmu->counters.append_ops += count * mmu->config.num_layers;
 }

@@ -23,6 +23,14 @@ typedef struct b2_dev_mat {
 int b2_backend_is_cuda(const att1_backend *backend);
 const char *b2_backend_name(const att1_backend *backend);
 
+/* KV-MMU hooks for a decode context whose batch items are sessions
+ * (att1_kv_mmu.c; att1_b200_infer_use_kv_mmu) */
+int b2_kv_mmu_session_slot(const att1_kv_mmu *mmu, uint64_t session_id, size_t *slot);
+size_t b2_kv_mmu_length(const att1_kv_mmu *mmu, size_t slot, size_t layer);
+const att1_kv_mmu_config *b2_kv_mmu_config(const att1_kv_mmu *mmu);
+att1_status_t b2_kv_mmu_reserve(att1_kv_mmu *mmu, size_t slot, size_t first, size_t count);
+void b2_kv_mmu_advance(att1_kv_mmu *mmu, size_t slot, size_t count);
+
 /* status of a CUDA runtime call */
 static inline att1_status_t b2_cuda_status(cudaError_t e)
 {

@@ -143,6 +143,15 @@ size_t att1_b200_infer_device_bytes(const att1_infer_t *infer);
  * b2_attn, and the QKV epilogue may append the next one. */
 att1_status_t att1_b200_kv_mmu_layout(const att1_kv_mmu *mmu, uint64_t session_id, size_t layer_id,
                                       b2_kv_layout *out);
+/* Batch item b of the context keeps its KV in KV-MMU session session_ids[b]:
+ * pages are mapped on demand as positions advance, and the MMU's lengths and
+ * append counters follow the steps, so the sessions can be read, looked up
+ * and destroyed through att1_kv_mmu.h. The sessions must be empty, sit in
+ * consecutive slots in batch order (created one after another) and match the
+ * context (layers, KV heads, head_dim; max_positions >= max_seq). Only before
+ * the first step and on one GPU; prefill and export_kv are unsupported while a
+ * KV-MMU is in use. NULL returns to the context's own page pools. */
+att1_status_t att1_b200_infer_use_kv_mmu(att1_infer_t *infer, att1_kv_mmu *mmu, const uint64_t *session_ids);
 
 #ifdef __cplusplus
 }

@@ -285,3 +285,69 @@ def test_attention_reads_kv_mmu_pages(b2, both, hd):
         assert e <= 1e-5, f"rel err {e:.3e}; worst head/dim {np.unravel_index(np.abs(got - want).argmax(), got.shape)}"
     finally:
         ours.att1_kv_mmu_destroy(h)
+
+
+@pytest.mark.gpu
+def test_decode_on_kv_mmu_sessions_matches_own_pools(b2, both):
+    """A two-sequence decode context whose KV lives in KV-MMU sessions
+    (att1_b200_infer_use_kv_mmu; another session's appends interleave so the
+    pages are scattered) gives bit-identical logits and tokens to the same
+    context on its own page pools; the sessions then read back, through the
+    KV-MMU API, exactly the K/V that context exports, and the counters show one
+    page allocation per (session, layer, 8 positions)."""
+    ours, _ = both
+    L = b2.lib()
+    cfg = b2.Config.make(1000, 2, 4, 2, 128, 256, 64, dtype=4)
+    Hkv, hd, layers = 2, 32, 2
+    mc = b2.KvMmuConfig(4, 48, layers, Hkv, hd, 8, 64)
+    h = C.c_void_p()
+    assert ours.att1_kv_mmu_create(C.byref(mc), C.byref(h)) == 0
+    a = ref = None
+    try:
+        for sid in (7, 8, 99):
+            assert ours.att1_kv_mmu_create_session(h, sid) == 0
+        a = b2.Infer.synth(cfg, 5, batch=2)
+        ref = b2.Infer.synth(cfg, 5, batch=2)
+        bad = (C.c_uint64 * 2)(8, 7)
+        assert L.att1_b200_infer_use_kv_mmu(a.h, h, bad) == -9          # slots out of batch order
+        sids = (C.c_uint64 * 2)(7, 8)
+        assert L.att1_b200_infer_use_kv_mmu(a.h, h, sids) == 0
+        rng = np.random.default_rng(5)
+        noise = np.zeros(Hkv * hd, np.float32)
+        npos = 0
+        for step in range(20):
+            if step % 3 == 0:  # the other session takes pages between the context's
+                for l in range(layers):
+                    assert ours.att1_kv_mmu_append(h, 99, l, npos, noise.ctypes.data, noise.ctypes.data) == 0
+                npos += 1
+            toks = [int(t) for t in rng.integers(0, 1000, 2)]
+            assert list(a.decode_batch(toks)) == list(ref.decode_batch(toks))
+            assert np.array_equal(a.logits(), ref.logits())
+        a.run_steps(5)
+        ref.run_steps(5)
+        toks = [3, 4]
+        assert list(a.decode_batch(toks)) == list(ref.decode_batch(toks))
+        assert np.array_equal(a.logits(), ref.logits())
+        n = 26
+        assert L.att1_b200_infer_use_kv_mmu(a.h, None, None) == -8    # only at position 0
+        with pytest.raises(b2.Att1Error):
+            a.prefill([1, 2])                                           # prefill needs the own pools
+        k = b2.KvMmuCounters()
+        ours.att1_kv_mmu_get_counters(h, C.byref(k))
+        assert k.page_allocations == 2 * layers * ((n + 7) // 8) + layers * ((npos + 7) // 8)
+        assert k.append_ops == 2 * layers * n + layers * npos
+        for item, sid in enumerate((7, 8)):
+            for l in range(layers):
+                ek = np.zeros((n, Hkv, hd), np.float32)
+                ev = np.zeros((n, Hkv, hd), np.float32)
+                assert L.att1_b200_infer_export_kv(ref.h, item, l, n, ek.ctypes.data, ev.ctypes.data) == 0
+                for hh in range(Hkv):
+                    gk = np.zeros((n, hd), np.float32)
+                    gv = np.zeros((n, hd), np.float32)
+                    assert ours.att1_kv_mmu_copy_range(h, sid, l, hh, 0, n, gk.ctypes.data, gv.ctypes.data) == 0
+                    assert np.array_equal(gk, ek[:, hh]) and np.array_equal(gv, ev[:, hh])
+    finally:
+        for x in (a, ref):
+            if x is not None:
+                x.close()
+        ours.att1_kv_mmu_destroy(h)
