@@ -185,13 +185,13 @@ __device__ __forceinline__ uint64_t *tp_flag(uint8_t *region, uint32_t point, ui
 
 __device__ __forceinline__ uint64_t *tp_key(uint8_t *region, const b2_tp &tp, uint32_t src, uint32_t item)
 {
-    return reinterpret_cast<uint64_t *>(region) + (size_t)(tp.points + 1) * B2_TP_MAX + src * 16 + item;
+    return reinterpret_cast<uint64_t *>(region) + (size_t)(tp.points + 1) * B2_TP_MAX + src * B2_TP_MAX_ITEMS + item;
 }
 
 __device__ __forceinline__ float *tp_slot(uint8_t *region, const b2_tp &tp, uint32_t point, uint32_t src)
 {
     float *slots = reinterpret_cast<float *>(reinterpret_cast<uint64_t *>(region) + (size_t)(tp.points + 1) * B2_TP_MAX +
-                                             B2_TP_MAX * 16);
+                                             B2_TP_MAX * B2_TP_MAX_ITEMS);
     if (point < tp.points) return slots + ((size_t)point * B2_TP_MAX + src) * tp.slot_floats;
     return slots + (size_t)tp.points * B2_TP_MAX * tp.slot_floats + (size_t)src * tp.logit_floats;
 }

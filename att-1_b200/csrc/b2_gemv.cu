@@ -325,7 +325,7 @@ extern "C" int b2_gemv(const b2_gemv_args *a, void *stream)
 
 extern "C" size_t b2_tp_region_bytes(uint32_t points, uint32_t slot_floats, uint32_t logit_floats)
 {
-    return ((size_t)(points + 1) * B2_TP_MAX + B2_TP_MAX * 16) * sizeof(uint64_t) +
+    return ((size_t)(points + 1) * B2_TP_MAX + B2_TP_MAX * B2_TP_MAX_ITEMS) * sizeof(uint64_t) +
            ((size_t)points * B2_TP_MAX * slot_floats + (size_t)B2_TP_MAX * logit_floats) * sizeof(float);
 }
 

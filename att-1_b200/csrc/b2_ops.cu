@@ -88,6 +88,74 @@ __global__ void step_end_tp_kernel(const b2_tp tp, uint32_t batch, uint32_t *tok
     if (threadIdx.x == 0) *const_cast<uint32_t *>(tp.epoch) += 1;
 }
 
+// ---- tensor-parallel exchange for the GEMM route (the GEMVs fuse it) ----------------
+
+// This rank's partial x[n] into its slot of `point` on every rank; the CTAs
+// chain with one system-scope acquire-release add each, and the CTA that
+// completes the kernel publishes the point with release stores.
+__global__ void tp_push_kernel(const float *__restrict__ x, uint32_t n, const b2_tp tp, uint32_t point)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const float4 *src = reinterpret_cast<const float4 *>(x);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += gridDim.x * blockDim.x) {
+        const float4 v = __ldcg(src + i);
+        for (uint32_t s = 0; s < tp.world; ++s)
+            reinterpret_cast<float4 *>(tp_slot(tp.peer[s], tp, point, tp.rank))[i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atom_add_acq_rel_sys(tp.done, 1) == (int)gridDim.x - 1) {
+        *tp.done = 0;
+        tp_signal(tp, point);
+    }
+}
+
+// out = resid + the ranks' slots of `point` added in rank order, once every
+// rank has published it (bounded wait).
+__global__ void tp_sum_kernel(const float *resid, float *out, uint32_t n, const b2_tp tp, uint32_t point, int32_t *err)
+{
+    __shared__ int ok;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) ok = tp_wait(tp, point, err) ? 1 : 0;
+    __syncthreads();
+    if (!ok) return;
+    uint8_t *own = tp.peer[tp.rank];
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += gridDim.x * blockDim.x) {
+        float4 v = __ldcg(reinterpret_cast<const float4 *>(tp_slot(own, tp, point, 0)) + i);
+        for (uint32_t s = 1; s < tp.world; ++s) {
+            const float4 w = __ldcg(reinterpret_cast<const float4 *>(tp_slot(own, tp, point, s)) + i);
+            v = make_float4(__fadd_rn(v.x, w.x), __fadd_rn(v.y, w.y), __fadd_rn(v.z, w.z), __fadd_rn(v.w, w.w));
+        }
+        const float4 r = __ldcg(reinterpret_cast<const float4 *>(resid) + i);
+        reinterpret_cast<float4 *>(out)[i] =
+            make_float4(__fadd_rn(r.x, v.x), __fadd_rn(r.y, v.y), __fadd_rn(r.z, v.z), __fadd_rn(r.w, v.w));
+    }
+}
+
+// This rank's logits [batch][rows] and argmax keys into every rank's logits
+// slot and key row; publishes point tp.points (b2_step_end_tp waits for it).
+__global__ void tp_push_logits_kernel(const float *__restrict__ logits, uint32_t batch, uint32_t rows,
+                                      const unsigned long long *argmax, const b2_tp tp)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const size_t n = (size_t)batch * rows;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float v = __ldcg(logits + i);
+        for (uint32_t s = 0; s < tp.world; ++s) tp_slot(tp.peer[s], tp, tp.points, tp.rank)[i] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atom_add_acq_rel_sys(tp.done, 1) == (int)gridDim.x - 1) {
+        *tp.done = 0;
+        for (uint32_t b = 0; b < batch; ++b) {
+            const unsigned long long key = __ldcg(argmax + b);
+            for (uint32_t q = 0; q < tp.world; ++q) *tp_key(tp.peer[q], tp, tp.rank, b) = key;
+        }
+        tp_signal(tp, tp.points);
+    }
+}
+
 __global__ void rmsnorm_kernel(float *dst, const float *src, const float *w, uint32_t n, float eps)
 {
     __shared__ float red[32];
@@ -214,16 +282,67 @@ extern "C" int b2_step_end(const unsigned long long *argmax, uint32_t batch, uin
 extern "C" int b2_step_end_tp(const b2_tp *tp, uint32_t batch, uint32_t *tokens, int32_t *positions, int32_t *err,
                               int pdl, void *stream)
 {
-    if (tp == nullptr || tokens == nullptr || positions == nullptr || batch == 0 || batch > 16) return -1;
+    if (tp == nullptr || tokens == nullptr || positions == nullptr || batch == 0 || batch > B2_TP_MAX_ITEMS)
+        return -1;
     if (tp->world < 2 || tp->world > B2_TP_MAX || tp->rank >= tp->world || tp->epoch == nullptr ||
         tp->peer[tp->rank] == nullptr)
         return -1;
     b2_tp t = *tp;
     void *args[] = {&t, &batch, &tokens, &positions, &err};
-    return launch_pdl((const void *)step_end_tp_kernel, dim3(1), dim3(32), pdl, (cudaStream_t)stream, args) ==
-                   cudaSuccess
+    return launch_pdl((const void *)step_end_tp_kernel, dim3(1), dim3((batch + 31) / 32 * 32), pdl,
+                      (cudaStream_t)stream, args) == cudaSuccess
                ? 0
                : -8;
+}
+
+static int tp_args_ok(const b2_tp *tp)
+{
+    if (tp == nullptr || tp->world < 2 || tp->world > B2_TP_MAX || tp->rank >= tp->world || tp->epoch == nullptr ||
+        tp->done == nullptr)
+        return 0;
+    for (uint32_t s = 0; s < tp->world; ++s)
+        if (tp->peer[s] == nullptr || ((uintptr_t)tp->peer[s] & 15)) return 0;
+    return tp->slot_floats % 4 == 0;
+}
+
+static uint32_t tp_grid(size_t n)
+{
+    const size_t want = (n + 255) / 256;
+    const size_t cap = (size_t)sm_count() * 2;
+    return (uint32_t)(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+extern "C" int b2_tp_push(const float *x, uint32_t n, const b2_tp *tp, uint32_t point, void *stream)
+{
+    if (x == nullptr || !tp_args_ok(tp) || n == 0 || n % 4 || n > tp->slot_floats || point >= tp->points ||
+        ((uintptr_t)x & 15))
+        return -1;
+    const b2_tp t = *tp;
+    tp_push_kernel<<<tp_grid(n / 4), 256, 0, (cudaStream_t)stream>>>(x, n, t, point);
+    return launched(cudaGetLastError());
+}
+
+extern "C" int b2_tp_sum(const float *resid, float *out, uint32_t n, const b2_tp *tp, uint32_t point, int32_t *err,
+                         void *stream)
+{
+    if (resid == nullptr || out == nullptr || !tp_args_ok(tp) || n == 0 || n % 4 || n > tp->slot_floats ||
+        point >= tp->points || ((uintptr_t)resid & 15) || ((uintptr_t)out & 15))
+        return -1;
+    const b2_tp t = *tp;
+    tp_sum_kernel<<<tp_grid(n / 4), 256, 0, (cudaStream_t)stream>>>(resid, out, n, t, point, err);
+    return launched(cudaGetLastError());
+}
+
+extern "C" int b2_tp_push_logits(const float *logits, uint32_t batch, uint32_t rows,
+                                 const unsigned long long *argmax, const b2_tp *tp, void *stream)
+{
+    if (logits == nullptr || argmax == nullptr || !tp_args_ok(tp) || batch == 0 || batch > B2_TP_MAX_ITEMS ||
+        rows == 0 || (size_t)batch * rows > tp->logit_floats)
+        return -1;
+    const b2_tp t = *tp;
+    tp_push_logits_kernel<<<tp_grid((size_t)batch * rows), 256, 0, (cudaStream_t)stream>>>(logits, batch, rows,
+                                                                                           argmax, t);
+    return launched(cudaGetLastError());
 }
 
 extern "C" int b2_rmsnorm(float *dst, const float *src, const float *w, uint32_t n, float eps, void *stream)

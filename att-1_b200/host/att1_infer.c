@@ -83,7 +83,7 @@ struct att1_infer {
     size_t mmu_slot0;
     /* decode through the tensor-core GEMM (batches the GEMVs cannot hold) */
     int use_dense;
-    float *y_qkv, *y_gu;
+    float *y_qkv, *y_gu, *y_part;
     void *xs, *gscratch;
     size_t xs_bytes, gscratch_bytes;
     /* prompt prefill buffers for up to pf_cap tokens (allocated on first use) */
@@ -218,6 +218,7 @@ static void release(att1_infer_t *inf)
     dfree(inf->counters);
     dfree(inf->y_qkv);
     dfree(inf->y_gu);
+    dfree(inf->y_part);
     dfree(inf->xs);
     dfree(inf->gscratch);
     free_prefill(inf);
@@ -508,11 +509,7 @@ static att1_status_t build_args(att1_infer_t *inf)
     inf->a_out.scratch_bytes = need;
     inf->a_out.counters = inf->counters;
     inf->a_out.counters_len = inf->counters_len;
-    if (inf->use_dense) {
-        /* the tensor-parallel exchange lives in the GEMV epilogues */
-        if (inf->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
-        return dense_alloc(inf);
-    }
+    if (inf->use_dense) return dense_alloc(inf);
     return build_plan(inf);
 }
 
@@ -1235,7 +1232,7 @@ void *att1_b200_infer_stream(const att1_infer_t *infer)
 /* Buffers of one pass of m rows (a decode batch, or a prompt chunk). */
 typedef struct dense_bufs {
     uint32_t m;
-    float *x, *h, *q, *ctx, *hs, *y_qkv, *y_gu;
+    float *x, *h, *q, *ctx, *hs, *y_qkv, *y_gu, *y_part; /* y_part: a rank's partial [m][d] (tensor parallel) */
     const int32_t *positions, *page_table;
     void *xs, *gscratch, *ascratch;
     size_t xs_bytes, gscratch_bytes, ascratch_bytes;
@@ -1310,7 +1307,15 @@ static int dense_layer(att1_infer_t *inf, uint32_t l, const dense_bufs *b, cudaS
     at.counters_len = b->acounters_len;
     at.pdl = inf->use_pdl;
     if ((rc = b2_attn(&at, st)) != 0) return rc;
-    if ((rc = dense_gemm(inf, b, &L->wo, b->ctx, inf->q_rows, NULL, 0.0f, B2_EPI_RESID, b->h, d, b->x, st)) != 0)
+    if (inf->tp_world > 1) {
+        /* this rank's heads' share of WO; h = x + the ranks' shares in rank order */
+        if ((rc = dense_gemm(inf, b, &L->wo, b->ctx, inf->q_rows, NULL, 0.0f, B2_EPI_STORE, b->y_part, d, NULL,
+                             st)) != 0 ||
+            (rc = b2_tp_push(b->y_part, b->m * d, &inf->tp_base, 2 * l, st)) != 0 ||
+            (rc = b2_tp_sum(b->x, b->h, b->m * d, &inf->tp_base, 2 * l, inf->err_d, st)) != 0)
+            return rc;
+    } else if ((rc = dense_gemm(inf, b, &L->wo, b->ctx, inf->q_rows, NULL, 0.0f, B2_EPI_RESID, b->h, d, b->x,
+                                st)) != 0)
         return rc;
     if ((rc = dense_gemm(inf, b, &L->gu, b->h, d, L->ffn_norm, c->eps, B2_EPI_STORE, b->y_gu, 2 * inf->ffl, NULL,
                          st)) != 0)
@@ -1326,6 +1331,13 @@ static int dense_layer(att1_infer_t *inf, uint32_t l, const dense_bufs *b, cudaS
     r.err = inf->err_d;
     r.pdl = inf->use_pdl;
     if ((rc = b2_rows_epilogue(&r, st)) != 0) return rc;
+    if (inf->tp_world > 1) {
+        if ((rc = dense_gemm(inf, b, &L->down, b->hs, inf->ffl, NULL, 0.0f, B2_EPI_STORE, b->y_part, d, NULL, st)) !=
+                0 ||
+            (rc = b2_tp_push(b->y_part, b->m * d, &inf->tp_base, 2 * l + 1, st)) != 0)
+            return rc;
+        return b2_tp_sum(b->h, b->x, b->m * d, &inf->tp_base, 2 * l + 1, inf->err_d, st);
+    }
     return dense_gemm(inf, b, &L->down, b->hs, inf->ffl, NULL, 0.0f, B2_EPI_RESID, b->x, d, b->h, st);
 }
 
@@ -1371,15 +1383,19 @@ static att1_status_t dense_alloc(att1_infer_t *inf)
     att1_status_t st;
     dfree(inf->y_qkv);
     dfree(inf->y_gu);
+    dfree(inf->y_part);
     dfree(inf->xs);
     dfree(inf->gscratch);
-    inf->y_qkv = inf->y_gu = NULL;
+    inf->y_qkv = inf->y_gu = inf->y_part = NULL;
     inf->xs = inf->gscratch = NULL;
     inf->xs_bytes = dense_xs(inf, B);
     inf->gscratch_bytes = dense_gscratch(inf, B);
     if ((st = dalloc(inf, (void **)&inf->y_qkv, (size_t)B * (inf->q_rows + 2 * inf->kv_rows) * sizeof(float))) ||
         (st = dalloc(inf, (void **)&inf->y_gu, (size_t)B * 2 * inf->ffl * sizeof(float))) ||
         (st = dalloc(inf, &inf->xs, inf->xs_bytes)) || (st = dalloc(inf, &inf->gscratch, inf->gscratch_bytes)))
+        return st;
+    if (inf->tp_world > 1 &&
+        (st = dalloc(inf, (void **)&inf->y_part, (size_t)B * inf->cfg.d_model * sizeof(float))) != ATT1_OK)
         return st;
     return ATT1_OK;
 }
@@ -1395,6 +1411,7 @@ static void decode_bufs(att1_infer_t *inf, dense_bufs *b)
     b->hs = inf->hs;
     b->y_qkv = inf->y_qkv;
     b->y_gu = inf->y_gu;
+    b->y_part = inf->y_part;
     b->positions = inf->pos_d;
     b->page_table = NULL; /* each layer's own table rows (kv_layout) */
     b->xs = inf->xs;
@@ -1424,7 +1441,9 @@ static int dense_head(att1_infer_t *inf, const dense_bufs *b, cudaStream_t st)
     r.row_offset = inf->v_off;
     r.err = inf->err_d;
     r.pdl = inf->use_pdl;
-    return b2_rows_epilogue(&r, st);
+    if ((rc = b2_rows_epilogue(&r, st)) != 0 || inf->tp_world == 1) return rc;
+    /* this rank's vocabulary rows and argmax keys to every rank */
+    return b2_tp_push_logits(inf->logits, b->m, inf->vl, inf->argmax_d, &inf->tp_base, st);
 }
 
 static int enqueue_kernels(att1_infer_t *inf)
@@ -1440,6 +1459,8 @@ static int enqueue_kernels(att1_infer_t *inf)
         for (l = 0; l < c->n_layers && rc == 0; l++) rc = dense_layer(inf, l, &b, st);
         if (rc == 0) rc = dense_head(inf, &b, st);
         if (rc != 0) return rc;
+        if (inf->tp_world > 1)
+            return b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
         return b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
     }
     for (l = 0; l < c->n_layers && rc == 0; l++) {

@@ -139,7 +139,7 @@ enum b2_epilogue {
  * Each rank owns one exchange region (b2_tp_region_bytes) in its device
  * memory that every rank can store to (NVLink peer access or CUDA IPC
  * mappings). Layout: flags [points+1][B2_TP_MAX] u64 | argmax keys
- * [B2_TP_MAX][16] u64 | slots [points][B2_TP_MAX][slot_floats] f32 | logits
+ * [B2_TP_MAX][B2_TP_MAX_ITEMS] u64 | slots [points][B2_TP_MAX][slot_floats] f32 | logits
  * slots [B2_TP_MAX][logit_floats] f32. Rank s contributes to point p by
  * storing into slot (p, s) of every rank and then setting flag (p, s) of
  * every rank to the step epoch + 1; a consumer waits for all flags of p and
@@ -149,6 +149,7 @@ enum b2_epilogue {
  */
 #define B2_TP_MAX 8
 #define B2_TP_NONE 0xFFFFFFFFu
+#define B2_TP_MAX_ITEMS 64        /* argmax keys per rank in an exchange region */
 
 typedef struct b2_tp {
     uint32_t rank, world;         /* world 0 or 1: no exchange */
@@ -166,6 +167,20 @@ typedef struct b2_tp {
 } b2_tp;
 
 size_t b2_tp_region_bytes(uint32_t points, uint32_t slot_floats, uint32_t logit_floats);
+
+/* The same exchange for the tensor-core GEMM route, as kernels of their own:
+ * b2_tp_push writes this rank's partial x[n] into its slot of `point` in every
+ * rank's region and publishes the point; b2_tp_sum waits (bounded) until every
+ * rank has and writes out = resid + sum of the ranks' slots in rank order
+ * (out may equal resid); b2_tp_push_logits writes logits [batch][rows] and the
+ * argmax keys into every rank's logits slot and publishes point tp->points,
+ * for b2_step_end_tp. n is at most tp->slot_floats, a multiple of 4. No
+ * counterpart in the reference, whose decode runs on one CPU process. */
+int b2_tp_push(const float *x, uint32_t n, const b2_tp *tp, uint32_t point, void *stream);
+int b2_tp_sum(const float *resid, float *out, uint32_t n, const b2_tp *tp, uint32_t point, int32_t *err,
+              void *stream);
+int b2_tp_push_logits(const float *logits, uint32_t batch, uint32_t rows, const unsigned long long *argmax,
+                      const b2_tp *tp, void *stream);
 
 typedef struct b2_kv_layout {
     float *k_pool, *v_pool;       /* page pools of one layer */

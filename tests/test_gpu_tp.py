@@ -70,6 +70,42 @@ def test_tp2_in_process_matches_oracle(b2, orc):
         r.close()
 
 
+@need2
+def test_tp2_dense_batch_matches_oracle(b2, orc):
+    """20 sequences per step: above the GEMVs' batch, so every projection runs
+    on the tensor-core GEMM and the exchange runs as kernels of its own (push,
+    rank-ordered sum, logits all-gather). Each sequence is replayed alone on
+    the oracle's full model."""
+    ocfg = O.Config.make(**OCFG)
+    cfg = make_cfg(b2, ocfg)
+    batch, steps, seed = 20, 6, 91
+    ranks = [b2.Infer.synth_tp(cfg, seed, r, 2, batch=batch) for r in range(2)]
+    b2.Infer.tp_connect_local(ranks)
+    toks = [[int(t) for t in orc.synth_tokens(seed + b, steps, ocfg.vocab)] for b in range(batch)]
+    glog, gtok = [], []
+    for s in range(steps):
+        for r in ranks:
+            r.step_async([toks[b][s] for b in range(batch)])
+        outs = [r.step_wait() for r in ranks]
+        assert (outs[0] == outs[1]).all()
+        gtok.append(outs[0])
+        logs = [r.logits() for r in ranks]
+        assert (logs[0] == logs[1]).all()
+        glog.append(logs[0])
+    for r in ranks:
+        r.close()
+    om = orc.model(ocfg, seed, threads=8)
+    for b in range(batch):
+        om.reset()
+        for s in range(steps):
+            clog, _ = om.decode(toks[b][s])
+            e = rel_err(glog[s][b], clog)
+            assert e <= LOGITS_RTOL, f"step {s} item {b}: rel err {e:.3e}"
+            top2 = np.sort(clog)[-2:]
+            gap = (top2[1] - top2[0]) / max(np.abs(clog).max(), 1e-30)
+            assert gap <= 2 * LOGITS_RTOL or int(gtok[s][b]) == int(np.argmax(clog))
+
+
 def _ipc_rank(rank, port, out_dir):
     import sys
     sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))
