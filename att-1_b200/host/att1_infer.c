@@ -91,6 +91,8 @@ struct att1_infer {
     float *pf_x, *pf_h, *pf_q, *pf_ctx, *pf_hs, *pf_yqkv, *pf_ygu;
     uint32_t *pf_tok;
     int32_t *pf_pos, *pf_pt, *pf_counters;
+    int32_t *pf_mpt; /* KV-MMU session: its rows of every layer, [layer][pf_cap][pages_per_seq] */
+    size_t pf_mpt_elems;
     unsigned long long *pf_keys;
     void *pf_xs, *pf_gscratch, *pf_ascratch;
     size_t pf_xs_bytes, pf_gscratch_bytes, pf_ascratch_bytes;
@@ -169,11 +171,14 @@ static void free_prefill(att1_infer_t *inf)
     dfree(inf->pf_tok);
     dfree(inf->pf_pos);
     dfree(inf->pf_pt);
+    dfree(inf->pf_mpt);
     dfree(inf->pf_counters);
     dfree(inf->pf_keys);
     dfree(inf->pf_xs);
     dfree(inf->pf_gscratch);
     dfree(inf->pf_ascratch);
+    inf->pf_mpt = NULL;
+    inf->pf_mpt_elems = 0;
     inf->pf_cap = 0;
 }
 
@@ -1233,7 +1238,8 @@ void *att1_b200_infer_stream(const att1_infer_t *infer)
 typedef struct dense_bufs {
     uint32_t m;
     float *x, *h, *q, *ctx, *hs, *y_qkv, *y_gu, *y_part; /* y_part: a rank's partial [m][d] (tensor parallel) */
-    const int32_t *positions, *page_table;
+    const int32_t *positions, *page_table; /* page_table: NULL = each layer's own (kv_layout) */
+    size_t pt_layer_stride;                /* int32 elements from one layer's page_table rows to the next's */
     void *xs, *gscratch, *ascratch;
     size_t xs_bytes, gscratch_bytes, ascratch_bytes;
     int32_t *acounters;
@@ -1291,7 +1297,7 @@ static int dense_layer(att1_infer_t *inf, uint32_t l, const dense_bufs *b, cudaS
     r.rope_freq = inf->rope_freq;
     r.positions = b->positions;
     r.kv = kv_layout(inf, l);
-    if (b->page_table != NULL) r.kv.page_table = b->page_table;
+    if (b->page_table != NULL) r.kv.page_table = b->page_table + (size_t)l * b->pt_layer_stride;
     r.err = inf->err_d;
     r.pdl = inf->use_pdl;
     if ((rc = b2_rows_epilogue(&r, st)) != 0) return rc;
@@ -1700,25 +1706,60 @@ static att1_status_t prefill_alloc(att1_infer_t *inf, uint32_t cap)
     return ATT1_OK;
 }
 
+/* Prefill into a KV-MMU session: every row of a chunk is a position of the
+ * session, so each layer's block repeats the session's row of that layer
+ * (pages for the whole prompt are mapped before this). */
+static att1_status_t prefill_mmu_table(att1_infer_t *inf, uint32_t rows, size_t *layer_stride)
+{
+    const uint32_t L = inf->cfg.n_layers;
+    size_t pps, need, i;
+    uint32_t l;
+    int32_t *pt;
+    att1_status_t st;
+    cudaError_t e;
+    b2_kv_mmu_row(inf->mmu, inf->mmu_slot0, 0, &pps);
+    need = (size_t)L * rows * pps;
+    if (need > inf->pf_mpt_elems) {
+        dfree(inf->pf_mpt);
+        inf->pf_mpt = NULL;
+        inf->pf_mpt_elems = 0;
+        if ((st = dalloc(inf, (void **)&inf->pf_mpt, need * sizeof(int32_t))) != ATT1_OK) return st;
+        inf->pf_mpt_elems = need;
+    }
+    pt = malloc(need * sizeof(int32_t));
+    if (pt == NULL) return ATT1_ERR_OOM;
+    for (l = 0; l < L; l++) {
+        const int32_t *row = b2_kv_mmu_row(inf->mmu, inf->mmu_slot0, l, &pps);
+        for (i = 0; i < rows; i++) memcpy(pt + ((size_t)l * rows + i) * pps, row, pps * sizeof(int32_t));
+    }
+    e = cudaMemcpy(inf->pf_mpt, pt, need * sizeof(int32_t), cudaMemcpyHostToDevice);
+    free(pt);
+    *layer_stride = (size_t)rows * pps;
+    return b2_cuda_status(e);
+}
+
 att1_status_t att1_b200_infer_prefill(att1_infer_t *inf, const uint32_t *tokens, size_t n, uint32_t *out_token)
 {
     const att1_b200_config *c;
     cudaStream_t st;
     int32_t *pos_h;
-    size_t done = 0, i;
+    size_t done = 0, i, mpt_stride = 0;
     uint32_t cap, m = 0;
     att1_status_t s;
     int rc = 0;
     if (inf == NULL || tokens == NULL || out_token == NULL || n == 0) return ATT1_ERR_INVALID_ARG;
     c = &inf->cfg;
     if (inf->batch != 1 || inf->step_pending || !backend_ok(inf)) return ATT1_ERR_STATE;
-    if (inf->tp_world > 1 || inf->mmu != NULL) return ATT1_ERR_UNSUPPORTED;
+    if (inf->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
     if (n > c->max_seq || inf->position + n > c->max_seq) return ATT1_ERR_INVALID_ARG;
     for (i = 0; i < n; i++)
         if (tokens[i] >= c->vocab) return ATT1_ERR_INVALID_ARG;
     if (cudaSetDevice(inf->device) != cudaSuccess) return ATT1_ERR_STATE;
     cap = n < PREFILL_CHUNK ? (uint32_t)n : PREFILL_CHUNK;
     if ((s = prefill_alloc(inf, cap)) != ATT1_OK) return s;
+    if (inf->mmu != NULL && ((s = b2_kv_mmu_reserve(inf->mmu, inf->mmu_slot0, inf->position, n)) != ATT1_OK ||
+                             (s = prefill_mmu_table(inf, cap, &mpt_stride)) != ATT1_OK))
+        return s;
     pos_h = malloc((size_t)cap * sizeof(int32_t));
     if (pos_h == NULL) return ATT1_ERR_OOM;
     st = inf->stream;
@@ -1744,7 +1785,8 @@ att1_status_t att1_b200_infer_prefill(att1_infer_t *inf, const uint32_t *tokens,
         b.y_qkv = inf->pf_yqkv;
         b.y_gu = inf->pf_ygu;
         b.positions = inf->pf_pos;
-        b.page_table = inf->pf_pt;
+        b.page_table = inf->mmu != NULL ? inf->pf_mpt : inf->pf_pt;
+        b.pt_layer_stride = mpt_stride;
         b.xs = inf->pf_xs;
         b.xs_bytes = inf->pf_xs_bytes;
         b.gscratch = inf->pf_gscratch;
@@ -1788,6 +1830,7 @@ att1_status_t att1_b200_infer_prefill(att1_infer_t *inf, const uint32_t *tokens,
     if (cudaStreamSynchronize(st) != cudaSuccess) return ATT1_ERR_STATE;
     inf->logits_valid = 0;
     if (*inf->err_h != 0) return recover(inf, *inf->err_h);
+    if (inf->mmu != NULL) b2_kv_mmu_advance(inf->mmu, inf->mmu_slot0, n);
     inf->position += n;
     *out_token = inf->out_h[0];
     return ATT1_OK;
@@ -1803,7 +1846,7 @@ att1_status_t att1_infer_generate(att1_infer_t *infer, const unsigned char *prom
     /* same contract as src/infer.c:882-928 */
     if (infer == NULL || prompt == NULL || out_tokens == NULL || out_token_count == NULL) return ATT1_ERR_INVALID_ARG;
     if (prompt_bytes == 0 || out_token_capacity < generated_token_count) return ATT1_ERR_INVALID_ARG;
-    if (infer->batch == 1 && infer->tp_world == 1 && infer->mmu == NULL) {
+    if (infer->batch == 1 && infer->tp_world == 1) {
         /* the prompt in one pass over the weights per chunk (same results as
          * the token-by-token loop of the reference) */
         uint32_t *ids = malloc(prompt_bytes * sizeof(uint32_t));

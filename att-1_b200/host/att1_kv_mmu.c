@@ -524,6 +524,13 @@ att1_status_t b2_kv_mmu_reserve(att1_kv_mmu *mmu, size_t slot, size_t first, siz
     return ATT1_OK;
 }
 
+/* Host copy of (slot, layer)'s page-table row: pages_per_seq entries, -1 = none. */
+const int32_t *b2_kv_mmu_row(const att1_kv_mmu *mmu, size_t slot, size_t layer, size_t *pages_per_seq)
+{
+    *pages_per_seq = mmu->pages_per_seq;
+    return mirror((att1_kv_mmu *)mmu, slot, layer);
+}
+
 /* The kernels appended `count` positions of (slot, every layer). */
 void b2_kv_mmu_advance(att1_kv_mmu *mmu, size_t slot, size_t count)
 {

@@ -30,6 +30,7 @@ size_t b2_kv_mmu_length(const att1_kv_mmu *mmu, size_t slot, size_t layer);
 const att1_kv_mmu_config *b2_kv_mmu_config(const att1_kv_mmu *mmu);
 att1_status_t b2_kv_mmu_reserve(att1_kv_mmu *mmu, size_t slot, size_t first, size_t count);
 void b2_kv_mmu_advance(att1_kv_mmu *mmu, size_t slot, size_t count);
+const int32_t *b2_kv_mmu_row(const att1_kv_mmu *mmu, size_t slot, size_t layer, size_t *pages_per_seq);
 
 /* status of a CUDA runtime call */
 static inline att1_status_t b2_cuda_status(cudaError_t e)

@@ -100,7 +100,9 @@ att1_status_t att1_b200_infer_step_wait(att1_infer_t *infer, uint32_t *out_token
 /* Prompt prefill (batch-1 contexts, one GPU): the same result as feeding
  * tokens[0..n) through att1_infer_decode_token one by one (KV cache, position,
  * logits of the last token, greedy next token in *out_token), computed with
- * the tensor-core GEMM over up to 512 prompt tokens at a time. */
+ * the tensor-core GEMM over up to 512 prompt tokens at a time. On a context
+ * using a KV-MMU (att1_b200_infer_use_kv_mmu) the prompt's K/V go into the
+ * session's pages, mapped for the whole prompt before the first kernel. */
 att1_status_t att1_b200_infer_prefill(att1_infer_t *infer, const uint32_t *tokens, size_t n, uint32_t *out_token);
 
 att1_status_t att1_b200_infer_decode_batch(att1_infer_t *infer, const uint32_t *tokens,
@@ -149,8 +151,9 @@ att1_status_t att1_b200_kv_mmu_layout(const att1_kv_mmu *mmu, uint64_t session_i
  * and destroyed through att1_kv_mmu.h. The sessions must be empty, sit in
  * consecutive slots in batch order (created one after another) and match the
  * context (layers, KV heads, head_dim; max_positions >= max_seq). Only before
- * the first step and on one GPU; prefill and export_kv are unsupported while a
- * KV-MMU is in use. NULL returns to the context's own page pools. */
+ * the first step and on one GPU; export_kv is unsupported while a KV-MMU is
+ * in use (read through att1_kv_mmu_copy_range). NULL returns to the context's
+ * own page pools. */
 att1_status_t att1_b200_infer_use_kv_mmu(att1_infer_t *infer, att1_kv_mmu *mmu, const uint64_t *session_ids);
 
 #ifdef __cplusplus

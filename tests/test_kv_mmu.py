@@ -331,7 +331,7 @@ def test_decode_on_kv_mmu_sessions_matches_own_pools(b2, both):
         n = 26
         assert L.att1_b200_infer_use_kv_mmu(a.h, None, None) == -8    # only at position 0
         with pytest.raises(b2.Att1Error):
-            a.prefill([1, 2])                                           # prefill needs the own pools
+            a.prefill([1, 2])                                           # prefill takes one sequence
         k = b2.KvMmuCounters()
         ours.att1_kv_mmu_get_counters(h, C.byref(k))
         assert k.page_allocations == 2 * layers * ((n + 7) // 8) + layers * ((npos + 7) // 8)
@@ -346,6 +346,67 @@ def test_decode_on_kv_mmu_sessions_matches_own_pools(b2, both):
                     gv = np.zeros((n, hd), np.float32)
                     assert ours.att1_kv_mmu_copy_range(h, sid, l, hh, 0, n, gk.ctypes.data, gv.ctypes.data) == 0
                     assert np.array_equal(gk, ek[:, hh]) and np.array_equal(gv, ev[:, hh])
+    finally:
+        for x in (a, ref):
+            if x is not None:
+                x.close()
+        ours.att1_kv_mmu_destroy(h)
+
+
+@pytest.mark.gpu
+def test_prefill_on_kv_mmu_session_matches_own_pools(b2, both):
+    """Prompt prefill into a KV-MMU session (pages for the whole prompt mapped
+    first, then the tensor-core pass appends there), decode steps with another
+    session taking pages in between, and a second prefill further on: tokens
+    and logits bit-identical to the same calls on the context's own pools, and
+    the session reads back the K/V that context exports."""
+    ours, _ = both
+    L = b2.lib()
+    cfg = b2.Config.make(1000, 2, 4, 2, 128, 256, 64, dtype=4)
+    Hkv, hd, layers = 2, 32, 2
+    mc = b2.KvMmuConfig(2, 48, layers, Hkv, hd, 8, 64)
+    h = C.c_void_p()
+    assert ours.att1_kv_mmu_create(C.byref(mc), C.byref(h)) == 0
+    a = ref = None
+    try:
+        for sid in (5, 99):
+            assert ours.att1_kv_mmu_create_session(h, sid) == 0
+        a = b2.Infer.synth(cfg, 11, batch=1)
+        ref = b2.Infer.synth(cfg, 11, batch=1)
+        assert L.att1_b200_infer_use_kv_mmu(a.h, h, (C.c_uint64 * 1)(5)) == 0
+        rng = np.random.default_rng(8)
+        noise = np.zeros(Hkv * hd, np.float32)
+        npos = 0
+        p1 = [int(t) for t in rng.integers(0, 1000, 19)]
+        assert a.prefill(p1) == ref.prefill(p1)
+        assert np.array_equal(a.logits(), ref.logits())
+        for _ in range(3):
+            for l in range(layers):
+                assert ours.att1_kv_mmu_append(h, 99, l, npos, noise.ctypes.data, noise.ctypes.data) == 0
+            npos += 1
+            t = int(rng.integers(0, 1000))
+            assert a.decode(t) == ref.decode(t)
+            assert np.array_equal(a.logits(), ref.logits())
+        p2 = [int(t) for t in rng.integers(0, 1000, 11)]
+        assert a.prefill(p2) == ref.prefill(p2)
+        assert np.array_equal(a.logits(), ref.logits())
+        n = 19 + 3 + 11
+        assert a.position() == ref.position() == n
+        k = b2.KvMmuCounters()
+        ours.att1_kv_mmu_get_counters(h, C.byref(k))
+        assert k.page_allocations == layers * ((n + 7) // 8) + layers * ((npos + 7) // 8)
+        assert k.append_ops == layers * n + layers * npos
+        with pytest.raises(b2.Att1Error):
+            a.prefill([1] * (64 - n + 1))                               # past max_positions
+        for l in range(layers):
+            ek = np.zeros((n, Hkv, hd), np.float32)
+            ev = np.zeros((n, Hkv, hd), np.float32)
+            assert L.att1_b200_infer_export_kv(ref.h, 0, l, n, ek.ctypes.data, ev.ctypes.data) == 0
+            for hh in range(Hkv):
+                gk = np.zeros((n, hd), np.float32)
+                gv = np.zeros((n, hd), np.float32)
+                assert ours.att1_kv_mmu_copy_range(h, 5, l, hh, 0, n, gk.ctypes.data, gv.ctypes.data) == 0
+                assert np.array_equal(gk, ek[:, hh]) and np.array_equal(gv, ev[:, hh])
     finally:
         for x in (a, ref):
             if x is not None:
