@@ -119,6 +119,11 @@ class TraceCounters(C.Structure):
         "kv_appends", "kv_key_reads", "kv_value_reads", "tile_layer_executions")]
 
 
+class SamplerConfig(C.Structure):
+    """att1_sampler_config (include/att1_sampler.h)."""
+    _fields_ = [("top_k", C.c_uint32), ("temperature", C.c_float)]
+
+
 class KvMmuConfig(C.Structure):
     """att1_kv_mmu_config (include/att1_kv_mmu.h)."""
     _fields_ = [(n, C.c_size_t) for n in ("max_sessions", "max_pages", "num_layers", "num_heads", "head_dim",
@@ -224,6 +229,9 @@ _SIGS = {
     "att1_kv_mmu_reset_counters": (None, [_P]),
     "att1_b200_kv_mmu_layout": (C.c_int, [_P, C.c_uint64, _SZ, C.POINTER(KVLayout)]),
     "att1_b200_infer_use_kv_mmu": (C.c_int, [_P, _P, C.POINTER(C.c_uint64)]),
+    "att1_b200_infer_set_sampler": (C.c_int, [_P, C.POINTER(SamplerConfig), C.c_uint64]),
+    "att1_sampler_greedy_f32": (C.c_int, [_P, _SZ, C.POINTER(C.c_uint32)]),
+    "b2_sample_topk": (C.c_int, [_P, _U32, _U32, _U32, _U32, C.c_float, C.c_uint64, _P, _P, C.c_int, _P]),
     # kernel ABI (b2_kernels.h)
     "b2_q4_bytes": (_SZ, [_U32, _U32]),
     "b2_q8_bytes": (_SZ, [_U32, _U32]),
@@ -379,6 +387,11 @@ class Infer:
         o = (C.c_uint32 * self.batch)()
         check("att1_b200_infer_decode_batch", lib().att1_b200_infer_decode_batch(self.h, t, o))
         return np.array(o[:], np.uint32)
+
+    def set_sampler(self, top_k: int = 0, temperature: float = 1.0, seed: int = 0) -> None:
+        """att1_b200_infer_set_sampler: top_k <= 1 is greedy."""
+        cfg = SamplerConfig(int(top_k), float(temperature))
+        check("att1_b200_infer_set_sampler", lib().att1_b200_infer_set_sampler(self.h, C.byref(cfg), int(seed)))
 
     def logits(self) -> np.ndarray:
         n = C.c_size_t(0)

@@ -241,6 +241,139 @@ __global__ void matmul_f32_kernel(float *dst, const float *lhs, const float *rhs
     dst[(size_t)r * cols + c] = s;
 }
 
+// ---- top-k / temperature sampling (step end, after the greedy token) --------------
+
+constexpr int kSampleThreads = 512;
+
+__device__ __forceinline__ uint32_t sample_key(float v) { return v != v ? 0u : ordered_key(v); }
+
+// Exclusive prefix sum of one value per thread over the block.
+__device__ uint32_t block_excl_scan(uint32_t v, uint32_t *warp_tot)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t acc = 0;
+        for (int w = 0; w < kSampleThreads / 32; ++w) {
+            const uint32_t t = warp_tot[w];
+            warp_tot[w] = acc;
+            acc += t;
+        }
+    }
+    __syncthreads();
+    const uint32_t r = warp_tot[warp] + inc - v;
+    __syncthreads();
+    return r;
+}
+
+// One CTA per item: the k largest logits by (value desc, id asc) through a
+// 4 x 8-bit radix select of the k-th key, gathered in id order and ranked;
+// weights exp((l - l_max) / T) summed in rank order; the token is the first
+// rank whose running sum exceeds u * sum, u = 24 bits of
+// splitmix64(splitmix64(seed) ^ (item << 32 | position)), position = the
+// position after this step (the one the token will take).
+__global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const float *logits, uint32_t vocab,
+                                                                     uint32_t stride, uint32_t k, float temperature,
+                                                                     unsigned long long seed,
+                                                                     const int32_t *positions, uint32_t *tokens)
+{
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sel[3];
+    __shared__ uint32_t warp_tot[kSampleThreads / 32];
+    __shared__ float cv[B2_MAX_TOP_K], sv[B2_MAX_TOP_K], w[B2_MAX_TOP_K];
+    __shared__ uint32_t ci[B2_MAX_TOP_K], si[B2_MAX_TOP_K];
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint32_t item = blockIdx.x;
+    const float *L = logits + (size_t)item * stride;
+    uint32_t prefix = 0, mask = 0, want = k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (uint32_t b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+            const uint32_t key = sample_key(__ldcg(L + i));
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t acc = 0, b = 255;
+            while (b > 0 && acc + hist[b] < want) acc += hist[b--];
+            sel[0] = prefix | (b << shift);
+            sel[1] = mask | (255u << shift);
+            sel[2] = want - acc;
+        }
+        __syncthreads();
+        prefix = sel[0];
+        mask = sel[1];
+        want = sel[2];
+        __syncthreads();
+    }
+    // prefix is the k-th largest key: every key above it and the `want`
+    // lowest ids equal to it, in id order
+    const uint32_t chunk = (vocab + blockDim.x - 1) / blockDim.x;
+    const uint32_t i0 = min(threadIdx.x * chunk, vocab), i1 = min(i0 + chunk, vocab);
+    uint32_t ngt = 0, neq = 0;
+    for (uint32_t i = i0; i < i1; ++i) {
+        const uint32_t key = sample_key(__ldcg(L + i));
+        ngt += key > prefix;
+        neq += key == prefix;
+    }
+    uint32_t ogt = block_excl_scan(ngt, warp_tot);
+    uint32_t oeq = block_excl_scan(neq, warp_tot);
+    const uint32_t n_gt = k - want;
+    for (uint32_t i = i0; i < i1; ++i) {
+        const float v = __ldcg(L + i);
+        const uint32_t key = sample_key(v);
+        if (key > prefix && ogt < n_gt) {
+            cv[ogt] = v;
+            ci[ogt] = i;
+            ++ogt;
+        } else if (key == prefix && oeq < want) {
+            cv[n_gt + oeq] = v;
+            ci[n_gt + oeq] = i;
+            ++oeq;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < k) {
+        const uint32_t me = sample_key(cv[threadIdx.x]), id = ci[threadIdx.x];
+        uint32_t r = 0;
+        for (uint32_t j = 0; j < k; ++j) {
+            const uint32_t kj = sample_key(cv[j]);
+            r += (kj > me || (kj == me && ci[j] < id)) ? 1u : 0u;
+        }
+        sv[r] = cv[threadIdx.x];
+        si[r] = id;
+    }
+    __syncthreads();
+    if (threadIdx.x < k) w[threadIdx.x] = expf(__fdiv_rn(__fsub_rn(sv[threadIdx.x], sv[0]), temperature));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t j = 0;
+        if (sv[0] != -INFINITY) {
+            float s = 0.0f;
+            for (uint32_t q = 0; q < k; ++q) s = __fadd_rn(s, w[q]);
+            const unsigned long long r =
+                splitmix64(splitmix64(seed) ^ (((unsigned long long)item << 32) | (uint32_t)positions[item]));
+            const float u = __fmul_rn((float)(uint32_t)(r >> 40), 5.9604644775390625e-8f);  // 2^-24
+            const float target = __fmul_rn(u, s);
+            float acc = 0.0f;
+            for (; j + 1 < k; ++j) {
+                acc = __fadd_rn(acc, w[j]);
+                if (acc > target) break;
+            }
+        }
+        tokens[item] = si[j];
+    }
+}
+
 }  // namespace b2
 
 using namespace b2;
@@ -385,4 +518,17 @@ extern "C" int b2_argmax(const float *v, uint32_t n, unsigned long long *key, vo
     if (e != cudaSuccess) return -8;
     argmax_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(v, n, key);
     return launched(cudaGetLastError());
+}
+
+extern "C" int b2_sample_topk(const float *logits, uint32_t batch, uint32_t vocab, uint32_t stride, uint32_t top_k,
+                              float temperature, unsigned long long seed, const int32_t *positions, uint32_t *tokens,
+                              int pdl, void *stream)
+{
+    if (logits == nullptr || positions == nullptr || tokens == nullptr || batch == 0 || vocab == 0 ||
+        stride < vocab || top_k == 0 || top_k > B2_MAX_TOP_K || top_k > vocab || !(temperature > 0.0f) ||
+        !(temperature <= FLT_MAX))
+        return -1;
+    void *args[] = {&logits, &vocab, &stride, &top_k, &temperature, &seed, &positions, &tokens};
+    return launched(launch_pdl((const void *)sample_topk_kernel, dim3(batch), dim3(kSampleThreads), pdl,
+                               (cudaStream_t)stream, args));
 }

@@ -25,6 +25,7 @@
 #include "att1_b200.h"
 #include "b2_host.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -83,6 +84,10 @@ struct att1_infer {
     size_t mmu_slot0;
     /* decode through the tensor-core GEMM (batches the GEMVs cannot hold) */
     int use_dense;
+    /* sampling: top_k <= 1 greedy; else b2_sample_topk after the step end */
+    uint32_t top_k;
+    float temperature;
+    uint64_t sample_seed;
     float *y_qkv, *y_gu, *y_part;
     void *xs, *gscratch;
     size_t xs_bytes, gscratch_bytes;
@@ -1452,6 +1457,15 @@ static int dense_head(att1_infer_t *inf, const dense_bufs *b, cudaStream_t st)
     return b2_tp_push_logits(inf->logits, b->m, inf->vl, inf->argmax_d, &inf->tp_base, st);
 }
 
+/* Top-k / temperature draw over the step's logits (greedy: nothing to do;
+ * the step end has written the argmax tokens and advanced the positions). */
+static int sample_step(att1_infer_t *inf, cudaStream_t st)
+{
+    if (inf->top_k <= 1) return 0;
+    return b2_sample_topk(inf->logits, inf->batch, inf->cfg.vocab, inf->vl, inf->top_k, inf->temperature,
+                          inf->sample_seed, inf->pos_d, inf->tokens_d, inf->use_pdl, st);
+}
+
 static int enqueue_kernels(att1_infer_t *inf)
 {
     const att1_b200_config *c = &inf->cfg;
@@ -1467,7 +1481,8 @@ static int enqueue_kernels(att1_infer_t *inf)
         if (rc != 0) return rc;
         if (inf->tp_world > 1)
             return b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
-        return b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+        rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+        return rc != 0 ? rc : sample_step(inf, st);
     }
     for (l = 0; l < c->n_layers && rc == 0; l++) {
         dev_layer *L = &inf->layers[l];
@@ -1481,14 +1496,15 @@ static int enqueue_kernels(att1_infer_t *inf)
     if (rc != 0) return rc;
     if (inf->tp_world > 1)
         return b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
-    return b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    return rc != 0 ? rc : sample_step(inf, st);
 }
 
 static int launch_step(att1_infer_t *inf)
 {
     /* contexts of several GPUs may be driven from one thread */
     if (cudaSetDevice(inf->device) != cudaSuccess) return -8;
-    if (inf->use_persistent && inf->plan) return b2_decode_step(inf->plan, inf->stream);
+    if (inf->use_persistent && inf->plan && inf->top_k <= 1) return b2_decode_step(inf->plan, inf->stream);
     if (inf->use_graph && !inf->graph_failed) {
         if (inf->exec == NULL) {
             cudaGraph_t g = NULL;
@@ -1820,6 +1836,7 @@ att1_status_t att1_b200_infer_prefill(att1_infer_t *inf, const uint32_t *tokens,
         }
     }
     if (rc == 0) rc = b2_step_end(inf->argmax_d, 1, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    if (rc == 0) rc = sample_step(inf, st);
     if (rc != 0) {
         cudaStreamSynchronize(st);
         cudaGetLastError();
@@ -1982,6 +1999,27 @@ att1_status_t att1_b200_infer_set_options(att1_infer_t *infer, int use_graph, in
     infer->graph_failed = 0;
     infer->use_graph = use_graph ? 1 : 0;
     set_pdl(infer, use_pdl ? 1 : 0);
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_set_sampler(att1_infer_t *infer, const att1_sampler_config *config, uint64_t seed)
+{
+    const int sample = config != NULL && config->top_k > 1;
+    if (infer == NULL) return ATT1_ERR_INVALID_ARG;
+    if (sample && (config->top_k > B2_MAX_TOP_K || config->top_k > infer->cfg.vocab ||
+                   !(config->temperature > 0.0f) || !(config->temperature <= FLT_MAX)))
+        return ATT1_ERR_INVALID_ARG;
+    if (sample && infer->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
+    if (infer->step_pending) return ATT1_ERR_STATE;
+    if (cudaSetDevice(infer->device) != cudaSuccess) return ATT1_ERR_STATE;
+    cudaStreamSynchronize(infer->stream);
+    if (infer->exec) { /* the captured step holds the old choice */
+        cudaGraphExecDestroy(infer->exec);
+        infer->exec = NULL;
+    }
+    infer->top_k = sample ? config->top_k : 0;
+    infer->temperature = sample ? config->temperature : 0.0f;
+    infer->sample_seed = seed;
     return ATT1_OK;
 }
 

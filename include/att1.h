@@ -10,6 +10,7 @@
 #include "att1_infer.h"
 #include "att1_model.h"
 #include "att1_quant.h"
+#include "att1_sampler.h"
 #include "att1_status.h"
 #include "att1_trace.h"
 #include "att1_b200.h"

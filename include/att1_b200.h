@@ -18,6 +18,7 @@
 
 #include "att1_infer.h"
 #include "att1_kv_mmu.h"
+#include "att1_sampler.h"
 #include "att1_status.h"
 #include "b2_kernels.h"
 
@@ -155,6 +156,15 @@ att1_status_t att1_b200_kv_mmu_layout(const att1_kv_mmu *mmu, uint64_t session_i
  * in use (read through att1_kv_mmu_copy_range). NULL returns to the context's
  * own page pools. */
 att1_status_t att1_b200_infer_use_kv_mmu(att1_infer_t *infer, att1_kv_mmu *mmu, const uint64_t *session_ids);
+
+/* Next-token sampling of every later step (decode, device-loop steps and the
+ * token after a prefill). NULL or top_k <= 1: greedy, the reference's sampler
+ * and the default. top_k 2..256 with a positive finite temperature: top-k /
+ * temperature sampling on the device (b2_sample_topk in b2_kernels.h); the
+ * draw for item b depends only on `seed`, b and the position the token takes,
+ * so a run repeats exactly. One GPU only (tensor-parallel contexts return
+ * ATT1_ERR_UNSUPPORTED); uses the per-kernel step, not the persistent one. */
+att1_status_t att1_b200_infer_set_sampler(att1_infer_t *infer, const att1_sampler_config *config, uint64_t seed);
 
 #ifdef __cplusplus
 }

@@ -273,6 +273,18 @@ int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *toke
  * positions and the epoch (tp->epoch is written through a cast). */
 int b2_step_end_tp(const b2_tp *tp, uint32_t batch, uint32_t *tokens, int32_t *positions, int32_t *err,
                    int pdl, void *stream);
+/* Top-k / temperature sampling after b2_step_end (which has advanced the
+ * positions): for item b, the top_k largest logits[b*stride + 0..vocab) by
+ * (value desc, id asc), weights w_i = expf((l_i - l_0) / temperature) summed
+ * in that order into s, u = (r >> 40) * 2^-24 with
+ * r = splitmix64(splitmix64(seed) ^ (b << 32 | positions[b])), and tokens[b]
+ * = the first i whose running sum exceeds u * s (the last if none). The
+ * reference declares att1_sampler_config (include/att1_sampler.h:7-10) but
+ * samples greedily only (src/sampler.c:5-34); top_k 1 reproduces that. */
+#define B2_MAX_TOP_K 256
+int b2_sample_topk(const float *logits, uint32_t batch, uint32_t vocab, uint32_t stride, uint32_t top_k,
+                   float temperature, unsigned long long seed, const int32_t *positions, uint32_t *tokens,
+                   int pdl, void *stream);
 
 /* ---- the whole decode step as one persistent launch ------------------------ */
 /*
