@@ -232,6 +232,8 @@ _SIGS = {
     "att1_b200_infer_set_sampler": (C.c_int, [_P, C.POINTER(SamplerConfig), C.c_uint64]),
     "att1_sampler_greedy_f32": (C.c_int, [_P, _SZ, C.POINTER(C.c_uint32)]),
     "b2_sample_topk": (C.c_int, [_P, _U32, _U32, _U32, _U32, C.c_float, C.c_uint64, _P, _P, C.c_int, _P]),
+    "b2_sample_topk_sharded": (C.c_int, [_P, _U32, _U32, _U32, _SZ, _U32, _U32, C.c_float, C.c_uint64, _P, _P,
+                                         C.c_int, _P]),
     # kernel ABI (b2_kernels.h)
     "b2_q4_bytes": (_SZ, [_U32, _U32]),
     "b2_q8_bytes": (_SZ, [_U32, _U32]),

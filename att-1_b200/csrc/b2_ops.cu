@@ -278,10 +278,15 @@ __device__ uint32_t block_excl_scan(uint32_t v, uint32_t *warp_tot)
 // weights exp((l - l_max) / T) summed in rank order; the token is the first
 // rank whose running sum exceeds u * sum, u = 24 bits of
 // splitmix64(splitmix64(seed) ^ (item << 32 | position)), position = the
-// position after this step (the one the token will take).
+// position after this step (the one the token will take). Logit (item, v)
+// sits at logits[(v / shard_rows) * shard_stride + item * item_stride +
+// v % shard_rows]: one shard for a plain [batch][stride] buffer, one per rank
+// for the tensor-parallel all-gather.
 __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const float *logits, uint32_t vocab,
-                                                                     uint32_t stride, uint32_t k, float temperature,
-                                                                     unsigned long long seed,
+                                                                     uint32_t shard_rows,
+                                                                     unsigned long long shard_stride,
+                                                                     uint32_t item_stride, uint32_t k,
+                                                                     float temperature, unsigned long long seed,
                                                                      const int32_t *positions, uint32_t *tokens)
 {
     __shared__ uint32_t hist[256];
@@ -291,16 +296,17 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const float
     __shared__ uint32_t ci[B2_MAX_TOP_K], si[B2_MAX_TOP_K];
     pdl_wait();
     pdl_launch_dependents();
-    const uint32_t item = blockIdx.x;
-    const float *L = logits + (size_t)item * stride;
+    const uint32_t item = blockIdx.x, nshards = vocab / shard_rows;
+    const float *L = logits + (size_t)item * item_stride;
     uint32_t prefix = 0, mask = 0, want = k;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (uint32_t b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-            const uint32_t key = sample_key(__ldcg(L + i));
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-        }
+        for (uint32_t s = 0; s < nshards; ++s)
+            for (uint32_t i = threadIdx.x; i < shard_rows; i += blockDim.x) {
+                const uint32_t key = sample_key(__ldcg(L + s * shard_stride + i));
+                if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+            }
         __syncthreads();
         if (threadIdx.x == 0) {
             uint32_t acc = 0, b = 255;
@@ -319,17 +325,26 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const float
     // lowest ids equal to it, in id order
     const uint32_t chunk = (vocab + blockDim.x - 1) / blockDim.x;
     const uint32_t i0 = min(threadIdx.x * chunk, vocab), i1 = min(i0 + chunk, vocab);
+    const uint32_t s0 = i0 / shard_rows, r0 = i0 - s0 * shard_rows;
     uint32_t ngt = 0, neq = 0;
-    for (uint32_t i = i0; i < i1; ++i) {
-        const uint32_t key = sample_key(__ldcg(L + i));
+    for (uint32_t i = i0, s = s0, r = r0; i < i1; ++i) {
+        const uint32_t key = sample_key(__ldcg(L + s * shard_stride + r));
         ngt += key > prefix;
         neq += key == prefix;
+        if (++r == shard_rows) {
+            r = 0;
+            ++s;
+        }
     }
     uint32_t ogt = block_excl_scan(ngt, warp_tot);
     uint32_t oeq = block_excl_scan(neq, warp_tot);
     const uint32_t n_gt = k - want;
-    for (uint32_t i = i0; i < i1; ++i) {
-        const float v = __ldcg(L + i);
+    for (uint32_t i = i0, s = s0, r = r0; i < i1; ++i) {
+        const float v = __ldcg(L + s * shard_stride + r);
+        if (++r == shard_rows) {
+            r = 0;
+            ++s;
+        }
         const uint32_t key = sample_key(v);
         if (key > prefix && ogt < n_gt) {
             cv[ogt] = v;
@@ -524,11 +539,22 @@ extern "C" int b2_sample_topk(const float *logits, uint32_t batch, uint32_t voca
                               float temperature, unsigned long long seed, const int32_t *positions, uint32_t *tokens,
                               int pdl, void *stream)
 {
+    return b2_sample_topk_sharded(logits, batch, vocab, vocab, 0, stride, top_k, temperature, seed, positions, tokens,
+                                  pdl, stream);
+}
+
+extern "C" int b2_sample_topk_sharded(const float *logits, uint32_t batch, uint32_t vocab, uint32_t shard_rows,
+                                      size_t shard_stride, uint32_t item_stride, uint32_t top_k, float temperature,
+                                      unsigned long long seed, const int32_t *positions, uint32_t *tokens, int pdl,
+                                      void *stream)
+{
     if (logits == nullptr || positions == nullptr || tokens == nullptr || batch == 0 || vocab == 0 ||
-        stride < vocab || top_k == 0 || top_k > B2_MAX_TOP_K || top_k > vocab || !(temperature > 0.0f) ||
-        !(temperature <= FLT_MAX))
+        shard_rows == 0 || vocab % shard_rows || item_stride < shard_rows || top_k == 0 || top_k > B2_MAX_TOP_K ||
+        top_k > vocab || !(temperature > 0.0f) || !(temperature <= FLT_MAX))
         return -1;
-    void *args[] = {&logits, &vocab, &stride, &top_k, &temperature, &seed, &positions, &tokens};
+    if (vocab > shard_rows && shard_stride < (size_t)(batch - 1) * item_stride + shard_rows) return -1;
+    unsigned long long ss = shard_stride;
+    void *args[] = {&logits, &vocab, &shard_rows, &ss, &item_stride, &top_k, &temperature, &seed, &positions, &tokens};
     return launched(launch_pdl((const void *)sample_topk_kernel, dim3(batch), dim3(kSampleThreads), pdl,
                                (cudaStream_t)stream, args));
 }

@@ -1462,6 +1462,15 @@ static int dense_head(att1_infer_t *inf, const dense_bufs *b, cudaStream_t st)
 static int sample_step(att1_infer_t *inf, cudaStream_t st)
 {
     if (inf->top_k <= 1) return 0;
+    if (inf->tp_world > 1) {
+        /* every rank draws from the same all-gathered logits: rank s's rows
+         * [batch][vl] in logits slot s of this rank's exchange region */
+        const float *all = (const float *)(inf->tp_region + b2_tp_region_bytes(2 * inf->cfg.n_layers,
+                                                                              inf->batch * inf->cfg.d_model, 0));
+        return b2_sample_topk_sharded(all, inf->batch, inf->cfg.vocab, inf->vl, (size_t)inf->batch * inf->vl, inf->vl,
+                                      inf->top_k, inf->temperature, inf->sample_seed, inf->pos_d, inf->tokens_d,
+                                      inf->use_pdl, st);
+    }
     return b2_sample_topk(inf->logits, inf->batch, inf->cfg.vocab, inf->vl, inf->top_k, inf->temperature,
                           inf->sample_seed, inf->pos_d, inf->tokens_d, inf->use_pdl, st);
 }
@@ -1480,8 +1489,9 @@ static int enqueue_kernels(att1_infer_t *inf)
         if (rc == 0) rc = dense_head(inf, &b, st);
         if (rc != 0) return rc;
         if (inf->tp_world > 1)
-            return b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
-        rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+            rc = b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+        else
+            rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
         return rc != 0 ? rc : sample_step(inf, st);
     }
     for (l = 0; l < c->n_layers && rc == 0; l++) {
@@ -1495,8 +1505,9 @@ static int enqueue_kernels(att1_infer_t *inf)
     if (rc == 0) rc = b2_gemv(&inf->a_out, st);
     if (rc != 0) return rc;
     if (inf->tp_world > 1)
-        return b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
-    rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+        rc = b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+    else
+        rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
     return rc != 0 ? rc : sample_step(inf, st);
 }
 
@@ -2009,7 +2020,6 @@ att1_status_t att1_b200_infer_set_sampler(att1_infer_t *infer, const att1_sample
     if (sample && (config->top_k > B2_MAX_TOP_K || config->top_k > infer->cfg.vocab ||
                    !(config->temperature > 0.0f) || !(config->temperature <= FLT_MAX)))
         return ATT1_ERR_INVALID_ARG;
-    if (sample && infer->tp_world > 1) return ATT1_ERR_UNSUPPORTED;
     if (infer->step_pending) return ATT1_ERR_STATE;
     if (cudaSetDevice(infer->device) != cudaSuccess) return ATT1_ERR_STATE;
     cudaStreamSynchronize(infer->stream);

@@ -162,8 +162,9 @@ att1_status_t att1_b200_infer_use_kv_mmu(att1_infer_t *infer, att1_kv_mmu *mmu, 
  * and the default. top_k 2..256 with a positive finite temperature: top-k /
  * temperature sampling on the device (b2_sample_topk in b2_kernels.h); the
  * draw for item b depends only on `seed`, b and the position the token takes,
- * so a run repeats exactly. One GPU only (tensor-parallel contexts return
- * ATT1_ERR_UNSUPPORTED); uses the per-kernel step, not the persistent one. */
+ * so a run repeats exactly. Tensor-parallel ranks draw from the all-gathered
+ * logits and agree on every token when all of them set the same sampler.
+ * Uses the per-kernel step, not the persistent one. */
 att1_status_t att1_b200_infer_set_sampler(att1_infer_t *infer, const att1_sampler_config *config, uint64_t seed);
 
 #ifdef __cplusplus

@@ -285,6 +285,13 @@ int b2_step_end_tp(const b2_tp *tp, uint32_t batch, uint32_t *tokens, int32_t *p
 int b2_sample_topk(const float *logits, uint32_t batch, uint32_t vocab, uint32_t stride, uint32_t top_k,
                    float temperature, unsigned long long seed, const int32_t *positions, uint32_t *tokens,
                    int pdl, void *stream);
+/* The same draw over logits split in vocab / shard_rows shards (the
+ * tensor-parallel all-gather: one per rank): logit (b, v) at
+ * logits[(v / shard_rows) * shard_stride + b * item_stride + v % shard_rows]. */
+int b2_sample_topk_sharded(const float *logits, uint32_t batch, uint32_t vocab, uint32_t shard_rows,
+                           size_t shard_stride, uint32_t item_stride, uint32_t top_k, float temperature,
+                           unsigned long long seed, const int32_t *positions, uint32_t *tokens, int pdl,
+                           void *stream);
 
 /* ---- the whole decode step as one persistent launch ------------------------ */
 /*

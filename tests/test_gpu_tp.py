@@ -106,6 +106,33 @@ def test_tp2_dense_batch_matches_oracle(b2, orc):
             assert gap <= 2 * LOGITS_RTOL or int(gtok[s][b]) == int(np.argmax(clog))
 
 
+@need2
+def test_tp2_sampler_same_tokens_on_both_ranks(b2):
+    """Top-k / temperature sampling under tensor parallelism: each rank draws
+    from its all-gathered logits, so both ranks return the same tokens, and
+    each token follows from the full-vocabulary logits by the restated rule."""
+    from test_sampler import agree
+    ocfg = O.Config.make(**OCFG)
+    cfg = make_cfg(b2, ocfg)
+    k, T, seed, batch = 16, 0.8, 5, 3
+    ranks = [b2.Infer.synth_tp(cfg, 77, r, 2, batch=batch) for r in range(2)]
+    b2.Infer.tp_connect_local(ranks)
+    for r in ranks:
+        r.set_sampler(k, T, seed)
+    toks = [1, 2, 3]
+    for _ in range(5):
+        for r in ranks:
+            r.step_async(toks)
+        outs = [r.step_wait() for r in ranks]
+        assert (outs[0] == outs[1]).all()
+        logits, pos = ranks[0].logits(), ranks[0].position()
+        for b in range(batch):
+            assert agree(outs[0][b], logits[b], k, T, seed, b, pos)
+        toks = [int(t) for t in outs[0]]
+    for r in ranks:
+        r.close()
+
+
 def _ipc_rank(rank, port, out_dir):
     import sys
     sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))

@@ -120,6 +120,33 @@ def test_sample_topk_kernel_matches_restatement(b2, torch, k, temperature):
 
 
 @pytest.mark.gpu
+def test_sample_topk_sharded_layout(b2, torch):
+    """Four vocabulary shards laid out [shard][item][rows] (the tensor-parallel
+    all-gather) draw the same tokens as the same logits in one [item][vocab]
+    buffer."""
+    V, S, B = 128256, 4, 3
+    R = V // S
+    rng = np.random.default_rng(12)
+    rows = rng.normal(0, 2, (B, V)).astype(np.float32)
+    sharded = np.ascontiguousarray(rows.reshape(B, S, R).transpose(1, 0, 2))
+    positions = np.array([9, 10, 11], np.int32)
+    pos = torch.from_numpy(positions).cuda()
+    flat, shd = torch.from_numpy(rows.reshape(-1)).cuda(), torch.from_numpy(sharded.reshape(-1)).cuda()
+    L = b2.lib()
+    a = torch.full((B,), -1, dtype=torch.int32, device="cuda")
+    c = torch.full((B,), -1, dtype=torch.int32, device="cuda")
+    assert L.b2_sample_topk(flat.data_ptr(), B, V, V, 40, 0.8, 6, pos.data_ptr(), a.data_ptr(), 0, None) == 0
+    assert L.b2_sample_topk_sharded(shd.data_ptr(), B, V, R, B * R, R, 40, 0.8, 6, pos.data_ptr(), c.data_ptr(),
+                                    0, None) == 0
+    torch.cuda.synchronize()
+    assert (a.cpu().numpy() == c.cpu().numpy()).all()
+    for b in range(B):
+        assert agree(int(a[b]), rows[b], 40, 0.8, 6, b, int(positions[b]))
+    assert L.b2_sample_topk_sharded(shd.data_ptr(), B, V, R + 1, B * R, R + 1, 40, 0.8, 6, pos.data_ptr(),
+                                    c.data_ptr(), 0, None) == -1                     # shards must tile the vocabulary
+
+
+@pytest.mark.gpu
 def test_context_sampler_decode_and_prefill(b2):
     """A 4-sequence context with top-k sampling: every step's tokens follow
     from that step's logits by the restated rule, a second context with the
