@@ -83,6 +83,25 @@ def test_sampler_restatement_edges():
     assert sample_ref(np.array([0.0, 100.0, -100.0], np.float32), 3, 0.5, 1, 2, 8)[0] == 1
 
 
+def test_sampler_rule_draws_the_topk_softmax():
+    """The stated rule samples softmax(l / T) restricted to the top k: over
+    20000 positions the frequencies of a 6-logit row with k = 4 match the
+    probabilities within 4 standard errors, and the two excluded ids never
+    appear."""
+    row = np.array([1.0, 3.0, 2.5, -1.0, 2.0, 0.5], np.float32)
+    k, T, n = 4, 1.5, 20000
+    top = [1, 2, 4, 0]
+    e = np.exp((row[top] - row[top].max()) / T)
+    p = e / e.sum()
+    counts = np.zeros(row.size)
+    for pos in range(n):
+        counts[sample_ref(row, k, T, 42, 0, pos)[0]] += 1
+    assert counts[3] == 0 and counts[5] == 0
+    f = counts[top] / n
+    se = np.sqrt(p * (1 - p) / n)
+    assert (np.abs(f - p) <= 4 * se).all(), (f, p)
+
+
 @pytest.fixture(scope="module")
 def torch():
     import torch
