@@ -399,7 +399,7 @@ __device__ __forceinline__ void dequant_store(const RawStep &raw, uint8_t *wst, 
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const GemmParams p)
+__global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
     const GemmSmem s = gemm_smem(smem, p);
@@ -642,7 +642,7 @@ static int gemm_check(const b2_gemm_args *a)
 template <int FMT>
 static cudaError_t launch_gemm(const GemmParams &p, const GemmPlan &pl, int pdl, cudaStream_t st)
 {
-    auto fn = gemm_kernel<FMT>;
+    auto fn = att1_qgemm_kernel<FMT>;
     // the whole shared-memory window (one CTA per SM either way): operand reads
     // of the tensor cores stay inside the CTA's allocation whatever the stage count
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemLimit);

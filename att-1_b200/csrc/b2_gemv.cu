@@ -60,7 +60,7 @@
 namespace b2 {
 
 template <int FMT, int NI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(kThreads, 1) att1_qgemv_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     GemvSmem s = gemv_smem(smem, p);
@@ -160,7 +160,7 @@ bool plan_gemv(const b2_gemv_args *a, GemvPlan &pl)
 template <int FMT, int NI>
 static cudaError_t launch_t(const GemvParams &p, const GemvPlan &pl, int pdl, cudaStream_t st)
 {
-    auto fn = gemv_kernel<FMT, NI>;
+    auto fn = att1_qgemv_kernel<FMT, NI>;
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -380,10 +380,12 @@ extern "C" int b2_gemv_noalloc(const b2_gemv_args *a, void *stream)
     b2_gemv_args c = *a;
     c.scratch = nullptr;
     c.counters = nullptr;
+    // every argument error is returned before the shared array is touched, so
+    // a rejected call cannot disturb a valid one still running on the device
     const int rc = gemv_check(&c);
-    if (rc != 0 && c.x != nullptr) return rc;
+    if (rc != 0) return rc;
     GemvPlan pl;
-    if (c.batch == 0 || !plan_gemv(&c, pl)) return rc != 0 ? rc : -9;
+    if (!plan_gemv(&c, pl)) return -9;
     const size_t need = pl.partial_bytes;
     const uint32_t ncnt = pl.counter_len;
     const size_t cnt_bytes = ((size_t)ncnt * sizeof(int32_t) + 255) & ~(size_t)255;

@@ -368,7 +368,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_topk_kernel(const float
         si[r] = id;
     }
     __syncthreads();
-    if (threadIdx.x < k) w[threadIdx.x] = expf(__fdiv_rn(__fsub_rn(sv[threadIdx.x], sv[0]), temperature));
+    // a +inf top logit takes all the probability: the +inf entries share it
+    // equally (exp of inf - inf would be NaN)
+    if (threadIdx.x < k)
+        w[threadIdx.x] = sv[0] == INFINITY ? (sv[threadIdx.x] == INFINITY ? 1.0f : 0.0f)
+                                           : expf(__fdiv_rn(__fsub_rn(sv[threadIdx.x], sv[0]), temperature));
     __syncthreads();
     if (threadIdx.x == 0) {
         uint32_t j = 0;

@@ -278,7 +278,9 @@ int b2_step_end_tp(const b2_tp *tp, uint32_t batch, uint32_t *tokens, int32_t *p
  * (value desc, id asc), weights w_i = expf((l_i - l_0) / temperature) summed
  * in that order into s, u = (r >> 40) * 2^-24 with
  * r = splitmix64(splitmix64(seed) ^ (b << 32 | positions[b])), and tokens[b]
- * = the first i whose running sum exceeds u * s (the last if none). The
+ * = the first i whose running sum exceeds u * s (the last if none). When the
+ * largest logit is +inf the weights are 1 for the +inf entries and 0 for the
+ * rest; when it is -inf (all top_k are -inf) the token is the first ranked. The
  * reference declares att1_sampler_config (include/att1_sampler.h:7-10) but
  * samples greedily only (src/sampler.c:5-34); top_k 1 reproduces that. */
 #define B2_MAX_TOP_K 256

@@ -33,7 +33,12 @@ def sample_ref(row, k, temperature, seed, item, position):
     row = np.asarray(row, np.float32)
     order = np.lexsort((np.arange(row.size), -row))[:k]
     v = row[order]
-    w = np.exp((v - v[0]) / np.float32(temperature)).astype(np.float32)
+    if v[0] == -np.inf:
+        return int(order[0]), np.inf
+    if v[0] == np.inf:                      # the +inf entries share all the weight
+        w = (v == np.inf).astype(np.float32)
+    else:
+        w = np.exp((v - v[0]) / np.float32(temperature)).astype(np.float32)
     s = np.float32(0)
     for x in w:
         s = np.float32(s + x)
@@ -77,6 +82,9 @@ def test_greedy_host_sampler_matches_reference(b2, ref):
 
 
 def test_sampler_restatement_edges():
+    inf_row = np.array([0.0, np.inf, 3.0, np.inf], np.float32)
+    assert {sample_ref(inf_row, 3, 1.0, 5, 0, p)[0] for p in range(64)} == {1, 3}
+    assert sample_ref(np.full(4, -np.inf, np.float32), 3, 1.0, 5, 0, 1)[0] == 0
     row = np.array([0.0, 5.0, 5.0, 1.0], np.float32)
     # top 1 and a huge-weight gap reduce to greedy (ties: lowest id)
     assert sample_ref(row, 1, 1.0, 9, 0, 3)[0] == 1
@@ -116,23 +124,29 @@ def test_sample_topk_kernel_matches_restatement(b2, torch, k, temperature):
     (ties straddle the k-th value), and a row with -inf entries."""
     V, stride = 128256, 128260
     rng = np.random.default_rng(k)
-    rows = np.zeros((3, stride), np.float32)
+    rows = np.zeros((4, stride), np.float32)
     rows[0, :V] = rng.normal(0, 3, V)
     rows[1, :V] = np.round(rng.normal(0, 2, V) * 2) / 2
     rows[2, :V] = rng.normal(0, 1, V)
     rows[2, rng.integers(0, V, 5000)] = -np.inf
-    positions = np.array([5, 17, 4095], np.int32)
+    rows[3, :V] = rng.normal(0, 1, V)
+    rows[3, [7, 90000, 128255]] = np.inf                   # +inf: only these three can be drawn
+    positions = np.array([5, 17, 4095, 33], np.int32)
     lg = torch.from_numpy(rows.reshape(-1)).cuda()
     pos = torch.from_numpy(positions).cuda()
     L = b2.lib()
-    for seed in (1, 2):
-        tok = torch.full((3,), -1, dtype=torch.int32, device="cuda")
-        assert L.b2_sample_topk(lg.data_ptr(), 3, V, stride, k, temperature, seed, pos.data_ptr(),
+    inf_draws = set()
+    for seed in (1, 2, 3, 4, 5, 6):
+        tok = torch.full((4,), -1, dtype=torch.int32, device="cuda")
+        assert L.b2_sample_topk(lg.data_ptr(), 4, V, stride, k, temperature, seed, pos.data_ptr(),
                                 tok.data_ptr(), 0, None) == 0
         torch.cuda.synchronize()
         got = tok.cpu().numpy().view(np.uint32)
-        for b in range(3):
+        for b in range(4):
             assert agree(got[b], rows[b, :V], k, temperature, seed, b, int(positions[b])), (b, got[b])
+        assert int(got[3]) in (7, 90000, 128255)
+        inf_draws.add(int(got[3]))
+    assert len(inf_draws) >= 2 or k == 2       # the +inf entries share the draw (k = 2 holds two of them)
     tok = torch.zeros(3, dtype=torch.int32, device="cuda")
     assert L.b2_sample_topk(lg.data_ptr(), 3, V, stride, 257, 1.0, 1, pos.data_ptr(), tok.data_ptr(), 0, None) == -1
     assert L.b2_sample_topk(lg.data_ptr(), 3, V, stride, 8, 0.0, 1, pos.data_ptr(), tok.data_ptr(), 0, None) == -1

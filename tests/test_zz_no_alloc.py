@@ -123,3 +123,10 @@ def test_noalloc_rejects_tiling_it_cannot_hold(b2, torch, orc):
     torch.cuda.synchronize()
     assert int(keep["err"].item()) == 0
     assert L.b2_gemv_noalloc(None, None) == -1
+    # an invalid call (no input vector) is rejected before the shared array is touched
+    bad, bkeep = make_args(b2, torch, 4, buf, None, rows, cols, np.ones((1, cols), dtype=np.float32))
+    bad.x = None
+    assert L.b2_gemv_noalloc(C.byref(bad), None) == -1
+    bad.x = bkeep["x"].data_ptr()
+    bad.out = None
+    assert L.b2_gemv_noalloc(C.byref(bad), None) == -1
