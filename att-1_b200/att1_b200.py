@@ -195,6 +195,8 @@ _SIGS = {
     "att1_b200_infer_export_q4": (C.c_int, [_P, _U32, _U32, _P, _P]),
     "att1_b200_infer_export_q8": (C.c_int, [_P, _U32, _U32, _P, _P]),
     "att1_b200_infer_export_kv": (C.c_int, [_P, _U32, _U32, _SZ, _P, _P]),
+    "att1_b200_infer_import_kv": (C.c_int, [_P, _U32, _U32, _SZ, _P, _P]),
+    "att1_b200_infer_seek": (C.c_int, [_P, _SZ]),
     "att1_b200_infer_device_bytes": (_SZ, [_P]),
     # backend vtable (att1_backend.h)
     "att1_backend_cuda_available": (C.c_int, []),
@@ -443,6 +445,18 @@ class Infer:
         check("att1_b200_infer_export_kv",
               lib().att1_b200_infer_export_kv(self.h, item, layer, count, k.ctypes.data, v.ctypes.data))
         return k, v
+
+    def import_kv(self, item: int, layer: int, keys, values, row: int):
+        """K/V rows [0, count) of one sequence and layer, each [count][n_kv_heads][head_dim];
+        row = n_kv_heads * head_dim of this context (its shard under tensor parallelism)."""
+        k = np.ascontiguousarray(keys, np.float32).reshape(-1)
+        v = np.ascontiguousarray(values, np.float32).reshape(-1)
+        assert k.size == v.size and k.size % row == 0
+        check("att1_b200_infer_import_kv",
+              lib().att1_b200_infer_import_kv(self.h, item, layer, k.size // row, k.ctypes.data, v.ctypes.data))
+
+    def seek(self, position: int):
+        check("att1_b200_infer_seek", lib().att1_b200_infer_seek(self.h, position))
 
     def device_bytes(self) -> int:
         return lib().att1_b200_infer_device_bytes(self.h)

@@ -241,6 +241,46 @@ __global__ void matmul_f32_kernel(float *dst, const float *lhs, const float *rhs
     dst[(size_t)r * cols + c] = s;
 }
 
+// Quantised products in the reference's own operation order, one thread per
+// output: sum over groups in order, then over the group's columns, of
+// x * (q * scale), each product and sum rounded on its own (no contraction),
+// as src/quant.c:340-393 and src/matmul_q8.c:3-40 compiled without FMA. W is
+// in the reference layout. Used by the backend vtable for the shapes the
+// unit-layout GEMV does not tile (q4 group 16, columns not a multiple of 32).
+__global__ void matmul_q4_ordered_kernel(float *dst, const float *lhs, uint32_t cols, const uint8_t *packed,
+                                         const float *scales, uint32_t rows, uint32_t group)
+{
+    const uint32_t o = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+    if (o >= rows) return;
+    const uint32_t ng = cols / group;
+    const uint8_t *p = packed + (size_t)o * (cols / 2);
+    const float *x = lhs + (size_t)r * cols;
+    float sum = 0.0f;
+    for (uint32_t g = 0; g < ng; ++g) {
+        const float sc = scales[(size_t)o * ng + g];
+        for (uint32_t j = g * group; j < (g + 1) * group; j += 2) {
+            const uint32_t b = p[j >> 1];
+            const float lo = (float)((int32_t)(b << 28) >> 28), hi = (float)((int32_t)(b << 24) >> 28);
+            sum = __fadd_rn(sum, __fmul_rn(x[j], __fmul_rn(lo, sc)));
+            sum = __fadd_rn(sum, __fmul_rn(x[j + 1], __fmul_rn(hi, sc)));
+        }
+    }
+    dst[(size_t)r * rows + o] = sum;
+}
+
+__global__ void matmul_q8_ordered_kernel(float *dst, const float *lhs, uint32_t cols, const int8_t *values,
+                                         const float *scales, uint32_t rows)
+{
+    const uint32_t o = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+    if (o >= rows) return;
+    const int8_t *v = values + (size_t)o * cols;
+    const float *x = lhs + (size_t)r * cols;
+    const float sc = scales[o];
+    float sum = 0.0f;
+    for (uint32_t c = 0; c < cols; ++c) sum = __fadd_rn(sum, __fmul_rn(x[c], __fmul_rn((float)v[c], sc)));
+    dst[(size_t)r * rows + o] = sum;
+}
+
 // ---- top-k / temperature sampling (step end, after the greedy token) --------------
 
 constexpr int kSampleThreads = 512;
@@ -403,6 +443,27 @@ extern "C" int b2_matmul_f32(float *dst, const float *lhs, const float *rhs, uin
     if (!dst || !lhs || !rhs || rows == 0 || cols == 0 || inner == 0 || rows > 65535) return -1;
     matmul_f32_kernel<<<dim3((cols + 127) / 128, rows), 128, 0, (cudaStream_t)stream>>>(dst, lhs, rhs, rows, cols,
                                                                                         inner);
+    return cudaGetLastError() == cudaSuccess ? 0 : -8;
+}
+
+extern "C" int b2_matmul_q4_ordered(float *dst, const float *lhs, uint32_t m, uint32_t cols, const uint8_t *packed,
+                                    const float *scales, uint32_t rows, uint32_t group, void *stream)
+{
+    // group: a power of two in [16, 128] dividing cols (include/att1_quant.h)
+    if (!dst || !lhs || !packed || !scales || m == 0 || m > 65535 || rows == 0 || cols == 0 || group < 16 ||
+        group > 128 || (group & (group - 1)) || cols % group)
+        return -1;
+    matmul_q4_ordered_kernel<<<dim3((rows + 127) / 128, m), 128, 0, (cudaStream_t)stream>>>(dst, lhs, cols, packed,
+                                                                                             scales, rows, group);
+    return cudaGetLastError() == cudaSuccess ? 0 : -8;
+}
+
+extern "C" int b2_matmul_q8_ordered(float *dst, const float *lhs, uint32_t m, uint32_t cols, const int8_t *values,
+                                    const float *scales, uint32_t rows, void *stream)
+{
+    if (!dst || !lhs || !values || !scales || m == 0 || m > 65535 || rows == 0 || cols == 0) return -1;
+    matmul_q8_ordered_kernel<<<dim3((rows + 127) / 128, m), 128, 0, (cudaStream_t)stream>>>(dst, lhs, cols, values,
+                                                                                             scales, rows);
     return cudaGetLastError() == cudaSuccess ? 0 : -8;
 }
 

@@ -21,7 +21,10 @@
 typedef struct cached_mat {
     const void *key;
     size_t rows, cols;
-    b2_dev_mat m;
+    b2_dev_mat m;       /* unit layout for b2_gemv */
+    void *raw;          /* or: the reference layout (packed / values, then scales) for the ordered kernels */
+    size_t raw_scales;  /* byte offset of the scales in raw */
+    uint32_t group;
 } cached_mat;
 
 typedef struct cuda_backend {
@@ -164,6 +167,72 @@ static int mat_init(b2_dev_mat *m, uint32_t fmt, uint32_t rows, uint32_t cols)
     return 0;
 }
 
+/* The unit layout holds q4 groups of 32, 64 or 128 and columns in multiples
+ * of 32; anything else the reference accepts (group 16, other column counts)
+ * runs the ordered kernels on a device copy of the reference layout. */
+static int q4_unit_ok(const att1_q4_matrix *w)
+{
+    return (w->group_size == 32 || w->group_size == 64 || w->group_size == 128) && w->cols % 32 == 0 &&
+           w->rows <= 0xFFFFFFFFu && w->cols <= 0xFFFFFFFFu;
+}
+
+static int q4_valid(const att1_q4_matrix *w)
+{
+    const uint32_t g = w->group_size;
+    return w->packed != NULL && w->scales != NULL && w->rows > 0 && w->cols > 0 && g >= 16 && g <= 128 &&
+           (g & (g - 1)) == 0 && w->cols % g == 0 && w->rows <= 0xFFFFFFFFu && w->cols <= 0xFFFFFFFFu;
+}
+
+static const cached_mat *raw_weight(cuda_backend *c, const void *key, const void *data, size_t data_bytes,
+                                    const float *scales, size_t scale_bytes, size_t rows, size_t cols, uint32_t group)
+{
+    cached_mat *e = cache_find(c, key, rows, cols);
+    const size_t off = (data_bytes + 255) & ~(size_t)255;
+    if (e != NULL) return e;
+    e = cache_add(c);
+    if (e == NULL) return NULL;
+    if (cudaMalloc(&e->raw, off + scale_bytes) != cudaSuccess ||
+        cudaMemcpy(e->raw, data, data_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy((uint8_t *)e->raw + off, scales, scale_bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        if (e->raw) cudaFree(e->raw);
+        c->n_cache--;
+        return NULL;
+    }
+    e->raw_scales = off;
+    e->group = group;
+    e->key = key;
+    e->rows = rows;
+    e->cols = cols;
+    return e;
+}
+
+/* dst[lhs_rows][rows] = lhs * W^T through the ordered kernels */
+static int run_ordered(cuda_backend *c, const cached_mat *e, int fmt, float *dst, const float *lhs, size_t lhs_rows)
+{
+    const size_t rows = e->rows, cols = e->cols;
+    size_t done = 0;
+    if (ensure(c, 0, lhs_rows * cols * sizeof(float)) || ensure(c, 1, lhs_rows * rows * sizeof(float))) return -1;
+    if (cudaMemcpyAsync(c->buf[0], lhs, lhs_rows * cols * sizeof(float), cudaMemcpyHostToDevice, c->stream) !=
+        cudaSuccess)
+        return -1;
+    while (done < lhs_rows) {
+        const uint32_t nb = (uint32_t)((lhs_rows - done) > 65535 ? 65535 : (lhs_rows - done));
+        float *out = (float *)c->buf[1] + done * rows;
+        const float *x = (const float *)c->buf[0] + done * cols;
+        const float *sc = (const float *)((const uint8_t *)e->raw + e->raw_scales);
+        const int rc = fmt == 4 ? b2_matmul_q4_ordered(out, x, nb, (uint32_t)cols, e->raw, sc, (uint32_t)rows,
+                                                      e->group, c->stream)
+                                : b2_matmul_q8_ordered(out, x, nb, (uint32_t)cols, e->raw, sc, (uint32_t)rows,
+                                                      c->stream);
+        if (rc != 0) return -1;
+        done += nb;
+    }
+    if (cudaMemcpyAsync(dst, c->buf[1], lhs_rows * rows * sizeof(float), cudaMemcpyDeviceToHost, c->stream) !=
+        cudaSuccess)
+        return -1;
+    return finish(c);
+}
+
 static const b2_dev_mat *q4_weight(cuda_backend *c, const att1_q4_matrix *w)
 {
     cached_mat *e = cache_find(c, w->packed, w->rows, w->cols);
@@ -237,10 +306,12 @@ static int run_gemv(cuda_backend *c, const b2_dev_mat *m, float *dst, const floa
     if (cudaMemcpyAsync(c->buf[0], lhs, lhs_rows * cols * sizeof(float), cudaMemcpyHostToDevice, c->stream) !=
         cudaSuccess)
         return -1;
+    uint32_t most = 16;
     while (done < lhs_rows) {
-        const uint32_t nb = (uint32_t)((lhs_rows - done) > 16 ? 16 : (lhs_rows - done));
+        const uint32_t nb = (uint32_t)((lhs_rows - done) > most ? most : (lhs_rows - done));
         b2_gemv_args a;
         size_t need;
+        int rc;
         memset(&a, 0, sizeof(a));
         a.w = m->w;
         a.batch = nb;
@@ -256,7 +327,12 @@ static int run_gemv(cuda_backend *c, const b2_dev_mat *m, float *dst, const floa
         a.scratch_bytes = c->scratch_cap;
         a.counters = c->counters;
         a.counters_len = c->counters_cap;
-        if (b2_gemv(&a, c->stream) != 0) return -1;
+        rc = b2_gemv(&a, c->stream);
+        if (rc == ATT1_ERR_UNSUPPORTED && nb > 1) { /* x's digit planes too large for nb items: fewer */
+            most = nb / 2;
+            continue;
+        }
+        if (rc != 0) return -1;
         done += nb;
     }
     if (cudaMemcpyAsync(dst, c->buf[1], lhs_rows * rows * sizeof(float), cudaMemcpyDeviceToHost, c->stream) !=
@@ -270,9 +346,15 @@ static int cuda_matmul_q4(att1_backend *b, float *dst, const float *lhs, size_t 
 {
     cuda_backend *c = cb(b);
     const b2_dev_mat *m;
-    if (dst == NULL || lhs == NULL || w == NULL || w->packed == NULL || w->scales == NULL || lhs_rows == 0 ||
-        lhs_cols == 0 || lhs_cols != w->cols || w->rows == 0)
+    if (dst == NULL || lhs == NULL || w == NULL || lhs_rows == 0 || lhs_cols == 0 || !q4_valid(w) ||
+        lhs_cols != w->cols)
         return -1;
+    if (!q4_unit_ok(w)) {
+        const cached_mat *e = raw_weight(c, w->packed, w->packed, w->rows * w->cols / 2, w->scales,
+                                         w->rows * (w->cols / w->group_size) * sizeof(float), w->rows, w->cols,
+                                         w->group_size);
+        return e == NULL ? -1 : run_ordered(c, e, 4, dst, lhs, lhs_rows);
+    }
     m = q4_weight(c, w);
     if (m == NULL) return -1;
     return run_gemv(c, m, dst, lhs, lhs_rows, lhs_cols);
@@ -284,8 +366,13 @@ static int cuda_matmul_q8(att1_backend *b, float *dst, const float *lhs, size_t 
     cuda_backend *c = cb(b);
     const b2_dev_mat *m;
     if (dst == NULL || lhs == NULL || w == NULL || w->values == NULL || w->scales == NULL || lhs_rows == 0 ||
-        lhs_cols == 0 || lhs_cols != w->cols || w->rows == 0 || (w->cols % 32) != 0)
+        lhs_cols == 0 || lhs_cols != w->cols || w->rows == 0 || w->rows > 0xFFFFFFFFu || w->cols > 0xFFFFFFFFu)
         return -1;
+    if (w->cols % 32 != 0) {
+        const cached_mat *e = raw_weight(c, w->values, w->values, w->rows * w->cols, w->scales,
+                                         w->rows * sizeof(float), w->rows, w->cols, 0);
+        return e == NULL ? -1 : run_ordered(c, e, 8, dst, lhs, lhs_rows);
+    }
     m = q8_weight(c, w);
     if (m == NULL) return -1;
     return run_gemv(c, m, dst, lhs, lhs_rows, lhs_cols);
@@ -433,6 +520,7 @@ void att1_backend_destroy(att1_backend *b)
         for (i = 0; i < c->n_cache; i++) {
             if (c->cache[i].m.data) cudaFree(c->cache[i].m.data);
             if (c->cache[i].m.row_scale) cudaFree(c->cache[i].m.row_scale);
+            if (c->cache[i].raw) cudaFree(c->cache[i].raw);
         }
         free(c->cache);
         for (i = 0; i < 3; i++)

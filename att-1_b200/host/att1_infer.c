@@ -1076,7 +1076,9 @@ static att1_status_t load_shard(att1_infer_t *inf, uint32_t fmt, b2_dev_mat *m, 
 
 /* Validate (src/model_view.c:221-366) and upload one precision's weights
  * (this rank's shard under tensor parallelism). */
-static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, uint32_t fmt)
+/* check_only: validate every tensor the precision needs and load nothing, so a
+ * precision switch that the file cannot serve leaves the context as it was. */
+static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, uint32_t fmt, int check_only)
 {
     const att1_model_config *mc = &m->config;
     const uint64_t d = mc->d_model, f = mc->d_ff, V = mc->vocab_size;
@@ -1115,7 +1117,7 @@ static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, 
                                       : is_shape(t[k], ATT1_MODEL_DTYPE_F32, 2, in_d, out_d)))
                 return ATT1_ERR_SHAPE;
         }
-        {
+        if (!check_only) {
             dev_layer *L = &inf->layers[l];
             const uint64_t r = inf->tp_rank, qr = inf->q_rows, kr = inf->kv_rows, fl = inf->ffl;
             if ((st = load_shard(inf, fmt, &L->qkv, 0, t[0], NULL, 1, r * qr, qr)) ||
@@ -1128,6 +1130,7 @@ static att1_status_t load_model_weights(att1_infer_t *inf, const att1_model *m, 
                 return st;
         }
     }
+    if (check_only) return ATT1_OK;
     if ((st = load_shard(inf, fmt, &inf->output, 0, outw, NULL, 1, inf->v_off, inf->vl)) ||
         (st = upload_f32(inf, inf->embed, emb)) || (st = upload_f32(inf, inf->out_norm, onorm)))
         return st;
@@ -1162,7 +1165,7 @@ static att1_status_t create_model(const att1_model *model, uint32_t dtype, float
     st = new_context(&c, 1, rank, world, &inf);
     if (st != ATT1_OK) return st;
     inf->model = model;
-    if ((st = alloc_weights(inf, dtype)) || (st = alloc_common(inf)) || (st = load_model_weights(inf, model, dtype)))
+    if ((st = alloc_weights(inf, dtype)) || (st = alloc_common(inf)) || (st = load_model_weights(inf, model, dtype, 0)))
         goto fail;
     /* a tensor-parallel rank is finished when it is connected to its peers */
     if (world > 1) {
@@ -1984,6 +1987,9 @@ att1_status_t att1_infer_set_backend(att1_infer_t *infer, att1_backend *backend)
     if (want != infer->cfg.dtype) {
         /* switch precision: re-prepare weights from the model (src/infer.c:982-1012) */
         if (infer->model == NULL) return ATT1_ERR_UNSUPPORTED;
+        /* the reference keeps its backend when the file cannot serve the new
+         * precision (src/infer.c:982-1012): so does this context */
+        if ((st = load_model_weights(infer, infer->model, want, 1)) != ATT1_OK) return st;
         cudaStreamSynchronize(infer->stream);
         if (infer->exec) {
             cudaGraphExecDestroy(infer->exec);
@@ -1991,7 +1997,7 @@ att1_status_t att1_infer_set_backend(att1_infer_t *infer, att1_backend *backend)
         }
         free_weights(infer);
         infer->cfg.dtype = want;
-        if ((st = alloc_weights(infer, want)) || (st = load_model_weights(infer, infer->model, want))) return st;
+        if ((st = alloc_weights(infer, want)) || (st = load_model_weights(infer, infer->model, want, 0))) return st;
         if ((st = build_args(infer)) != ATT1_OK) return st;
     }
     if (infer->backend) att1_backend_destroy(infer->backend);
@@ -2132,6 +2138,57 @@ att1_status_t att1_b200_infer_sync(att1_infer_t *infer)
         infer->position = 0; /* device positions are unknown after a fault */
         return recover(infer, *infer->err_h);
     }
+    return ATT1_OK;
+}
+
+/* ---- KV restore and seek --------------------------------------------------------------------------------- */
+
+/* Host [count][hkv][hd] rows -> the item's pages of one layer: one strided copy
+ * per (page, KV head), since a page keeps each head's tokens contiguous. */
+att1_status_t att1_b200_infer_import_kv(att1_infer_t *infer, uint32_t item, uint32_t layer, size_t count,
+                                        const float *keys, const float *values)
+{
+    size_t p0;
+    uint32_t h;
+    if (infer != NULL && infer->mmu != NULL) return ATT1_ERR_UNSUPPORTED; /* write through the KV-MMU */
+    if (infer == NULL || keys == NULL || values == NULL || item >= infer->batch || layer >= infer->cfg.n_layers ||
+        count > infer->cfg.max_seq)
+        return ATT1_ERR_INVALID_ARG;
+    if (infer->step_pending) return ATT1_ERR_STATE;
+    {
+        const size_t hd = infer->head_dim, row = (size_t)infer->hkv * hd, pt = infer->page_tokens;
+        for (p0 = 0; p0 < count; p0 += pt) {
+            const size_t n = count - p0 < pt ? count - p0 : pt;
+            const size_t page = (size_t)item * infer->pages_per_seq + p0 / pt;
+            for (h = 0; h < infer->hkv; h++) {
+                const size_t off = (size_t)layer * infer->layer_pool_elems + ((page * infer->hkv + h) * pt) * hd;
+                const size_t src = p0 * row + (size_t)h * hd;
+                if (cudaMemcpy2DAsync(infer->k_pool + off, hd * sizeof(float), keys + src, row * sizeof(float),
+                                      hd * sizeof(float), n, cudaMemcpyHostToDevice, infer->stream) != cudaSuccess ||
+                    cudaMemcpy2DAsync(infer->v_pool + off, hd * sizeof(float), values + src, row * sizeof(float),
+                                      hd * sizeof(float), n, cudaMemcpyHostToDevice, infer->stream) != cudaSuccess)
+                    return ATT1_ERR_STATE;
+            }
+        }
+    }
+    /* the host arrays are the caller's: finish reading them before returning */
+    return cudaStreamSynchronize(infer->stream) == cudaSuccess ? ATT1_OK : ATT1_ERR_STATE;
+}
+
+att1_status_t att1_b200_infer_seek(att1_infer_t *infer, size_t position)
+{
+    int32_t pos[ATT1_B200_MAX_BATCH];
+    uint32_t b;
+    if (infer == NULL || position >= infer->cfg.max_seq) return ATT1_ERR_INVALID_ARG;
+    if (infer->mmu != NULL) return ATT1_ERR_UNSUPPORTED;
+    if (infer->step_pending) return ATT1_ERR_STATE;
+    for (b = 0; b < infer->batch; b++) pos[b] = (int32_t)position;
+    if (cudaMemcpyAsync(infer->pos_d, pos, infer->batch * sizeof(int32_t), cudaMemcpyHostToDevice, infer->stream) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(infer->stream) != cudaSuccess)
+        return ATT1_ERR_STATE;
+    infer->position = position;
+    infer->logits_valid = 0;
     return ATT1_OK;
 }
 

@@ -136,6 +136,19 @@ att1_status_t att1_b200_infer_export_q8(const att1_infer_t *infer, uint32_t laye
  * [count][n_kv_heads][head_dim] f32. */
 att1_status_t att1_b200_infer_export_kv(const att1_infer_t *infer, uint32_t item, uint32_t layer,
                                         size_t count, float *keys, float *values);
+/* Write KV of one sequence and layer, positions [0, count), from
+ * [count][n_kv_heads][head_dim] f32 host arrays (the layout export_kv reads;
+ * under tensor parallelism this rank's KV heads): restores a saved cache, or
+ * sets up a deep context for a test without decoding its prefix. Returns after
+ * the host arrays have been read. Not on a context using a KV-MMU (its
+ * sessions are written through att1_kv_mmu.h). */
+att1_status_t att1_b200_infer_import_kv(att1_infer_t *infer, uint32_t item, uint32_t layer, size_t count,
+                                        const float *keys, const float *values);
+/* Continue every sequence at `position` (< max_seq): the next decode step
+ * attends positions [0, position] and appends there, so [0, position) must
+ * hold KV (decoded or imported). Tensor-parallel ranks seek together. Not on a
+ * context using a KV-MMU. */
+att1_status_t att1_b200_infer_seek(att1_infer_t *infer, size_t position);
 /* Device bytes held by the context (weights, KV pages, buffers). */
 size_t att1_b200_infer_device_bytes(const att1_infer_t *infer);
 

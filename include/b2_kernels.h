@@ -119,6 +119,19 @@ int b2_q8_quantize_f32(void *dst, float *row_scale, uint32_t tile_offset, uint32
 int b2_matmul_f32(float *dst, const float *lhs, const float *rhs, uint32_t rows, uint32_t cols,
                   uint32_t inner, void *stream);
 
+/* dst[m][rows] = lhs[m][cols] * W^T with W in the reference layout (q4:
+ * packed [rows][cols/2] + scales [rows][cols/group]; q8: values [rows][cols] +
+ * scales [rows]), in the reference's own operation order (att1_matmul_q4xf32,
+ * src/quant.c:340-393; att1_matmul_q8xf32, src/matmul_q8.c:3-40: groups and
+ * columns in order, sum += x * (q * scale) without contraction), so results
+ * equal the reference's bit for bit. One thread per output: the backend
+ * vtable uses them for shapes the unit-layout GEMV does not tile (q4 group 16,
+ * columns not a multiple of 32); decode uses b2_gemv. */
+int b2_matmul_q4_ordered(float *dst, const float *lhs, uint32_t m, uint32_t cols, const uint8_t *packed,
+                         const float *scales, uint32_t rows, uint32_t group, void *stream);
+int b2_matmul_q8_ordered(float *dst, const float *lhs, uint32_t m, uint32_t cols, const int8_t *values,
+                         const float *scales, uint32_t rows, void *stream);
+
 /* f32 tensor of N(0, std) values (bit-identical to the oracle generator). */
 int b2_synth_f32(float *dst, size_t count, uint64_t seed, uint64_t tensor_id, float std,
                  void *stream);

@@ -476,6 +476,60 @@ struct or_state {
     float *x, *xn, *q, *k, *v, *ctx, *att, *h1, *gate, *up, *hs, *tmp, *scores;
 };
 
+/* Rows quantise independently (per row, or per group inside a row), so a
+ * matrix is cut into row ranges quantised on their own threads; the bytes are
+ * those of one call over the whole matrix. */
+typedef struct quant_job {
+    const float *w;
+    size_t rows, cols;
+    uint32_t group, dtype;
+    uint8_t *packed;
+    int8_t *values;
+    float *scales;
+    int rc;
+} quant_job;
+
+static void *quant_thread(void *arg)
+{
+    quant_job *j = arg;
+    j->rc = j->dtype == OR_Q4 ? or_q4_quantize(j->w, j->rows, j->cols, j->group, j->packed, j->scales)
+                              : or_q8_quantize(j->w, j->rows, j->cols, j->values, j->scales);
+    return NULL;
+}
+
+static int quantize_mt(const float *w, size_t rows, size_t cols, const or_config *cfg, or_mat *m, int threads)
+{
+    quant_job jobs[64];
+    pthread_t tid[64];
+    int started[64];
+    size_t per, r0;
+    int t, n, rc = 0;
+    if (threads < 1) threads = 1;
+    if (threads > 64) threads = 64;
+    if ((size_t)threads > rows) threads = (int)rows;
+    per = (rows + (size_t)threads - 1) / (size_t)threads;
+    for (n = 0, r0 = 0; r0 < rows; n++, r0 += per) {
+        const size_t r = rows - r0 < per ? rows - r0 : per;
+        quant_job *j = &jobs[n];
+        j->w = w + r0 * cols;
+        j->rows = r;
+        j->cols = cols;
+        j->group = cfg->group;
+        j->dtype = cfg->dtype;
+        j->packed = m->packed ? m->packed + r0 * cols / 2 : NULL;
+        j->values = m->values ? m->values + r0 * cols : NULL;
+        j->scales = cfg->dtype == OR_Q4 ? m->scales + r0 * (cols / cfg->group) : m->scales + r0;
+        j->rc = -1;
+    }
+    for (t = 0; t < n; t++) started[t] = pthread_create(&tid[t], NULL, quant_thread, &jobs[t]) == 0;
+    for (t = 0; t < n; t++) {
+        if (started[t]) pthread_join(tid[t], NULL);
+        else quant_thread(&jobs[t]);
+        if (jobs[t].rc != 0) rc = -1;
+    }
+    return rc;
+}
+
 static int mat_build(or_mat *m, const or_config *cfg, uint64_t seed,
                      uint64_t tid, size_t rows, size_t cols, int threads)
 {
@@ -490,13 +544,11 @@ static int mat_build(or_mat *m, const or_config *cfg, uint64_t seed,
     if (cfg->dtype == OR_Q4) {
         m->packed = malloc(rows * cols / 2);
         m->scales = malloc(rows * (cols / cfg->group) * sizeof(float));
-        rc = (m->packed && m->scales) ?
-             or_q4_quantize(w, rows, cols, cfg->group, m->packed, m->scales) : -1;
+        rc = (m->packed && m->scales) ? quantize_mt(w, rows, cols, cfg, m, threads) : -1;
     } else {
         m->values = malloc(rows * cols);
         m->scales = malloc(rows * sizeof(float));
-        rc = (m->values && m->scales) ?
-             or_q8_quantize(w, rows, cols, m->values, m->scales) : -1;
+        rc = (m->values && m->scales) ? quantize_mt(w, rows, cols, cfg, m, threads) : -1;
     }
     free(w);
     return rc;
@@ -704,6 +756,29 @@ const float *or_state_keys(const or_state *s, uint32_t layer)
 const float *or_state_values(const or_state *s, uint32_t layer)
 {
     return s ? s->values[layer] : NULL;
+}
+
+/* Test set-up, no reference counterpart: write K/V rows [0, count) of one layer
+ * ([count][Hkv][hd], the layer's own layout) and continue at a position, so a
+ * parity test can start deep in the context without decoding its prefix. */
+int or_state_import_kv(const or_model *m, or_state *s, uint32_t layer, size_t count,
+                       const float *keys, const float *values)
+{
+    size_t kvd;
+    if (m == NULL || s == NULL || keys == NULL || values == NULL || layer >= m->cfg.n_layers ||
+        count > m->cfg.max_seq)
+        return -1;
+    kvd = (size_t)m->head_dim * m->cfg.n_kv_heads;
+    memcpy(s->keys[layer], keys, count * kvd * sizeof(float));
+    memcpy(s->values[layer], values, count * kvd * sizeof(float));
+    return 0;
+}
+
+int or_state_seek(const or_model *m, or_state *s, size_t position)
+{
+    if (m == NULL || s == NULL || position >= m->cfg.max_seq) return -1;
+    s->pos = position;
+    return 0;
 }
 
 static int mat_apply(const or_model *m, const or_mat *w, float *dst,

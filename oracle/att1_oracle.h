@@ -110,6 +110,12 @@ size_t or_state_position(const or_state *s);
 /* One decode step (src/infer.c:656-880). logits may be NULL. */
 int or_decode(const or_model *m, or_state *s, uint32_t token, float *logits,
               uint32_t *out_token, int threads);
+/* Test set-up (no reference counterpart): K/V rows [0, count) of one layer
+ * from [count][n_kv_heads][head_dim] arrays, and the position the next decode
+ * takes, so a test can start deep in a context without decoding its prefix. */
+int or_state_import_kv(const or_model *m, or_state *s, uint32_t layer, size_t count,
+                       const float *keys, const float *values);
+int or_state_seek(const or_model *m, or_state *s, size_t position);
 /* KV views for checks: layer l, [max_seq][n_kv_heads][head_dim]. */
 const float *or_state_keys(const or_state *s, uint32_t layer);
 const float *or_state_values(const or_state *s, uint32_t layer);

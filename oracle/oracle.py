@@ -112,6 +112,8 @@ class Oracle(_Lib):
         s("or_state_values", _F, C.c_void_p, C.c_uint32)
         s("or_decode", C.c_int, C.c_void_p, C.c_void_p, C.c_uint32, _F,
           C.POINTER(C.c_uint32), C.c_int)
+        s("or_state_import_kv", C.c_int, C.c_void_p, C.c_void_p, C.c_uint32, _SZ, _F, _F)
+        s("or_state_seek", C.c_int, C.c_void_p, C.c_void_p, _SZ)
 
     # ---- element functions ----
     def synth_normal(self, seed, tensor_id, count, std=0.02, first=0):
@@ -213,9 +215,20 @@ class OracleModel:
         if self.state:
             self.o.lib.or_state_free(self.state)
             self.state = None
-        if self.ptr:
+        if self.ptr and getattr(self, "owner", True):
             self.o.lib.or_model_free(self.ptr)
-            self.ptr = None
+        self.ptr = None
+
+    def spawn(self) -> "OracleModel":
+        """Another decode state (sequence) over the same weights; close it before
+        the model it was spawned from."""
+        other = OracleModel.__new__(OracleModel)
+        other.o, other.cfg, other.seed, other.threads = self.o, self.cfg, self.seed, self.threads
+        other.ptr, other.owner = self.ptr, False
+        other.state = self.o.lib.or_state_create(self.ptr)
+        if not other.state:
+            raise MemoryError("or_state_create failed")
+        return other
 
     __del__ = close
 
@@ -255,6 +268,20 @@ class OracleModel:
         values = np.ctypeslib.as_array(p, (rows * cols,)).copy()
         scales = np.ctypeslib.as_array(s, (rows,)).copy()
         return values, scales, rows, cols
+
+    def import_kv(self, layer, keys, values):
+        """K/V rows [0, count) of one layer, each [count][n_kv_heads][head_dim]."""
+        keys = np.ascontiguousarray(keys, np.float32)
+        values = np.ascontiguousarray(values, np.float32)
+        hd = self.cfg.d_model // self.cfg.n_heads
+        count = keys.size // (self.cfg.n_kv_heads * hd)
+        assert keys.size == values.size == count * self.cfg.n_kv_heads * hd
+        if self.o.lib.or_state_import_kv(self.ptr, self.state, layer, count, _fp(keys), _fp(values)) != 0:
+            raise ValueError("or_state_import_kv rejected its arguments")
+
+    def seek(self, position):
+        if self.o.lib.or_state_seek(self.ptr, self.state, position) != 0:
+            raise ValueError("or_state_seek rejected the position")
 
     def keys(self, layer):
         hd = self.cfg.d_model // self.cfg.n_heads
