@@ -251,7 +251,7 @@ _SIGS = {
     "b2_gemv_counters_len": (_U32, [C.POINTER(GemvArgs)]),
     "b2_attn_counters_len": (_U32, [C.POINTER(AttnArgs)]),
     "b2_gemv": (C.c_int, [C.POINTER(GemvArgs), _P]),
-    "b2_gemv_noalloc": (C.c_int, [C.POINTER(GemvArgs), _P]),
+    "b2_attn_noalloc": (C.c_int, [C.POINTER(AttnArgs), _P]),
     "b2_gemm_xs_bytes": (_SZ, [_U32, _U32]),
     "b2_gemm_prep": (C.c_int, [_P, _U32, _U32, _U32, _P, _F, _P, _P, _P]),
     "b2_gemm_scratch_bytes": (_SZ, [C.POINTER(GemmArgs)]),

@@ -21,6 +21,8 @@
 // context.
 #include "b2_attn.cuh"
 
+#include <mutex>
+
 namespace b2 {
 
 constexpr int kAttnWarps = 16;     // consumer warps
@@ -445,4 +447,74 @@ extern "C" int b2_attn(const b2_attn_args *a, void *stream)
     attn_params(a, nchunks, p);
     const cudaError_t e = launch_attn(p, dim3(nchunks, a->n_kv_heads, a->batch), a->pdl, (cudaStream_t)stream);
     return e == cudaSuccess ? 0 : -8;
+}
+
+// ---- attention without any allocation ------------------------------------------
+//
+// For callers that cannot allocate device memory at the point where they run
+// the attention: code running inside a memory pool or arena it does not own,
+// code that must not synchronise the device (cudaMalloc and cudaFree can), and
+// host programs whose allocator is closed to plugins. b2_attn needs a buffer for
+// the position splits' partial results and a counter array from the caller;
+// b2_attn_noalloc takes both from one fixed array in device global memory, so
+// the caller passes only q, the KV pages, positions, the output and a stream.
+//
+// The array is B2_NOALLOC_SCRATCH_BYTES long and every GPU that loads this
+// library holds it until the process exits. A call whose split plan needs more
+// is rejected with ATT1_ERR_UNSUPPORTED (-9) before anything is touched, as is
+// any call b2_attn would reject. All calls on a device share the array: calls
+// that overlap on the GPU (two streams, or two host threads) race on it and
+// must be ordered by the caller. The array keeps the last call's contents; the
+// counters, which must start at zero, are cleared by an asynchronous memset at
+// every call (so a call cut short by a timed-out wait cannot poison the next).
+//
+// Host code only holds a stand-in for the array's name, not its device
+// address: the first call on each device looks the address up with
+// cudaGetSymbolAddress (with that device current) and caches it, so that first
+// call should come before any stream capture on that device. The cached
+// address belongs to the device's primary context; after a cudaDeviceReset the
+// next call would use a stale address, so reset the device only after the last
+// call. Nothing here allocates.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B2_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void *g_noalloc_base[kMaxDevices];
+std::mutex g_noalloc_mutex;
+}  // namespace
+
+extern "C" int b2_attn_noalloc(const b2_attn_args *a, void *stream)
+{
+    if (a == nullptr) return -1;
+    b2_attn_args c = *a;
+    c.scratch = nullptr;
+    c.counters = nullptr;
+    // every argument error is returned before the shared array is touched, so a
+    // rejected call cannot disturb a valid one still running on the device
+    const int rc = attn_check(&c);
+    if (rc != 0) return rc;
+    uint32_t nchunks, ncnt;
+    size_t need;
+    attn_sizes(&c, nchunks, need, ncnt);
+    const size_t cnt_bytes = ((size_t)ncnt * sizeof(int32_t) + 255) & ~(size_t)255;
+    if (cnt_bytes + need > (size_t)B2_NOALLOC_SCRATCH_BYTES) return -9;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -8;
+    void *base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        if (g_noalloc_base[dev] == nullptr) {
+            void *p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return -8;
+            g_noalloc_base[dev] = p;
+        }
+        base = g_noalloc_base[dev];
+    }
+    c.counters = reinterpret_cast<int32_t *>(base);
+    c.counters_len = ncnt;
+    c.scratch = reinterpret_cast<uint8_t *>(base) + cnt_bytes;
+    c.scratch_bytes = need;
+    if (cudaMemsetAsync(c.counters, 0, (size_t)ncnt * sizeof(int32_t), (cudaStream_t)stream) != cudaSuccess) return -8;
+    return b2_attn(&c, stream);
 }

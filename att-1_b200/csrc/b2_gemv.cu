@@ -55,7 +55,6 @@
 
 #include <cfloat>
 #include <cstdio>
-#include <mutex>
 #include <cuda_runtime.h>
 namespace b2 {
 
@@ -327,73 +326,4 @@ extern "C" size_t b2_tp_region_bytes(uint32_t points, uint32_t slot_floats, uint
 {
     return ((size_t)(points + 1) * B2_TP_MAX + B2_TP_MAX * B2_TP_MAX_ITEMS) * sizeof(uint64_t) +
            ((size_t)points * B2_TP_MAX * slot_floats + (size_t)B2_TP_MAX * logit_floats) * sizeof(float);
-}
-
-// ---- GEMV without any allocation ------------------------------------------------
-//
-// For callers that cannot allocate device memory at the point where they run a
-// GEMV: code that runs inside a memory pool or arena it does not own, code
-// that must not synchronise the device (cudaMalloc/cudaFree can), and hosts
-// whose allocator is closed to plugins. b2_gemv needs a partial-sum buffer and
-// a counter array from the caller; b2_gemv_noalloc takes both from one fixed
-// array in device global memory instead, so the caller passes only inputs,
-// outputs and the stream.
-//
-// The array is B2_NOALLOC_SCRATCH_BYTES long and lives in every GPU that loads
-// this library until the process exits. A call whose tiling needs more than
-// that is rejected with ATT1_ERR_UNSUPPORTED (-9) before anything is launched.
-// All calls on a device share the array: calls that overlap on the GPU (two
-// streams, or two host threads) race on it and must be ordered by the caller.
-// The array keeps the last call's contents; the counters that must start at
-// zero are cleared by an asynchronous memset at every call, so a call that was
-// cut short (a timed-out wait) does not poison the next one.
-//
-// The first call on each device looks up the array's device address with
-// cudaGetSymbolAddress (once per device, with that device current) and caches
-// it; that first call should come before any stream capture on that device.
-
-static __device__ __align__(256) unsigned char g_noalloc_scratch[B2_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-constexpr int kMaxDevices = 64;
-void *g_noalloc_base[kMaxDevices];
-std::mutex g_noalloc_mutex;
-}  // namespace
-
-extern "C" int b2_gemv_noalloc(const b2_gemv_args *a, void *stream)
-{
-    if (a == nullptr) return -1;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -8;
-    void *base = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-        if (g_noalloc_base[dev] == nullptr) {
-            // host code only holds a stand-in for g_noalloc_scratch: ask the
-            // runtime for the device address of this device's copy
-            void *p = nullptr;
-            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return -8;
-            g_noalloc_base[dev] = p;
-        }
-        base = g_noalloc_base[dev];
-    }
-    b2_gemv_args c = *a;
-    c.scratch = nullptr;
-    c.counters = nullptr;
-    // every argument error is returned before the shared array is touched, so
-    // a rejected call cannot disturb a valid one still running on the device
-    const int rc = gemv_check(&c);
-    if (rc != 0) return rc;
-    GemvPlan pl;
-    if (!plan_gemv(&c, pl)) return -9;
-    const size_t need = pl.partial_bytes;
-    const uint32_t ncnt = pl.counter_len;
-    const size_t cnt_bytes = ((size_t)ncnt * sizeof(int32_t) + 255) & ~(size_t)255;
-    if (cnt_bytes + need > (size_t)B2_NOALLOC_SCRATCH_BYTES) return -9;
-    c.counters = reinterpret_cast<int32_t *>(base);
-    c.counters_len = ncnt;
-    c.scratch = reinterpret_cast<uint8_t *>(base) + cnt_bytes;
-    c.scratch_bytes = need;
-    if (cudaMemsetAsync(c.counters, 0, (size_t)ncnt * sizeof(int32_t), (cudaStream_t)stream) != cudaSuccess) return -8;
-    return b2_gemv(&c, stream);
 }

@@ -239,19 +239,6 @@ size_t b2_gemv_scratch_bytes(const b2_gemv_args *a);
 uint32_t b2_gemv_counters_len(const b2_gemv_args *a);
 int b2_gemv(const b2_gemv_args *a, void *stream);
 
-/* b2_gemv for callers that cannot allocate device memory where they run it
- * (inside an arena or pool they do not own, or where a cudaMalloc/cudaFree
- * would synchronise the device). It has no counterpart in the reference.
- * The partial sums and tile counters come from one fixed array of
- * B2_NOALLOC_SCRATCH_BYTES in device memory (held by every GPU that loads the
- * library until exit); a->scratch and a->counters are ignored, everything
- * else is as for b2_gemv. Calls whose tiling needs more scratch return
- * ATT1_ERR_UNSUPPORTED (-9). All calls on a device share the array: calls
- * that overlap on the GPU race and must be ordered by the caller. The first
- * call on each device looks up the array's address and should come before
- * any stream capture on that device. Allocates nothing. */
-#define B2_NOALLOC_SCRATCH_BYTES (4u << 20)
-int b2_gemv_noalloc(const b2_gemv_args *a, void *stream);
 
 /* ---- single-query attention over the paged KV cache (split over positions) */
 typedef struct b2_attn_args {
@@ -272,6 +259,22 @@ typedef struct b2_attn_args {
 size_t b2_attn_scratch_bytes(const b2_attn_args *a);
 uint32_t b2_attn_counters_len(const b2_attn_args *a);
 int b2_attn(const b2_attn_args *a, void *stream);
+
+/* b2_attn for callers that cannot allocate device memory where they run it:
+ * code inside a memory pool or arena it does not own, code that must not
+ * synchronise the device (cudaMalloc / cudaFree can), or a host whose
+ * allocator is closed to plugins. It has no counterpart in the reference.
+ * The split partials and counters come from one fixed array of
+ * B2_NOALLOC_SCRATCH_BYTES in device memory (held by every GPU that loads the
+ * library until exit); a->scratch and a->counters are ignored, everything
+ * else is as for b2_attn, and calls b2_attn would reject are rejected before
+ * the array is touched. Plans that need more than the array return
+ * ATT1_ERR_UNSUPPORTED (-9). All calls on a device share the array: calls that
+ * overlap on the GPU race and must be ordered by the caller. The first call
+ * on each device looks up the array's address and should come before any
+ * stream capture on that device. Allocates nothing. */
+#define B2_NOALLOC_SCRATCH_BYTES (4u << 20)
+int b2_attn_noalloc(const b2_attn_args *a, void *stream);
 
 /* ---- per-token step kernels ------------------------------------------------ */
 /* x[b] = embed[tokens[b]]; argmax keys reset. Validates token ids. */
