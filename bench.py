@@ -118,36 +118,68 @@ class ClockSampler:
 # reference CPU path (oracle/_ref: the ATT-1 sources compiled as they are)
 # ---------------------------------------------------------------------------------------------
 
-def reference_cpu_sample(ctx, steps=2):
-    """Time the reference decode on a bounded sample of the 8B workload:
-    full-width layers with GQA expanded to the reference's MHA layout, KV
-    filled to ctx-1 positions, a 4096-entry lm_head; 1- and 2-layer models
-    separate the per-layer and the per-token parts, extrapolated to 32
-    layers and the 128256-entry vocabulary."""
+REF_SHIPPED = "libatt1ref_shipped.so"   # the reference Makefile's flags (no -O)
+
+
+def reference_cpu_sample(ctx, steps=2, warmup=1, threads=None, lib=None):
+    """Time the reference decode (oracle/_ref: the ATT-1 sources compiled as
+    they are, driven through its own block functions) on a bounded sample of
+    the 8B workload: full-width layers with GQA expanded to the reference's
+    MHA layout, KV filled to the context, a 4096-entry lm_head; a 1- and a
+    2-layer model separate the per-layer and the per-token parts, which are
+    extrapolated to 32 layers and the 128256-entry vocabulary. `steps` decode
+    steps are timed on each sample model after `warmup` untimed ones.
+    threads: host threads for the matmuls (row slices; None = all cores)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     cores = os.cpu_count() or 1
-    ref = O.Reference()
+    threads = cores if threads is None else threads
+    ref = O.Reference(O.REF_SO if lib is None else os.path.join(os.path.dirname(O.REF_SO), lib))
     times = {}
+    timed = 0.0
     vs = 4096
     for layers in (1, 2):
         cfg = O.Config.make(vocab=vs, n_layers=layers, n_heads=32, n_kv_heads=8, d_model=4096, d_ff=14336,
                             max_seq=ctx, dtype=O.Q4, eps=1e-5, theta=500000.0)
         m = ref.model(cfg, 11, threads=cores)
-        m.fill(ctx - 1 - steps)
-        m.decode(5)  # warm caches
+        m.set_threads(threads)
+        m.fill(ctx - 1 - steps - warmup)
+        for i in range(warmup):
+            m.decode(5 + i)
         t0 = time.perf_counter()
         for i in range(steps):
             m.decode(7 + i)
-        times[layers] = (time.perf_counter() - t0) / steps
+        dt = time.perf_counter() - t0
+        timed += dt
+        times[layers] = dt / steps
         m.close()
     t_layer = max(times[2] - times[1], 1e-9)
     t_head = max(times[1] - t_layer, 0.0)
     t_tok = SHAPE["n_layers"] * t_layer + t_head * SHAPE["vocab"] / vs
-    sample = (f"reference att1 decode (oracle/_ref) at ctx {ctx}: 1- and 2-layer full-width models "
-              f"(GQA expanded to MHA), lm_head 4096 rows, {steps} steps each; "
-              f"{t_layer * 1e3:.1f} ms/layer, extrapolated to 32 layers + 128256-row lm_head")
-    return 1.0 / t_tok, cores, sample
+    sample = (f"reference att1 decode at ctx {ctx}: 1- and 2-layer full-width models (GQA expanded to MHA), "
+              f"lm_head 4096 rows, {steps} timed steps each after {warmup} untimed; {t_layer * 1e3:.1f} ms/layer, "
+              f"extrapolated to 32 layers + 128256-row lm_head")
+    return {"value": 1.0 / t_tok, "cores": threads, "host_cores": cores, "sample": sample, "timed_region_s": timed,
+            "ms_per_layer": t_layer * 1e3}
+
+
+def reference_single_core_rows(ctx):
+    """The reference as its own Makefile builds it (no -O) and at -O2, on one
+    host core each (its math is single-threaded): one timed step per sample
+    model, extrapolated like reference_cpu_sample."""
+    rows = []
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    for build, lib in (("as shipped (no -O, reference Makefile:10)", REF_SHIPPED), ("-O2", None)):
+        path = os.path.join(os.path.dirname(O.REF_SO), lib) if lib else O.REF_SO
+        if not os.path.exists(path):
+            rows.append({"build": build, "unavailable": f"{os.path.basename(path)} not built"})
+            continue
+        r = reference_cpu_sample(ctx, steps=1, warmup=0, threads=1, lib=lib)
+        rows.append({"build": build, "value": r["value"], "unit": "tokens/s",
+                     "cores": f"1 of {r['host_cores']} host cores", "ms_per_layer": r["ms_per_layer"],
+                     "timed_region_s": r["timed_region_s"], "extrapolated": True})
+    return rows
 
 
 # ---------------------------------------------------------------------------------------------
@@ -370,8 +402,9 @@ def run_b200(args, rank, world, local_rank):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            v, cores, sample = reference_cpu_sample(ctx)
-            cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}
+            r = reference_cpu_sample(ctx)
+            cpu = {"value": r["value"], "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
+                   "sample": r["sample"], "extrapolated": True}
         value = args.batch * 1000.0 / ms * (world if args.replicas else 1)
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -399,16 +432,27 @@ def run_b200(args, rank, world, local_rank):
 
 
 def run_reference(args, rank):
+    """The reference CPU arm: the ATT-1 decode compiled from its sources,
+    timed on this host on a bounded sample of the 8B workload (the full
+    model decodes at seconds per token on the CPU) and extrapolated; the
+    steps reported are the steps timed on each sample model."""
     if rank != 0:
         return None
-    v, cores, sample = reference_cpu_sample(args.ctx, steps=max(1, min(args.steps, 3)))
+    steps = max(1, args.steps)
+    r = reference_cpu_sample(args.ctx, steps=steps, warmup=max(0, args.warmup))
+    v = r["value"]
+    single = reference_single_core_rows(args.ctx) if not args.no_cpu else []
     return {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "q4xf32", "data": "synthetic",
+        "extrapolated": True,
+        "timed_region_s": r["timed_region_s"],
         "config": {"workload": "llama3-8b-shape q4 decode", "global_batch": 1, "seq_len": args.ctx,
-                   "parallelism": "cpu"},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample},
+                   "parallelism": "cpu", "sample": "1- and 2-layer full-width models, lm_head 4096 rows; "
+                   "steps are timed on each and extrapolated to 32 layers and 128256 rows"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
+                         "sample": r["sample"], "extrapolated": True, "single_core": single},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
