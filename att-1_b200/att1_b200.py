@@ -64,7 +64,8 @@ class TpArgs(C.Structure):
     _fields_ = [("rank", C.c_uint32), ("world", C.c_uint32), ("peer", C.c_void_p * 8), ("points", C.c_uint32),
                 ("slot_floats", C.c_uint32), ("logit_floats", C.c_uint32), ("epoch", C.c_void_p),
                 ("done", C.c_void_p), ("out_point", C.c_uint32), ("in_point", C.c_uint32),
-                ("in_resid", C.c_void_p), ("in_out", C.c_void_p), ("row_offset", C.c_uint32)]
+                ("in_resid", C.c_void_p), ("in_out", C.c_void_p), ("row_offset", C.c_uint32),
+                ("wait_polls", C.c_uint32)]
 
 
 class GemvArgs(C.Structure):
@@ -178,6 +179,8 @@ _SIGS = {
     "att1_b200_infer_tp_handle": (C.c_int, [_P, _P]),
     "att1_b200_infer_tp_connect": (C.c_int, [_P, _P]),
     "att1_b200_infer_tp_connect_local": (C.c_int, [C.POINTER(_P), _U32]),
+    "att1_b200_infer_tp_set_wait": (C.c_int, [_P, _U32]),
+    "att1_b200_infer_tp_reset": (C.c_int, [_P]),
     "att1_b200_infer_tp_disconnect": (C.c_int, [_P]),
     "att1_b200_infer_step_async": (C.c_int, [_P, C.POINTER(_U32)]),
     "att1_b200_infer_step_wait": (C.c_int, [_P, C.POINTER(_U32)]),
@@ -336,6 +339,12 @@ class Infer:
         """handles: every rank's tp_handle() in rank order."""
         blob = b"".join(handles)
         check("att1_b200_infer_tp_connect", lib().att1_b200_infer_tp_connect(self.h, C.c_char_p(blob)))
+
+    def tp_set_wait(self, polls: int) -> None:
+        check("att1_b200_infer_tp_set_wait", lib().att1_b200_infer_tp_set_wait(self.h, polls))
+
+    def tp_reset(self) -> None:
+        check("att1_b200_infer_tp_reset", lib().att1_b200_infer_tp_reset(self.h))
 
     def tp_disconnect(self) -> None:
         check("att1_b200_infer_tp_disconnect", lib().att1_b200_infer_tp_disconnect(self.h))

@@ -228,11 +228,12 @@ __device__ __forceinline__ uint64_t tp_want(const b2_tp &tp)
 __device__ __forceinline__ bool tp_wait(const b2_tp &tp, uint32_t point, int32_t *err)
 {
     const uint64_t want = tp_want(tp);
+    const uint32_t limit = tp.wait_polls != 0 ? tp.wait_polls : (1u << 24);
     uint8_t *own = tp.peer[tp.rank];
     for (uint32_t s = 0; s < tp.world; ++s) {
         uint32_t spins = 0;
         while (ld_acquire_sys(tp_flag(own, point, s)) < want) {
-            if (++spins > (1u << 24)) {
+            if (++spins > limit) {
                 raise_error(err, B2_ERR_TIMEOUT);
                 return false;
             }

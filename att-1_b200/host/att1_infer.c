@@ -51,6 +51,7 @@ struct att1_infer {
     uint32_t *tp_epoch;
     int32_t *tp_done;
     int tp_ready;
+    uint32_t tp_wait_polls;            /* bound of every exchange wait (0: the kernels' default) */
     b2_tp tp_base;                     /* exchange description shared by the step's kernels */
     int device;
     cudaStream_t stream;
@@ -359,6 +360,7 @@ static void tp_wire(att1_infer_t *inf)
     t.logit_floats = inf->batch * inf->vl;
     t.epoch = inf->tp_epoch;
     t.done = inf->tp_done;
+    t.wait_polls = inf->tp_wait_polls;
     t.in_point = B2_TP_NONE;
     t.out_point = B2_TP_NONE;
     inf->tp_base = t;
@@ -825,6 +827,44 @@ att1_status_t att1_b200_infer_tp_disconnect(att1_infer_t *infer)
         if (s != infer->tp_rank) infer->tp_peer[s] = NULL;
     }
     infer->tp_ready = 0;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_infer_tp_set_wait(att1_infer_t *infer, uint32_t polls)
+{
+    if (infer == NULL || infer->tp_world < 2) return ATT1_ERR_INVALID_ARG;
+    if (infer->step_pending) return ATT1_ERR_STATE;
+    cudaSetDevice(infer->device);
+    cudaStreamSynchronize(infer->stream);
+    if (infer->exec) { /* the graph holds the kernels' parameters: capture again */
+        cudaGraphExecDestroy(infer->exec);
+        infer->exec = NULL;
+    }
+    infer->tp_wait_polls = polls;
+    if (!infer->tp_ready) return ATT1_OK; /* wired at connect */
+    return build_args(infer);
+}
+
+/* The exchange region holds flags that carry a step epoch: a rank whose step
+ * failed (a timed-out wait) may have published points of that step that the
+ * others never consumed. Zeroing every rank's flags and epochs, with no rank
+ * stepping, puts all of them back at epoch 0 together. */
+att1_status_t att1_b200_infer_tp_reset(att1_infer_t *infer)
+{
+    const att1_b200_config *c;
+    size_t flag_bytes;
+    if (infer == NULL || infer->tp_world < 2) return ATT1_ERR_INVALID_ARG;
+    if (infer->step_pending) return ATT1_ERR_STATE;
+    c = &infer->cfg;
+    cudaSetDevice(infer->device);
+    flag_bytes = ((size_t)(2 * c->n_layers + 1) * B2_TP_MAX + B2_TP_MAX * B2_TP_MAX_ITEMS) * sizeof(uint64_t);
+    if (cudaStreamSynchronize(infer->stream) != cudaSuccess ||
+        cudaMemsetAsync(infer->tp_region, 0, flag_bytes, infer->stream) != cudaSuccess ||
+        cudaMemsetAsync(infer->tp_epoch, 0, sizeof(uint32_t), infer->stream) != cudaSuccess ||
+        cudaMemsetAsync(infer->tp_done, 0, sizeof(int32_t), infer->stream) != cudaSuccess ||
+        cudaMemsetAsync(infer->err_d, 0, sizeof(int32_t), infer->stream) != cudaSuccess ||
+        cudaStreamSynchronize(infer->stream) != cudaSuccess)
+        return ATT1_ERR_STATE;
     return ATT1_OK;
 }
 

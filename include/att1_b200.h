@@ -93,6 +93,16 @@ att1_status_t att1_b200_infer_tp_connect(att1_infer_t *infer, const void *handle
 att1_status_t att1_b200_infer_tp_disconnect(att1_infer_t *infer);
 /* All ranks of one process (rank r on its own device), connected by peer access. */
 att1_status_t att1_b200_infer_tp_connect_local(att1_infer_t *const *infers, uint32_t world);
+/* Bound of every wait for another rank inside the step's kernels, in polls of
+ * the flag (about 0.1 us each; 0 = 2^24). A wait that runs out ends the step
+ * with ATT1_ERR_TIMEOUT and the context stays usable. */
+att1_status_t att1_b200_infer_tp_set_wait(att1_infer_t *infer, uint32_t polls);
+/* After a step failed on any rank (e.g. ATT1_ERR_TIMEOUT because another rank
+ * did not take it): with no rank stepping, call on every rank, synchronise the
+ * ranks on the host, then step together again. Clears this rank's exchange
+ * flags and step epoch; positions are the host's (the failed step did not
+ * advance them). */
+att1_status_t att1_b200_infer_tp_reset(att1_infer_t *infer);
 /* A step in two halves, so one thread can drive several ranks: queue the
  * step on every rank, then wait for each. */
 att1_status_t att1_b200_infer_step_async(att1_infer_t *infer, const uint32_t *tokens);

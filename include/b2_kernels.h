@@ -177,6 +177,7 @@ typedef struct b2_tp {
     const float *in_resid;        /* [batch][cols] residual added by that prologue */
     float *in_out;                /* [batch][cols]: the prologue stores the summed input here, may be NULL */
     uint32_t row_offset;          /* LOGITS: vocabulary id of local row 0 */
+    uint32_t wait_polls;          /* polls of a flag before a wait gives up (B2_ERR_TIMEOUT); 0 = 2^24 */
 } b2_tp;
 
 size_t b2_tp_region_bytes(uint32_t points, uint32_t slot_floats, uint32_t logit_floats);

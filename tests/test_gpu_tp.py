@@ -1,12 +1,16 @@
-"""Tensor-parallel decode on two GPUs against the single-model oracle.
+"""Tensor-parallel decode on 2, 4 and 8 GPUs against the single-model oracle.
 
-Two ranks (one GPU each) hold the shards of a synthetic model and exchange
+N ranks (one GPU each) hold the shards of a synthetic model and exchange
 partial results through each other's device memory inside the step kernels
 (B2_EPI_PUSH epilogues, summing prologues, logits all-gather). Teacher-forced
-logits of the rank-0 context (all vocabulary rows) must match the oracle's
-full model at the parity tolerance, and both ranks must produce the same
-tokens. Once with both ranks in this process (peer access), once as two
-processes connected by CUDA IPC handles exchanged over gloo.
+logits of every rank's context (all vocabulary rows) must match the oracle's
+full model at the parity tolerance, and all ranks must produce the same
+tokens. With all ranks in this process (peer access), and as N processes
+connected by CUDA IPC handles exchanged over gloo. The reference's cluster
+API (att1_cluster_infer_*, tile_count N) on .att1 files is checked against
+the oracle too (reference src/cluster_infer.c:865-1163; its own test
+tests/test_cluster_infer.c:27-75 checks cluster == single tile). Each test
+runs for every world size the machine has GPUs for.
 """
 import os
 import socket
@@ -30,8 +34,11 @@ def _gpus():
 
 
 need2 = pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+WORLDS = [pytest.param(w, marks=pytest.mark.skipif(_gpus() < w, reason=f"needs {w} GPUs")) for w in (2, 4, 8)]
 
-OCFG = dict(vocab=2048, n_layers=2, n_heads=8, n_kv_heads=2, d_model=256, d_ff=512, max_seq=64,
+# divisible by every world size: 16 query / 8 KV heads of 32, SwiGLU rows and
+# vocabulary rows split evenly, 32-aligned WO / down input columns per rank
+OCFG = dict(vocab=2048, n_layers=2, n_heads=16, n_kv_heads=8, d_model=512, d_ff=1024, max_seq=64,
             dtype=O.Q4, eps=1e-5, theta=10000.0)
 
 
@@ -44,11 +51,11 @@ def make_cfg(b2, ocfg):
                           ocfg.max_seq, dtype=ocfg.dtype, eps=ocfg.eps, final_eps=ocfg.final_eps, theta=ocfg.theta)
 
 
-@need2
-def test_tp2_in_process_matches_oracle(b2, orc):
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_in_process_matches_oracle(b2, orc, world):
     ocfg = O.Config.make(**OCFG)
     cfg = make_cfg(b2, ocfg)
-    ranks = [b2.Infer.synth_tp(cfg, 77, r, 2) for r in range(2)]
+    ranks = [b2.Infer.synth_tp(cfg, 77, r, world) for r in range(world)]
     b2.Infer.tp_connect_local(ranks)
     om = orc.model(ocfg, 77, threads=8)
     toks = orc.synth_tokens(5, 24, ocfg.vocab)
@@ -56,7 +63,7 @@ def test_tp2_in_process_matches_oracle(b2, orc):
         for r in ranks:
             r.step_async([int(t)])
         outs = [r.step_wait() for r in ranks]
-        assert outs[0][0] == outs[1][0]
+        assert all(o[0] == outs[0][0] for o in outs)
         clog, ctok = om.decode(int(t))
         for r in ranks:
             e = rel_err(r.logits()[0], clog)
@@ -70,8 +77,8 @@ def test_tp2_in_process_matches_oracle(b2, orc):
         r.close()
 
 
-@need2
-def test_tp2_dense_batch_matches_oracle(b2, orc):
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_dense_batch_matches_oracle(b2, orc, world):
     """20 sequences per step: above the GEMVs' batch, so every projection runs
     on the tensor-core GEMM and the exchange runs as kernels of its own (push,
     rank-ordered sum, logits all-gather). Each sequence is replayed alone on
@@ -79,7 +86,7 @@ def test_tp2_dense_batch_matches_oracle(b2, orc):
     ocfg = O.Config.make(**OCFG)
     cfg = make_cfg(b2, ocfg)
     batch, steps, seed = 20, 6, 91
-    ranks = [b2.Infer.synth_tp(cfg, seed, r, 2, batch=batch) for r in range(2)]
+    ranks = [b2.Infer.synth_tp(cfg, seed, r, world, batch=batch) for r in range(world)]
     b2.Infer.tp_connect_local(ranks)
     toks = [[int(t) for t in orc.synth_tokens(seed + b, steps, ocfg.vocab)] for b in range(batch)]
     glog, gtok = [], []
@@ -87,10 +94,10 @@ def test_tp2_dense_batch_matches_oracle(b2, orc):
         for r in ranks:
             r.step_async([toks[b][s] for b in range(batch)])
         outs = [r.step_wait() for r in ranks]
-        assert (outs[0] == outs[1]).all()
+        assert all((o == outs[0]).all() for o in outs)
         gtok.append(outs[0])
         logs = [r.logits() for r in ranks]
-        assert (logs[0] == logs[1]).all()
+        assert all((lg == logs[0]).all() for lg in logs)
         glog.append(logs[0])
     for r in ranks:
         r.close()
@@ -106,16 +113,16 @@ def test_tp2_dense_batch_matches_oracle(b2, orc):
             assert gap <= 2 * LOGITS_RTOL or int(gtok[s][b]) == int(np.argmax(clog))
 
 
-@need2
-def test_tp2_sampler_same_tokens_on_both_ranks(b2):
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_sampler_same_tokens_on_every_rank(b2, world):
     """Top-k / temperature sampling under tensor parallelism: each rank draws
-    from its all-gathered logits, so both ranks return the same tokens, and
+    from its all-gathered logits, so every rank returns the same tokens, and
     each token follows from the full-vocabulary logits by the restated rule."""
     from test_sampler import agree
     ocfg = O.Config.make(**OCFG)
     cfg = make_cfg(b2, ocfg)
     k, T, seed, batch = 16, 0.8, 5, 3
-    ranks = [b2.Infer.synth_tp(cfg, 77, r, 2, batch=batch) for r in range(2)]
+    ranks = [b2.Infer.synth_tp(cfg, 77, r, world, batch=batch) for r in range(world)]
     b2.Infer.tp_connect_local(ranks)
     for r in ranks:
         r.set_sampler(k, T, seed)
@@ -124,7 +131,7 @@ def test_tp2_sampler_same_tokens_on_both_ranks(b2):
         for r in ranks:
             r.step_async(toks)
         outs = [r.step_wait() for r in ranks]
-        assert (outs[0] == outs[1]).all()
+        assert all((o == outs[0]).all() for o in outs)
         logits, pos = ranks[0].logits(), ranks[0].position()
         for b in range(batch):
             assert agree(outs[0][b], logits[b], k, T, seed, b, pos)
@@ -133,7 +140,7 @@ def test_tp2_sampler_same_tokens_on_both_ranks(b2):
         r.close()
 
 
-def _ipc_rank(rank, port, out_dir):
+def _ipc_rank(rank, world, port, out_dir):
     import sys
     sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -143,10 +150,10 @@ def _ipc_rank(rank, port, out_dir):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=2)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
     ocfg = O2.Config.make(**OCFG)
-    inf = b2.Infer.synth_tp(make_cfg(b2, ocfg), 77, rank, 2)
-    handles = [None, None]
+    inf = b2.Infer.synth_tp(make_cfg(b2, ocfg), 77, rank, world)
+    handles = [None] * world
     dist.all_gather_object(handles, inf.tp_handle())
     inf.tp_connect(handles)
     orc = O2.Oracle()
@@ -163,32 +170,38 @@ def _ipc_rank(rank, port, out_dir):
     dist.destroy_process_group()
 
 
-@need2
-def test_tp2_two_processes_ipc_matches_oracle(orc, tmp_path):
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_processes_ipc_matches_oracle(orc, tmp_path, world):
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.spawn(_ipc_rank, args=(port, str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_ipc_rank, args=(world, port, str(tmp_path)), nprocs=world, join=True)
     ocfg = O.Config.make(**OCFG)
     om = orc.model(ocfg, 77, threads=8)
     toks = orc.synth_tokens(5, 12, ocfg.vocab)
-    res = [np.load(tmp_path / f"tp_rank{r}.npy", allow_pickle=True).item() for r in range(2)]
-    assert res[0]["tokens"] == res[1]["tokens"]
+    res = [np.load(tmp_path / f"tp_rank{r}.npy", allow_pickle=True).item() for r in range(world)]
+    assert all(r["tokens"] == res[0]["tokens"] for r in res)
     for s, t in enumerate(toks):
         clog, _ = om.decode(int(t))
-        for r in range(2):
+        for r in range(world):
             assert rel_err(res[r]["logits"][s], clog) <= LOGITS_RTOL
 
 
-def _cluster_vs_single(b2, orc, tmp_path, dtype):
-    """att1_cluster_infer_* with tile_count 2 on a .att1 file against the
-    single-device context of the same file: same tokens, logits within the
-    parity tolerance, per-tile counters advanced."""
+def _cluster_vs_oracle(b2, orc, tmp_path, dtype, world):
+    """att1_cluster_infer_* with tile_count = world on a .att1 file against the
+    oracle's model of the same file (eps 1e-6, theta 1e4, the reference's
+    file-model settings; q8 for an f32 file) and against the single-device
+    context: logits within the parity tolerance, the same tokens where the
+    oracle's top two are apart, per-tile counters advanced."""
     import ctypes as C
     import att1file
+    V, NL, H, D, F = 512, 2, 8, 256, 512
     path = str(tmp_path / f"m_{dtype}.att1")
-    att1file.synth_model_file(path, orc, 512, 2, 4, 128, 256, 64, dtype, 21)
+    att1file.synth_model_file(path, orc, V, NL, H, D, F, 64, dtype, 21)
+    ocfg = O.Config.make(vocab=V, n_layers=NL, n_heads=H, n_kv_heads=H, d_model=D, d_ff=F, max_seq=64,
+                         dtype=O.Q4 if dtype == "q4" else O.Q8, eps=1e-6, theta=10000.0)
+    om = orc.model(ocfg, 21, threads=8)
     L = b2.lib()
     m = b2.Model()
     assert L.att1_model_load(path.encode(), C.byref(m)) == 0
@@ -196,42 +209,86 @@ def _cluster_vs_single(b2, orc, tmp_path, dtype):
     create = L.att1_infer_create_q4 if dtype == "q4" else L.att1_infer_create
     ccreate = L.att1_cluster_infer_create_q4 if dtype == "q4" else L.att1_cluster_infer_create
     assert create(C.byref(m), C.byref(single)) == 0
-    cfg = b2.ClusterConfig(2, 0, 0, 0)
+    cfg = b2.ClusterConfig(world, 0, 0, 0)
     assert ccreate(C.byref(m), C.byref(cfg), C.byref(cl)) == 0
     try:
-        toks = orc.synth_tokens(9, 12, 512)
+        toks = orc.synth_tokens(9, 12, V)
         for t in toks:
             a, b = C.c_uint32(), C.c_uint32()
             assert L.att1_infer_decode_token(single, int(t), C.byref(a)) == 0
             assert L.att1_cluster_infer_decode_token(cl, int(t), C.byref(b)) == 0
             n1, n2 = C.c_size_t(), C.c_size_t()
-            l1 = np.ctypeslib.as_array(L.att1_infer_logits(single, C.byref(n1)), (512,)).copy()
-            l2 = np.ctypeslib.as_array(L.att1_cluster_infer_logits(cl, C.byref(n2)), (512,)).copy()
-            assert n1.value == n2.value == 512
-            assert rel_err(l2, l1) <= LOGITS_RTOL
-            top2 = np.sort(l1)[-2:]
-            if (top2[1] - top2[0]) / np.abs(l1).max() > 2 * LOGITS_RTOL:
-                assert a.value == b.value
+            l1 = np.ctypeslib.as_array(L.att1_infer_logits(single, C.byref(n1)), (V,)).copy()
+            l2 = np.ctypeslib.as_array(L.att1_cluster_infer_logits(cl, C.byref(n2)), (V,)).copy()
+            assert n1.value == n2.value == V
+            want, _ = om.decode(int(t))
+            assert rel_err(l2, want) <= LOGITS_RTOL
+            assert rel_err(l1, want) <= LOGITS_RTOL
+            top2 = np.sort(want)[-2:]
+            if (top2[1] - top2[0]) / np.abs(want).max() > 2 * LOGITS_RTOL:
+                assert a.value == b.value == int(np.argmax(want))
         pos = C.c_size_t()
         assert L.att1_cluster_infer_position(cl, C.byref(pos)) == 0 and pos.value == 12
-        for tile in range(2):
+        for tile in range(world):
             k = b2.TileCounters()
             assert L.att1_cluster_infer_get_tile_counters(cl, tile, C.byref(k)) == 0
-            assert k.layers_run == 12 * 2 and k.activations_sent == 12 * 2 * 2
-            assert (k.layer_start, k.layer_end) == (0, 2)
+            assert k.layers_run == 12 * NL and k.activations_sent == 12 * NL * 2
+            assert (k.layer_start, k.layer_end) == (0, NL)
     finally:
         L.att1_cluster_infer_destroy(cl)
         L.att1_infer_destroy(single)
         L.att1_model_free(C.byref(m))
 
 
-@need2
-def test_cluster_two_tiles_q4_file(b2, orc, tmp_path):
-    _cluster_vs_single(b2, orc, tmp_path, "q4")
+@pytest.mark.parametrize("world", WORLDS)
+def test_cluster_tiles_q4_file(b2, orc, tmp_path, world):
+    _cluster_vs_oracle(b2, orc, tmp_path, "q4", world)
 
 
-@need2
-def test_cluster_two_tiles_f32_file_q8(b2, orc, tmp_path):
+@pytest.mark.parametrize("world", WORLDS)
+def test_cluster_tiles_f32_file_q8(b2, orc, tmp_path, world):
     """f32 file through att1_cluster_infer_create: q8 weights quantised per
     whole output row before the row-parallel split."""
-    _cluster_vs_single(b2, orc, tmp_path, "f32")
+    _cluster_vs_oracle(b2, orc, tmp_path, "f32", world)
+
+
+@need2
+def test_tp_wait_runs_out_and_ranks_recover(b2, orc):
+    """A rank that never takes its step: the other rank's bounded waits for
+    its exchange flags run out (a flag nothing sets), the step ends with
+    ATT1_ERR_TIMEOUT instead of a hang or a fault, the position stays where it
+    was, and after att1_b200_infer_tp_reset on both ranks the next joint steps
+    (repeating the failed one) match the oracle."""
+    ocfg = O.Config.make(**OCFG)
+    cfg = make_cfg(b2, ocfg)
+    ranks = [b2.Infer.synth_tp(cfg, 77, r, 2) for r in range(2)]
+    b2.Infer.tp_connect_local(ranks)
+    om = orc.model(ocfg, 77, threads=8)
+    toks = [int(t) for t in orc.synth_tokens(5, 4, ocfg.vocab)]
+    try:
+        for r in ranks:
+            r.step_async([toks[0]])
+        for r in ranks:
+            r.step_wait()
+        om.decode(toks[0])
+        for r in ranks:
+            r.tp_set_wait(1 << 12)                     # about half a millisecond per wait
+        ranks[0].step_async([toks[1]])                 # rank 1 does not take this step
+        with pytest.raises(b2.Att1Error) as e:
+            ranks[0].step_wait()
+        assert e.value.rc == -11                       # ATT1_ERR_TIMEOUT
+        assert ranks[0].position() == 1 and ranks[1].position() == 1
+        for r in ranks:
+            r.tp_reset()
+            r.tp_set_wait(0)
+        for t in toks[1:]:
+            for r in ranks:
+                r.step_async([t])
+            outs = [r.step_wait() for r in ranks]
+            assert outs[0][0] == outs[1][0]
+            clog, _ = om.decode(t)
+            for r in ranks:
+                assert rel_err(r.logits()[0], clog) <= LOGITS_RTOL
+    finally:
+        for r in ranks:
+            r.close()
