@@ -25,14 +25,14 @@
 
 namespace b2 {
 
-constexpr int kAttnWarps = 16;     // consumer warps
-constexpr int kAttnThreads = kAttnWarps * 32 + 32;  // + one producer warp
+constexpr int kAttnWarps = 16;     // consumer warps (upper bound over the variants)
 constexpr uint32_t kSub = 32;       // positions per sub-tile
 constexpr uint32_t kBufs = 6;       // sub-tile buffers (ring stages)
 constexpr int kCtasPerSm = 1;       // resident CTAs per SM the split count aims at
 
+template <int NW>
 struct ConsumerWarps {
-    __device__ void operator()() const { asm volatile("bar.sync 1, %0;" ::"n"(kAttnWarps * 32) : "memory"); }
+    __device__ void operator()() const { asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory"); }
 };
 
 __host__ __device__ constexpr size_t attn_ring_smem(uint32_t hd)
@@ -41,36 +41,31 @@ __host__ __device__ constexpr size_t attn_ring_smem(uint32_t hd)
     return 2 * kBufs * 8 + 2 * (size_t)kBufs * kSub * hd * sizeof(float) + 16;
 }
 
-// Merge two online-softmax states (m, l, o) of one query head.
-__device__ __forceinline__ void soft_merge4(float &m, float &l, float4 &o, float m2, float l2, float4 o2)
-{
-    const float M = fmaxf(m, m2);
-    if (M == -INFINITY) return;  // both empty
-    const float f1 = expf(m - M), f2 = expf(m2 - M);
-    l = fmaf(l, f1, l2 * f2);
-    o = make_float4(fmaf(o.x, f1, o2.x * f2), fmaf(o.y, f1, o2.y * f2), fmaf(o.z, f1, o2.z * f2),
-                    fmaf(o.w, f1, o2.w * f2));
-    m = M;
-}
-
 // CTA (split, KV head, item) owns a contiguous range of one KV head's
 // positions (about one CTA per SM over the step). Inside a page a KV head's
 // rows are contiguous, so a producer warp streams the range through a ring of
 // kBufs shared-memory sub-tiles with 1-D bulk copies (TMA; "full" mbarrier
-// per stage, counted in bytes). Sixteen consumer warps take positions of each
-// sub-tile (LP lanes per position, 4*V4 dimensions per lane: float4 chunk v of
-// lane sl holds dimensions 4*(sl + v*LP)..+3, so a lane group's loads of one
-// chunk are contiguous), compute the
-// scores of the query heads that share the KV head with a halving exchange
-// (each step hands half of the heads to the partner lane), keep an online
-// softmax and the weighted V sum per lane, and release the stage on its
-// "empty" mbarrier, so warps never wait for one another while streaming.
-// At the end the lane groups and the warps are merged.
-template <int LP, int MG, int V4>  // lanes per position, query heads per KV head (bound), float4s per lane
-__global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnParams p)
+// per stage, counted in bytes). NW consumer warps take positions of each
+// sub-tile, LP lanes per position and NP positions per lane group at a time.
+// Scores: float4 chunk v of lane sl holds dimensions 4*(sl + v*LP)..+3 of q
+// and k for every query head of the group; the partial dot products are
+// summed over the LP lanes with a halving exchange (each step hands half of
+// the heads to the partner lane), after which the HL = LP / MG lanes of head
+// group h = sl / HL all hold the full score of query head h. Values: those HL
+// lanes split the head's dimensions (chunk w of lane hl holds dimensions
+// 4*(hl + w*HL)..+3), so each lane keeps the online softmax (max, sum) and the
+// weighted V sum of its own query head only: no score is broadcast and every
+// exponential is computed once per head. Lanes release the stage on its
+// "empty" mbarrier, so warps never wait for one another while streaming. At
+// the end the lane groups and the warps are merged.
+template <int LP, int MG, int V4, int NW, int NP>
+__global__ void __launch_bounds__(NW * 32 + 32, 1) attn_ring_kernel(const AttnParams p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int PPW = 32 / LP;
+    constexpr int PPW = 32 / LP;          // positions per warp pass
+    constexpr int HL = LP / MG;           // lanes per query head in the value sums
+    constexpr int VW = V4 * MG;           // float4 chunks of V per lane
+    static_assert(HL >= 1, "at most LP query heads per KV head");
     const uint32_t split = blockIdx.x, S = gridDim.x, kvh = blockIdx.y, item = blockIdx.z;
     const uint32_t hd = p.head_dim, G = p.group;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,13 +96,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
     if (threadIdx.x == 0) {
         for (uint32_t b = 0; b < kBufs; ++b) {
             mbar_init(&full[b], 1);
-            mbar_init(&empty[b], kAttnWarps);
+            mbar_init(&empty[b], NW);
         }
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kAttnWarps) {
+    if (warp == NW) {
         // producer: sub-tile t of the range into stage t % kBufs (page pieces are contiguous)
         const uint32_t rowb = hd * sizeof(float);
         bool waited = false;
@@ -141,12 +136,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
     pdl_wait();
     pdl_launch_dependents();
     const int sub = lane / LP, sl = lane % LP;
-    uint32_t dv[V4];
-    bool dval[V4];
+    const int hsel = sl / HL, hl = sl % HL;       // query head of this lane's value sums, its lane in the head
+    const bool hval = hsel < (int)G;
+    uint32_t dv[V4], dw[VW];
+    bool dval[V4], dwv[VW];
 #pragma unroll
     for (int v = 0; v < V4; ++v) {
         dv[v] = 4 * (sl + v * LP);
         dval[v] = dv[v] < hd;
+    }
+#pragma unroll
+    for (int w = 0; w < VW; ++w) {
+        dw[w] = 4 * (hl + w * HL);
+        dwv[w] = dw[w] < hd;
     }
     float4 qv[MG][V4];
 #pragma unroll
@@ -158,40 +160,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
                 qv[gq][v] = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)item * p.n_heads * hd +
                                                                     (size_t)(kvh * G + gq) * hd + dv[v]));
         }
-    float m[MG], l[MG];
-    float4 o[MG][V4];
+    float m = -INFINITY, l = 0.0f;
+    float4 o[VW];
 #pragma unroll
-    for (int gq = 0; gq < MG; ++gq) {
-        m[gq] = -INFINITY;
-        l[gq] = 0.0f;
-#pragma unroll
-        for (int v = 0; v < V4; ++v) o[gq][v] = make_float4(0, 0, 0, 0);
-    }
+    for (int w = 0; w < VW; ++w) o[w] = make_float4(0, 0, 0, 0);
     bool ok = true;
+    constexpr uint32_t kStride = NW * PPW;     // positions of one pass of every warp's lane groups
     for (uint32_t t = 0; t < ntiles; ++t) {
         const uint32_t buf = t % kBufs, nt = min(kSub, n - t * kSub);
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&full[buf], (t / kBufs) & 1u, p.err));
         const float *K = Kb + (size_t)buf * kSub * hd, *V = Vb + (size_t)buf * kSub * hd;
-        // this warp's positions of the sub-tile (warp-uniform trip count); a lane
-        // group takes two at a time only when the warps' groups cannot cover
-        // the sub-tile in one pass (NP = 1: the second would always be empty)
-        constexpr uint32_t kStride = kAttnWarps * PPW;
-        constexpr int NP = kStride < kSub ? 2 : 1;
+        // this warp's positions of the sub-tile (warp-uniform trip count)
         for (uint32_t wb = warp * PPW; wb < nt; wb += NP * kStride) {
-            const uint32_t ra = wb + sub, rb = ra + kStride;
-            const bool va = ok && ra < nt, vb = NP == 2 && ok && rb < nt;
-            float4 k4[NP][V4], v4[NP][V4];
+            uint32_t r[NP];
+            bool va[NP];
+            float4 k4[NP][V4];
 #pragma unroll
-            for (int v = 0; v < V4; ++v) {
-                const float4 z = make_float4(0, 0, 0, 0);
-                k4[0][v] = (va && dval[v]) ? *reinterpret_cast<const float4 *>(K + ra * hd + dv[v]) : z;
-                v4[0][v] = (va && dval[v]) ? *reinterpret_cast<const float4 *>(V + ra * hd + dv[v]) : z;
-                if constexpr (NP == 2) {
-                    k4[NP - 1][v] = vb && dval[v] ? *reinterpret_cast<const float4 *>(K + rb * hd + dv[v]) : z;
-                    v4[NP - 1][v] = vb && dval[v] ? *reinterpret_cast<const float4 *>(V + rb * hd + dv[v]) : z;
-                }
+            for (int j = 0; j < NP; ++j) {
+                r[j] = wb + sub + j * kStride;
+                va[j] = ok && r[j] < nt;
+#pragma unroll
+                for (int v = 0; v < V4; ++v)
+                    k4[j][v] = (va[j] && dval[v]) ? *reinterpret_cast<const float4 *>(K + r[j] * hd + dv[v])
+                                                  : make_float4(0, 0, 0, 0);
             }
-            float mine[NP];
+            float sc[NP];
 #pragma unroll
             for (int j = 0; j < NP; ++j) {
                 float dot[MG];
@@ -206,7 +199,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
                 // sum over the LP lanes of the position: while more than one head
                 // is left each exchange hands half of them to the partner lane
                 // (the upper lane keeps the upper half), then plain exchanges;
-                // lane sl ends with head (top log2 MG bits of sl)
+                // lane sl ends with head sl / HL
 #pragma unroll
                 for (int cnt = MG, off = LP / 2; off > 0; off >>= 1) {
                     if (cnt > 1) {
@@ -222,94 +215,93 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
                         dot[0] += __shfl_xor_sync(0xffffffffu, dot[0], off);
                     }
                 }
-                mine[j] = __fmul_rn(dot[0], p.inv_sqrt);  // src/attention.c:521-523
+                sc[j] = __fmul_rn(dot[0], p.inv_sqrt);  // src/attention.c:521-523
             }
-            // online softmax over both positions at once, per query head
+            // online softmax of this lane's head over the NP positions, then the
+            // weighted values of its dimension chunks
+            if (hval && va[0]) {
+                float nm = m;
 #pragma unroll
-            for (int gq = 0; gq < MG; ++gq) {
-                if (gq < (int)G) {
-                    const int src = (sub * LP) | (gq * (LP / MG));  // a lane holding head gq
-                    const float sa = __shfl_sync(0xffffffffu, mine[0], src);
-                    const float sb = NP == 2 ? __shfl_sync(0xffffffffu, mine[NP - 1], src) : 0.0f;
-                    if (va) {
-                        const float nm = fmaxf(m[gq], vb ? fmaxf(sa, sb) : sa);
-                        const float corr = __expf(m[gq] - nm);
-                        const float pa = __expf(sa - nm), pb = vb ? __expf(sb - nm) : 0.0f;
-                        l[gq] = fmaf(l[gq], corr, pa + pb);
+                for (int j = 0; j < NP; ++j)
+                    if (va[j]) nm = fmaxf(nm, sc[j]);
+                const float corr = __expf(m - nm);
+                float pj[NP];
+                float psum = 0.0f;
 #pragma unroll
-                        for (int v = 0; v < V4; ++v) {
-                            float4 w = make_float4(pa * v4[0][v].x, pa * v4[0][v].y, pa * v4[0][v].z, pa * v4[0][v].w);
-                            if constexpr (NP == 2)
-                                w = make_float4(fmaf(pb, v4[NP - 1][v].x, w.x), fmaf(pb, v4[NP - 1][v].y, w.y),
-                                                fmaf(pb, v4[NP - 1][v].z, w.z), fmaf(pb, v4[NP - 1][v].w, w.w));
-                            o[gq][v] = make_float4(fmaf(o[gq][v].x, corr, w.x), fmaf(o[gq][v].y, corr, w.y),
-                                                   fmaf(o[gq][v].z, corr, w.z), fmaf(o[gq][v].w, corr, w.w));
-                        }
-                        m[gq] = nm;
-                    }
+                for (int j = 0; j < NP; ++j) {
+                    pj[j] = va[j] ? __expf(sc[j] - nm) : 0.0f;
+                    psum += pj[j];
                 }
+                l = fmaf(l, corr, psum);
+#pragma unroll
+                for (int w = 0; w < VW; ++w) {
+                    float4 acc = make_float4(o[w].x * corr, o[w].y * corr, o[w].z * corr, o[w].w * corr);
+#pragma unroll
+                    for (int j = 0; j < NP; ++j) {
+                        if (va[j] && dwv[w]) {
+                            const float4 vv = *reinterpret_cast<const float4 *>(V + r[j] * hd + dw[w]);
+                            acc = make_float4(fmaf(pj[j], vv.x, acc.x), fmaf(pj[j], vv.y, acc.y),
+                                              fmaf(pj[j], vv.z, acc.z), fmaf(pj[j], vv.w, acc.w));
+                        }
+                    }
+                    o[w] = acc;
+                }
+                m = nm;
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[buf]);
     }
-    // merge the lane groups of the warp (positions differ, dimensions match)
+    // merge the lane groups of the warp (positions differ, head and dimensions match)
 #pragma unroll
     for (int off = LP; off < 32; off <<= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+        const float l2 = __shfl_xor_sync(0xffffffffu, l, off);
+        float4 o2[VW];
 #pragma unroll
-        for (int gq = 0; gq < MG; ++gq) {
-            const float m2 = __shfl_xor_sync(0xffffffffu, m[gq], off);
-            const float l2 = __shfl_xor_sync(0xffffffffu, l[gq], off);
-            float4 o2[V4];
+        for (int w = 0; w < VW; ++w) {
+            o2[w].x = __shfl_xor_sync(0xffffffffu, o[w].x, off);
+            o2[w].y = __shfl_xor_sync(0xffffffffu, o[w].y, off);
+            o2[w].z = __shfl_xor_sync(0xffffffffu, o[w].z, off);
+            o2[w].w = __shfl_xor_sync(0xffffffffu, o[w].w, off);
+        }
+        const float M = fmaxf(m, m2);
+        if (M != -INFINITY) {
+            const float f1 = expf(m - M), f2 = expf(m2 - M);
+            l = fmaf(l, f1, l2 * f2);
 #pragma unroll
-            for (int v = 0; v < V4; ++v) {
-                o2[v].x = __shfl_xor_sync(0xffffffffu, o[gq][v].x, off);
-                o2[v].y = __shfl_xor_sync(0xffffffffu, o[gq][v].y, off);
-                o2[v].z = __shfl_xor_sync(0xffffffffu, o[gq][v].z, off);
-                o2[v].w = __shfl_xor_sync(0xffffffffu, o[gq][v].w, off);
-            }
-            // the chunks share one (m, l): merge them with the same factors
-            const float M = fmaxf(m[gq], m2);
-            if (M != -INFINITY) {
-                const float f1 = expf(m[gq] - M), f2 = expf(m2 - M);
-                l[gq] = fmaf(l[gq], f1, l2 * f2);
-#pragma unroll
-                for (int v = 0; v < V4; ++v)
-                    o[gq][v] = make_float4(fmaf(o[gq][v].x, f1, o2[v].x * f2), fmaf(o[gq][v].y, f1, o2[v].y * f2),
-                                           fmaf(o[gq][v].z, f1, o2[v].z * f2), fmaf(o[gq][v].w, f1, o2[v].w * f2));
-                m[gq] = M;
-            }
+            for (int w = 0; w < VW; ++w)
+                o[w] = make_float4(fmaf(o[w].x, f1, o2[w].x * f2), fmaf(o[w].y, f1, o2[w].y * f2),
+                                   fmaf(o[w].z, f1, o2[w].z * f2), fmaf(o[w].w, f1, o2[w].w * f2));
+            m = M;
         }
     }
     // merge the warps: state in shared memory (the ring is drained)
-    ConsumerWarps SYNC;
+    ConsumerWarps<NW> SYNC;
     SYNC();
-    float *wm = Kb, *wl = Kb + kAttnWarps * MG, *wo = Kb + 2 * kAttnWarps * MG;  // wo [warps][MG][hd]
-#pragma unroll
-    for (int gq = 0; gq < MG; ++gq) {
-        if (gq < (int)G && sub == 0) {
-            if (sl == 0) {
-                wm[warp * MG + gq] = m[gq];
-                wl[warp * MG + gq] = l[gq];
-            }
-#pragma unroll
-            for (int v = 0; v < V4; ++v)
-                if (dval[v]) *reinterpret_cast<float4 *>(wo + ((size_t)warp * MG + gq) * hd + dv[v]) = o[gq][v];
+    float *wm = Kb, *wl = Kb + NW * MG, *wo = Kb + 2 * NW * MG;  // wo [warps][MG][hd]
+    if (hval && sub == 0) {
+        if (hl == 0) {
+            wm[warp * MG + hsel] = m;
+            wl[warp * MG + hsel] = l;
         }
+#pragma unroll
+        for (int w = 0; w < VW; ++w)
+            if (dwv[w]) *reinterpret_cast<float4 *>(wo + ((size_t)warp * MG + hsel) * hd + dw[w]) = o[w];
     }
     SYNC();
     float *part_base = p.partial + ((size_t)(item * p.n_kv_heads + kvh) * p.nchunks_max) * G * (hd + 2);
     float *part = part_base + (size_t)split * G * (hd + 2);
-    const uint32_t nthreads = kAttnWarps * 32;
+    const uint32_t nthreads = NW * 32;
     for (uint32_t i = threadIdx.x; i < G * (hd + 2); i += nthreads) {
         const uint32_t gq = i / (hd + 2), d = i % (hd + 2);
         float M = -INFINITY;
-        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * MG + gq]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * MG + gq]);
         float v = 0.0f;
         if (d == 0) {
             v = M;
         } else {
-            for (int w = 0; w < kAttnWarps; ++w) {
+            for (int w = 0; w < NW; ++w) {
                 const float wmv = wm[w * MG + gq];
                 if (wmv == -INFINITY) continue;  // warp saw no position
                 v = fmaf(d == 1 ? wl[w * MG + gq] : wo[((size_t)w * MG + gq) * hd + d - 2], expf(wmv - M), v);
@@ -317,15 +309,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_ring_kernel(const AttnPa
         }
         part[i] = v;
     }
-    attn_publish(p, Kb + 2 * kAttnWarps * MG + (size_t)kAttnWarps * MG * hd, last, item, kvh, nactive, part_base,
-                 nthreads, SYNC);
+    attn_publish(p, Kb + 2 * NW * MG + (size_t)NW * MG * hd, last, item, kvh, nactive, part_base, nthreads, SYNC);
 }
+
+template <int NW, int NP>
+static const void *attn_fn(uint32_t hd, int mg)
+{
+    switch (attn_lanes(hd) * 10 + mg) {
+    case 84: return (const void *)attn_ring_kernel<8, 4, 1, NW, NP>;
+    case 88: return (const void *)attn_ring_kernel<8, 8, 1, NW, NP>;
+    case 164: return (const void *)attn_ring_kernel<16, 4, 1, NW, NP>;
+    case 168: return (const void *)attn_ring_kernel<16, 8, 1, NW, NP>;
+    case 324: return (const void *)attn_ring_kernel<32, 4, 1, NW, NP>;
+    default: return (const void *)attn_ring_kernel<32, 8, 1, NW, NP>;
+    }
+}
+
+// Consumer warps and positions per lane group at a time. Measured at the 8B
+// shape, context 4096 (one launch, CUDA events): 16 warps x 2 positions
+// 15.7 us; 16 x 1 16.8 us; 8 x 4 16.5 us; 8 x 2 18.0 us.
+constexpr int kNW = 16, kNP = 2;
 
 static cudaError_t launch_attn(const AttnParams &p, dim3 grid, int pdl, cudaStream_t st)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kAttnThreads);
+    cfg.blockDim = dim3(kNW * 32 + 32);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -334,18 +343,7 @@ static cudaError_t launch_attn(const AttnParams &p, dim3 grid, int pdl, cudaStre
     cfg.numAttrs = 1;
     const int mg = p.group <= 4 ? 4 : 8;
     cfg.dynamicSmemBytes = attn_ring_smem(p.head_dim);
-    const void *fn;
-    // one float4 of dimensions per lane: 8, 16 or 32 lanes per position (16
-    // lanes x 8 dimensions for head_dim 128 measured slower in the decode step:
-    // 2.37 vs 2.29 ms, at the 96-register limit of 17 warps)
-    switch (attn_lanes(p.head_dim) * 10 + mg) {
-    case 84: fn = (const void *)attn_ring_kernel<8, 4, 1>; break;
-    case 88: fn = (const void *)attn_ring_kernel<8, 8, 1>; break;
-    case 164: fn = (const void *)attn_ring_kernel<16, 4, 1>; break;
-    case 168: fn = (const void *)attn_ring_kernel<16, 8, 1>; break;
-    case 324: fn = (const void *)attn_ring_kernel<32, 4, 1>; break;
-    default: fn = (const void *)attn_ring_kernel<32, 8, 1>; break;
-    }
+    const void *fn = attn_fn<kNW, kNP>(p.head_dim, mg);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
     if (e != cudaSuccess) return e;
     void *args[] = {const_cast<AttnParams *>(&p)};

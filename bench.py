@@ -289,6 +289,63 @@ def time_attention(b2, torch, reps=30, ctx=4096, layers=8):
     return algo, ms
 
 
+def time_prefill(b2, torch, n=512, seed=3):
+    """Prompt prefill of the 8B shape: n tokens through att1_b200_infer_prefill
+    (tcgen05 dequant-GEMM for every projection, causal attention) on a fresh
+    context, CUDA events on the context's stream."""
+    import numpy as np
+    cfg = b2.Config.make(SHAPE["vocab"], SHAPE["n_layers"], SHAPE["n_heads"], SHAPE["n_kv_heads"], SHAPE["d_model"],
+                         SHAPE["d_ff"], 4096, dtype=4, eps=SHAPE["eps"], theta=SHAPE["theta"])
+    inf = b2.Infer.synth(cfg, seed)
+    toks = np.random.default_rng(seed).integers(0, SHAPE["vocab"], size=n)
+    inf.prefill(toks[:64])           # warm-up (plans, first launches)
+    inf.seek(0)
+    st = torch.cuda.ExternalStream(inf.stream())
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    inf.prefill(toks)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    inf.close()
+    d, F, V, L = SHAPE["d_model"], SHAPE["d_ff"], SHAPE["vocab"], SHAPE["n_layers"]
+    hd = d // SHAPE["n_heads"]
+    params = L * (d * (SHAPE["n_heads"] + 2 * SHAPE["n_kv_heads"]) * hd + d * d + 3 * F * d) + V * d
+    flops = 2.0 * n * params                        # the products of the reference's f32 matmuls
+    return {"tokens": n, "ms": ms, "tokens_per_s": n / (ms * 1e-3), "useful_tflops": flops / (ms * 1e-3) / 1e12,
+            "note": "useful = 2 * tokens * weights (f32-equivalent products); the GEMM issues 2 bf16 MMAs "
+                    "per product (x hi/lo as one operand, w hi/lo) for q4"}
+
+
+def time_batch_decode(b2, torch, batch=32, ctx=1024, steps=10, seed=4):
+    """Decode of `batch` sequences at context ~ctx through the tensor-core
+    route (batches above what the GEMVs hold), device-loop steps timed with
+    CUDA events. The KV of positions before ctx is the context's own
+    (zero-initialised) pages: the attention reads ctx positions per sequence
+    either way."""
+    cfg = b2.Config.make(SHAPE["vocab"], SHAPE["n_layers"], SHAPE["n_heads"], SHAPE["n_kv_heads"], SHAPE["d_model"],
+                         SHAPE["d_ff"], ctx + 64, dtype=4, eps=SHAPE["eps"], theta=SHAPE["theta"])
+    inf = b2.Infer.synth(cfg, seed, batch=batch)
+    inf.decode_batch(list(range(1, batch + 1)))
+    inf.seek(ctx - steps - 3)
+    inf.run_steps(3)
+    inf.sync()
+    st = torch.cuda.ExternalStream(inf.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    inf.run_steps(steps)
+    e1.record(st)
+    inf.sync()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    inf.close()
+    by = step_bytes(ctx - steps // 2, batch)
+    peak, _ = measured_peak()
+    return {"batch": batch, "ctx": ctx, "ms_per_step": ms, "tokens_per_s": batch * 1000.0 / ms,
+            "hbm_frac": by / (ms * 1e-3) / (peak * 1e9), "step_bytes": by}
+
+
 def load_traffic():
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -382,6 +439,10 @@ def run_b200(args, rank, world, local_rank):
         dist.barrier()
     inf.close()
     algo, kms = time_dominant_gemv(b2, torch, reps=4 if args.no_graph else 30)
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras["prefill_8b"] = time_prefill(b2, torch)
+        extras["decode_8b_batch32"] = time_batch_decode(b2, torch)
     peak, peak_kind = measured_peak()
     achieved = algo / (kms * 1e-3) / 1e9
     traffics = load_traffic()
@@ -424,6 +485,7 @@ def run_b200(args, rank, world, local_rank):
             "roofline": roofline,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "extras": extras,
         }
     if dist:
         dist.barrier()
@@ -468,6 +530,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
+    ap.add_argument("--no-extras", action="store_true", help="skip the prefill and batch-32 side measurements")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch kernels one by one without graph or PDL (for ncu launch lists)")
     ap.add_argument("--replicas", action="store_true",
