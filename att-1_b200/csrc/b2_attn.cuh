@@ -107,50 +107,28 @@ __device__ void attn_publish(const AttnParams &p, float *stage, int *last_flag, 
         SYNC();  // the flag may be rewritten by the next chunk of this CTA
         return;
     }
-    // final combine over chunks, in chunk order: the (max, sum) of every chunk
-    // and query head go to shared memory (the warp state area is free now)
-    // while each thread already has the loads of its first output element's
-    // values in flight (up to kPre chunks), so the two L2 round trips overlap
-    constexpr uint32_t kPre = 24;
+    // final combine over chunks, in chunk order: first the (max, sum) of every
+    // chunk and query head, loaded in parallel into shared memory (the warp
+    // state area is free now), then each output element
     float *cm = stage;                   // [nactive][G] maxima
     float *cl = stage + nactive * G;     // [nactive][G] sums
-    const size_t cstride = (size_t)G * (hd + 2);
-    float pre[kPre];
-    const uint32_t i0 = threadIdx.x;
-    if (i0 < G * hd) {
-        const float *pe = part_base + (i0 / hd) * (hd + 2) + 2 + i0 % hd;
-#pragma unroll
-        for (uint32_t c = 0; c < kPre; ++c)
-            if (c < nactive) pre[c] = ld_cg(pe + c * cstride);
-    }
     for (uint32_t i = threadIdx.x; i < nactive * G; i += nthreads) {
         const uint32_t c = i / G, gq = i % G;
-        const float *pc = part_base + (size_t)c * cstride + gq * (hd + 2);
+        const float *pc = part_base + (size_t)c * G * (hd + 2) + gq * (hd + 2);
         cm[i] = ld_cg(pc);
         cl[i] = ld_cg(pc + 1);
     }
     SYNC();
     for (uint32_t i = threadIdx.x; i < G * hd; i += nthreads) {
         const uint32_t gq = i / hd, d = i % hd;
-        const float *pe = part_base + gq * (hd + 2) + 2 + d;
         float M = -INFINITY;
         for (uint32_t c = 0; c < nactive; ++c) M = fmaxf(M, cm[c * G + gq]);
         float L = 0.0f, O = 0.0f;
-        uint32_t c = 0;
-        if (i == i0) {
-#pragma unroll
-            for (; c < kPre; ++c) {
-                if (c >= nactive) break;
-                const float f = expf(cm[c * G + gq] - M);
-                L = fmaf(cl[c * G + gq], f, L);
-                O = fmaf(pre[c], f, O);
-            }
-        }
 #pragma unroll 8
-        for (; c < nactive; ++c) {
+        for (uint32_t c = 0; c < nactive; ++c) {
             const float f = expf(cm[c * G + gq] - M);
             L = fmaf(cl[c * G + gq], f, L);
-            O = fmaf(ld_cg(pe + c * cstride), f, O);
+            O = fmaf(ld_cg(part_base + (size_t)c * G * (hd + 2) + gq * (hd + 2) + 2 + d), f, O);
         }
         p.ctx[(size_t)item * p.n_heads * hd + (size_t)(kvh * G + gq) * hd + d] = __fdiv_rn(O, L);
     }
