@@ -346,6 +346,47 @@ def time_batch_decode(b2, torch, batch=32, ctx=1024, steps=10, seed=4):
             "hbm_frac": by / (ms * 1e-3) / (peak * 1e9), "step_bytes": by}
 
 
+def time_gemm(b2, torch, m=512, rows=14336 * 2, cols=4096, reps=10):
+    """The tcgen05 dequant GEMM alone: m rows of x (prefill tokens or decode
+    sequences) against a q4 [rows x cols] matrix in the unit layout (the
+    gate/up shape by default), x prepared once; back-to-back launches timed
+    with CUDA events. Returns useful flops (2 m rows cols) and bf16 MMA flops
+    (two bf16 MMAs per product for q4: x hi/lo stacked against w hi, and w lo
+    against x hi)."""
+    import ctypes as C
+    L = b2.lib()
+    w = torch.zeros(L.b2_q4_bytes(rows, cols), dtype=torch.uint8, device="cuda")
+    assert L.b2_q4_synth(w.data_ptr(), 0, rows, cols, 5, 100, 101, 0.02, b2.ROWS_GATEUP, None) == 0
+    x = torch.randn(m * cols, device="cuda")
+    xs = torch.zeros(L.b2_gemm_xs_bytes(m, cols), dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert L.b2_gemm_prep(x.data_ptr(), cols, m, cols, None, 1e-5, xs.data_ptr(), err.data_ptr(), None) == 0
+    out = torch.zeros(m * rows, device="cuda")
+    a = b2.GemmArgs()
+    a.w = b2.QWeight(w.data_ptr(), None, 4, rows, cols, rows // 16, cols // 64)
+    a.xs, a.m, a.epilogue, a.out, a.out_stride, a.err = xs.data_ptr(), m, 0, out.data_ptr(), rows, err.data_ptr()
+    need = L.b2_gemm_scratch_bytes(C.byref(a))
+    scratch = torch.zeros(max(need, 16), dtype=torch.uint8, device="cuda")
+    a.scratch, a.scratch_bytes = scratch.data_ptr(), need
+    stream = torch.cuda.Stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            assert L.b2_gemm(C.byref(a), sp) == 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            L.b2_gemm(C.byref(a), sp)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * m * rows * cols
+    return {"m": m, "rows": rows, "cols": cols, "launch_ms": ms, "useful_tflops": flops / (ms * 1e-3) / 1e12,
+            "bf16_mma_tflops": 2 * flops / (ms * 1e-3) / 1e12, "weight_GBps": q4_bytes(rows, cols) / (ms * 1e-3) / 1e9}
+
+
 def load_traffic():
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -537,8 +578,9 @@ def main():
                     help="with several GPUs: independent replicas instead of one tensor-parallel model")
     ap.add_argument("--persistent", action="store_true",
                     help="run each step as one persistent launch instead of the per-operation kernel sequence")
-    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "attn"],
-                    help="time only one kernel and print it (for ncu captures): the gate/up GEMV (default) or the attention at context 4096")
+    ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "attn", "gemm"],
+                    help="time only one kernel and print it (for ncu captures): the gate/up GEMV (default), the "
+                         "attention at context 4096, or the tcgen05 GEMM at the gate/up shape for --batch rows")
     ap.add_argument("--layers", type=int, default=SHAPE["n_layers"],
                     help="decoder depth (profiling runs only; the metric is defined at 32)")
     args = ap.parse_args()
@@ -550,6 +592,10 @@ def main():
         import torch
         import att1_b200 as b2
         torch.cuda.set_device(local_rank)
+        if args.kernel_only == "gemm":
+            r = time_gemm(b2, torch, m=args.batch, reps=args.steps)
+            print(json.dumps(dict(r, kernel="att1_qgemm_kernel q4 gate/up 28672x4096")), flush=True)
+            return
         if args.kernel_only == "attn":
             algo, kms = time_attention(b2, torch, reps=args.steps)
             name = "attention 8B shape, context 4096 (32 query / 8 KV heads, hd 128)"
