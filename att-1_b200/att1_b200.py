@@ -179,6 +179,8 @@ _SIGS = {
     "att1_b200_infer_tp_handle": (C.c_int, [_P, _P]),
     "att1_b200_infer_tp_connect": (C.c_int, [_P, _P]),
     "att1_b200_infer_tp_connect_local": (C.c_int, [C.POINTER(_P), _U32]),
+    "att1_b200_nccl_unique_id": (C.c_int, [_P]),
+    "att1_b200_infer_tp_connect_nccl": (C.c_int, [_P, _P]),
     "att1_b200_infer_tp_set_wait": (C.c_int, [_P, _U32]),
     "att1_b200_infer_tp_reset": (C.c_int, [_P]),
     "att1_b200_infer_tp_disconnect": (C.c_int, [_P]),
@@ -289,6 +291,7 @@ def lib() -> C.CDLL:
 
 
 TP_HANDLE_BYTES = 64
+NCCL_ID_BYTES = 128
 
 
 def check(fn: str, rc: int) -> None:
@@ -339,6 +342,17 @@ class Infer:
         """handles: every rank's tp_handle() in rank order."""
         blob = b"".join(handles)
         check("att1_b200_infer_tp_connect", lib().att1_b200_infer_tp_connect(self.h, C.c_char_p(blob)))
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(NCCL_ID_BYTES)
+        check("att1_b200_nccl_unique_id", lib().att1_b200_nccl_unique_id(buf))
+        return buf.raw
+
+    def tp_connect_nccl(self, nccl_id: bytes) -> None:
+        """The NCCL comparison arm: every rank calls this with rank 0's id, together."""
+        check("att1_b200_infer_tp_connect_nccl",
+              lib().att1_b200_infer_tp_connect_nccl(self.h, C.c_char_p(bytes(nccl_id))))
 
     def tp_set_wait(self, polls: int) -> None:
         check("att1_b200_infer_tp_set_wait", lib().att1_b200_infer_tp_set_wait(self.h, polls))

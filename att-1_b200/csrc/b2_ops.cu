@@ -88,6 +88,24 @@ __global__ void step_end_tp_kernel(const b2_tp tp, uint32_t batch, uint32_t *tok
     if (threadIdx.x == 0) *const_cast<uint32_t *>(tp.epoch) += 1;
 }
 
+// Greedy token from argmax keys gathered over `world` ranks ([world][batch]).
+__global__ void step_end_keys_kernel(const unsigned long long *keys, uint32_t world, uint32_t batch, uint32_t *tokens,
+                                     int32_t *positions, int32_t *err)
+{
+    pdl_wait();
+    pdl_launch_dependents();
+    const uint32_t item = threadIdx.x;
+    if (item >= batch) return;
+    unsigned long long key = 0ull;
+    for (uint32_t s = 0; s < world; ++s) {
+        const unsigned long long k = __ldcg(keys + (size_t)s * batch + item);
+        key = k > key ? k : key;
+    }
+    if (key == 0ull) raise_error(err, B2_ERR_NAN_LOGITS);
+    else tokens[item] = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
+    positions[item] += 1;
+}
+
 // ---- tensor-parallel exchange for the GEMM route (the GEMVs fuse it) ----------------
 
 // This rank's partial x[n] into its slot of `point` on every rank; the CTAs
@@ -468,6 +486,15 @@ extern "C" int b2_matmul_q8_ordered(float *dst, const float *lhs, uint32_t m, ui
 }
 
 static int launched(cudaError_t e) { return e == cudaSuccess ? 0 : -8; }
+
+extern "C" int b2_step_end_keys(const unsigned long long *keys, uint32_t world, uint32_t batch, uint32_t *tokens,
+                                int32_t *positions, int32_t *err, int pdl, void *stream)
+{
+    if (!keys || !tokens || !positions || world == 0 || world > B2_TP_MAX || batch == 0 || batch > 1024) return -1;
+    void *args[] = {(void *)&keys, (void *)&world, (void *)&batch, (void *)&tokens, (void *)&positions, (void *)&err};
+    return launched(launch_pdl((const void *)step_end_keys_kernel, dim3(1), dim3(batch <= 32 ? 32 : (batch + 31) / 32 * 32),
+                               pdl, (cudaStream_t)stream, args));
+}
 
 extern "C" int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_model, const uint32_t *tokens,
                              uint32_t batch, float *x, unsigned long long *argmax, int32_t *err, int pdl,

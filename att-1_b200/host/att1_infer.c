@@ -52,6 +52,10 @@ struct att1_infer {
     int32_t *tp_done;
     int tp_ready;
     uint32_t tp_wait_polls;            /* bound of every exchange wait (0: the kernels' default) */
+    /* the exchange through an NCCL communicator instead of peer memory
+     * (att1_b200_infer_tp_connect_nccl): ncclComm_t, gathered argmax keys [world][batch] */
+    void *nccl_comm;
+    unsigned long long *nccl_keys;
     b2_tp tp_base;                     /* exchange description shared by the step's kernels */
     int device;
     cudaStream_t stream;
@@ -240,6 +244,8 @@ static void release(att1_infer_t *inf)
     if (inf->backend) att1_backend_destroy(inf->backend);
     for (l = 0; l < B2_TP_MAX; l++)
         if (inf->tp_opened[l]) cudaIpcCloseMemHandle(inf->tp_peer[l]);
+    if (inf->nccl_comm) b2_nccl_comm_destroy(inf->nccl_comm);
+    dfree(inf->nccl_keys);
     dfree(inf->tp_region);
     dfree(inf->tp_epoch);
     dfree(inf->tp_done);
@@ -393,6 +399,27 @@ static void tp_wire(att1_infer_t *inf)
     inf->tp_base.out_point = t.points;
 }
 
+/* The comparison arm (att1_b200_infer_tp_connect_nccl): the one-GPU wiring
+ * with partial sums. WO and down add the residual on rank 0 only, so the sum
+ * of every rank's output (ncclAllReduce after each) is the residual plus all
+ * partials; the lm_head keeps this rank's vocabulary rows and global ids for
+ * its argmax keys, gathered after it. */
+static void nccl_wire(att1_infer_t *inf)
+{
+    const att1_b200_config *c = &inf->cfg;
+    uint32_t l;
+    for (l = 0; l < c->n_layers; l++) {
+        dev_layer *L = &inf->layers[l];
+        if (inf->tp_rank != 0) {
+            L->a_wo.epilogue = B2_EPI_STORE;
+            L->a_wo.resid = NULL;
+            L->a_down.epilogue = B2_EPI_STORE;
+            L->a_down.resid = NULL;
+        }
+    }
+    inf->a_out.tp.row_offset = inf->v_off;
+}
+
 static att1_status_t build_args(att1_infer_t *inf)
 {
     const att1_b200_config *c = &inf->cfg;
@@ -472,7 +499,10 @@ static att1_status_t build_args(att1_infer_t *inf)
         a->out_stride = inf->vl;
         a->argmax = inf->argmax_d;
     }
-    if (inf->tp_world > 1) tp_wire(inf);
+    if (inf->tp_world > 1) {
+        if (inf->nccl_comm != NULL) nccl_wire(inf);
+        else tp_wire(inf);
+    }
     /* One partial-sum region and one counter array serve every kernel: they
      * run one after another and each leaves its counters at zero. */
     inf->use_dense = inf->batch > 16;
@@ -827,6 +857,32 @@ att1_status_t att1_b200_infer_tp_disconnect(att1_infer_t *infer)
         if (s != infer->tp_rank) infer->tp_peer[s] = NULL;
     }
     infer->tp_ready = 0;
+    return ATT1_OK;
+}
+
+att1_status_t att1_b200_nccl_unique_id(void *id)
+{
+    if (id == NULL) return ATT1_ERR_INVALID_ARG;
+    if (!b2_nccl_available()) return ATT1_ERR_UNSUPPORTED;
+    return b2_nccl_unique_id(id) == 0 ? ATT1_OK : ATT1_ERR_STATE;
+}
+
+att1_status_t att1_b200_infer_tp_connect_nccl(att1_infer_t *infer, const void *id)
+{
+    att1_status_t st;
+    if (infer == NULL || id == NULL || infer->tp_world < 2 || infer->tp_ready) return ATT1_ERR_INVALID_ARG;
+    if (!b2_nccl_available() || infer->batch > 16 || infer->use_dense) return ATT1_ERR_UNSUPPORTED;
+    if (cudaSetDevice(infer->device) != cudaSuccess) return ATT1_ERR_STATE;
+    if ((st = dalloc(infer, (void **)&infer->nccl_keys,
+                     (size_t)infer->tp_world * infer->batch * sizeof(unsigned long long))) != ATT1_OK)
+        return st;
+    if (b2_nccl_comm_init(&infer->nccl_comm, (int)infer->tp_world, id, (int)infer->tp_rank) != 0) {
+        infer->nccl_comm = NULL;
+        return ATT1_ERR_STATE;
+    }
+    infer->tp_peer[infer->tp_rank] = infer->tp_region;
+    if ((st = tp_finish(infer)) != ATT1_OK) return st;
+    if (infer->use_dense) return ATT1_ERR_UNSUPPORTED; /* the plan put this batch on the tensor-core route */
     return ATT1_OK;
 }
 
@@ -1535,6 +1591,29 @@ static int enqueue_kernels(att1_infer_t *inf)
             rc = b2_step_end_tp(&inf->tp_base, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
         else
             rc = b2_step_end(inf->argmax_d, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d, inf->use_pdl, st);
+        return rc != 0 ? rc : sample_step(inf, st);
+    }
+    if (inf->nccl_comm != NULL) {
+        const size_t n = (size_t)inf->batch * c->d_model;
+        float *gathered = (float *)(inf->tp_region + b2_tp_region_bytes(2 * c->n_layers, (uint32_t)n, 0));
+        for (l = 0; l < c->n_layers && rc == 0; l++) {
+            dev_layer *L = &inf->layers[l];
+            rc |= b2_gemv(&L->a_qkv, st);
+            rc |= b2_attn(&L->a_attn, st);
+            rc |= b2_gemv(&L->a_wo, st);
+            rc |= b2_nccl_allreduce_sum_f32(inf->h1, n, inf->nccl_comm, st);
+            rc |= b2_gemv(&L->a_gu, st);
+            rc |= b2_gemv(&L->a_down, st);
+            rc |= b2_nccl_allreduce_sum_f32(inf->x, n, inf->nccl_comm, st);
+        }
+        if (rc == 0) rc = b2_gemv(&inf->a_out, st);
+        if (rc == 0) rc = b2_nccl_allgather(inf->logits, gathered, (size_t)inf->batch * inf->vl * sizeof(float),
+                                            inf->nccl_comm, st);
+        if (rc == 0) rc = b2_nccl_allgather(inf->argmax_d, inf->nccl_keys, (size_t)inf->batch * sizeof(unsigned long long),
+                                            inf->nccl_comm, st);
+        if (rc == 0)
+            rc = b2_step_end_keys(inf->nccl_keys, inf->tp_world, inf->batch, inf->tokens_d, inf->pos_d, inf->err_d,
+                                  inf->use_pdl, st);
         return rc != 0 ? rc : sample_step(inf, st);
     }
     for (l = 0; l < c->n_layers && rc == 0; l++) {

@@ -32,6 +32,15 @@ att1_status_t b2_kv_mmu_reserve(att1_kv_mmu *mmu, size_t slot, size_t first, siz
 void b2_kv_mmu_advance(att1_kv_mmu *mmu, size_t slot, size_t count);
 const int32_t *b2_kv_mmu_row(const att1_kv_mmu *mmu, size_t slot, size_t layer, size_t *pages_per_seq);
 
+/* NCCL collectives of the tensor-parallel comparison arm (att1_nccl.c; NCCL is
+ * loaded at run time) */
+int b2_nccl_available(void);
+int b2_nccl_unique_id(void *id);
+int b2_nccl_comm_init(void **comm, int world, const void *id, int rank);
+void b2_nccl_comm_destroy(void *comm);
+int b2_nccl_allreduce_sum_f32(float *buf, size_t count, void *comm, cudaStream_t st);
+int b2_nccl_allgather(const void *send, void *recv, size_t bytes_per_rank, void *comm, cudaStream_t st);
+
 /* status of a CUDA runtime call */
 static inline att1_status_t b2_cuda_status(cudaError_t e)
 {

@@ -414,9 +414,15 @@ def run_b200(args, rank, world, local_rank):
         # tensor parallel: this rank's shard; ranks exchange their exchange-region
         # handles (CUDA IPC) over the process group, then connect
         inf = b2.Infer.synth_tp(cfg, args.seed, rank, world, batch=args.batch, device=local_rank)
-        handles = [None] * world
-        dist.all_gather_object(handles, inf.tp_handle())
-        inf.tp_connect(handles)
+        if args.tp_exchange == "nccl":
+            # comparison arm: the exchange as NCCL collectives on the step's stream
+            ids = [b2.Infer.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(ids, src=0)
+            inf.tp_connect_nccl(ids[0])
+        else:
+            handles = [None] * world
+            dist.all_gather_object(handles, inf.tp_handle())
+            inf.tp_connect(handles)
     else:
         b2.lib().att1_b200_set_device(local_rank)
         inf = b2.Infer.synth(cfg, args.seed, batch=args.batch)
@@ -516,6 +522,7 @@ def run_b200(args, rank, world, local_rank):
             "config": {"workload": "llama3-8b-shape q4 decode", "global_batch": args.batch * (world if args.replicas else 1),
                        "seq_len": ctx, "context_at_timed_steps": pos_timed,
                        "parallelism": (f"replicas{world}" if args.replicas else f"tp{world}"),
+                       "tp_exchange": None if world == 1 or args.replicas else args.tp_exchange,
                        "step_launch": "one persistent kernel" if persistent else "kernel sequence (CUDA graph)",
                        "l2": "inputs larger than L2 (5.8 GB streamed per step)",
                        "step_bytes": bytes_step,
@@ -574,6 +581,9 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the prefill and batch-32 side measurements")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch kernels one by one without graph or PDL (for ncu launch lists)")
+    ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
+                    help="tensor parallel: partial sums exchanged by the step's kernels over peer memory (fused, "
+                         "the default) or by NCCL all-reduce / all-gather (the comparison arm)")
     ap.add_argument("--replicas", action="store_true",
                     help="with several GPUs: independent replicas instead of one tensor-parallel model")
     ap.add_argument("--persistent", action="store_true",

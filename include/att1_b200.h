@@ -93,6 +93,18 @@ att1_status_t att1_b200_infer_tp_connect(att1_infer_t *infer, const void *handle
 att1_status_t att1_b200_infer_tp_disconnect(att1_infer_t *infer);
 /* All ranks of one process (rank r on its own device), connected by peer access. */
 att1_status_t att1_b200_infer_tp_connect_local(att1_infer_t *const *infers, uint32_t world);
+/* The same tensor-parallel step with the exchange done by NCCL collectives on
+ * the step's stream instead of the kernels' peer-memory stores, for
+ * comparison: WO and down write partial sums (rank 0's carries the residual)
+ * that ncclAllReduce adds, and the lm_head's logits and argmax keys are
+ * gathered with ncclAllGather; logits and tokens are the same on every rank.
+ * NCCL (libnccl.so.2) is loaded at run time; ATT1_ERR_UNSUPPORTED without it
+ * and for batches that take the tensor-core route. One rank per process: rank
+ * 0 makes the id (ATT1_B200_NCCL_ID_BYTES bytes), every rank connects with it
+ * (a collective: all ranks call it together). Replaces tp_connect. */
+#define ATT1_B200_NCCL_ID_BYTES 128
+att1_status_t att1_b200_nccl_unique_id(void *id);
+att1_status_t att1_b200_infer_tp_connect_nccl(att1_infer_t *infer, const void *id);
 /* Bound of every wait for another rank inside the step's kernels, in polls of
  * the flag (about 0.1 us each; 0 = 2^24). A wait that runs out ends the step
  * with ATT1_ERR_TIMEOUT and the context stays usable. */

@@ -285,6 +285,11 @@ int b2_step_begin(const float *embed, uint32_t vocab, uint32_t d_model, const ui
 /* tokens[b] = argmax index; positions[b] += 1. */
 int b2_step_end(const unsigned long long *argmax, uint32_t batch, uint32_t *tokens,
                 int32_t *positions, int32_t *err, int pdl, void *stream);
+/* Step end over argmax keys gathered from `world` ranks ([world][batch], e.g.
+ * by an all-gather): the largest key per item is the greedy token (keys carry
+ * global vocabulary ids); positions advance. */
+int b2_step_end_keys(const unsigned long long *keys, uint32_t world, uint32_t batch, uint32_t *tokens,
+                     int32_t *positions, int32_t *err, int pdl, void *stream);
 /* Tensor parallel step end: waits for every rank's logits flag, takes the
  * largest argmax key over the ranks (the global greedy token), advances the
  * positions and the epoch (tp->epoch is written through a cast). */

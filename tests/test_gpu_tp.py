@@ -140,6 +140,60 @@ def test_tp_sampler_same_tokens_on_every_rank(b2, world):
         r.close()
 
 
+def _nccl_rank(rank, world, port, out_dir):
+    """One rank of the NCCL comparison arm: rank 0's NCCL id shared over gloo,
+    every rank connects with it, then the same teacher-forced stream."""
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch
+    import torch.distributed as dist
+    import att1_b200 as b2
+    import oracle as O2
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.cuda.set_device(rank)
+    ocfg = O2.Config.make(**OCFG)
+    inf = b2.Infer.synth_tp(make_cfg(b2, ocfg), 77, rank, world)
+    ids = [b2.Infer.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(ids, src=0)
+    inf.tp_connect_nccl(ids[0])
+    orc = O2.Oracle()
+    toks = orc.synth_tokens(5, 12, ocfg.vocab)
+    logits, out = [], []
+    for t in toks:
+        out.append(int(inf.decode(int(t))))
+        logits.append(inf.logits()[0].copy())
+    np.save(os.path.join(out_dir, f"nccl_rank{rank}.npy"), {"logits": np.stack(logits), "tokens": out},
+            allow_pickle=True)
+    dist.barrier()
+    inf.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_tp_nccl_arm_matches_oracle(orc, tmp_path, world):
+    """The comparison arm: the same step with the two per-layer all-reduces
+    and the logits all-gather as NCCL collectives (att1_b200_infer_tp_connect_nccl)
+    gives the oracle's logits and the same tokens on every rank."""
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_nccl_rank, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    ocfg = O.Config.make(**OCFG)
+    om = orc.model(ocfg, 77, threads=8)
+    toks = orc.synth_tokens(5, 12, ocfg.vocab)
+    res = [np.load(tmp_path / f"nccl_rank{r}.npy", allow_pickle=True).item() for r in range(world)]
+    assert all(r["tokens"] == res[0]["tokens"] for r in res)
+    for s, t in enumerate(toks):
+        clog, _ = om.decode(int(t))
+        for r in range(world):
+            assert rel_err(res[r]["logits"][s], clog) <= LOGITS_RTOL
+
+
 def _ipc_rank(rank, world, port, out_dir):
     import sys
     sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))
