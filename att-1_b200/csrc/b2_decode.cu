@@ -479,6 +479,9 @@ extern "C" int b2_decode_plan_create(const b2_decode_args *a, b2_decode_plan **o
     case 4: e = decode_prepare<4>(p); break;
     default: e = decode_prepare<8>(p); break;
     }
+    // the zero fills and the op table went through the legacy stream; steps run
+    // on the caller's (possibly non-blocking) stream, which does not wait for it
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
     if (e != cudaSuccess) {
         plan_free(p);
         return -8;

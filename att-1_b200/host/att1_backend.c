@@ -86,7 +86,10 @@ static int ensure_counters(cuda_backend *c, uint32_t n)
     c->counters = NULL;
     c->counters_cap = 0;
     if (cudaMalloc((void **)&c->counters, (size_t)n * sizeof(int32_t)) != cudaSuccess) return -1;
-    if (cudaMemset(c->counters, 0, (size_t)n * sizeof(int32_t)) != cudaSuccess) return -1;
+    /* zeroed on the backend's stream, ahead of the kernels that use them (a
+     * plain cudaMemset runs on the legacy stream, which a non-blocking stream
+     * does not wait for) */
+    if (cudaMemsetAsync(c->counters, 0, (size_t)n * sizeof(int32_t), c->stream) != cudaSuccess) return -1;
     c->counters_cap = n;
     return 0;
 }
@@ -97,8 +100,9 @@ static int finish(cuda_backend *c)
     if (cudaMemcpyAsync(&err, c->err, sizeof(err), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) return -1;
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return -1;
     if (err != 0) {
-        cudaMemset(c->err, 0, sizeof(int32_t));
-        if (c->counters) cudaMemset(c->counters, 0, (size_t)c->counters_cap * sizeof(int32_t));
+        cudaMemsetAsync(c->err, 0, sizeof(int32_t), c->stream);
+        if (c->counters) cudaMemsetAsync(c->counters, 0, (size_t)c->counters_cap * sizeof(int32_t), c->stream);
+        cudaStreamSynchronize(c->stream);
         return -1;
     }
     return 0;
@@ -149,7 +153,7 @@ static cached_mat *cache_add(cuda_backend *c)
     return &c->cache[c->n_cache++];
 }
 
-static int mat_init(b2_dev_mat *m, uint32_t fmt, uint32_t rows, uint32_t cols)
+static int mat_init(b2_dev_mat *m, uint32_t fmt, uint32_t rows, uint32_t cols, cudaStream_t st)
 {
     const size_t bytes = fmt == 4 ? b2_q4_bytes(rows, cols) : b2_q8_bytes(rows, cols);
     memset(m, 0, sizeof(*m));
@@ -158,9 +162,9 @@ static int mat_init(b2_dev_mat *m, uint32_t fmt, uint32_t rows, uint32_t cols)
     m->w.cols = cols;
     m->w.tiles = (rows + 15) / 16;
     m->w.kunits = fmt == 4 ? (cols + 63) / 64 : (cols + 31) / 32;
-    if (cudaMalloc(&m->data, bytes) != cudaSuccess || cudaMemset(m->data, 0, bytes) != cudaSuccess) return -1;
+    if (cudaMalloc(&m->data, bytes) != cudaSuccess || cudaMemsetAsync(m->data, 0, bytes, st) != cudaSuccess) return -1;
     if (fmt == 8 && (cudaMalloc((void **)&m->row_scale, (size_t)m->w.tiles * 16 * 4) != cudaSuccess ||
-                     cudaMemset(m->row_scale, 0, (size_t)m->w.tiles * 16 * 4) != cudaSuccess))
+                     cudaMemsetAsync(m->row_scale, 0, (size_t)m->w.tiles * 16 * 4, st) != cudaSuccess))
         return -1;
     m->w.data = m->data;
     m->w.row_scale = m->row_scale;
@@ -192,8 +196,10 @@ static const cached_mat *raw_weight(cuda_backend *c, const void *key, const void
     e = cache_add(c);
     if (e == NULL) return NULL;
     if (cudaMalloc(&e->raw, off + scale_bytes) != cudaSuccess ||
-        cudaMemcpy(e->raw, data, data_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy((uint8_t *)e->raw + off, scales, scale_bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaMemcpyAsync(e->raw, data, data_bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync((uint8_t *)e->raw + off, scales, scale_bytes, cudaMemcpyHostToDevice, c->stream) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess) {
         if (e->raw) cudaFree(e->raw);
         c->n_cache--;
         return NULL;
@@ -243,10 +249,11 @@ static const b2_dev_mat *q4_weight(cuda_backend *c, const att1_q4_matrix *w)
     if (w->rows > 0xFFFFFFFFu || w->cols > 0xFFFFFFFFu) return NULL;
     e = cache_add(c);
     if (e == NULL) return NULL;
-    if (mat_init(&e->m, 4, (uint32_t)w->rows, (uint32_t)w->cols) != 0 || cudaMalloc(&tmp, pb + sb) != cudaSuccess)
+    if (mat_init(&e->m, 4, (uint32_t)w->rows, (uint32_t)w->cols, c->stream) != 0 ||
+        cudaMalloc(&tmp, pb + sb) != cudaSuccess)
         goto fail;
-    if (cudaMemcpy(tmp, w->packed, pb, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy((uint8_t *)tmp + pb, w->scales, sb, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (cudaMemcpyAsync(tmp, w->packed, pb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync((uint8_t *)tmp + pb, w->scales, sb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
         goto fail;
     rc = b2_q4_pack(e->m.data, 0, (uint32_t)w->rows, (uint32_t)w->cols, tmp, (const float *)((uint8_t *)tmp + pb), NULL,
                     NULL, w->group_size, B2_ROWS_PLAIN, c->stream);
@@ -274,10 +281,11 @@ static const b2_dev_mat *q8_weight(cuda_backend *c, const att1_q8_matrix *w)
     if (w->rows > 0xFFFFFFFFu || w->cols > 0xFFFFFFFFu) return NULL;
     e = cache_add(c);
     if (e == NULL) return NULL;
-    if (mat_init(&e->m, 8, (uint32_t)w->rows, (uint32_t)w->cols) != 0 || cudaMalloc(&tmp, vb + sb) != cudaSuccess)
+    if (mat_init(&e->m, 8, (uint32_t)w->rows, (uint32_t)w->cols, c->stream) != 0 ||
+        cudaMalloc(&tmp, vb + sb) != cudaSuccess)
         goto fail;
-    if (cudaMemcpy(tmp, w->values, vb, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy((uint8_t *)tmp + vb, w->scales, sb, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (cudaMemcpyAsync(tmp, w->values, vb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync((uint8_t *)tmp + vb, w->scales, sb, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
         goto fail;
     rc = b2_q8_pack(e->m.data, e->m.row_scale, 0, (uint32_t)w->rows, (uint32_t)w->cols, tmp,
                     (const float *)((uint8_t *)tmp + vb), NULL, NULL, B2_ROWS_PLAIN, c->stream);
@@ -480,7 +488,8 @@ static att1_status_t create(const att1_backend_ops *ops, att1_backend **out)
     }
     if (cudaGetDevice(&c->device) != cudaSuccess || cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc((void **)&c->err, sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(c->err, 0, sizeof(int32_t)) != cudaSuccess ||
+        cudaMemsetAsync(c->err, 0, sizeof(int32_t), c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess ||
         cudaMalloc((void **)&c->key, sizeof(unsigned long long)) != cudaSuccess) {
         free(b);
         free(c);
@@ -500,13 +509,18 @@ att1_status_t att1_backend_default_create(att1_backend **out) { return create(&c
 att1_status_t att1_backend_cuda_copy_host_to_device(att1_backend *b, void *dst, const void *src, size_t bytes)
 {
     if (!b2_backend_is_cuda(b) || dst == NULL || src == NULL) return ATT1_ERR_INVALID_ARG;
-    return b2_cuda_status(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    /* ordered with the backend's kernels, and on the device when this returns */
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, cb(b)->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cb(b)->stream);
+    return b2_cuda_status(e);
 }
 
 att1_status_t att1_backend_cuda_copy_device_to_host(att1_backend *b, void *dst, const void *src, size_t bytes)
 {
     if (!b2_backend_is_cuda(b) || dst == NULL || src == NULL) return ATT1_ERR_INVALID_ARG;
-    return b2_cuda_status(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, cb(b)->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cb(b)->stream);
+    return b2_cuda_status(e);
 }
 
 void att1_backend_destroy(att1_backend *b)

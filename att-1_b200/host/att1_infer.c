@@ -610,8 +610,14 @@ static att1_status_t alloc_common(att1_infer_t *inf)
         for (i = 0; i < inf->pages_per_seq; i++) pt[(size_t)b * inf->pages_per_seq + i] = (int32_t)(b * inf->pages_per_seq + i);
     /* src/rope.c:21-22: freq of pair i/2 = 1 / powf(theta, i / head_dim), host libm */
     for (i = 0; i < inf->head_dim / 2; i++) freq[i] = 1.0f / powf(c->theta, (float)(2 * i) / (float)inf->head_dim);
-    e = cudaMemcpy(inf->page_table, pt, pages * sizeof(int32_t), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(inf->rope_freq, freq, (inf->head_dim / 2) * sizeof(float), cudaMemcpyHostToDevice);
+    /* on the context's stream, after dalloc's zero fill of the same buffers: a
+     * plain cudaMemcpy runs on the legacy stream, which does not wait for a
+     * non-blocking stream, so the fill could land after the table */
+    e = cudaMemcpyAsync(inf->page_table, pt, pages * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(inf->rope_freq, freq, (inf->head_dim / 2) * sizeof(float), cudaMemcpyHostToDevice,
+                            inf->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(inf->stream);
     free(pt);
     free(freq);
     if (e != cudaSuccess) return b2_cuda_status(e);
@@ -1843,9 +1849,13 @@ static att1_status_t prefill_alloc(att1_infer_t *inf, uint32_t cap)
         free_prefill(inf);
         return ATT1_ERR_OOM;
     }
-    e = cudaMemcpy(pt, inf->page_table, pps * sizeof(int32_t), cudaMemcpyDeviceToHost);
+    /* stream-ordered after pf_pt's zero fill (dalloc) */
+    e = cudaMemcpyAsync(pt, inf->page_table, pps * sizeof(int32_t), cudaMemcpyDeviceToHost, inf->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(inf->stream);
     for (i = 1; i < cap; i++) memcpy(pt + (size_t)i * pps, pt, pps * sizeof(int32_t));
-    if (e == cudaSuccess) e = cudaMemcpy(inf->pf_pt, pt, (size_t)cap * pps * sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(inf->pf_pt, pt, (size_t)cap * pps * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(inf->stream);
     free(pt);
     if (e != cudaSuccess) {
         free_prefill(inf);
@@ -1881,7 +1891,9 @@ static att1_status_t prefill_mmu_table(att1_infer_t *inf, uint32_t rows, size_t 
         const int32_t *row = b2_kv_mmu_row(inf->mmu, inf->mmu_slot0, l, &pps);
         for (i = 0; i < rows; i++) memcpy(pt + ((size_t)l * rows + i) * pps, row, pps * sizeof(int32_t));
     }
-    e = cudaMemcpy(inf->pf_mpt, pt, need * sizeof(int32_t), cudaMemcpyHostToDevice);
+    /* stream-ordered after pf_mpt's zero fill and before the prefill kernels */
+    e = cudaMemcpyAsync(inf->pf_mpt, pt, need * sizeof(int32_t), cudaMemcpyHostToDevice, inf->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(inf->stream);
     free(pt);
     *layer_stride = (size_t)rows * pps;
     return b2_cuda_status(e);
@@ -2044,13 +2056,14 @@ static const float *logits_host(const att1_infer_t *cinfer, size_t *out_count, s
                                                                                           infer->batch * infer->cfg.d_model,
                                                                                           0)) +
                                    (size_t)s * infer->batch * vl;
-                e = cudaMemcpy2D(infer->logits_h + (size_t)s * vl, V * sizeof(float), src, vl * sizeof(float),
-                                 vl * sizeof(float), infer->batch, cudaMemcpyDeviceToHost);
+                e = cudaMemcpy2DAsync(infer->logits_h + (size_t)s * vl, V * sizeof(float), src, vl * sizeof(float),
+                                      vl * sizeof(float), infer->batch, cudaMemcpyDeviceToHost, infer->stream);
             }
-        } else {
-            e = cudaMemcpy(infer->logits_h, infer->logits, (size_t)infer->batch * infer->cfg.vocab * sizeof(float),
-                           cudaMemcpyDeviceToHost);
+        } else if (e == cudaSuccess) {
+            e = cudaMemcpyAsync(infer->logits_h, infer->logits, (size_t)infer->batch * infer->cfg.vocab * sizeof(float),
+                                cudaMemcpyDeviceToHost, infer->stream);
         }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(infer->stream);
         if (e != cudaSuccess) {
             if (out_count) *out_count = 0;
             return NULL;

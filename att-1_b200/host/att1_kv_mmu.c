@@ -112,9 +112,12 @@ static int32_t map_page(att1_kv_mmu *mmu, size_t slot, size_t layer, size_t lp)
     }
     if (p == c->max_pages) return -1;
     pp = (int32_t)p;
+    /* the entry must be on the device before this returns: decode kernels on a
+     * non-blocking stream do not wait for the legacy stream's copy */
     if (cudaSetDevice(mmu->device) != cudaSuccess ||
         cudaMemcpy(mmu->page_table + dev_index(mmu, slot, layer, lp), &pp, sizeof(int32_t), cudaMemcpyHostToDevice) !=
-            cudaSuccess)
+            cudaSuccess ||
+        cudaStreamSynchronize(cudaStreamLegacy) != cudaSuccess)
         return -2;
     mmu->owner[p].active = 1;
     mmu->owner[p].slot = slot;
@@ -309,6 +312,9 @@ att1_status_t att1_kv_mmu_append(att1_kv_mmu *mmu, uint64_t session_id, size_t l
     if (e == cudaSuccess)
         e = cudaMemcpy2D(vdst, c->page_tokens * hd * sizeof(float), value, hd * sizeof(float), hd * sizeof(float),
                          c->num_heads, cudaMemcpyHostToDevice);
+    /* a pageable host-to-device copy may still be in flight when cudaMemcpy
+     * returns; kernels on other streams read the row next */
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
     if (e != cudaSuccess) {
         count_error(mmu);
         return b2_cuda_status(e);

@@ -217,3 +217,24 @@ def test_attention_8b_heads_context_4096(b2):
             e = np.abs(got[b] - want).max() / np.abs(want).max()
             assert e <= 1e-5, f"item {b}: rel err {e:.3e}"
         assert (cnt.cpu().numpy() == 0).all()
+
+
+def test_kv_rows_land_in_their_pages(b2):
+    """The K/V row a step appends lands in its own page at the full model size.
+    Creating the 8B shape queues gigabytes of zero fills on the context's
+    stream; the page table and RoPE frequencies are written after them on the
+    same stream, so no fill can land on the table afterwards (with the table
+    zeroed every position would map to page 0: the row at position 130 would
+    land in page 0 at row 2 and position 130's own slot would stay zero)."""
+    cfg = b2.Config.make(128256, 32, 32, 8, 4096, 14336, 4096, dtype=4, eps=1e-5, theta=500000.0)
+    inf = b2.Infer.synth(cfg, 77)
+    try:
+        inf.seek(130)
+        inf.decode(5)
+        row = 8 * 128
+        for layer in (0, 31):
+            k, v = inf.export_kv(0, layer, 131, row)
+            assert np.abs(k[130 * row:]).max() > 0 and np.abs(v[130 * row:]).max() > 0, layer
+            assert not k[:130 * row].any() and not v[:130 * row].any(), layer
+    finally:
+        inf.close()
