@@ -118,10 +118,10 @@ __global__ void __launch_bounds__(NW * 32 + 32, 1) attn_ring_kernel(const AttnPa
                 mbar_arrive_expect_tx(&full[buf], 2 * nt * rowb);
                 for (uint32_t r = 0; r < nt;) {
                     const uint32_t ps = p0 + r0 + r, run = min(nt - r, p.kv.page_tokens - ps % p.kv.page_tokens);
-                    bulk_g2s(Kb + ((size_t)buf * kSub + r) * hd, kv_row(p.kv, p.kv.k_pool, item, ps, kvh), run * rowb,
-                             &full[buf]);
-                    bulk_g2s(Vb + ((size_t)buf * kSub + r) * hd, kv_row(p.kv, p.kv.v_pool, item, ps, kvh), run * rowb,
-                             &full[buf]);
+                    bulk_g2s_stream(Kb + ((size_t)buf * kSub + r) * hd, kv_row(p.kv, p.kv.k_pool, item, ps, kvh),
+                                    run * rowb, &full[buf], l2_evict_first_policy());
+                    bulk_g2s_stream(Vb + ((size_t)buf * kSub + r) * hd, kv_row(p.kv, p.kv.v_pool, item, ps, kvh),
+                                    run * rowb, &full[buf], l2_evict_first_policy());
                     r += run;
                 }
             }

@@ -506,7 +506,8 @@ __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i
         }
         if (lane == 0) {
             mbar_arrive_expect_tx(&s.full[slot], n * UB);
-            bulk_g2s(s.ring + (size_t)slot * kStageUnits * UB, p.data + (size_t)sw.u * UB, n * UB, &s.full[slot]);
+            bulk_g2s_stream(s.ring + (size_t)slot * kStageUnits * UB, p.data + (size_t)sw.u * UB, n * UB, &s.full[slot],
+                            l2_evict_first_policy());
         }
         __syncwarp();
         sw.advance(n);
