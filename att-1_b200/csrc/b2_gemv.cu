@@ -76,10 +76,13 @@ __global__ void __launch_bounds__(kThreads, 1) att1_qgemv_kernel(const GemvParam
         }
         return;
     }
+    uint32_t t0, t1;
+    cta_range(p, t0, t1);
+    if (t0 != t1) gemv_zero_round(p, s);  // before the wait: nothing of the previous kernel's
     pdl_wait();
     pdl_launch_dependents();
     bool dead = false;
-    gemv_consume<FMT, NI>(p, s, i, dead);
+    gemv_consume<FMT, NI>(p, s, i, dead, true);
 }
 
 // ---- host side ------------------------------------------------------------------

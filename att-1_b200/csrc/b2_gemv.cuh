@@ -515,6 +515,16 @@ __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i
     return true;
 }
 
+// Clear the CTA's argmax key and the round's per-warp tile sums (consumer
+// threads). Reads nothing another kernel writes, so a launch can do it before
+// its programmatic-launch wait (`prezeroed` for gemv_consume).
+__device__ __forceinline__ void gemv_zero_round(const GemvParams &p, const GemvSmem &s)
+{
+    if (threadIdx.x < kMaxItems) s.cta_key[threadIdx.x] = 0ull;
+    const uint32_t parts_n = p.round_tiles * kWarps * 16 * p.batch;
+    for (uint32_t k = threadIdx.x; k < parts_n; k += kConsumers) s.parts[k] = 0.0f;
+}
+
 // Consumer warps (all kWarps of them): prologue, the CTA's stages of one GEMV
 // (ring position `i`, shared with the producer's count), per-tile sums and
 // epilogues. Warp w multiplies units w, w + kWarps, ... of every stage and
@@ -524,7 +534,7 @@ __device__ bool gemv_produce(const GemvParams &p, const GemvSmem &s, uint32_t &i
 // order (deterministic) and run the tile epilogues, one warp per tile. `dead`
 // (a wait timed out) keeps the stage protocol but skips the math and stores.
 template <int FMT, int NI>
-__device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &dead)
+__device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i, bool &dead, bool prezeroed = false)
 {
     constexpr uint32_t UB = Fmt<FMT>::kUnitBytes;
     constexpr uint32_t KW = Fmt<FMT>::kKW;
@@ -535,9 +545,8 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
     uint32_t t0, t1;
     cta_range(p, t0, t1);
     if (t0 == t1) return;  // no tiles for this CTA
-    if (threadIdx.x < kMaxItems) s.cta_key[threadIdx.x] = 0ull;
     const uint32_t parts_n = p.round_tiles * kWarps * SB;
-    for (uint32_t k = threadIdx.x; k < parts_n; k += kConsumers) s.parts[k] = 0.0f;
+    if (!prezeroed) gemv_zero_round(p, s);
     prepare_x<FMT>(p, s.xdig, s.item_scale, s.red);
     consumer_sync();
     if (s.xready != nullptr && threadIdx.x == 0) mbar_arrive(s.xready);
