@@ -22,19 +22,22 @@
 //               a token tile contiguous) into two slots of xk k steps each, one
 //               1-D bulk copy of ~32 KB per slot (an SM completes bulk copies at
 //               a bounded rate whatever their size);
-//   warp 1      one thread issues tcgen05.mma (M=128, N=BN, K=16) for every
-//               k step, then tcgen05.commit releases the W stage (and the X
-//               slot after its last k step). Each MMA has a fixed cost of
-//               roughly the read of its 4 KB weight operand, so for small BN
-//               (decode batches) this thread, not the dequant, sets the pace;
-//   warps 2..9  one per 16-row tile: read the tile's weight unit of each k
+//   warps 1, 2  one thread each issues tcgen05.mma (M=128, N=BN, K=16) for
+//               alternate k steps into its own accumulator (tensor-memory
+//               columns mw * acols), then tcgen05.commit releases the W stage
+//               (and each X slot once both have passed it). Issuing the MMAs of
+//               one k step costs a single thread about the read of their 4 KB
+//               weight operands, so for small BN (decode batches) one issuer
+//               set the pace; two take 126 -> 103 us for 32 tokens of the
+//               gate/up matrix (four: no further gain);
+//   warps 3..10 one per 16-row tile: read the tile's weight unit of each k
 //               step with 16-byte loads issued two k steps ahead (each lane's
 //               16 bytes are one fixed set of 32 weights), scale, split into
 //               bf16 hi/lo and store them in the operand layout; after the k
-//               loop they read the accumulator out of tensor memory (warp w
+//               loop they read the accumulators out of tensor memory (warp w
 //               reads TMEM lanes 32*(w%4)..: one output row per thread, the two
-//               warps of a lane quarter alternate 16-column chunks) and write Y,
-//               or the split's partial sums.
+//               warps of a lane quarter alternate 16-column chunks), add them
+//               in issuer order and write Y, or the split's partial sums.
 // Operands are K-major without swizzle: 8-row x 16-byte core matrices,
 // element (r, k) of a tile with R rows at byte
 //   (k / 8) * (R * 16) + (r / 8) * 128 + (r % 8) * 16 + (k % 8) * 2,
@@ -52,7 +55,8 @@ constexpr uint32_t kGemmBM = 128;          // output rows per CTA (8 tiles of 16
 constexpr uint32_t kGemmBK = 64;           // columns per k step
 constexpr uint32_t kGemmMaxBN = 256;       // tokens per CTA tile
 constexpr int kGemmDequantWarps = 8;      // one 16-row tile each
-constexpr int kGemmThreads = 64 + 32 * kGemmDequantWarps;  // + TMEM/X-copy warp + MMA warp
+constexpr int kGemmMmaWarps = 2;          // MMA issuers (up to), round-robin k steps, one accumulator each
+constexpr int kGemmThreads = 32 + 32 * kGemmMmaWarps + 32 * kGemmDequantWarps;  // + TMEM/X-copy warp
 constexpr uint32_t kGemmMaxStages = 6;      // W ring
 constexpr uint32_t kGemmXSlots = 2;         // X ring
 constexpr uint32_t kGemmXCopy = 32768;      // target bytes per X bulk copy
@@ -99,6 +103,7 @@ struct GemmParams {
     float *part;            // [splits][m][rows] when splits > 1
     uint32_t splits, ksplit;  // k steps per split
     uint32_t stages;        // W ring stages (one k step each)
+    uint32_t nmma;          // MMA warps in use (accumulators)
     uint32_t xk;            // k steps per X slot (one bulk copy)
     uint32_t off_x, off_w, tmem_cols;
     int32_t *err;
@@ -414,13 +419,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < kGemmXSlots; ++i) {
             mbar_init(&s.x_full[i], 1);
-            mbar_init(&s.x_empty[i], 1);
+            mbar_init(&s.x_empty[i], p.nmma);
         }
         for (uint32_t i = 0; i < kGemmMaxStages; ++i) {
             mbar_init(&s.w_full[i], 32 * kGemmDequantWarps);
             mbar_init(&s.w_empty[i], 1);
         }
-        mbar_init(s.acc_full, 1);
+        mbar_init(s.acc_full, p.nmma);
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(s.tmem_slot, p.tmem_cols);
@@ -445,59 +450,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
                          steps * xstage, &s.x_full[xs]);
             }
         }
-    } else if (warp == 1) {
-        if (lane == 0) {
+    } else if (warp <= (uint32_t)kGemmMmaWarps) {
+        // MMA warp mw issues k steps mw, mw + kGemmMmaWarps, ... into its own
+        // accumulator (columns mw * acols); every MMA warp releases every X slot
+        const uint32_t mw = warp - 1, nmma = p.nmma;
+        if (lane == 0 && mw < nmma) {
             const bool stk = gemm_stacked(p.bn);
+            const uint32_t acols = stk ? 2 * p.bn : p.bn;
+            const uint32_t acc = tmem + mw * acols;
             const uint32_t idesc = umma_idesc_bf16(kGemmBM, p.bn);
             const uint32_t idesc2 = umma_idesc_bf16(kGemmBM, 2 * p.bn);  // stacked: hi and lo rows
             const uint32_t xb = smem_u32(s.x), wb = smem_u32(s.w);
-            for (uint32_t i = 0; i < nk; ++i) {
-                const uint32_t st = i % p.stages, pass = i / p.stages;
-                const uint32_t j = i / p.xk, xs = j % kGemmXSlots, xi = i % p.xk;
-                if (xi == 0) mbar_wait_bounded(&s.x_full[xs], (j / kGemmXSlots) & 1, p.err);
-                mbar_wait_bounded(&s.w_full[st], pass & 1, p.err);
-                tc_fence_after();
-                const uint32_t xa = xb + (xs * p.xk + xi) * xstage, wa = wb + st * wstage;
-                if (stk) {
+            const uint32_t nslots = (nk + p.xk - 1) / p.xk;
+            bool first = true;
+            for (uint32_t j = 0; j < nslots; ++j) {
+                const uint32_t xs = j % kGemmXSlots;
+                // every MMA warp waits for every slot, even one without k steps
+                // of its own: its release of the slot then cannot run ahead into
+                // the slot's next fill
+                mbar_wait_bounded(&s.x_full[xs], (j / kGemmXSlots) & 1, p.err);
+                const uint32_t i_end = min(nk, (j + 1) * p.xk);
+                uint32_t i = j * p.xk;
+                i += (mw + nmma - i % nmma) % nmma;  // first k step of this warp
+                for (; i < i_end; i += nmma) {
+                    const uint32_t st = i % p.stages, pass = i / p.stages, xi = i % p.xk;
+                    mbar_wait_bounded(&s.w_full[st], pass & 1, p.err);
+                    tc_fence_after();
+                    const uint32_t xa = xb + (xs * p.xk + xi) * xstage, wa = wb + st * wstage;
+                    if (stk) {
 #pragma unroll
-                    for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
-                        const uint64_t a_hi = umma_desc(wa + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
-                        // rows 0..bn-1 of this descriptor are x_hi, bn..2bn-1 x_lo
-                        const uint64_t b = umma_desc(xa + kk * 2 * (2 * p.bn * 16), 2 * p.bn * 16, 128);
-                        umma_bf16(tmem, a_hi, b, idesc2, (i | kk) != 0);
-                        if constexpr (FMT == 4) {
-                            const uint64_t a_lo =
-                                umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
-                            umma_bf16(tmem, a_lo, b, idesc, 1);  // N = bn: the x_hi rows only
+                        for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
+                            const uint64_t a_hi = umma_desc(wa + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                            // rows 0..bn-1 of this descriptor are x_hi, bn..2bn-1 x_lo
+                            const uint64_t b = umma_desc(xa + kk * 2 * (2 * p.bn * 16), 2 * p.bn * 16, 128);
+                            umma_bf16(acc, a_hi, b, idesc2, !(first && kk == 0));
+                            if constexpr (FMT == 4) {
+                                const uint64_t a_lo =
+                                    umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                                umma_bf16(acc, a_lo, b, idesc, 1);  // N = bn: the x_hi rows only
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
+                            // 16 columns = two 8-column chunks
+                            const uint64_t a_hi = umma_desc(wa + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                            const uint64_t b_hi = umma_desc(xa + kk * 2 * (p.bn * 16), p.bn * 16, 128);
+                            const uint64_t b_lo = umma_desc(xa + xstage / 2 + kk * 2 * (p.bn * 16), p.bn * 16, 128);
+                            umma_bf16(acc, a_hi, b_hi, idesc, !(first && kk == 0));
+                            umma_bf16(acc, a_hi, b_lo, idesc, 1);
+                            if constexpr (FMT == 4) {
+                                const uint64_t a_lo =
+                                    umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
+                                umma_bf16(acc, a_lo, b_hi, idesc, 1);
+                            }
                         }
                     }
-                } else {
-#pragma unroll
-                for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
-                    // 16 columns = two 8-column chunks
-                    const uint64_t a_hi = umma_desc(wa + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
-                    const uint64_t b_hi = umma_desc(xa + kk * 2 * (p.bn * 16), p.bn * 16, 128);
-                    const uint64_t b_lo = umma_desc(xa + xstage / 2 + kk * 2 * (p.bn * 16), p.bn * 16, 128);
-                    umma_bf16(tmem, a_hi, b_hi, idesc, (i | kk) != 0);
-                    umma_bf16(tmem, a_hi, b_lo, idesc, 1);
-                    if constexpr (FMT == 4) {
-                        const uint64_t a_lo =
-                            umma_desc(wa + kGemmBM * kGemmBK * 2 + kk * 2 * (kGemmBM * 16), kGemmBM * 16, 128);
-                        umma_bf16(tmem, a_lo, b_hi, idesc, 1);
-                    }
+                    first = false;
+                    umma_commit(&s.w_empty[st]);
                 }
-                }
-                umma_commit(&s.w_empty[st]);
-                if (xi + 1 == p.xk || i + 1 == nk) umma_commit(&s.x_empty[xs]);
+                umma_commit(&s.x_empty[xs]);
             }
             umma_commit(s.acc_full);
-            // the accumulator must be complete before tensor memory is freed
+            // the accumulators must be complete before tensor memory is freed
             mbar_wait_bounded(s.acc_full, 0, p.err);
         }
     } else {
         // dequant warp d owns tile d of the row block; its loads run two k
         // steps ahead of the stores
-        const uint32_t d = warp - 2;
+        const uint32_t d = warp - 1 - kGemmMmaWarps;
         const uint32_t T = rb * 8 + d;
         RawStep r0 = load_step<FMT>(p, T, k0, lane);
         RawStep r1 = nk > 1 ? load_step<FMT>(p, T, k0 + 1, lane) : r0;
@@ -522,12 +543,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
         for (uint32_t c0 = 16 * part; c0 < p.bn; c0 += 32) {
             float v[16];
             if (nk > 0) {
+                // accumulator 0, then those of the other MMA warps that had k steps
+                const uint32_t acols = stk ? 2 * p.bn : p.bn;
                 tmem_ld16(tmem + ((q * 32) << 16) + c0, v);
                 if (stk) {  // + the x_lo columns
                     float v2[16];
                     tmem_ld16(tmem + ((q * 32) << 16) + p.bn + c0, v2);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] += v2[j];
+                }
+                for (uint32_t mw = 1; mw < p.nmma && mw < nk; ++mw) {
+                    float v3[16];
+                    tmem_ld16(tmem + ((q * 32) << 16) + mw * acols + c0, v3);
+                    if (stk) {
+                        float v4[16];
+                        tmem_ld16(tmem + ((q * 32) << 16) + mw * acols + p.bn + c0, v4);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v3[j] += v4[j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] += v3[j];
                 }
             } else {
 #pragma unroll
@@ -573,7 +608,7 @@ __global__ void gemm_reduce_kernel(const float *__restrict__ part, uint32_t spli
 // ---- host side ------------------------------------------------------------------------------
 
 struct GemmPlan {
-    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, xk, smem, off_x, off_w, tmem_cols;
+    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, xk, smem, off_x, off_w, tmem_cols, nmma;
 };
 
 static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
@@ -604,8 +639,12 @@ static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
     pl.off_x = head;
     pl.off_w = head + kGemmXSlots * xk * xst;
     pl.smem = pl.off_w + st * wst;
+    // as many MMA warps (accumulators) as fit the 512 tensor-memory columns
+    const uint32_t acols = gemm_stacked(pl.bn) ? 2 * pl.bn : pl.bn;
+    pl.nmma = kGemmMmaWarps;
+    while (pl.nmma > 1 && pl.nmma * acols > 512) pl.nmma >>= 1;
     uint32_t tc = 32;
-    while (tc < (gemm_stacked(pl.bn) ? 2 * pl.bn : pl.bn)) tc <<= 1;
+    while (tc < pl.nmma * acols) tc <<= 1;
     pl.tmem_cols = tc;
     // k splits: fill the SMs when row blocks x token tiles do not, at least 4 k steps each
     uint32_t splits = a->splits;
@@ -727,6 +766,7 @@ extern "C" int b2_gemm(const b2_gemm_args *a, void *stream)
     p.off_x = pl.off_x;
     p.off_w = pl.off_w;
     p.tmem_cols = pl.tmem_cols;
+    p.nmma = pl.nmma;
     p.err = a->err;
     cudaStream_t st = (cudaStream_t)stream;
     cudaError_t e = a->w.format == 4 ? launch_gemm<4>(p, pl, a->pdl, st) : launch_gemm<8>(p, pl, a->pdl, st);

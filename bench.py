@@ -346,6 +346,101 @@ def time_batch_decode(b2, torch, batch=32, ctx=1024, steps=10, seed=4):
             "hbm_frac": by / (ms * 1e-3) / (peak * 1e9), "step_bytes": by}
 
 
+def time_decode_config(b2, torch, shape, dtype, batch, ctx, steps=20, seed=6):
+    """Decode of another named configuration: `batch` sequences of a synthetic
+    model of `shape` (dtype 4 = q4, 8 = q8) at context ~ctx (reached by seeking;
+    the attention reads every position either way), device-loop steps timed
+    with CUDA events after 3 warm-up steps."""
+    cfg = b2.Config.make(shape["vocab"], shape["n_layers"], shape["n_heads"], shape["n_kv_heads"], shape["d_model"],
+                         shape["d_ff"], shape["max_seq"], dtype=dtype, eps=shape["eps"], theta=shape["theta"])
+    inf = b2.Infer.synth(cfg, seed, batch=batch)
+    inf.decode_batch(list(range(1, batch + 1)))
+    inf.seek(max(1, ctx - steps - 3))
+    inf.run_steps(3)
+    inf.sync()
+    st = torch.cuda.ExternalStream(inf.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    inf.run_steps(steps)
+    e1.record(st)
+    inf.sync()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    inf.close()
+    return {"batch": batch, "ctx": ctx, "dtype": "q4" if dtype == 4 else "q8", "ms_per_step": ms,
+            "tokens_per_s": batch * 1000.0 / ms}
+
+
+def time_matvec(b2, torch, rows, cols, batch, reps=40):
+    """The q4 matvec microbenchmark: W [rows x cols] (seeded N(0, 0.02), packed
+    by the reference q4 rule on the device) times `batch` vectors x ~ N(0, 1),
+    no norm, plain epilogue; weights rotated over copies covering more than L2,
+    back-to-back launches timed with CUDA events. Returns HBM GB/s of the
+    algorithmic bytes (weights + x + out) and the fraction of the measured peak."""
+    import ctypes as C
+    L = b2.lib()
+    wbytes = L.b2_q4_bytes(rows, cols)
+    nbuf = max(2, -(-300_000_000 // wbytes))
+    bufs = [torch.zeros(wbytes, dtype=torch.uint8, device="cuda") for _ in range(nbuf)]
+    for i, b in enumerate(bufs):
+        assert L.b2_q4_synth(b.data_ptr(), 0, rows, cols, 7, 200 + i, 0, 0.02, b2.ROWS_PLAIN, None) == 0
+    x = torch.randn(batch * cols, device="cuda")
+    out = torch.zeros(batch * rows, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = []
+    for b in bufs:
+        a = b2.GemvArgs()
+        a.w = b2.QWeight(b.data_ptr(), None, 4, rows, cols, rows // 16, cols // 64)
+        a.batch, a.x, a.x_stride = batch, x.data_ptr(), cols
+        a.epilogue, a.out, a.out_stride, a.err = 0, out.data_ptr(), rows, err.data_ptr()
+        args.append(a)
+    need = L.b2_gemv_scratch_bytes(C.byref(args[0]))
+    scratch = torch.zeros(max(need, 16), dtype=torch.uint8, device="cuda")
+    counters = torch.zeros(max(1, L.b2_gemv_counters_len(C.byref(args[0]))), dtype=torch.int32, device="cuda")
+    for a in args:
+        a.scratch, a.scratch_bytes = scratch.data_ptr(), need
+        a.counters, a.counters_len = counters.data_ptr(), counters.numel()
+    stream = torch.cuda.Stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(2 * nbuf):
+            assert L.b2_gemv(C.byref(args[i % nbuf]), sp) == 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            L.b2_gemv(C.byref(args[i % nbuf]), sp)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ms = e0.elapsed_time(e1) / reps
+    algo = q4_bytes(rows, cols) + 4 * batch * (cols + rows)
+    peak, _ = measured_peak()
+    gbs = algo / (ms * 1e-3) / 1e9
+    return {"rows": rows, "cols": cols, "batch": batch, "launch_us": ms * 1e3, "GB/s": gbs, "frac": gbs / peak}
+
+
+SMALL_GQA = {"vocab": 49152, "n_layers": 30, "n_heads": 9, "n_kv_heads": 3, "d_model": 576, "d_ff": 1536,
+             "max_seq": 2048, "eps": 1e-5, "theta": 10000.0}
+TINY_Q8 = {"vocab": 32000, "n_layers": 6, "n_heads": 6, "n_kv_heads": 6, "d_model": 288, "d_ff": 768,
+           "max_seq": 256, "eps": 1e-5, "theta": 10000.0}
+
+
+def other_configs(b2, torch):
+    """One line per other named workload (synthetic weights of that shape)."""
+    out = {}
+    # tiny q8 decoder: 16-token prompt + 128 greedy tokens, timed at the end of the run
+    out["tiny_q8_b1"] = time_decode_config(b2, torch, TINY_Q8, 8, 1, 16 + 128)
+    # small GQA q4 decoder near the end of its 2048 context, batch 1 and 16
+    out["small_gqa_b1"] = time_decode_config(b2, torch, SMALL_GQA, 4, 1, 2040)
+    out["small_gqa_b16"] = time_decode_config(b2, torch, SMALL_GQA, 4, 16, 2040)
+    # q4 matvec microbenchmark
+    for rows in (4096, 14336):
+        for batch in (1, 8):
+            out[f"matvec_q4_{rows}x4096_b{batch}"] = time_matvec(b2, torch, rows, 4096, batch)
+    return out
+
+
 def time_gemm(b2, torch, m=512, rows=14336 * 2, cols=4096, reps=10):
     """The tcgen05 dequant GEMM alone: m rows of x (prefill tokens or decode
     sequences) against a q4 [rows x cols] matrix in the unit layout (the
@@ -494,6 +589,7 @@ def run_b200(args, rank, world, local_rank):
     if world == 1 and not args.no_extras:
         extras["prefill_8b"] = time_prefill(b2, torch)
         extras["decode_8b_batch32"] = time_batch_decode(b2, torch)
+        extras.update(other_configs(b2, torch))
     peak, peak_kind = measured_peak()
     achieved = algo / (kms * 1e-3) / 1e9
     traffics = load_traffic()
