@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     s.item_scale = s.red + kMaxItems * kWarps * 2;
     s.cta_key = reinterpret_cast<unsigned long long *>(s.item_scale + kMaxItems);
     s.stages = dp.stages;
+    s.xready = nullptr;  // no x gate: the producer streams ahead across operations
     int *flag = reinterpret_cast<int *>(s.cta_key + kMaxItems);
     // the current operation's parameters, double-buffered: operation k is
     // copied into slot k & 1 while other warps may still read operation k - 1
