@@ -99,18 +99,21 @@ __device__ __forceinline__ void store_digits(const GemvParams &p, uint8_t *xdig,
 {
     constexpr uint32_t KW = Fmt<FMT>::kKW;
     const float vv[4] = {v.x, v.y, v.z, v.w};
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
+    // q = round(v * sc), |q| < 2^22, as balanced base-256 digits d0 + 256 d1 +
+    // 65536 d2 (each in [-128, 127]): digit i is byte i of q + 0x808080 minus
+    // 128. sc is a power of two, so v * sc is exact and adding 1.5 * 2^23
+    // rounds it to an integer in the low mantissa bits (round to nearest even,
+    // as a float-to-int conversion); byte permutes then gather the four
+    // elements' digits into one word per plane.
+    uint32_t u[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int q = finite ? __float2int_rn(__fmul_rn(vv[i], sc)) : 0;
-        const int d0 = ((q + 128) & 255) - 128;
-        const int q1 = (q - d0) >> 8;
-        const int d1 = ((q1 + 128) & 255) - 128;
-        const int d2 = (q1 - d1) >> 8;
-        w0 |= ((uint32_t)d0 & 0xFFu) << (8 * i);
-        w1 |= ((uint32_t)d1 & 0xFFu) << (8 * i);
-        w2 |= ((uint32_t)d2 & 0xFFu) << (8 * i);
-    }
+    for (int i = 0; i < 4; ++i)
+        u[i] = finite ? __float_as_uint(__fmaf_rn(vv[i], sc, 12582912.0f)) - (0x4B400000u - 0x808080u) : 0x808080u;
+    const uint32_t lo01 = __byte_perm(u[0], u[1], 0x5140), lo23 = __byte_perm(u[2], u[3], 0x5140);
+    const uint32_t hi01 = __byte_perm(u[0], u[1], 0x0062), hi23 = __byte_perm(u[2], u[3], 0x0062);
+    const uint32_t w0 = __byte_perm(lo01, lo23, 0x5410) ^ 0x80808080u;
+    const uint32_t w1 = __byte_perm(lo01, lo23, 0x7632) ^ 0x80808080u;
+    const uint32_t w2 = __byte_perm(hi01, hi23, 0x5410) ^ 0x80808080u;
     const uint32_t unit = k / KW, kk = k % KW;
     const uint32_t gi = kk >> 5, r = kk & 31;
     const uint32_t half = r >> 4, t = (r & 15) >> 2;
