@@ -203,6 +203,7 @@ _SIGS = {
     "att1_b200_infer_import_kv": (C.c_int, [_P, _U32, _U32, _SZ, _P, _P]),
     "att1_b200_infer_seek": (C.c_int, [_P, _SZ]),
     "att1_b200_infer_device_bytes": (_SZ, [_P]),
+    "att1_b200_infer_step_launches": (_SZ, [_P]),
     # backend vtable (att1_backend.h)
     "att1_backend_cuda_available": (C.c_int, []),
     "att1_backend_cuda_create": (C.c_int, [C.POINTER(_P)]),
@@ -483,3 +484,7 @@ class Infer:
 
     def device_bytes(self) -> int:
         return lib().att1_b200_infer_device_bytes(self.h)
+
+    def step_launches(self) -> int:
+        """Operations in one step of the captured CUDA graph (0 before a graph step)."""
+        return lib().att1_b200_infer_step_launches(self.h)

@@ -89,6 +89,7 @@ struct att1_infer {
     size_t mmu_slot0;
     /* decode through the tensor-core GEMM (batches the GEMVs cannot hold) */
     int use_dense;
+    size_t graph_nodes; /* operations in the captured step graph (0: not captured) */
     /* sampling: top_k <= 1 greedy; else b2_sample_topk after the step end */
     uint32_t top_k;
     float temperature;
@@ -1655,6 +1656,7 @@ static int launch_step(att1_infer_t *inf)
             }
             rc = enqueue_kernels(inf);
             if (cudaStreamEndCapture(inf->stream, &g) != cudaSuccess || rc != 0 ||
+                cudaGraphGetNodes(g, NULL, &inf->graph_nodes) != cudaSuccess ||
                 cudaGraphInstantiate(&inf->exec, g, 0) != cudaSuccess) {
                 if (g) cudaGraphDestroy(g);
                 inf->exec = NULL;
@@ -2322,6 +2324,11 @@ att1_status_t att1_b200_infer_seek(att1_infer_t *infer, size_t position)
     infer->position = position;
     infer->logits_valid = 0;
     return ATT1_OK;
+}
+
+size_t att1_b200_infer_step_launches(const att1_infer_t *infer)
+{
+    return infer != NULL && infer->exec != NULL ? infer->graph_nodes : 0;
 }
 
 /* ---- read-back for parity tests ---------------------------------------------------------------------------- */

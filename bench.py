@@ -45,6 +45,11 @@ sys.path.insert(0, os.path.join(ROOT, "att-1_b200"))
 SHAPE = dict(vocab=128256, n_layers=32, n_heads=32, n_kv_heads=8, d_model=4096, d_ff=14336,
              theta=500000.0, eps=1e-5)
 METRIC = "q4 decode tokens/s (Llama-3-8B shape, batch 1, ctx 4096)"
+WORKLOAD = "llama3-8b-shape q4 decode"
+# the Llama-70B-shaped workload: 8-way tensor parallel, batch 64 at context 8192
+SHAPE_70B = dict(vocab=128256, n_layers=80, n_heads=64, n_kv_heads=8, d_model=8192, d_ff=28672,
+                 theta=500000.0, eps=1e-5)
+METRIC_70B = "q4 decode tokens/s (Llama-70B shape, batch 64, ctx 8192)"
 
 
 def q4_bytes(r, c):
@@ -557,6 +562,7 @@ def run_b200(args, rank, world, local_rank):
     clocks = clk.stop()
     ms = e0.elapsed_time(e1) / args.steps
     pos_timed = inf.position()
+    graph_ops = inf.step_launches()  # operations in one step of the captured graph (0 without graphs)
 
     # end to end through att1_infer_decode_token / att1_b200_infer_decode_batch
     toks = inf.decode_batch(np.asarray(tok))
@@ -593,10 +599,12 @@ def run_b200(args, rank, world, local_rank):
     peak, peak_kind = measured_peak()
     achieved = algo / (kms * 1e-3) / 1e9
     traffics = load_traffic()
-    bytes_step = step_bytes(pos_timed - args.steps // 2, args.batch)
-    gemv_line = {"kernel": "gemv_q4 gate/up 28672x4096 (RMSNorm+SwiGLU fused), standalone launches",
+    bytes_step = step_bytes(pos_timed - args.steps // 2, args.batch, dict(SHAPE, n_layers=args.layers))
+    gemv_line = {"kernel": f"gemv_q4 gate/up {2 * SHAPE['d_ff']}x{SHAPE['d_model']} (RMSNorm+SwiGLU fused), "
+                           "standalone launches",
                  "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                 "traffic": traffics.get("gemv_q4_gateup_28672x4096"), "algorithmic_bytes": algo, "launch_ms": kms}
+                 "traffic": traffics.get(f"gemv_q4_gateup_{2 * SHAPE['d_ff']}x{SHAPE['d_model']}"),
+                 "algorithmic_bytes": algo, "launch_ms": kms}
     if persistent:
         # the step is one launch of the decode kernel: its algorithmic bytes are the step's
         step_achieved = bytes_step / (ms * 1e-3) / 1e9
@@ -618,18 +626,19 @@ def run_b200(args, rank, world, local_rank):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak" if args.replicas else "strong", "vs_baseline": None, "dtype": "q4xf32",
-            "data": "synthetic (seeded N(0,0.02) weights quantised on device; random 512-token prompt)",
-            "config": {"workload": "llama3-8b-shape q4 decode", "global_batch": args.batch * (world if args.replicas else 1),
+            "data": (f"synthetic (seeded N(0,0.02) weights quantised on device; random {args.prompt}-token prompt"
+                     + ("; context reached by seeking)" if args.seek_fill else ")")),
+            "config": {"workload": WORKLOAD, "global_batch": args.batch * (world if args.replicas else 1),
                        "seq_len": ctx, "context_at_timed_steps": pos_timed,
                        "parallelism": (f"replicas{world}" if args.replicas else f"tp{world}"),
                        "tp_exchange": None if world == 1 or args.replicas else args.tp_exchange,
                        "step_launch": "one persistent kernel" if persistent else "kernel sequence (CUDA graph)",
-                       "l2": "inputs larger than L2 (5.8 GB streamed per step)",
+                       "l2": f"inputs larger than L2 ({bytes_step / 1e9:.1f} GB streamed per step)",
                        "step_bytes": bytes_step,
                        "step_hbm_frac": bytes_step / (ms * 1e-3) / (peak * 1e9 * (1 if args.replicas else world))},
             "e2e": {"value": args.batch * 1000.0 / e2e_ms * (world if args.replicas else 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch + 4},
-            "gpu_launches": args.steps * (1 if persistent else 3 + 5 * args.layers),
+            "gpu_launches": args.steps * (1 if persistent else (graph_ops or 3 + 5 * args.layers)),
             "roofline": roofline,
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -678,6 +687,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
+    ap.add_argument("--shape", default="8b", choices=["8b", "70b"],
+                    help="70b: the Llama-70B-shaped workload (batch 64, context 8192, tensor parallel over the "
+                         "launched ranks, context reached by seeking, no CPU leg or side measurements)")
     ap.add_argument("--no-extras", action="store_true", help="skip the prefill and batch-32 side measurements")
     ap.add_argument("--seek-fill", action="store_true",
                     help="reach the timed context by seeking instead of decoding (short runs, e.g. under ncu)")
@@ -693,9 +705,18 @@ def main():
     ap.add_argument("--kernel-only", nargs="?", const="gemv", choices=["gemv", "attn", "gemm"],
                     help="time only one kernel and print it (for ncu captures): the gate/up GEMV (default), the "
                          "attention at context 4096, or the tcgen05 GEMM at the gate/up shape for --batch rows")
-    ap.add_argument("--layers", type=int, default=SHAPE["n_layers"],
-                    help="decoder depth (profiling runs only; the metric is defined at 32)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder depth (profiling and functional runs only; the metric is defined at the shape's "
+                         "depth: 32 for 8b, 80 for 70b)")
     args = ap.parse_args()
+    if args.shape == "70b":
+        global METRIC, WORKLOAD
+        SHAPE.update(SHAPE_70B)
+        METRIC, WORKLOAD = METRIC_70B, "llama-70b-shape q4 decode"
+        args.batch, args.ctx, args.prompt = 64, 8192, 8
+        args.seek_fill, args.no_cpu, args.no_extras = True, True, True
+    if args.layers is None:
+        args.layers = SHAPE["n_layers"]
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

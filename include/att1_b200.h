@@ -171,6 +171,10 @@ att1_status_t att1_b200_infer_import_kv(att1_infer_t *infer, uint32_t item, uint
  * hold KV (decoded or imported). Tensor-parallel ranks seek together. Not on a
  * context using a KV-MMU. */
 att1_status_t att1_b200_infer_seek(att1_infer_t *infer, size_t position);
+/* Operations (kernel launches and the copies captured with them) in one step
+ * of the context's CUDA graph, once a step has run with graphs on; 0 before
+ * that or without graphs. No reference counterpart. */
+size_t att1_b200_infer_step_launches(const att1_infer_t *infer);
 /* Device bytes held by the context (weights, KV pages, buffers). */
 size_t att1_b200_infer_device_bytes(const att1_infer_t *infer);
 

@@ -159,17 +159,18 @@ def test_import_kv_round_trip_and_limits(b2):
         inf.close()
 
 
-def test_attention_8b_heads_context_4096(b2):
-    """b2_attn alone at the 8B attention shape: 32 query heads on 8 KV heads
-    of 128, two sequences at positions 4095 and 2047 of a 4096-position
-    capacity (so the grid has all its position splits), pages of 64 tokens in
-    a shuffled order, against a float64 attention: max error <= 1e-5 of the
-    largest output."""
+@pytest.mark.parametrize("H", [32, 64])
+def test_attention_8b_heads_context_4096(b2, H):
+    """b2_attn alone at the 8B attention shape (32 query heads on 8 KV heads of
+    128) and the 70B one (64 on 8: eight query heads per KV head), two
+    sequences at positions 4095 and 2047 of a 4096-position capacity (so the
+    grid has all its position splits), pages of 64 tokens in a shuffled order,
+    against a float64 attention: max error <= 1e-5 of the largest output."""
     import ctypes as C
 
     import torch
     L = b2.lib()
-    H, Hkv, hd, T, cap, B = 32, 8, 128, 64, 4096, 2
+    Hkv, hd, T, cap, B = 8, 128, 64, 4096, 2
     pps = cap // T
     rng = np.random.default_rng(17)
     pages = rng.permutation(B * pps).astype(np.int32)
