@@ -16,7 +16,8 @@
 // point plus f32 summation, far inside the 1e-3 logits tolerance.
 //
 // Work split. CTA (row block, token tile, k split) computes a 128-row x BN-token
-// tile of Y over a range of 64-column k steps:
+// tile of Y over a range of 64-column k steps (for BN <= 64: two 128-row blocks,
+// each with its own MMA warps, dequant warps and accumulators; below for one):
 //   warp 0      allocates tensor memory and streams the prepared X tiles
 //               (b2_gemm_prep writes them in the MMA operand layout, k steps of
 //               a token tile contiguous) into two slots of xk k steps each, one
@@ -55,8 +56,12 @@ constexpr uint32_t kGemmBM = 128;          // output rows per CTA (8 tiles of 16
 constexpr uint32_t kGemmBK = 64;           // columns per k step
 constexpr uint32_t kGemmMaxBN = 256;       // tokens per CTA tile
 constexpr int kGemmDequantWarps = 8;      // one 16-row tile each
-constexpr int kGemmMmaWarps = 2;          // MMA issuers (up to), round-robin k steps, one accumulator each
-constexpr int kGemmThreads = 32 + 32 * kGemmMmaWarps + 32 * kGemmDequantWarps;  // + TMEM/X-copy warp
+constexpr int kGemmMmaWarps = 2;          // MMA issuers per 128-row block, alternate k steps, one accumulator each
+// threads of a CTA over RBM 128-row blocks: the TMEM/X-copy warp, the MMA
+// warps and the dequantising warps of every row block
+template <int RBM>
+__host__ __device__ constexpr int gemm_threads() { return 32 + 32 * kGemmMmaWarps * RBM + 32 * kGemmDequantWarps * RBM; }
+constexpr uint32_t kGemmRb2MaxBn = 64;     // token tiles up to this size take two row blocks per CTA
 constexpr uint32_t kGemmMaxStages = 6;      // W ring
 constexpr uint32_t kGemmXSlots = 2;         // X ring
 constexpr uint32_t kGemmXCopy = 32768;      // target bytes per X bulk copy
@@ -103,7 +108,8 @@ struct GemmParams {
     float *part;            // [splits][m][rows] when splits > 1
     uint32_t splits, ksplit;  // k steps per split
     uint32_t stages;        // W ring stages (one k step each)
-    uint32_t nmma;          // MMA warps in use (accumulators)
+    uint32_t nmma;          // MMA warps in use (accumulators): kGemmMmaWarps per row block
+    uint32_t rbm;           // 128-row blocks per CTA (1 or 2)
     uint32_t xk;            // k steps per X slot (one bulk copy)
     uint32_t off_x, off_w, tmem_cols;
     int32_t *err;
@@ -403,8 +409,8 @@ __device__ __forceinline__ void dequant_store(const RawStep &raw, uint8_t *wst, 
     }
 }
 
-template <int FMT>
-__global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmParams p)
+template <int FMT, int RBM>
+__global__ void __launch_bounds__(gemm_threads<RBM>(), 1) att1_qgemm_kernel(const GemmParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
     const GemmSmem s = gemm_smem(smem, p);
@@ -414,7 +420,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
     const uint32_t k1 = min(p.ksteps, k0 + p.ksplit);
     const uint32_t nk = k1 > k0 ? k1 - k0 : 0;
     const uint32_t xstage = gemm_x_stage_bytes(p.bn);
-    constexpr uint32_t wstage = gemm_w_stage_bytes(FMT);
+    constexpr uint32_t wst1 = gemm_w_stage_bytes(FMT);  // one row block's part of a W stage
+    constexpr uint32_t wstage = RBM * wst1;
 
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < kGemmXSlots; ++i) {
@@ -422,8 +429,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
             mbar_init(&s.x_empty[i], p.nmma);
         }
         for (uint32_t i = 0; i < kGemmMaxStages; ++i) {
-            mbar_init(&s.w_full[i], 32 * kGemmDequantWarps);
-            mbar_init(&s.w_empty[i], 1);
+            mbar_init(&s.w_full[i], 32 * kGemmDequantWarps * RBM);
+            mbar_init(&s.w_empty[i], RBM);  // one commit per row block's MMA warp of the k step
         }
         mbar_init(s.acc_full, p.nmma);
         fence_mbar_init();
@@ -450,10 +457,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
                          steps * xstage, &s.x_full[xs]);
             }
         }
-    } else if (warp <= (uint32_t)kGemmMmaWarps) {
-        // MMA warp mw issues k steps mw, mw + kGemmMmaWarps, ... into its own
-        // accumulator (columns mw * acols); every MMA warp releases every X slot
-        const uint32_t mw = warp - 1, nmma = p.nmma;
+    } else if (warp <= (uint32_t)(kGemmMmaWarps * RBM)) {
+        // MMA warp mw works on row block h = mw / 2 and issues k steps of parity
+        // mw % 2 into its own accumulator (columns mw * acols); every MMA warp
+        // releases every X slot
+        const uint32_t mw = warp - 1, nmma = p.nmma, h = mw / kGemmMmaWarps, par = mw % kGemmMmaWarps;
         if (lane == 0 && mw < nmma) {
             const bool stk = gemm_stacked(p.bn);
             const uint32_t acols = stk ? 2 * p.bn : p.bn;
@@ -471,12 +479,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
                 mbar_wait_bounded(&s.x_full[xs], (j / kGemmXSlots) & 1, p.err);
                 const uint32_t i_end = min(nk, (j + 1) * p.xk);
                 uint32_t i = j * p.xk;
-                i += (mw + nmma - i % nmma) % nmma;  // first k step of this warp
-                for (; i < i_end; i += nmma) {
+                i += (par + kGemmMmaWarps - i % kGemmMmaWarps) % kGemmMmaWarps;  // first k step of this warp
+                for (; i < i_end; i += kGemmMmaWarps) {
                     const uint32_t st = i % p.stages, pass = i / p.stages, xi = i % p.xk;
                     mbar_wait_bounded(&s.w_full[st], pass & 1, p.err);
                     tc_fence_after();
-                    const uint32_t xa = xb + (xs * p.xk + xi) * xstage, wa = wb + st * wstage;
+                    const uint32_t xa = xb + (xs * p.xk + xi) * xstage, wa = wb + st * wstage + h * wst1;
                     if (stk) {
 #pragma unroll
                         for (uint32_t kk = 0; kk < kGemmBK / 16; ++kk) {
@@ -518,8 +526,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
     } else {
         // dequant warp d owns tile d of the row block; its loads run two k
         // steps ahead of the stores
-        const uint32_t d = warp - 1 - kGemmMmaWarps;
-        const uint32_t T = rb * 8 + d;
+        const uint32_t d = warp - 1 - kGemmMmaWarps * RBM;  // 0 .. 8 * RBM - 1
+        const uint32_t T = rb * 8 * RBM + d;
         RawStep r0 = load_step<FMT>(p, T, k0, lane);
         RawStep r1 = nk > 1 ? load_step<FMT>(p, T, k0 + 1, lane) : r0;
         for (uint32_t i = 0; i < nk; ++i) {
@@ -528,14 +536,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
             r0 = r1;
             if (i + 2 < nk) r1 = load_step<FMT>(p, T, k0 + i + 2, lane);
             if (pass > 0) mbar_wait_bounded(&s.w_empty[st], (pass - 1) & 1, p.err);
-            dequant_store<FMT>(cur, s.w + st * wstage, d, lane);
+            dequant_store<FMT>(cur, s.w + st * wstage + (d / 8) * wst1, d % 8, lane);
             fence_proxy_async();
             mbar_arrive(&s.w_full[st]);
         }
         // epilogue: TMEM lane = output row, column = token
         // (two warps per TMEM lane quarter take alternate 16-column chunks)
-        const uint32_t q = warp & 3, part = d >> 2;
-        const uint32_t o = rb * kGemmBM + q * 32 + lane;
+        // warp w reads TMEM lanes 32*(w%4)..; among the dequant warps of one lane
+        // quarter, j = d / 4 picks the row block (j % RBM) and the half of the
+        // 16-column chunks (j / RBM)
+        const uint32_t q = warp & 3, j4 = d >> 2, h = j4 % RBM, part = j4 / RBM;
+        const uint32_t o = (rb * RBM + h) * kGemmBM + q * 32 + lane;
         const bool ok = nk == 0 || mbar_wait_bounded(s.acc_full, 0, p.err);
         tc_fence_after();
         const float rs = (FMT == 8 && o < p.rows) ? __ldg(p.row_scale + o) : 1.0f;
@@ -543,21 +554,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) att1_qgemm_kernel(const GemmP
         for (uint32_t c0 = 16 * part; c0 < p.bn; c0 += 32) {
             float v[16];
             if (nk > 0) {
-                // accumulator 0, then those of the other MMA warps that had k steps
+                // the row block's first accumulator, then its second if that
+                // MMA warp had k steps
                 const uint32_t acols = stk ? 2 * p.bn : p.bn;
-                tmem_ld16(tmem + ((q * 32) << 16) + c0, v);
+                const uint32_t a0 = h * kGemmMmaWarps * acols;
+                tmem_ld16(tmem + ((q * 32) << 16) + a0 + c0, v);
                 if (stk) {  // + the x_lo columns
                     float v2[16];
-                    tmem_ld16(tmem + ((q * 32) << 16) + p.bn + c0, v2);
+                    tmem_ld16(tmem + ((q * 32) << 16) + a0 + p.bn + c0, v2);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] += v2[j];
                 }
-                for (uint32_t mw = 1; mw < p.nmma && mw < nk; ++mw) {
+                for (uint32_t a = 1; a < (uint32_t)kGemmMmaWarps && a < nk; ++a) {
                     float v3[16];
-                    tmem_ld16(tmem + ((q * 32) << 16) + mw * acols + c0, v3);
+                    tmem_ld16(tmem + ((q * 32) << 16) + a0 + a * acols + c0, v3);
                     if (stk) {
                         float v4[16];
-                        tmem_ld16(tmem + ((q * 32) << 16) + mw * acols + p.bn + c0, v4);
+                        tmem_ld16(tmem + ((q * 32) << 16) + a0 + a * acols + p.bn + c0, v4);
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v3[j] += v4[j];
                     }
@@ -608,16 +621,22 @@ __global__ void gemm_reduce_kernel(const float *__restrict__ part, uint32_t spli
 // ---- host side ------------------------------------------------------------------------------
 
 struct GemmPlan {
-    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, xk, smem, off_x, off_w, tmem_cols, nmma;
+    uint32_t ntiles, bn, row_blocks, ksteps, splits, ksplit, stages, xk, smem, off_x, off_w, tmem_cols, nmma, rbm;
 };
 
 static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
 {
     const b2_qweight &w = a->w;
     gemm_token_tiles(a->m, pl.ntiles, pl.bn);
-    pl.row_blocks = (w.tiles + 7) / 8;
+    // small token tiles (decode batches): two 128-row blocks per CTA, so each k
+    // step of the stage protocol carries twice the weights (the MMA issue and
+    // the stage round trip, not the weight bytes, pace a k step there); their
+    // four accumulators fit the 512 tensor-memory columns up to kGemmRb2MaxBn
+    const uint32_t acols = gemm_stacked(pl.bn) ? 2 * pl.bn : pl.bn;
+    pl.rbm = (pl.bn <= kGemmRb2MaxBn && 2 * kGemmMmaWarps * acols <= 512) ? 2 : 1;
+    pl.row_blocks = (w.tiles + 8 * pl.rbm - 1) / (8 * pl.rbm);
     pl.ksteps = (w.cols + kGemmBK - 1) / kGemmBK;
-    const uint32_t xst = gemm_x_stage_bytes(pl.bn), wst = gemm_w_stage_bytes(w.format);
+    const uint32_t xst = gemm_x_stage_bytes(pl.bn), wst = pl.rbm * gemm_w_stage_bytes(w.format);
     const uint32_t head = 1024;  // mbarriers + TMEM slot, then 1 KB-aligned rings
     // X: two slots of xk k steps (about kGemmXCopy bytes per bulk copy: an SM
     // completes bulk copies at a bounded rate whatever their size); W: the rest
@@ -628,7 +647,8 @@ static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
     for (;; xk = xk > 1 ? xk / 2 : 0) {
         if (xk == 0) return false;
         const uint32_t xbytes = kGemmXSlots * xk * xst;
-        if (head + xbytes + 2 * wst <= kGemmSmemLimit) {
+        // at least two W stages; with two row blocks, a third before larger X copies
+        if (head + xbytes + (pl.rbm == 2 && xk > 1 ? 3 : 2) * wst <= kGemmSmemLimit) {
             st = (kGemmSmemLimit - head - xbytes) / wst;
             break;
         }
@@ -639,10 +659,9 @@ static bool plan_gemm(const b2_gemm_args *a, GemmPlan &pl)
     pl.off_x = head;
     pl.off_w = head + kGemmXSlots * xk * xst;
     pl.smem = pl.off_w + st * wst;
-    // as many MMA warps (accumulators) as fit the 512 tensor-memory columns
-    const uint32_t acols = gemm_stacked(pl.bn) ? 2 * pl.bn : pl.bn;
-    pl.nmma = kGemmMmaWarps;
-    while (pl.nmma > 1 && pl.nmma * acols > 512) pl.nmma >>= 1;
+    // kGemmMmaWarps accumulators per row block (2 * 256 columns at most with one)
+    pl.nmma = kGemmMmaWarps * pl.rbm;
+    if (pl.nmma * acols > 512) return false;
     uint32_t tc = 32;
     while (tc < pl.nmma * acols) tc <<= 1;
     pl.tmem_cols = tc;
@@ -678,17 +697,17 @@ static int gemm_check(const b2_gemm_args *a)
     return 0;
 }
 
-template <int FMT>
+template <int FMT, int RBM>
 static cudaError_t launch_gemm(const GemmParams &p, const GemmPlan &pl, int pdl, cudaStream_t st)
 {
-    auto fn = att1_qgemm_kernel<FMT>;
+    auto fn = att1_qgemm_kernel<FMT, RBM>;
     // the whole shared-memory window (one CTA per SM either way): operand reads
     // of the tensor cores stay inside the CTA's allocation whatever the stage count
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmemLimit);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.row_blocks, pl.ntiles, pl.splits);
-    cfg.blockDim = dim3(kGemmThreads);
+    cfg.blockDim = dim3(gemm_threads<RBM>());
     cfg.dynamicSmemBytes = kGemmSmemLimit;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -767,9 +786,11 @@ extern "C" int b2_gemm(const b2_gemm_args *a, void *stream)
     p.off_w = pl.off_w;
     p.tmem_cols = pl.tmem_cols;
     p.nmma = pl.nmma;
+    p.rbm = pl.rbm;
     p.err = a->err;
     cudaStream_t st = (cudaStream_t)stream;
-    cudaError_t e = a->w.format == 4 ? launch_gemm<4>(p, pl, a->pdl, st) : launch_gemm<8>(p, pl, a->pdl, st);
+    cudaError_t e = a->w.format == 4 ? (pl.rbm == 2 ? launch_gemm<4, 2>(p, pl, a->pdl, st) : launch_gemm<4, 1>(p, pl, a->pdl, st))
+                                     : (pl.rbm == 2 ? launch_gemm<8, 2>(p, pl, a->pdl, st) : launch_gemm<8, 1>(p, pl, a->pdl, st));
     if (e != cudaSuccess) return -8;
     if (pl.splits > 1) {
         const size_t total = (size_t)a->m * a->w.rows;
