@@ -164,7 +164,7 @@ __device__ __forceinline__ void consumer_sync()
 // scale, from the item's sum of squares and max |x * w| (max |x| without a norm).
 template <int FMT>
 __device__ __forceinline__ void item_setup(const GemvParams &p, uint32_t b, float ss, float mw, float *inv_out,
-                                           float *sc_out, bool *finite_out, float *item_scale)
+                                           float *sc_out, bool *finite_out, float *item_scale, bool writer)
 {
     float inv = 1.0f, bound = mw;
     if (p.norm_w != nullptr) {
@@ -177,13 +177,13 @@ __device__ __forceinline__ void item_setup(const GemvParams &p, uint32_t b, floa
     *inv_out = inv;
     *sc_out = ldexpf(1.0f, -E);
     *finite_out = finite;
-    if (threadIdx.x == 0) {
+    if (writer) {
         item_scale[b] = ldexpf(1.0f, E - (FMT == 4 ? 4 : 0));
         if (!finite) raise_error(p.err, B2_ERR_NONFINITE);
     }
 }
 
-template <int FMT>
+template <int FMT, int NI>
 __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale, float *red)
 {
     const uint32_t cols = p.cols;
@@ -226,7 +226,7 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
         }
         float inv, sc;
         bool finite;
-        item_setup<FMT>(p, 0, tss, tmw, &inv, &sc, &finite, item_scale);
+        item_setup<FMT>(p, 0, tss, tmw, &inv, &sc, &finite, item_scale, threadIdx.x == 0);
 #pragma unroll
         for (int i = 0; i < kPrologueVec; ++i) {
             const uint32_t k = threadIdx.x * 4 + i * stride;
@@ -234,37 +234,110 @@ __device__ void prepare_x(const GemvParams &p, uint8_t *xdig, float *item_scale,
         }
         return;
     }
-    // general path: statistics of every item in one reduction round, then the digits
-    float *stats = red;  // [kMaxItems][kWarps][2]
-    for (uint32_t b = 0; b < p.batch; ++b) {
+    if constexpr (NI == 1) {
+        // one or two items (the decode kernels of batch 1 and 2): the items one
+        // after another. This instantiation also runs the batch-1 step, whose
+        // kernel stays as small as it was (the wider path below, compiled into it,
+        // made the batch-1 step 8 % slower).
+        float *stats = red;  // [kMaxItems][kWarps][2]
+        for (uint32_t b = 0; b < p.batch; ++b) {
+            float ss = 0.0f, mw = 0.0f;
+            for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+                const float4 v = load_x4(p, b, k);
+                ss += sumsq4(v);
+                mw = fmaxf(mw, absmax4(norm ? mul4(v, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k))) : v));
+            }
+            ss = warp_sum(ss);
+            mw = warp_max(mw);
+            if (lane == 0) {
+                stats[(b * kWarps + warp) * 2] = ss;
+                stats[(b * kWarps + warp) * 2 + 1] = mw;
+            }
+        }
+        consumer_sync();
+        for (uint32_t b = 0; b < p.batch; ++b) {
+            float tss = 0.0f, tmw = 0.0f;
+    #pragma unroll
+            for (int i = 0; i < kWarps; ++i) {
+                tss += stats[(b * kWarps + i) * 2];
+                tmw = fmaxf(tmw, stats[(b * kWarps + i) * 2 + 1]);
+            }
+            float inv, sc;
+            bool finite;
+            item_setup<FMT>(p, b, tss, tmw, &inv, &sc, &finite, item_scale, threadIdx.x == 0);
+            for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
+                float4 v = load_x4(p, b, k);
+                if (norm) v = normed(v, inv, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)));
+                store_digits<FMT>(p, xdig, b, k, v, sc, finite);
+            }
+        }
+    } else {
+        // general path (several items, or a row longer than the registers hold):
+        // the items side by side, kConsumers / Bp threads (whole warps) each, Bp the
+        // batch rounded up to a power of two. One pass of loads for every item, the
+        // item's statistics from its own warps in warp order, then the digits, from
+        // registers when a thread's share of the row fits them. (Taking the items
+        // one after another costs a load round trip and a reduction per item.)
+        uint32_t Bp = 1;
+        while (Bp < p.batch) Bp <<= 1;
+        const uint32_t TPI = kConsumers / Bp, wpi = TPI / 32;
+        const uint32_t b = threadIdx.x / TPI, u = threadIdx.x % TPI;
+        const bool live = b < p.batch;
+        const uint32_t istride = TPI * 4;
+        const bool held = cols <= istride * kPrologueVec;
+        float *stats = red;  // [kWarps][2]
         float ss = 0.0f, mw = 0.0f;
-        for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-            const float4 v = load_x4(p, b, k);
-            ss += sumsq4(v);
-            mw = fmaxf(mw, absmax4(norm ? mul4(v, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k))) : v));
+        float4 v[kPrologueVec], w[kPrologueVec];
+        if (held) {
+    #pragma unroll
+            for (int i = 0; i < kPrologueVec; ++i) {
+                const uint32_t k = u * 4 + i * istride;
+                const bool in = live && k < cols;
+                v[i] = in ? load_x4(p, b, k) : make_float4(0, 0, 0, 0);
+                w[i] = (in && norm) ? __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)) : make_float4(1, 1, 1, 1);
+            }
+    #pragma unroll
+            for (int i = 0; i < kPrologueVec; ++i) {
+                ss += sumsq4(v[i]);
+                mw = fmaxf(mw, absmax4(norm ? mul4(v[i], w[i]) : v[i]));
+            }
+        } else if (live) {
+    #pragma unroll 4
+            for (uint32_t k = u * 4; k < cols; k += istride) {
+                const float4 x = load_x4(p, b, k);
+                ss += sumsq4(x);
+                mw = fmaxf(mw, absmax4(norm ? mul4(x, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k))) : x));
+            }
         }
         ss = warp_sum(ss);
         mw = warp_max(mw);
         if (lane == 0) {
-            stats[(b * kWarps + warp) * 2] = ss;
-            stats[(b * kWarps + warp) * 2 + 1] = mw;
+            stats[warp * 2] = ss;
+            stats[warp * 2 + 1] = mw;
         }
-    }
-    consumer_sync();
-    for (uint32_t b = 0; b < p.batch; ++b) {
+        consumer_sync();
+        if (!live) return;
         float tss = 0.0f, tmw = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kWarps; ++i) {
-            tss += stats[(b * kWarps + i) * 2];
-            tmw = fmaxf(tmw, stats[(b * kWarps + i) * 2 + 1]);
+        for (uint32_t j = 0; j < wpi; ++j) {
+            tss += stats[(b * wpi + j) * 2];
+            tmw = fmaxf(tmw, stats[(b * wpi + j) * 2 + 1]);
         }
         float inv, sc;
         bool finite;
-        item_setup<FMT>(p, b, tss, tmw, &inv, &sc, &finite, item_scale);
-        for (uint32_t k = threadIdx.x * 4; k < cols; k += stride) {
-            float4 v = load_x4(p, b, k);
-            if (norm) v = normed(v, inv, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)));
-            store_digits<FMT>(p, xdig, b, k, v, sc, finite);
+        item_setup<FMT>(p, b, tss, tmw, &inv, &sc, &finite, item_scale, u == 0);
+        if (held) {
+    #pragma unroll
+            for (int i = 0; i < kPrologueVec; ++i) {
+                const uint32_t k = u * 4 + i * istride;
+                if (k < cols) store_digits<FMT>(p, xdig, b, k, norm ? normed(v[i], inv, w[i]) : v[i], sc, finite);
+            }
+        } else {
+    #pragma unroll 4
+            for (uint32_t k = u * 4; k < cols; k += istride) {
+                float4 x = load_x4(p, b, k);
+                if (norm) x = normed(x, inv, __ldg(reinterpret_cast<const float4 *>(p.norm_w + k)));
+                store_digits<FMT>(p, xdig, b, k, x, sc, finite);
+            }
         }
     }
 }
@@ -550,7 +623,7 @@ __device__ void gemv_consume(const GemvParams &p, const GemvSmem &s, uint32_t &i
     if (t0 == t1) return;  // no tiles for this CTA
     const uint32_t parts_n = p.round_tiles * kWarps * SB;
     if (!prezeroed) gemv_zero_round(p, s);
-    prepare_x<FMT>(p, s.xdig, s.item_scale, s.red);
+    prepare_x<FMT, NI>(p, s.xdig, s.item_scale, s.red);
     consumer_sync();
     if (s.xready != nullptr && threadIdx.x == 0) mbar_arrive(s.xready);
 
